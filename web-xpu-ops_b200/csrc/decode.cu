@@ -1,0 +1,699 @@
+// decode.cu — the resident Q8 Llama decode step (llm/engine-q8-resident.ts
+// `runDecodeStep`, :1774-1892) as one CUDA graph per engine.
+//
+// Per token the graph runs, in stream order (each kernel may start early
+// under programmatic dependent launch and waits before reading its inputs):
+//   embed      hidden = gatherDequantRows(embed, token)        (weights-q8.ts:207-222)
+//   per layer  qkv   = [wq;wk;wv] . rmsnorm(hidden)  + RoPE on q,k, K/V -> cache[pos]
+//              attn  = grouped attention over cache[0..pos]  (ops/gqa, sEff = pos+1)
+//              hidB  = hidden + wo . attn                    (matvecQ8Residual)
+//              gated = silu(wg . rmsnorm(hidB)) * (wu . ...) (matvecQ8Ffn)
+//              hidden= hidB + wdown . gated                  (matvecQ8Residual)
+//   head       logits = lm_head . rmsnorm(hidden)
+//   argmax     next token (llm/engine.ts:226-232); the position advances.
+// The token and the position live in device memory, so the captured graph is
+// replayed unchanged for every token.
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "matvec_launch.cuh"
+
+namespace xpu {
+
+int pack_q8_dev_i8(const int8_t* codes, int64_t N, int64_t K, uint32_t* packed, cudaStream_t s);
+
+namespace {
+
+// --------------------------------------------------------------- kernels --
+__global__ void embed_kernel(const int8_t* __restrict__ codes, const float* __restrict__ scale, int vocab, int hidden,
+                             const int32_t* __restrict__ token, float* __restrict__ out) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int t = *token;
+  const bool ok = t >= 0 && t < vocab;  // out-of-range ids gather zeros
+  const double s = ok ? (double)scale[t] : 0.0;
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x)
+    out[c] = ok ? (float)((double)codes[(int64_t)t * hidden + c] * s) : 0.0f;
+}
+
+struct AttnParams {
+  const float* q;  // [H * hd], roped
+  const float* kcache;
+  const float* vcache;  // [kvH, S, hd]
+  const int32_t* pos;
+  float* part_m;    // [H][nsplit]
+  float* part_l;    // [H][nsplit]
+  float* part_acc;  // [H][nsplit][hd]
+  unsigned int* counter;  // [kvH], zero between launches
+  float* out;             // [H * hd]
+  int H, kvH, hd, S, nsplit, chunk_max;
+  float scale;
+};
+
+// One CTA per (kv head, position split): the G = H / kvH query heads that
+// share the kv head (ops/gqa/reference.ts:199-201) read each K/V row once.
+// Partial softmax statistics go to scratch; the last CTA of a kv head (an
+// atomic ticket, no waiting) merges the splits.
+__global__ void __launch_bounds__(256) attn_decode_kernel(AttnParams a) {
+  extern __shared__ float sm[];
+  const int g = blockIdx.x, sp = blockIdx.y;
+  const int G = a.H / a.kvH, hd = a.hd;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, nw = blockDim.x / 32;
+  float* q_s = sm;                   // [G][hd]
+  float* p_s = q_s + G * hd;         // [G][chunk_max]
+  float* stat = p_s + G * a.chunk_max;  // [G][2]
+  __shared__ unsigned int is_last;
+
+  griddep_launch_dependents();
+  griddep_wait();
+  const int L = *a.pos + 1;  // sEff: positions 0..pos are resident
+  const int chunk = (L + a.nsplit - 1) / a.nsplit;
+  const int j0 = sp * chunk, j1 = min(L, j0 + chunk), n = max(0, j1 - j0);
+
+  for (int i = tid; i < G * hd; i += blockDim.x) q_s[i] = a.q[(g * G) * hd + i];
+  __syncthreads();
+
+  // scores: a warp per position, lanes across the head dimension
+  const float* kb = a.kcache + (int64_t)g * a.S * hd;
+  for (int j = j0 + warp; j < j1; j += nw) {
+    const float* kr = kb + (int64_t)j * hd;
+    for (int h = 0; h < G; ++h) {
+      float d = 0.0f;
+      for (int c = lane; c < hd; c += 32) d = fmaf(q_s[h * hd + c], kr[c], d);
+      d = warp_sum(d);
+      if (lane == 0) p_s[h * a.chunk_max + (j - j0)] = d * a.scale;
+    }
+  }
+  __syncthreads();
+  // per-head max and sum of exp over this split
+  for (int h = warp; h < G; h += nw) {
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, p_s[h * a.chunk_max + j]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.0f;
+    for (int j = lane; j < n; j += 32) {
+      float e = expf(p_s[h * a.chunk_max + j] - m);
+      p_s[h * a.chunk_max + j] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      stat[2 * h] = m;
+      stat[2 * h + 1] = l;
+    }
+  }
+  __syncthreads();
+  const float* vb = a.vcache + (int64_t)g * a.S * hd;
+  for (int i = tid; i < G * hd; i += blockDim.x) {
+    const int h = i / hd, c = i % hd;
+    float acc = 0.0f;
+    for (int j = 0; j < n; ++j) acc = fmaf(p_s[h * a.chunk_max + j], vb[(int64_t)(j0 + j) * hd + c], acc);
+    const int hh = g * G + h;
+    a.part_acc[((int64_t)hh * a.nsplit + sp) * hd + c] = acc;
+    if (c == 0) {
+      a.part_m[hh * a.nsplit + sp] = n > 0 ? stat[2 * h] : -INFINITY;
+      a.part_l[hh * a.nsplit + sp] = n > 0 ? stat[2 * h + 1] : 0.0f;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = atomicAdd(&a.counter[g], 1u) == (unsigned)(a.nsplit - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int i = tid; i < G * hd; i += blockDim.x) {
+    const int h = g * G + i / hd, c = i % hd;
+    float M = -INFINITY;
+    for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, __ldcg(&a.part_m[h * a.nsplit + s]));
+    float l = 0.0f, o = 0.0f;
+    for (int s = 0; s < a.nsplit; ++s) {
+      float m = __ldcg(&a.part_m[h * a.nsplit + s]);
+      if (m == -INFINITY) continue;
+      float w = expf(m - M);
+      l = fmaf(__ldcg(&a.part_l[h * a.nsplit + s]), w, l);
+      o = fmaf(__ldcg(&a.part_acc[((int64_t)h * a.nsplit + s) * hd + c]), w, o);
+    }
+    a.out[h * hd + c] = o / l;
+  }
+  if (tid == 0) a.counter[g] = 0;
+}
+
+// Greedy next token (llm/engine.ts:226-232: the first maximal index; values
+// that are NaN never win, and a NaN at index 0 makes the answer 0 because
+// nothing compares greater than it), then the step's bookkeeping: the token
+// is logged at gen[pos], becomes the next step's input, and the position
+// advances.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int n, int32_t* next,
+                                                       int32_t* cur_token, int32_t* pos, int32_t* gen, int max_seq) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  constexpr int kNone = 0x7fffffff;
+  griddep_launch_dependents();
+  griddep_wait();
+  float best = -INFINITY;
+  int idx = kNone;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i];
+    if (v == v && (idx == kNone || v > best)) {  // ascending i: ties keep the first
+      best = v;
+      idx = i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) {
+      best = ov;
+      idx = oi;
+    }
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) {
+    bv[warp] = best;
+    bi[warp] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x + 31) / 32; ++w)
+      if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
+        best = bv[w];
+        idx = bi[w];
+      }
+    if (n == 0 || idx == kNone || x[0] != x[0]) idx = 0;
+    const int p = *pos;
+    if (p >= 0 && p < max_seq) gen[p] = idx;
+    *next = idx;
+    *cur_token = idx;
+    *pos = p + 1;
+  }
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------- engine --
+struct Linear {
+  uint32_t* w = nullptr;
+  float* s = nullptr;
+  int64_t n = 0, k = 0;
+};
+
+struct Layer {
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  Linear qkv, wo, gate, up, down;
+  float* kcache = nullptr;
+  float* vcache = nullptr;
+};
+
+}  // namespace xpu
+
+struct xpu_llama {
+  xpu_llama_config c{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  std::vector<xpu::Layer> layers;
+  int8_t* embed_codes = nullptr;
+  float* embed_scale = nullptr;
+  float* final_norm = nullptr;
+  xpu::Linear lm_head;
+  double* inv_freq = nullptr;
+  // activations and step state
+  float *hidden_a = nullptr, *hidden_b = nullptr, *q = nullptr, *attn = nullptr, *gated = nullptr, *logits = nullptr;
+  float *part_m = nullptr, *part_l = nullptr, *part_acc = nullptr;
+  unsigned int* counter = nullptr;
+  int32_t *d_token = nullptr, *d_next = nullptr, *d_pos = nullptr;
+  int32_t* d_gen = nullptr;  // [max_seq] argmax of the step at each position
+  int nsplit = 1, chunk_max = 1;
+  // pinned host staging
+  int32_t* h_tokens = nullptr;  // [max_seq] one slot per position
+  int32_t* h_misc = nullptr;    // [4]
+  float* h_logits = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int32_t tokens_so_far = 0;
+};
+
+namespace xpu {
+namespace {
+
+template <typename T>
+int dev_alloc(xpu_llama* e, T** p, size_t count) {
+  void* v = nullptr;
+  size_t bytes = count * sizeof(T);
+  if (bytes == 0) bytes = 16;
+  cudaError_t err = cudaMalloc(&v, bytes);
+  if (err != cudaSuccess) return cuda_status(err, "cudaMalloc (engine)");
+  e->allocs.push_back(v);
+  *p = static_cast<T*>(v);
+  return XPU_OK;
+}
+
+int check_linear(const char* name, const xpu_q8_linear& l, int64_t n, int64_t k) {
+  XPU_REQUIRE(l.codes && l.scale, XPU_EINVAL, "LlamaWeightsQ8: %s has no codes/scale", name);
+  XPU_REQUIRE(l.rows == n && l.cols == k, XPU_EINVAL,
+              "LlamaWeightsQ8: %s has shape [%lld, %lld], expected [%lld, %lld]", name, (long long)l.rows,
+              (long long)l.cols, (long long)n, (long long)k);
+  return XPU_OK;
+}
+
+// Uploads int8 codes (host) and packs them into rows [row_off, row_off+n)
+// of `dst` (llm/weights-q8.ts:137-139 packInt8Rows, on the device).
+int upload_pack(xpu_llama* e, const xpu_q8_linear& src, uint32_t* dst_w, float* dst_s, int64_t row_off,
+                int8_t* tmp) {
+  const int64_t W = (src.cols + 3) / 4;
+  XPU_TRY_CUDA(cudaMemcpyAsync(tmp, src.codes, (size_t)(src.rows * src.cols), cudaMemcpyHostToDevice, e->stream));
+  int rc = pack_q8_dev_i8(tmp, src.rows, src.cols, dst_w + row_off * W, e->stream);
+  if (rc) return rc;
+  XPU_TRY_CUDA(cudaMemcpyAsync(dst_s + row_off, src.scale, (size_t)src.rows * 4, cudaMemcpyHostToDevice, e->stream));
+  // tmp is reused by the next call: finish this one first
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  return XPU_OK;
+}
+
+int alloc_linear(xpu_llama* e, Linear& l, int64_t n, int64_t k) {
+  l.n = n;
+  l.k = k;
+  int rc = dev_alloc(e, &l.w, (size_t)(n * ((k + 3) / 4)));
+  if (rc) return rc;
+  return dev_alloc(e, &l.s, (size_t)n);
+}
+
+// Records one decode step on e->stream (inside stream capture).
+int record_step(xpu_llama* e) {
+  const xpu_llama_config& c = e->c;
+  const int64_t h = c.hidden_size, hd = c.head_dim;
+  const int64_t qd = (int64_t)c.num_heads * hd, kvd = (int64_t)c.num_kv_heads * hd;
+  LaunchOpts first{e->stream, false}, dep{e->stream, true};
+
+  XPU_TRY_CUDA(launch_ex(embed_kernel, dim3(1), dim3(256), 0, first, (const int8_t*)e->embed_codes,
+                         (const float*)e->embed_scale, c.vocab_size, c.hidden_size, (const int32_t*)e->d_token,
+                         e->hidden_a));
+  unsigned int* err = device_error_word();
+  for (int l = 0; l < c.num_layers; ++l) {
+    Layer& L = e->layers[l];
+    MvParams p{};
+    p.err = err;
+    // Q/K/V with rmsnorm prologue, RoPE + KV write epilogue.
+    p.w = L.qkv.w;
+    p.s = L.qkv.s;
+    p.x = e->hidden_a;
+    p.gamma = L.attn_norm;
+    p.eps = c.rms_norm_eps;
+    p.y = e->q;
+    p.N = qd + 2 * kvd;
+    p.K = h;
+    p.q_rows = (int)qd;
+    p.kv_rows = (int)kvd;
+    p.head_dim = (int)hd;
+    p.max_seq = c.max_seq_len;
+    p.pos = e->d_pos;
+    p.inv_freq = e->inv_freq;
+    p.kcache = L.kcache;
+    p.vcache = L.vcache;
+    int rc = run_matvec(p, EPI_QKV, PRO_RMSNORM, dep);
+    if (rc) return rc;
+    // attention
+    AttnParams a{};
+    a.q = e->q;
+    a.kcache = L.kcache;
+    a.vcache = L.vcache;
+    a.pos = e->d_pos;
+    a.part_m = e->part_m;
+    a.part_l = e->part_l;
+    a.part_acc = e->part_acc;
+    a.counter = e->counter;
+    a.out = e->attn;
+    a.H = c.num_heads;
+    a.kvH = c.num_kv_heads;
+    a.hd = c.head_dim;
+    a.S = c.max_seq_len;
+    a.nsplit = e->nsplit;
+    a.chunk_max = e->chunk_max;
+    a.scale = (float)(1.0 / sqrt((double)hd));
+    const int G = c.num_heads / c.num_kv_heads;
+    size_t smem = sizeof(float) * ((size_t)G * hd + (size_t)G * e->chunk_max + 2 * G);
+    XPU_TRY_CUDA(launch_ex(attn_decode_kernel, dim3(c.num_kv_heads, e->nsplit), dim3(256), smem, dep, a));
+    // o-proj + residual
+    MvParams o{};
+    o.err = err;
+    o.w = L.wo.w;
+    o.s = L.wo.s;
+    o.x = e->attn;
+    o.residual = e->hidden_a;
+    o.y = e->hidden_b;
+    o.N = h;
+    o.K = qd;
+    rc = run_matvec(o, EPI_RESID, PRO_PLAIN, dep);
+    if (rc) return rc;
+    // gate/up + silu with rmsnorm prologue
+    MvParams f{};
+    f.err = err;
+    f.w = L.gate.w;
+    f.s = L.gate.s;
+    f.w2 = L.up.w;
+    f.s2 = L.up.s;
+    f.x = e->hidden_b;
+    f.gamma = L.ffn_norm;
+    f.eps = c.rms_norm_eps;
+    f.y = e->gated;
+    f.N = c.ffn_hidden;
+    f.K = h;
+    rc = run_matvec(f, EPI_FFN, PRO_RMSNORM, dep);
+    if (rc) return rc;
+    // down + residual
+    MvParams d{};
+    d.err = err;
+    d.w = L.down.w;
+    d.s = L.down.s;
+    d.x = e->gated;
+    d.residual = e->hidden_b;
+    d.y = e->hidden_a;
+    d.N = h;
+    d.K = c.ffn_hidden;
+    rc = run_matvec(d, EPI_RESID, PRO_PLAIN, dep);
+    if (rc) return rc;
+  }
+  MvParams hp{};
+  hp.err = err;
+  hp.w = e->lm_head.w;
+  hp.s = e->lm_head.s;
+  hp.x = e->hidden_a;
+  hp.gamma = e->final_norm;
+  hp.eps = c.rms_norm_eps;
+  hp.y = e->logits;
+  hp.N = c.vocab_size;
+  hp.K = h;
+  int rc = run_matvec(hp, EPI_PLAIN, PRO_RMSNORM, dep);
+  if (rc) return rc;
+  XPU_TRY_CUDA(launch_ex(argmax_kernel, dim3(1), dim3(1024), 0, dep, (const float*)e->logits, c.vocab_size,
+                         e->d_next, e->d_token, e->d_pos, e->d_gen, c.max_seq_len));
+  return XPU_OK;
+}
+
+int build_graph(xpu_llama* e) {
+  cudaGraph_t g = nullptr;
+  XPU_TRY_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = record_step(e);
+  cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return cuda_status(ce, "cudaStreamEndCapture");
+  ce = cudaGraphInstantiate(&e->exec, g, 0);
+  cudaGraphDestroy(g);
+  if (ce != cudaSuccess) return cuda_status(ce, "cudaGraphInstantiate");
+  return XPU_OK;
+}
+
+int set_device_pos(xpu_llama* e, int32_t pos) {
+  e->h_misc[0] = pos;
+  XPU_TRY_CUDA(cudaMemcpyAsync(e->d_pos, &e->h_misc[0], 4, cudaMemcpyHostToDevice, e->stream));
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  return XPU_OK;
+}
+
+void destroy_engine(xpu_llama* e) {
+  if (!e) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  if (e->exec) cudaGraphExecDestroy(e->exec);
+  for (void* p : e->allocs) cudaFree(p);
+  if (e->h_tokens) cudaFreeHost(e->h_tokens);
+  if (e->h_misc) cudaFreeHost(e->h_misc);
+  if (e->h_logits) cudaFreeHost(e->h_logits);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  cudaSetDevice(prev);
+  delete e;
+}
+
+int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, int device, xpu_llama** out) {
+  XPU_REQUIRE(cfg && w && out, XPU_EINVAL, "xpu_llama_create: null pointer");
+  const xpu_llama_config& c = *cfg;
+  XPU_REQUIRE(c.num_layers >= 0 && c.hidden_size > 0 && c.num_heads > 0 && c.num_kv_heads > 0 && c.head_dim > 0 &&
+                  c.ffn_hidden > 0 && c.vocab_size > 0 && c.max_seq_len > 0,
+              XPU_EINVAL, "xpu_llama_create: every size in the config must be positive");
+  XPU_REQUIRE(c.num_heads % c.num_kv_heads == 0, XPU_EINVAL,
+              "groupedAttention(): kvHeads=%d must divide H=%d; a ragged split has no defensible grouping",
+              c.num_kv_heads, c.num_heads);
+  XPU_REQUIRE(c.head_dim % 2 == 0, XPU_EINVAL, "rope: headDim must be even, got %d", c.head_dim);
+  XPU_REQUIRE(w->num_layers == c.num_layers && (c.num_layers == 0 || w->layers), XPU_EINVAL,
+              "LlamaWeightsQ8: %d layers, expected %d", w->num_layers, c.num_layers);
+  XPU_REQUIRE(w->final_norm, XPU_EINVAL, "LlamaWeightsQ8: finalNorm missing");
+  const int64_t h = c.hidden_size, hd = c.head_dim;
+  const int64_t qd = (int64_t)c.num_heads * hd, kvd = (int64_t)c.num_kv_heads * hd;
+  int rc;
+  if ((rc = check_linear("embedTokens", w->embed_tokens, c.vocab_size, h))) return rc;
+  if ((rc = check_linear("lmHead", w->lm_head, c.vocab_size, h))) return rc;
+  for (int i = 0; i < c.num_layers; ++i) {
+    const xpu_llama_layer_q8& L = w->layers[i];
+    XPU_REQUIRE(L.attn_norm && L.ffn_norm, XPU_EINVAL, "LlamaWeightsQ8: layers[%d] norm missing", i);
+    if ((rc = check_linear("wq", L.wq, qd, h)) || (rc = check_linear("wk", L.wk, kvd, h)) ||
+        (rc = check_linear("wv", L.wv, kvd, h)) || (rc = check_linear("wo", L.wo, h, qd)) ||
+        (rc = check_linear("wGate", L.w_gate, c.ffn_hidden, h)) || (rc = check_linear("wUp", L.w_up, c.ffn_hidden, h)) ||
+        (rc = check_linear("wDown", L.w_down, h, c.ffn_hidden)))
+      return rc;
+  }
+
+  XPU_TRY_CUDA(cudaSetDevice(device));
+  xpu_llama* e = new xpu_llama();
+  e->c = c;
+  e->device = device;
+  auto fail = [&](int code) {
+    destroy_engine(e);
+    return code;
+  };
+  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return fail(cuda_status(cudaGetLastError(), "cudaStreamCreate"));
+
+  int64_t max_codes = (int64_t)c.vocab_size * h;
+  for (int i = 0; i < c.num_layers; ++i) max_codes = std::max<int64_t>(max_codes, (int64_t)c.ffn_hidden * h);
+  int8_t* tmp = nullptr;
+  if ((rc = dev_alloc(e, &tmp, (size_t)max_codes))) return fail(rc);
+
+  e->layers.resize(c.num_layers);
+  const size_t cache = (size_t)c.num_kv_heads * c.max_seq_len * hd;
+  for (int i = 0; i < c.num_layers; ++i) {
+    const xpu_llama_layer_q8& S = w->layers[i];
+    Layer& L = e->layers[i];
+    if ((rc = dev_alloc(e, &L.attn_norm, h)) || (rc = dev_alloc(e, &L.ffn_norm, h))) return fail(rc);
+    if (cudaMemcpy(L.attn_norm, S.attn_norm, h * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(L.ffn_norm, S.ffn_norm, h * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(cuda_status(cudaGetLastError(), "upload norms"));
+    if ((rc = alloc_linear(e, L.qkv, qd + 2 * kvd, h)) || (rc = alloc_linear(e, L.wo, h, qd)) ||
+        (rc = alloc_linear(e, L.gate, c.ffn_hidden, h)) || (rc = alloc_linear(e, L.up, c.ffn_hidden, h)) ||
+        (rc = alloc_linear(e, L.down, h, c.ffn_hidden)))
+      return fail(rc);
+    if ((rc = upload_pack(e, S.wq, L.qkv.w, L.qkv.s, 0, tmp)) ||
+        (rc = upload_pack(e, S.wk, L.qkv.w, L.qkv.s, qd, tmp)) ||
+        (rc = upload_pack(e, S.wv, L.qkv.w, L.qkv.s, qd + kvd, tmp)) ||
+        (rc = upload_pack(e, S.wo, L.wo.w, L.wo.s, 0, tmp)) ||
+        (rc = upload_pack(e, S.w_gate, L.gate.w, L.gate.s, 0, tmp)) ||
+        (rc = upload_pack(e, S.w_up, L.up.w, L.up.s, 0, tmp)) ||
+        (rc = upload_pack(e, S.w_down, L.down.w, L.down.s, 0, tmp)))
+      return fail(rc);
+    if ((rc = dev_alloc(e, &L.kcache, cache)) || (rc = dev_alloc(e, &L.vcache, cache))) return fail(rc);
+    if (cudaMemset(L.kcache, 0, cache * 4) != cudaSuccess || cudaMemset(L.vcache, 0, cache * 4) != cudaSuccess)
+      return fail(cuda_status(cudaGetLastError(), "cudaMemset cache"));
+  }
+  if ((rc = alloc_linear(e, e->lm_head, c.vocab_size, h)) ||
+      (rc = upload_pack(e, w->lm_head, e->lm_head.w, e->lm_head.s, 0, tmp)))
+    return fail(rc);
+  if ((rc = dev_alloc(e, &e->embed_codes, (size_t)c.vocab_size * h)) || (rc = dev_alloc(e, &e->embed_scale, c.vocab_size)) ||
+      (rc = dev_alloc(e, &e->final_norm, h)))
+    return fail(rc);
+  if (cudaMemcpy(e->embed_codes, w->embed_tokens.codes, (size_t)c.vocab_size * h, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(e->embed_scale, w->embed_tokens.scale, (size_t)c.vocab_size * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(e->final_norm, w->final_norm, h * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    return fail(cuda_status(cudaGetLastError(), "upload embed/final norm"));
+
+  // RoPE inverse frequencies, ops/rope/reference.ts:226-244 with the
+  // unscaled parameters (:154-166): the ramp term is an exact zero.
+  std::vector<double> inv(hd / 2);
+  for (int64_t i = 0; i < hd / 2; ++i) {
+    double extrapolation = pow(c.rope_theta, (-2.0 * (double)i) / (double)hd);
+    double interpolation = extrapolation / 1.0;
+    double ramp = fmin(fmax((double)i / 1.0, 0.0), 1.0);
+    inv[i] = extrapolation + (interpolation - extrapolation) * ramp;
+  }
+  if ((rc = dev_alloc(e, &e->inv_freq, inv.size()))) return fail(rc);
+  if (cudaMemcpy(e->inv_freq, inv.data(), inv.size() * 8, cudaMemcpyHostToDevice) != cudaSuccess)
+    return fail(cuda_status(cudaGetLastError(), "upload inv_freq"));
+
+  // Position splits for attention: about two CTAs per SM over all kv heads,
+  // at least 8 positions per split.
+  const int sms = device_info().sm_count;
+  e->nsplit = std::max(1, std::min((2 * sms + c.num_kv_heads - 1) / c.num_kv_heads, (c.max_seq_len + 7) / 8));
+  e->chunk_max = (c.max_seq_len + e->nsplit - 1) / e->nsplit;
+  if ((rc = dev_alloc(e, &e->hidden_a, h)) || (rc = dev_alloc(e, &e->hidden_b, h)) || (rc = dev_alloc(e, &e->q, qd)) ||
+      (rc = dev_alloc(e, &e->attn, qd)) || (rc = dev_alloc(e, &e->gated, c.ffn_hidden)) ||
+      (rc = dev_alloc(e, &e->logits, c.vocab_size)) ||
+      (rc = dev_alloc(e, &e->part_m, (size_t)c.num_heads * e->nsplit)) ||
+      (rc = dev_alloc(e, &e->part_l, (size_t)c.num_heads * e->nsplit)) ||
+      (rc = dev_alloc(e, &e->part_acc, (size_t)c.num_heads * e->nsplit * hd)) ||
+      (rc = dev_alloc(e, &e->counter, c.num_kv_heads)) || (rc = dev_alloc(e, &e->d_token, 4)) ||
+      (rc = dev_alloc(e, &e->d_next, 4)) || (rc = dev_alloc(e, &e->d_pos, 4)) ||
+      (rc = dev_alloc(e, &e->d_gen, (size_t)c.max_seq_len)))
+    return fail(rc);
+  if (cudaMemset(e->counter, 0, c.num_kv_heads * 4) != cudaSuccess || cudaMemset(e->d_token, 0, 16) != cudaSuccess ||
+      cudaMemset(e->d_next, 0, 16) != cudaSuccess || cudaMemset(e->d_pos, 0, 16) != cudaSuccess ||
+      cudaMemset(e->logits, 0, (size_t)c.vocab_size * 4) != cudaSuccess)
+    return fail(cuda_status(cudaGetLastError(), "cudaMemset state"));
+  if (cudaMallocHost(&e->h_tokens, (size_t)c.max_seq_len * 4) != cudaSuccess ||
+      cudaMallocHost(&e->h_misc, 16) != cudaSuccess ||
+      cudaMallocHost(&e->h_logits, (size_t)c.vocab_size * 4) != cudaSuccess)
+    return fail(cuda_status(cudaGetLastError(), "cudaMallocHost"));
+  if (cudaDeviceSynchronize() != cudaSuccess) return fail(cuda_status(cudaGetLastError(), "create sync"));
+  if ((rc = build_graph(e))) return fail(rc);
+  *out = e;
+  return XPU_OK;
+}
+
+}  // namespace
+}  // namespace xpu
+
+using namespace xpu;
+
+extern "C" {
+
+int xpu_llama_create(const xpu_llama_config* config, const xpu_llama_weights_q8* weights, int device,
+                     xpu_llama** engine) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  int rc = create_engine(config, weights, device, engine);
+  cudaSetDevice(prev);
+  return rc;
+}
+
+int xpu_llama_forward(xpu_llama* e, const int32_t* tokens, int32_t n, float* logits, int32_t* argmax) {
+  XPU_REQUIRE(e, XPU_EINVAL, "LlamaEngineQ8Resident.forward: null engine");
+  XPU_REQUIRE(n > 0 && tokens, XPU_EINVAL, "LlamaEngineQ8Resident.forward: tokens must be non-empty");
+  XPU_REQUIRE(e->tokens_so_far == 0 || n == 1, XPU_ESTATE,
+              "LlamaEngineQ8Resident.forward: after prefill, every call must be exactly one token (decode)");
+  XPU_REQUIRE((int64_t)e->tokens_so_far + n <= e->c.max_seq_len, XPU_ERANGE,
+              "LlamaEngineQ8Resident.forward: position %lld exceeds maxSeqLen=%d",
+              (long long)e->tokens_so_far + n, e->c.max_seq_len);
+  XPU_TRY_CUDA(cudaSetDevice(e->device));
+  const int32_t base = e->tokens_so_far;
+  memcpy(e->h_tokens + base, tokens, (size_t)n * 4);
+  for (int32_t t = 0; t < n; ++t) {
+    XPU_TRY_CUDA(cudaMemcpyAsync(e->d_token, e->h_tokens + base + t, 4, cudaMemcpyHostToDevice, e->stream));
+    XPU_TRY_CUDA(cudaGraphLaunch(e->exec, e->stream));
+  }
+  if (logits)
+    XPU_TRY_CUDA(cudaMemcpyAsync(e->h_logits, e->logits, (size_t)e->c.vocab_size * 4, cudaMemcpyDeviceToHost, e->stream));
+  XPU_TRY_CUDA(cudaMemcpyAsync(&e->h_misc[1], e->d_next, 4, cudaMemcpyDeviceToHost, e->stream));
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  int rc = check_device_error();
+  if (rc) return rc;
+  e->tokens_so_far = base + n;
+  if (logits) memcpy(logits, e->h_logits, (size_t)e->c.vocab_size * 4);
+  if (argmax) *argmax = e->h_misc[1];
+  return XPU_OK;
+}
+
+int xpu_llama_decode_dev(xpu_llama* e, const int32_t* token_dev, int32_t* next_dev) {
+  XPU_REQUIRE(e && token_dev, XPU_EINVAL, "xpu_llama_decode_dev: null pointer");
+  XPU_REQUIRE(e->tokens_so_far + 1 <= e->c.max_seq_len, XPU_ERANGE,
+              "LlamaEngineQ8Resident.forward: position %d exceeds maxSeqLen=%d", e->tokens_so_far + 1,
+              e->c.max_seq_len);
+  XPU_TRY_CUDA(cudaSetDevice(e->device));
+  if (token_dev != e->d_token)
+    XPU_TRY_CUDA(cudaMemcpyAsync(e->d_token, token_dev, 4, cudaMemcpyDeviceToDevice, e->stream));
+  XPU_TRY_CUDA(cudaGraphLaunch(e->exec, e->stream));
+  if (next_dev) XPU_TRY_CUDA(cudaMemcpyAsync(next_dev, e->d_next, 4, cudaMemcpyDeviceToDevice, e->stream));
+  e->tokens_so_far += 1;
+  return XPU_OK;
+}
+
+int xpu_llama_greedy_steps(xpu_llama* e, int32_t first_token, int32_t steps, int32_t* tokens_out) {
+  XPU_REQUIRE(e && steps >= 0, XPU_EINVAL, "xpu_llama_greedy_steps: bad arguments");
+  XPU_REQUIRE(e->tokens_so_far > 0, XPU_ESTATE, "xpu_llama_greedy_steps: prefill first (forward or set_kv)");
+  XPU_REQUIRE((int64_t)e->tokens_so_far + steps <= e->c.max_seq_len, XPU_ERANGE,
+              "LlamaEngineQ8Resident.forward: position %lld exceeds maxSeqLen=%d",
+              (long long)e->tokens_so_far + steps, e->c.max_seq_len);
+  XPU_TRY_CUDA(cudaSetDevice(e->device));
+  const int32_t base = e->tokens_so_far;
+  e->h_tokens[base] = first_token;
+  XPU_TRY_CUDA(cudaMemcpyAsync(e->d_token, e->h_tokens + base, 4, cudaMemcpyHostToDevice, e->stream));
+  for (int32_t s = 0; s < steps; ++s) XPU_TRY_CUDA(cudaGraphLaunch(e->exec, e->stream));
+  if (tokens_out && steps > 0)
+    XPU_TRY_CUDA(cudaMemcpyAsync(tokens_out, e->d_gen + base, (size_t)steps * 4, cudaMemcpyDeviceToHost, e->stream));
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  int rc = check_device_error();
+  if (rc) return rc;
+  e->tokens_so_far = base + steps;
+  return XPU_OK;
+}
+
+int xpu_llama_logits_dev(xpu_llama* e, float** logits_dev) {
+  XPU_REQUIRE(e && logits_dev, XPU_EINVAL, "xpu_llama_logits_dev: null pointer");
+  *logits_dev = e->logits;
+  return XPU_OK;
+}
+
+int xpu_llama_stream(xpu_llama* e, void** stream) {
+  XPU_REQUIRE(e && stream, XPU_EINVAL, "xpu_llama_stream: null pointer");
+  *stream = (void*)e->stream;
+  return XPU_OK;
+}
+
+int xpu_llama_reset(xpu_llama* e) {
+  XPU_REQUIRE(e, XPU_EINVAL, "xpu_llama_reset: null engine");
+  XPU_TRY_CUDA(cudaSetDevice(e->device));
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  int rc = set_device_pos(e, 0);
+  if (rc) return rc;
+  e->tokens_so_far = 0;
+  return XPU_OK;
+}
+
+int xpu_llama_position(const xpu_llama* e, int32_t* position) {
+  XPU_REQUIRE(e && position, XPU_EINVAL, "xpu_llama_position: null pointer");
+  *position = e->tokens_so_far;
+  return XPU_OK;
+}
+
+int xpu_llama_set_kv(xpu_llama* e, int32_t layer, const float* k, const float* v, int32_t npos) {
+  XPU_REQUIRE(e && k && v, XPU_EINVAL, "xpu_llama_set_kv: null pointer");
+  XPU_REQUIRE(layer >= 0 && layer < e->c.num_layers, XPU_EINVAL, "xpu_llama_set_kv: layer %d out of range", layer);
+  XPU_REQUIRE(npos >= 0 && npos <= e->c.max_seq_len, XPU_ERANGE, "xpu_llama_set_kv: npos %d exceeds maxSeqLen=%d",
+              npos, e->c.max_seq_len);
+  XPU_TRY_CUDA(cudaSetDevice(e->device));
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  const int64_t hd = e->c.head_dim, S = e->c.max_seq_len;
+  Layer& L = e->layers[layer];
+  for (int64_t h = 0; h < e->c.num_kv_heads; ++h) {
+    XPU_TRY_CUDA(cudaMemcpy(L.kcache + h * S * hd, k + h * (int64_t)npos * hd, (size_t)npos * hd * 4, cudaMemcpyHostToDevice));
+    XPU_TRY_CUDA(cudaMemcpy(L.vcache + h * S * hd, v + h * (int64_t)npos * hd, (size_t)npos * hd * 4, cudaMemcpyHostToDevice));
+  }
+  int rc = set_device_pos(e, npos);
+  if (rc) return rc;
+  e->tokens_so_far = npos;
+  return XPU_OK;
+}
+
+int xpu_llama_poison_kv(xpu_llama* e, float value) {
+  XPU_REQUIRE(e, XPU_EINVAL, "xpu_llama_poison_kv: null engine");
+  XPU_TRY_CUDA(cudaSetDevice(e->device));
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  const size_t n = (size_t)e->c.num_kv_heads * e->c.max_seq_len * e->c.head_dim;
+  std::vector<float> buf(n, value);
+  for (Layer& L : e->layers) {
+    XPU_TRY_CUDA(cudaMemcpy(L.kcache, buf.data(), n * 4, cudaMemcpyHostToDevice));
+    XPU_TRY_CUDA(cudaMemcpy(L.vcache, buf.data(), n * 4, cudaMemcpyHostToDevice));
+  }
+  return XPU_OK;
+}
+
+int xpu_llama_destroy(xpu_llama* e) {
+  destroy_engine(e);
+  return XPU_OK;
+}
+
+}  // extern "C"

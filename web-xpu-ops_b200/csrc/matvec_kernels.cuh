@@ -1,0 +1,381 @@
+// matvec_kernels.cuh — the W8A32 matvecQ8 GEMV family for sm_100a.
+//
+// Semantics (ops/matvec/reference.ts:117-131): y[n] = (sum_k code[n,k] *
+// x[k]) * scale[n], codes packed four per u32 word LSB-first, rows of
+// W = ceil(K/4) words.  Epilogues add the fused forms of the reference:
+// matvecQ8Residual (:235-242), matvecQ8Ffn (:196-207), and, for the decode
+// step, the Q/K/V projection with RoPE (ops/rope/reference.ts:324-406) and
+// the KV-cache write of llm/engine-q8-resident.ts:1848-1851.  A prologue can
+// fuse ops/rmsnorm/reference.ts:80-96 in front of the dot product.
+//
+// Two kernels:
+//  * mv_bulk_kernel — rows 16-byte aligned (W % 4 == 0, aligned base).  A
+//    persistent CTA per SM; one producer thread streams blocks of RB rows
+//    (contiguous in memory) into a shared-memory ring with cp.async.bulk
+//    (the 1-D TMA copy) completing on mbarriers; consumer warps read the
+//    block with 128-bit shared loads.  Each consumer thread owns fixed
+//    16-column slices of K and keeps x for them in registers for the whole
+//    launch, so x is read from memory once per CTA and shared memory
+//    carries weights only.
+//  * mv_gen_kernel — any alignment, any K.  Direct 128-bit loads on the
+//    16-byte grid of the buffer; a word of a neighbouring row (a load that
+//    straddles a row boundary) or a padding lane multiplies a zero of the
+//    zero-padded x staged in shared memory, so nothing outside a row counts.
+#pragma once
+
+#include "common.cuh"
+
+namespace xpu {
+
+enum Epi : int { EPI_PLAIN = 0, EPI_RESID = 1, EPI_FFN = 2, EPI_QKV = 3 };
+enum Pro : int { PRO_PLAIN = 0, PRO_RMSNORM = 1 };
+
+struct MvParams {
+  const uint32_t* w;   // weight (gate weight for FFN)
+  const uint32_t* w2;  // up weight (FFN)
+  const float* s;      // scale (gate scale for FFN)
+  const float* s2;     // up scale (FFN)
+  const float* x;      // input vector, or the un-normalised hidden for PRO_RMSNORM
+  const float* gamma;  // rmsnorm gain (PRO_RMSNORM)
+  double eps;          // rmsnorm eps
+  const float* residual;
+  float* y;
+  int64_t N, K, W;
+  // EPI_QKV: rows [0, q_rows) are q, [q_rows, q_rows + kv_rows) k, then v.
+  int q_rows, kv_rows, head_dim, max_seq;
+  const int32_t* pos;      // device position (RoPE offset and cache slot)
+  const double* inv_freq;  // [head_dim/2] RoPE inverse frequencies (f64)
+  float* kcache;           // [kv_heads, max_seq, head_dim]
+  float* vcache;
+  // bulk kernel geometry
+  int ncw;             // consumer warps
+  int stages;          // ring depth
+  uint32_t stage_off;  // byte offset of the ring in dynamic shared memory
+  uint32_t stage_stride;
+  unsigned int* err;   // device error word
+};
+
+// ------------------------------------------------------------- epilogues --
+__device__ __forceinline__ float silu_f32(float g) {
+  // ops/activation/reference.ts:91-92, f64 then stored f32.
+  double x = (double)g;
+  return (float)(x / (1.0 + exp(-x)));
+}
+
+// Writes output row(s) of a unit from the per-warp partial sums in shared
+// memory (`rb[w * RT + r]`, w < nw): one call per output row, per row pair
+// for QKV (thread t handles unit rows 2t, 2t+1).
+template <int EPI, int RB, int RT>
+__device__ __forceinline__ void mv_epilogue(const MvParams& p, int64_t row0, int t, const float* rb, int nw) {
+  auto sum = [&](int r) {
+    float v = 0.0f;
+    for (int w = 0; w < nw; ++w) v += rb[w * RT + r];
+    return v;
+  };
+  if constexpr (EPI == EPI_PLAIN) {
+    int64_t row = row0 + t;
+    if (row < p.N) p.y[row] = __fmul_rn(sum(t), p.s[row]);
+  } else if constexpr (EPI == EPI_RESID) {
+    int64_t row = row0 + t;
+    if (row < p.N) p.y[row] = __fadd_rn(p.residual[row], __fmul_rn(sum(t), p.s[row]));
+  } else if constexpr (EPI == EPI_FFN) {
+    int64_t row = row0 + t;
+    if (row < p.N) {
+      float g = __fmul_rn(sum(t), p.s[row]);
+      float u = __fmul_rn(sum(RB + t), p.s2[row]);
+      p.y[row] = __fmul_rn(silu_f32(g), u);
+    }
+  } else {  // EPI_QKV
+    int64_t r0 = row0 + 2 * t;  // N is even (every region is whole heads)
+    if (r0 >= p.N) return;
+    float a = __fmul_rn(sum(2 * t), p.s[r0]);
+    float b = __fmul_rn(sum(2 * t + 1), p.s[r0 + 1]);
+    const int pos = *p.pos;
+    const int64_t qk_end = (int64_t)p.q_rows + p.kv_rows;
+    if (r0 < qk_end) {
+      // RoPE on the adjacent pair (ops/rope/reference.ts:379-401), f64.
+      int64_t local = r0 < p.q_rows ? r0 : r0 - p.q_rows;
+      int pair = (int)((local % p.head_dim) / 2);
+      double theta = (double)pos * p.inv_freq[pair];
+      double sn, cs;
+      sincos(theta, &sn, &cs);
+      double x0 = a, x1 = b;
+      a = (float)(x0 * cs - x1 * sn);
+      b = (float)(x0 * sn + x1 * cs);
+    }
+    if (r0 < p.q_rows) {
+      p.y[r0] = a;
+      p.y[r0 + 1] = b;
+    } else {
+      // KV cache write at slot `pos` (llm/engine-q8-resident.ts:1848-1851):
+      // cache[(h * maxSeqLen + pos) * headDim + d].
+      bool is_k = r0 < qk_end;
+      int64_t local = is_k ? r0 - p.q_rows : r0 - qk_end;
+      int64_t h = local / p.head_dim, d = local % p.head_dim;
+      float* cache = is_k ? p.kcache : p.vcache;
+      float* dst = cache + ((h * p.max_seq + pos) * p.head_dim + d);
+      dst[0] = a;
+      dst[1] = b;
+    }
+  }
+}
+
+// Outputs written per unit: one thread per row, per pair for QKV.
+template <int EPI, int RB>
+__host__ __device__ constexpr int mv_outputs_per_unit() {
+  return EPI == EPI_QKV ? RB / 2 : RB;
+}
+
+// x for the consumer thread's columns, 16 floats per column c (x[16c..16c+15],
+// zero past K).  With PRO_RMSNORM the CTA first reduces sum(x^2) in f64
+// (named barrier `bar` over `nthreads`), then applies
+// f32(x * (1/sqrt(ss/K + eps)) * gamma) as ops/rmsnorm/reference.ts:89-93.
+template <int CPT, int PRO>
+__device__ __forceinline__ void load_x_cols(const MvParams& p, int tid, int nthreads, int64_t U, double* red_d,
+                                            int bar, f2 (&xr)[CPT][8]) {
+  float xv[CPT][16];
+  double ss = 0.0;
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    int64_t c = tid + (int64_t)j * nthreads;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      int64_t k = 16 * c + i;
+      float v = (c < U && k < p.K) ? p.x[k] : 0.0f;
+      xv[j][i] = v;
+      if constexpr (PRO == PRO_RMSNORM) ss += (double)v * (double)v;
+    }
+  }
+  if constexpr (PRO == PRO_RMSNORM) {
+    // Columns beyond U (threads with no column) contribute 0.  Threads cover
+    // U*16 >= K entries, so every x[k] is counted exactly once.
+    double s = warp_sum_d(ss);
+    int warp = tid / 32, lane = tid % 32, nw = nthreads / 32;
+    if (lane == 0) red_d[warp] = s;
+    named_bar_sync(bar, nthreads);
+    double tot = 0.0;
+    for (int w = 0; w < nw; ++w) tot += red_d[w];
+    double scale = 1.0 / sqrt(tot / (double)p.K + p.eps);
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      int64_t c = tid + (int64_t)j * nthreads;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        int64_t k = 16 * c + i;
+        if (c < U && k < p.K) xv[j][i] = (float)((double)xv[j][i] * scale * (double)p.gamma[k]);
+      }
+    }
+    named_bar_sync(bar, nthreads);  // red_d is reused by the caller
+  }
+#pragma unroll
+  for (int j = 0; j < CPT; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xr[j][i] = make_f2(xv[j][2 * i], xv[j][2 * i + 1]);
+}
+
+// ------------------------------------------------------------ bulk kernel --
+// RT = rows per unit across all weight streams (FFN: RB gate + RB up rows).
+// Plans with RT >= 4 have at most 8 consumer warps (their stage size caps K);
+// RT <= 2 can use 16.
+template <int RT, int CPT, int EPI, int PRO>
+__global__ void __launch_bounds__(RT >= 4 ? 288 : 544, 1) mv_bulk_kernel(MvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int NSTREAM = EPI == EPI_FFN ? 2 : 1;
+  constexpr int RB = RT / NSTREAM;
+  const int ncw = p.ncw, nct = ncw * 32, S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  float* red = reinterpret_cast<float*>(empty + S);            // [2][ncw][RT]
+  double* red_d = reinterpret_cast<double*>(red + 2 * 16 * RT);  // [16]
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
+  const int64_t units = (p.N + RB - 1) / RB;
+  const int64_t U = p.W / 4;  // uint4 per row
+  const uint32_t row_bytes = (uint32_t)(p.W * 4);
+
+  griddep_launch_dependents();
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ncw);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == ncw) {
+    // ---------------- producer: one thread streams row blocks ----------------
+    if (lane != 0) return;
+    const uint64_t policy = evict_first_policy();
+    int64_t issued = 0;
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++issued) {
+      const int s = (int)(issued % S);
+      if (issued >= S && !mbar_wait(&empty[s], (uint32_t)((issued / S - 1) & 1), p.err)) break;
+      const int64_t row0 = u * RB;
+      const int rows = (int)(p.N - row0 < RB ? p.N - row0 : RB);
+      const uint32_t bytes = rows * row_bytes;
+      uint8_t* dst = smem + p.stage_off + (size_t)s * p.stage_stride;
+      mbar_arrive_expect_tx(&full[s], bytes * NSTREAM);
+      bulk_g2s(dst, p.w + row0 * p.W, bytes, &full[s], policy);
+      if constexpr (NSTREAM == 2) bulk_g2s(dst + (size_t)RB * row_bytes, p.w2 + row0 * p.W, bytes, &full[s], policy);
+    }
+    // Every issued copy must land before the CTA may exit (error path).
+    for (int64_t i = (issued > S ? issued - S : 0); i < issued; ++i)
+      mbar_wait(&full[i % S], (uint32_t)((i / S) & 1), p.err);
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  griddep_wait();  // x, gamma, residual and outputs belong to predecessors
+  f2 xr[CPT][8];
+  load_x_cols<CPT, PRO>(p, tid, nct, U, red_d, 1, xr);
+
+  const f2 zero2 = make_f2(0.0f, 0.0f);
+  int64_t it = 0;
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+    const int s = (int)(it % S);
+    const bool ok = mbar_wait(&full[s], (uint32_t)((it / S) & 1), p.err);
+    if (!ok) abort_flag = 1;
+    const int64_t row0 = u * RB;
+    const int rows = (int)(p.N - row0 < RB ? p.N - row0 : RB);
+    const uint4* st = reinterpret_cast<const uint4*>(smem + p.stage_off + (size_t)s * p.stage_stride);
+
+    f2 acc[RT][4];
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[r][k] = zero2;
+    if (ok) {
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const int64_t c = tid + (int64_t)j * nct;
+        if (c < U) {
+#pragma unroll
+          for (int r = 0; r < RT; ++r) {
+            if ((r % RB) < rows) {
+              uint4 w = st[r * U + c];
+              dot16(w, xr[j], acc[r]);
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // stage may be refilled
+
+    float* rb = red + (it & 1) * 16 * RT;
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      float v = warp_sum(hsum4(acc[r]));
+      if (lane == 0) rb[warp * RT + r] = v;
+    }
+    named_bar_sync(1, nct);
+    if (abort_flag) break;
+    constexpr int OUTS = mv_outputs_per_unit<EPI, RB>();
+    if (tid < OUTS) mv_epilogue<EPI, RB, RT>(p, row0, tid, rb, ncw);
+  }
+}
+
+// --------------------------------------------------------- general kernel --
+// Units of RB rows (RB = 2: a QKV pair, or gate+up for FFN with RB = 1).
+// x staged in shared memory as xs[16 + k] = x[k] with at least 16 zeros on
+// both sides, so a 16-code slice whose first code sits at column kc (which
+// can be negative or past K for straddling loads) reads xs[16 + kc ...].
+template <int RT, int EPI, int PRO>
+__global__ void __launch_bounds__(256) mv_gen_kernel(MvParams p, int64_t off_words) {
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[8][RT];
+  __shared__ double red_d[8];
+  constexpr int NSTREAM = EPI == EPI_FFN ? 2 : 1;
+  constexpr int RB = RT / NSTREAM;
+  const int tid = threadIdx.x, nt = blockDim.x, warp = tid / 32, lane = tid % 32;
+  const int64_t units = (p.N + RB - 1) / RB;
+  const int64_t total_words = p.N * p.W;
+  // Full uint4 slots of the 16-byte grid starting at the aligned base.
+  const int64_t q_first_full = off_words == 0 ? 0 : 1;
+  const int64_t q_last_full = (off_words + total_words) / 4 - 1;
+  const uint32_t* base = p.w - off_words;  // 16-byte aligned
+  const uint32_t* base2 = p.w2 ? p.w2 - off_words : nullptr;
+
+  griddep_launch_dependents();
+  griddep_wait();
+  // Stage x (normalised for PRO_RMSNORM) with zero padding.
+  const int64_t xs_len = 16 + 4 * p.W + 32;
+  double ss = 0.0;
+  for (int64_t i = tid; i < xs_len; i += nt) {
+    int64_t k = i - 16;
+    float v = (k >= 0 && k < p.K) ? p.x[k] : 0.0f;
+    xs[i] = v;
+    if constexpr (PRO == PRO_RMSNORM) ss += (double)v * (double)v;
+  }
+  if constexpr (PRO == PRO_RMSNORM) {
+    double s = warp_sum_d(ss);
+    if (lane == 0) red_d[warp] = s;
+    __syncthreads();
+    double tot = 0.0;
+    for (int w = 0; w < nt / 32; ++w) tot += red_d[w];
+    double scale = 1.0 / sqrt(tot / (double)p.K + p.eps);
+    for (int64_t k = tid; k < p.K; k += nt) xs[16 + k] = (float)((double)xs[16 + k] * scale * (double)p.gamma[k]);
+  }
+  __syncthreads();
+
+  const f2 zero2 = make_f2(0.0f, 0.0f);
+  int64_t it = 0;
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+    const int64_t row0 = u * RB;
+    f2 acc[RT][4];
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[r][k] = zero2;
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      const int64_t row = row0 + (r % RB);
+      if (row >= p.N) continue;
+      const uint32_t* b = (NSTREAM == 2 && r >= RB) ? base2 : base;
+      const int64_t g0 = off_words + row * p.W;
+      const int64_t q0 = g0 >> 2;
+      const int o = (int)(g0 & 3);
+      const int64_t nq = (o + p.W + 3) >> 2;
+#pragma unroll 4
+      for (int64_t c = tid; c < nq; c += nt) {
+        const int64_t q = q0 + c;
+        uint4 w;
+        if (q >= q_first_full && q <= q_last_full) {
+          w = ldg_stream_v4(b + 4 * q);
+        } else {  // partial slot at either end of the buffer
+          uint32_t v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            int64_t gw = 4 * q + e;
+            v[e] = (gw >= off_words && gw < off_words + total_words) ? ldg_stream_u32(b + gw) : 0u;
+          }
+          w = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+        const float4* xp = reinterpret_cast<const float4*>(xs + 16 + 16 * c - 4 * o);
+        f2 xv[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float4 t = xp[e];
+          xv[2 * e] = make_f2(t.x, t.y);
+          xv[2 * e + 1] = make_f2(t.z, t.w);
+        }
+        dot16(w, xv, acc[r]);
+      }
+    }
+    float* rb = &red[0][0];
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      float v = warp_sum(hsum4(acc[r]));
+      if (lane == 0) red[warp][r] = v;
+    }
+    __syncthreads();
+    constexpr int OUTS = mv_outputs_per_unit<EPI, RB>();
+    if (tid < OUTS) mv_epilogue<EPI, RB, RT>(p, row0, tid, rb, nt / 32);
+    __syncthreads();
+  }
+}
+
+}  // namespace xpu

@@ -1,0 +1,78 @@
+// matvec_launch.cuh — host-side selection of the GEMV kernel geometry and the
+// per-(epilogue, prologue) launch entry points (each compiled in its own
+// translation unit so the instantiations build in parallel).
+#pragma once
+
+#include "common.cuh"
+#include "matvec_kernels.cuh"
+
+namespace xpu {
+
+// Geometry chosen by plan_matvec().
+struct MvPlan {
+  bool bulk = false;  // bulk-copy (TMA) kernel, else the general kernel
+  int rt = 0, cpt = 0, ncw = 0, stages = 0;
+  dim3 grid, block;
+  size_t smem = 0;
+  int64_t off_words = 0;  // general kernel: words from the 16-byte grid to w
+};
+
+// Chooses the kernel and its geometry; XPU_OK or XPU_EINVAL (with message).
+int plan_matvec(MvParams& p, int epi, int pro, MvPlan& plan);
+
+// Per-(EPI, PRO) launchers, defined in matvec_<combo>.cu.
+template <int EPI, int PRO>
+int launch_mv(const MvParams& p, const MvPlan& plan, const LaunchOpts& o);
+
+// Plans and launches; the single entry used by the C ABI and the engine.
+int run_matvec(MvParams p, int epi, int pro, const LaunchOpts& o);
+
+// Launch helper: cudaLaunchKernelEx with the PDL attribute when requested.
+template <typename... Args>
+cudaError_t launch_ex(void (*kernel)(Args...), dim3 grid, dim3 block, size_t smem, const LaunchOpts& o,
+                      Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = o.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = o.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// Raises the dynamic shared memory limit of `kernel` on the current device
+// once per (kernel, device).
+cudaError_t ensure_smem_attr(const void* kernel, size_t bytes);
+
+template <int EPI, int PRO>
+int launch_mv_impl(const MvParams& p, const MvPlan& plan, const LaunchOpts& o) {
+  void (*k)(MvParams) = nullptr;
+  if (plan.bulk) {
+#define XPU_MV_CASE(RT_, CPT_)                                      \
+  if (plan.rt == RT_ && plan.cpt == CPT_) k = mv_bulk_kernel<RT_, CPT_, EPI, PRO>;
+    if constexpr (EPI != EPI_FFN && EPI != EPI_QKV) {
+      XPU_MV_CASE(1, 1) XPU_MV_CASE(1, 2) XPU_MV_CASE(1, 3) XPU_MV_CASE(1, 4)
+    }
+    XPU_MV_CASE(2, 1) XPU_MV_CASE(2, 2) XPU_MV_CASE(2, 3) XPU_MV_CASE(2, 4)
+    XPU_MV_CASE(4, 1) XPU_MV_CASE(4, 2)
+    XPU_MV_CASE(8, 1)
+#undef XPU_MV_CASE
+    if (!k) {
+      set_error("matvecQ8: no bulk kernel for rt=%d cpt=%d", plan.rt, plan.cpt);
+      return XPU_EINVAL;
+    }
+    XPU_TRY_CUDA(ensure_smem_attr((const void*)k, plan.smem));
+    XPU_TRY_CUDA(launch_ex(k, plan.grid, plan.block, plan.smem, o, p));
+  } else {
+    void (*g)(MvParams, int64_t) = mv_gen_kernel<2, EPI, PRO>;
+    XPU_TRY_CUDA(ensure_smem_attr((const void*)g, plan.smem));
+    XPU_TRY_CUDA(launch_ex(g, plan.grid, plan.block, plan.smem, o, p, plan.off_words));
+  }
+  return XPU_OK;
+}
+
+}  // namespace xpu

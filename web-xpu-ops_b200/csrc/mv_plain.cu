@@ -1,0 +1,10 @@
+// Instantiates the matvecQ8 kernels for (EPI_PLAIN, PRO_PLAIN); one translation
+// unit per epilogue/prologue pair so they compile in parallel.
+#include "matvec_launch.cuh"
+
+namespace xpu {
+template <>
+int launch_mv<EPI_PLAIN, PRO_PLAIN>(const MvParams& p, const MvPlan& plan, const LaunchOpts& o) {
+  return launch_mv_impl<EPI_PLAIN, PRO_PLAIN>(p, plan, o);
+}
+}  // namespace xpu

@@ -1,0 +1,180 @@
+// quantize.cu — per-row absmax int8 quantization, packQ8, their fusion, and
+// the seeded synthetic-data generator.
+//
+// Bit-exactness with ops/quantize/reference.ts:13-38: absmax is exact (a max
+// of |x|), `absmax / 127` and `127 / absmax` are IEEE f64 divisions (CUDA's
+// f64 `/` is correctly rounded), `x * inverse` is one f64 multiply, and
+// Math.round is `floor(v) + (v - floor(v) >= 0.5)` — ties toward +infinity,
+// the form llm/tools/quant_common.py:52-55 proves equal to Math.round.  A NaN
+// anywhere in a row makes absmax NaN (JS Math.max propagates it), so the
+// scale is NaN and every code 0 (Int32Array stores NaN as 0).
+#include "common.cuh"
+
+namespace xpu {
+
+namespace {
+
+__device__ __forceinline__ int32_t js_round_clamp(double v) {
+  if (v != v) return 0;  // NaN -> Int32Array 0
+  double f = floor(v);
+  double r = f + ((v - f) >= 0.5 ? 1.0 : 0.0);
+  r = r < -127.0 ? -127.0 : (r > 127.0 ? 127.0 : r);
+  return (int32_t)r;
+}
+
+// Row statistics: absmax (NaN if any element is NaN) -> (scale, inverse).
+struct RowScale {
+  float scale;
+  double inverse;
+};
+
+__device__ RowScale row_scale(const float* row, int64_t D) {
+  __shared__ float red_max[32];
+  __shared__ int red_nan[32];
+  float m = 0.0f;
+  int nan = 0;
+  for (int64_t i = threadIdx.x; i < D; i += blockDim.x) {
+    float a = fabsf(row[i]);
+    if (a != a) nan = 1;
+    else m = fmaxf(m, a);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+  }
+  int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = (blockDim.x + 31) / 32;
+  if (lane == 0) {
+    red_max[warp] = m;
+    red_nan[warp] = nan;
+  }
+  __syncthreads();
+  float tm = 0.0f;
+  int tn = 0;
+  for (int w = 0; w < nw; ++w) {
+    tm = fmaxf(tm, red_max[w]);
+    tn |= red_nan[w];
+  }
+  __syncthreads();  // red_* reused by the next row
+  double absmax = tn ? (double)NAN : (double)tm;
+  RowScale rs;
+  rs.scale = absmax == 0.0 ? 1.0f : (float)(absmax / 127.0);
+  rs.inverse = absmax == 0.0 ? 0.0 : 127.0 / absmax;
+  return rs;
+}
+
+__global__ void quantize_kernel(const float* __restrict__ in, int64_t N, int64_t D, int32_t* __restrict__ out,
+                                float* __restrict__ scales) {
+  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+    const float* r = in + row * D;
+    RowScale rs = row_scale(r, D);
+    if (threadIdx.x == 0) scales[row] = rs.scale;
+    for (int64_t i = threadIdx.x; i < D; i += blockDim.x) out[row * D + i] = js_round_clamp((double)r[i] * rs.inverse);
+  }
+}
+
+// packQ8 (ops/matvec/reference.ts:267-283): word w of a row holds codes
+// 4w..4w+3 least-significant byte first; lanes at or past K stay 0.
+template <typename CodeT>
+__global__ void pack_kernel(const CodeT* __restrict__ codes, int64_t N, int64_t K, uint32_t* __restrict__ packed) {
+  const int64_t W = (K + 3) / 4, total = N * W;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t row = i / W, word = i - row * W;
+    uint32_t bits = 0;
+#pragma unroll
+    for (int lane = 0; lane < 4; ++lane) {
+      int64_t col = word * 4 + lane;
+      if (col < K) bits |= ((uint32_t)(int32_t)codes[row * K + col] & 0xffu) << (8 * lane);
+    }
+    packed[i] = bits;
+  }
+}
+
+__global__ void quantize_pack_kernel(const float* __restrict__ in, int64_t N, int64_t K, uint32_t* __restrict__ packed,
+                                     float* __restrict__ scales) {
+  const int64_t W = (K + 3) / 4;
+  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+    const float* r = in + row * K;
+    RowScale rs = row_scale(r, K);
+    if (threadIdx.x == 0) scales[row] = rs.scale;
+    for (int64_t w = threadIdx.x; w < W; w += blockDim.x) {
+      uint32_t bits = 0;
+#pragma unroll
+      for (int lane = 0; lane < 4; ++lane) {
+        int64_t col = 4 * w + lane;
+        if (col < K) bits |= ((uint32_t)js_round_clamp((double)r[col] * rs.inverse) & 0xffu) << (8 * lane);
+      }
+      packed[row * W + w] = bits;
+    }
+  }
+}
+
+// splitmix64's output mix (Steele, Lea, Flood 2014), used as a counter hash.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ uint64_t hash3(uint64_t seed, uint64_t i, uint64_t lane) {
+  return mix64(seed * 0x9E3779B97F4A7C15ull + (3 * i + lane + 1) * 0xD1B54A32D192ED03ull);
+}
+
+__global__ void fill_normal_kernel(float* out, int64_t n, uint64_t seed, double mean, double stdv, double frac,
+                                   double mul) {
+  const double inv53 = 1.0 / 9007199254740992.0;  // 2^-53
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    double u1 = (double)((hash3(seed, i, 0) >> 11) + 1) * inv53;  // (0, 1]
+    double u2 = (double)(hash3(seed, i, 1) >> 11) * inv53;        // [0, 1)
+    double z = sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
+    double v = mean + stdv * z;
+    if (frac > 0.0 && (double)(hash3(seed, i, 2) >> 11) * inv53 < frac) v *= mul;
+    out[i] = (float)v;
+  }
+}
+
+int grid_for(int64_t work, int per_block) {
+  int64_t g = (work + per_block - 1) / per_block;
+  int64_t cap = (int64_t)device_info().sm_count * 16;
+  return (int)(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
+}  // namespace
+
+int quantize_dev(const float* in, int64_t N, int64_t D, int32_t* out, float* scales, cudaStream_t s) {
+  if (N == 0) return XPU_OK;
+  quantize_kernel<<<grid_for(N, 1), 256, 0, s>>>(in, N, D, out, scales);
+  XPU_TRY_CUDA(cudaGetLastError());
+  return XPU_OK;
+}
+
+int pack_q8_dev_i32(const int32_t* codes, int64_t N, int64_t K, uint32_t* packed, cudaStream_t s) {
+  int64_t total = N * ((K + 3) / 4);
+  if (total == 0) return XPU_OK;
+  pack_kernel<int32_t><<<grid_for(total, 256), 256, 0, s>>>(codes, N, K, packed);
+  XPU_TRY_CUDA(cudaGetLastError());
+  return XPU_OK;
+}
+
+int pack_q8_dev_i8(const int8_t* codes, int64_t N, int64_t K, uint32_t* packed, cudaStream_t s) {
+  int64_t total = N * ((K + 3) / 4);
+  if (total == 0) return XPU_OK;
+  pack_kernel<int8_t><<<grid_for(total, 256), 256, 0, s>>>(codes, N, K, packed);
+  XPU_TRY_CUDA(cudaGetLastError());
+  return XPU_OK;
+}
+
+int quantize_pack_dev(const float* w, int64_t N, int64_t K, uint32_t* packed, float* scales, cudaStream_t s) {
+  if (N == 0) return XPU_OK;
+  quantize_pack_kernel<<<grid_for(N, 1), 256, 0, s>>>(w, N, K, packed, scales);
+  XPU_TRY_CUDA(cudaGetLastError());
+  return XPU_OK;
+}
+
+int fill_normal_dev(float* out, int64_t n, uint64_t seed, double mean, double stdv, double frac, double mul,
+                    cudaStream_t s) {
+  if (n == 0) return XPU_OK;
+  fill_normal_kernel<<<grid_for(n, 256), 256, 0, s>>>(out, n, seed, mean, stdv, frac, mul);
+  XPU_TRY_CUDA(cudaGetLastError());
+  return XPU_OK;
+}
+
+}  // namespace xpu

@@ -1,0 +1,170 @@
+// runtime.cu — status plumbing, device queries and the memory/stream entry
+// points of the C ABI.
+#include <stdarg.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace xpu {
+
+namespace {
+thread_local std::string t_last_error;
+}
+
+void set_error(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+}
+
+void clear_error() { t_last_error.clear(); }
+
+int cuda_status(cudaError_t e, const char* what) {
+  set_error("CUDA error %s (%s) in %s", cudaGetErrorName(e), cudaGetErrorString(e), what);
+  return e == cudaErrorMemoryAllocation ? XPU_ENOMEM : XPU_ECUDA;
+}
+
+__device__ unsigned int g_device_error = 0;
+
+unsigned int* device_error_word() {
+  static std::mutex mu;
+  static std::unordered_map<int, unsigned int*> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  unsigned int* p = nullptr;
+  if (cudaGetSymbolAddress((void**)&p, g_device_error) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  cache.emplace(dev, p);
+  return p;
+}
+
+int check_device_error() {
+  unsigned int v = 0, zero = 0;
+  XPU_TRY_CUDA(cudaMemcpyFromSymbol(&v, g_device_error, sizeof v));
+  if (v) {
+    XPU_TRY_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof zero));
+    set_error("a bounded device-side wait timed out (device error word 0x%x)", v);
+    return XPU_ETIMEOUT;
+  }
+  return XPU_OK;
+}
+
+const DeviceInfo& device_info() {
+  static std::mutex mu;
+  static std::unordered_map<int, DeviceInfo> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  DeviceInfo di;
+  cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&di.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (di.sm_count <= 0) di.sm_count = 1;
+  if (di.max_smem_optin <= 0) di.max_smem_optin = 48 * 1024;
+  return cache.emplace(dev, di).first->second;
+}
+
+cudaError_t ensure_smem_attr(const void* kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  static std::mutex mu;
+  static std::unordered_map<const void*, std::unordered_map<int, size_t>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& have = done[kernel][dev];
+  if (have >= bytes) return cudaSuccess;
+  // Raise to the device maximum once, so later, larger plans need no call.
+  size_t want = (size_t)device_info().max_smem_optin;
+  if (want < bytes) want = bytes;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
+  if (e == cudaSuccess) have = want;
+  return e;
+}
+
+}  // namespace xpu
+
+using namespace xpu;
+
+extern "C" {
+
+const char* xpu_last_error(void) { return t_last_error.c_str(); }
+
+int xpu_abi_version(void) { return 1; }
+
+int xpu_device_count(int* count) {
+  XPU_REQUIRE(count, XPU_EINVAL, "xpu_device_count: null pointer");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) {
+    cudaGetLastError();
+    n = 0;
+  } else if (e != cudaSuccess) {
+    return cuda_status(e, "cudaGetDeviceCount");
+  }
+  *count = n;
+  return XPU_OK;
+}
+
+int xpu_set_device(int device) {
+  XPU_TRY_CUDA(cudaSetDevice(device));
+  return XPU_OK;
+}
+
+int xpu_malloc(void** ptr, size_t bytes) {
+  XPU_REQUIRE(ptr, XPU_EINVAL, "xpu_malloc: null pointer");
+  *ptr = nullptr;
+  if (bytes == 0) return XPU_OK;
+  XPU_TRY_CUDA(cudaMalloc(ptr, bytes));
+  return XPU_OK;
+}
+
+int xpu_free(void* ptr) {
+  if (ptr) XPU_TRY_CUDA(cudaFree(ptr));
+  return XPU_OK;
+}
+
+int xpu_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream) {
+  if (!bytes) return XPU_OK;
+  XPU_REQUIRE(dst && src, XPU_EINVAL, "xpu_memcpy_h2d: null pointer");
+  XPU_TRY_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream));
+  return XPU_OK;
+}
+
+int xpu_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream) {
+  if (!bytes) return XPU_OK;
+  XPU_REQUIRE(dst && src, XPU_EINVAL, "xpu_memcpy_d2h: null pointer");
+  XPU_TRY_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  return XPU_OK;
+}
+
+int xpu_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream) {
+  if (!bytes) return XPU_OK;
+  XPU_REQUIRE(dst && src, XPU_EINVAL, "xpu_memcpy_d2d: null pointer");
+  XPU_TRY_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+  return XPU_OK;
+}
+
+int xpu_memset(void* dst, int value, size_t bytes, void* stream) {
+  if (!bytes) return XPU_OK;
+  XPU_REQUIRE(dst, XPU_EINVAL, "xpu_memset: null pointer");
+  XPU_TRY_CUDA(cudaMemsetAsync(dst, value, bytes, (cudaStream_t)stream));
+  return XPU_OK;
+}
+
+int xpu_stream_sync(void* stream) {
+  XPU_TRY_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  return check_device_error();
+}
+
+}  // extern "C"
