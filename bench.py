@@ -1,0 +1,523 @@
+#!/usr/bin/env python
+"""Benchmark of the matvecQ8 hot path on B200s (one process per GPU).
+
+Headline workload (second part, which at N = 1 is the
+1-GPU 28672 x 8192 target GEMV 80 times over): a stack of 80 Q8 matrices
+[28672 x 8192] (W ~ N(0, 0.02^2), per-row absmax scales) applied to one
+x ~ N(0, 1).  Rows are sharded across the N GPUs (28672 / N rows of every
+matrix per GPU) and the output slices are gathered with an NCCL all-gather,
+so total work is fixed as N grows (strong scaling).  A step is one pass over
+the whole stack.  The weights (18.8 GB / N per GPU) are far larger than L2,
+so no flush is needed between steps.
+
+Metric: achieved HBM GB/s of algorithmic bytes (codes + scales + x + y of
+every matrix; x counted once per GPU), whole job.  Also reported:
+  - e2e: the same metric through the C ABI with host buffers: each step
+    copies x from pinned host memory, runs the stack and the gather, and
+    reads y back to pinned host memory;
+  - roofline of the GEMV kernel (bytes per launch / average launch time,
+    CUDA events on the launching stream) against MEASURED_PEAKS.json;
+  - cpu_baseline (N = 1): the CPU oracle, a restatement of the reference's
+    reference.ts, single-threaded like JavaScript, on one of the matrices;
+  - decode: Q8 decode tokens/s of a ~1.1B Llama (config 4) from a 2048
+    position context, 128 greedy steps, replicated on every GPU.
+
+`--impl reference` times the reference's CPU implementation of the path
+(the oracle port; the TypeScript cannot run here) with every host thread.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "web-xpu-ops_b200"))
+sys.path.insert(0, str(ROOT))
+
+MATRICES, ROWS, COLS = 80, 28672, 8192
+METRIC = "matvecQ8 achieved HBM GB/s vs B200 peak; Q8 decode tokens/s, 1-8 GPUs"
+
+
+def parse():
+    global ROWS, COLS
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--matrices", type=int, default=MATRICES)
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--decode-steps", type=int, default=128)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--rows", type=int, default=ROWS, help=argparse.SUPPRESS)
+    ap.add_argument("--cols", type=int, default=COLS, help=argparse.SUPPRESS)
+    args = ap.parse_args()
+    ROWS, COLS = args.rows, args.cols
+    return args
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def algorithmic_bytes(rows: int, K: int, matrices: int) -> int:
+    """codes + scales + y of `rows` rows per matrix, and x once (SURVEY 8(d) formula per launch, x shared)."""
+    W = (K + 3) // 4
+    return matrices * (rows * W * 4 + rows * 4 + rows * 4) + K * 4
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(kernel_key: str):
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get(kernel_key)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.idx = {str(i) for i in gpu_indices}
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.flush()
+        rows = []
+        for line in Path(self.out.name).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) == 9 and f[0] in self.idx:
+                rows.append(f)
+        os.unlink(self.out.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        for r in rows:
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows),
+                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
+
+
+def physical_gpu(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local < len(ids) and ids[local].isdigit():
+            return int(ids[local])
+    return local
+
+
+# ------------------------------------------------------------- our arm ---
+
+def build_stack(torch, ops, rank, world, matrices, stream):
+    """This GPU's row shard of every matrix, generated and quantized on the
+    device: rows [rank*R, (rank+1)*R) of matrix m are elements
+    [rank*R*K, (rank+1)*R*K) of the seed-m stream, the same for any N."""
+    from xpuops.synth import tensor_seed
+
+    R, K, W = ROWS // world, COLS, COLS // 4
+    dev = torch.device("cuda", torch.cuda.current_device())
+    weights = torch.empty(matrices * R * W, dtype=torch.int32, device=dev)
+    scales = torch.empty(matrices * R, dtype=torch.float32, device=dev)
+    tmp = torch.empty(R * K, dtype=torch.float32, device=dev)
+    for m in range(matrices):
+        ops.fill_normal_dev(tmp, R * K, tensor_seed(0, m), 0.0, 0.02, stream=stream, start=rank * R * K)
+        ops.quantizePackQ8_dev(tmp, R, K, weights.data_ptr() + 4 * m * R * W, scales.data_ptr() + 4 * m * R,
+                               stream=stream)
+    x = torch.empty(K, dtype=torch.float32, device=dev)
+    ops.fill_normal_dev(x, K, tensor_seed(1, 0), 0.0, 1.0, stream=stream)
+    torch.cuda.synchronize()
+    del tmp
+    return weights, scales, x, R
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+
+    from xpuops import ops
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    M, K = args.matrices, COLS
+    weights, scales, x, R = build_stack(torch, ops, rank, world, M, sp)
+    W = K // 4
+    y_local = torch.empty(M * R, dtype=torch.float32, device="cuda")
+    y_full = torch.empty(world * M * R, dtype=torch.float32, device="cuda")
+
+    def step():
+        ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
+        if world > 1:
+            dist.all_gather_into_tensor(y_full, y_local)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    sampler = ClockSampler([physical_gpu(i) for i in range(world)]) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0.record(stream)
+    for i in range(args.steps):
+        g_events[i][0].record(stream)
+        ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
+        g_events[i][1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(y_full, y_local)
+    t1.record(stream)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    total_ms = max_over_ranks(t0.elapsed_time(t1))
+    gemv_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in g_events))
+
+    bytes_rank = algorithmic_bytes(R, K, M)
+    bytes_job = bytes_rank * world
+    value = bytes_job * args.steps / (total_ms / 1e3) / 1e9
+    per_launch_bytes = algorithmic_bytes(R, K, 1)
+    avg_launch_s = gemv_ms / 1e3 / (args.steps * M)
+    achieved = per_launch_bytes / avg_launch_s / 1e9
+    peak, peak_src = measured_peaks()
+    traffic = ncu_traffic(f"mv_bulk_kernel_{R}x{K}")
+
+    # e2e: host x in, host y out, through the C ABI, per step
+    x_host = torch.empty(K, dtype=torch.float32).pin_memory()
+    x_host.copy_(x.cpu())
+    y_host = torch.empty(world * M * R, dtype=torch.float32).pin_memory()
+    for _ in range(3):
+        x.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(y_full if world > 1 else y_local, non_blocking=True)
+        stream.synchronize()
+    e2e_steps = max(10, args.steps // 4)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        x.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(y_full if world > 1 else y_local, non_blocking=True)
+        stream.synchronize()  # the host reads y every step
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = bytes_job * e2e_steps / (e2e_ms / 1e3) / 1e9
+
+    decode = None
+    if not args.no_decode:
+        decode = run_decode(args, torch, world, max_over_ranks, barrier)
+
+    cpu = None
+    if world == 1 and rank == 0:
+        cpu = cpu_baseline(weights, scales, x, R, K, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(3, args.warmup),
+            "ms_per_step": round(total_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "int8*f32",
+            "data": "synthetic (seeded N(0, 0.02^2) weights quantized per row, x ~ N(0, 1))",
+            "config": {
+                "workload": f"matvecQ8 stack: {M} x [{ROWS} x {COLS}] Q8 on one x, rows sharded over {world} GPU(s)"
+                            + (", NCCL all-gather of y" if world > 1 else ""),
+                "matrices": M, "N": ROWS, "K": COLS, "rows_per_gpu": R,
+                "bytes_per_step": bytes_job, "l2": "no flush: 18.8 GB / N of weights per step >> 126 MB L2",
+                "parallelism": f"row-shard x{world}",
+            },
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "traffic": traffic, "kernel": "mv_bulk_kernel (matvecQ8, bulk-copy path)",
+                         "launch_ms": round(avg_launch_s * 1e3, 5)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": K * 4,
+                    "d2h_bytes_per_step": world * M * R * 4, "ms_per_step": round(e2e_ms / e2e_steps, 4)},
+            "gpu_launches": args.steps * M * world,
+            "gpu_launches_per_rank": args.steps * M,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "decode": decode,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(weights, scales, x, R, K, seconds):
+    """The oracle (a restatement of ops/matvec/reference.ts#matvecQ8, f64,
+    single-threaded like JavaScript) on matrix 0, repeated for ~`seconds`."""
+    import oracle.oracle as orc
+
+    W = K // 4
+    w = weights[: R * W].cpu().numpy().view(np.uint32)
+    s = scales[:R].cpu().numpy()
+    xv = x.cpu().numpy()
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        orc.matvec_q8(w, s, xv, R, K)
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or passes >= 200:
+            break
+    gbs = algorithmic_bytes(R, K, 1) * passes / el / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"matrix 0 of the stack ([{R} x {K}]), {passes} passes, {el:.1f} s, single thread",
+            "cpu": _cpu_model()}
+
+
+def _cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip() + f" x{os.cpu_count()}"
+    except OSError:
+        pass
+    return f"{os.cpu_count()} cpus"
+
+
+def decode_bytes_per_token(cfg, pos: int) -> int:
+    """Algorithmic bytes of one decode step at position `pos` (the cache
+    holds pos + 1 entries once this step's K/V are written)."""
+    c = cfg
+    q, kv = c.numHeads * c.headDim, c.numKvHeads * c.headDim
+    per_layer_rows = q + 2 * kv + c.hiddenSize + 2 * c.ffnHidden + c.hiddenSize
+    per_layer_codes = (q + 2 * kv) * c.hiddenSize + c.hiddenSize * q + 2 * c.ffnHidden * c.hiddenSize + \
+        c.hiddenSize * c.ffnHidden
+    codes = c.numLayers * per_layer_codes + c.vocabSize * c.hiddenSize
+    scales = 4 * (c.numLayers * per_layer_rows + c.vocabSize)
+    norms = 4 * c.hiddenSize * (2 * c.numLayers + 1)
+    kv_read = c.numLayers * 2 * c.numKvHeads * (pos + 1) * c.headDim * 4
+    kv_write = c.numLayers * 2 * kv * 4
+    return codes + scales + norms + kv_read + kv_write + c.hiddenSize * 2
+
+
+def random_q8_linear_dev(torch, ops, rows, cols, seed, std=0.02):
+    """Seeded N(0, std^2) weights quantized on the device, returned as host
+    int8 codes + f32 scales (the engine's QuantizedLinear input)."""
+    from xpuops.llama import QuantizedLinear
+
+    f = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+    ops.fill_normal_dev(f, rows * cols, seed, 0.0, std, stream=torch.cuda.current_stream().cuda_stream)
+    codes = torch.empty(rows * cols, dtype=torch.int32, device="cuda")
+    sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+    ops.quantize_dev(f, rows, cols, codes, sc, stream=torch.cuda.current_stream().cuda_stream)
+    return QuantizedLinear(codes.to(torch.int8).cpu().numpy(), sc.cpu().numpy())
+
+
+def run_decode(args, torch, world, max_over_ranks, barrier):
+    """Config 4: random-init ~1.1B Llama, f32 KV cache prefilled with N(0, 1)
+    to 2048 positions, 128 greedy steps from a random token id."""
+    from xpuops import LLAMA_1B_DECODE_CONFIG, LlamaEngineQ8Resident, ops
+    from xpuops.llama import LlamaLayerWeightsQ8, LlamaWeightsQ8
+    from xpuops.synth import tensor_seed
+
+    cfg = LLAMA_1B_DECODE_CONFIG
+    c = cfg
+    q, kv = c.numHeads * c.headDim, c.numKvHeads * c.headDim
+    idx = iter(range(100_000))
+    lin = lambda n, k: random_q8_linear_dev(torch, ops, n, k, tensor_seed(40, next(idx)))
+    ones = np.ones(c.hiddenSize, np.float32)  # HF default RMSNorm init
+    layers = [LlamaLayerWeightsQ8(attnNorm=ones, wq=lin(q, c.hiddenSize), wk=lin(kv, c.hiddenSize),
+                                  wv=lin(kv, c.hiddenSize), wo=lin(c.hiddenSize, q), ffnNorm=ones,
+                                  wGate=lin(c.ffnHidden, c.hiddenSize), wUp=lin(c.ffnHidden, c.hiddenSize),
+                                  wDown=lin(c.hiddenSize, c.ffnHidden)) for _ in range(c.numLayers)]
+    weights = LlamaWeightsQ8(embedTokens=random_q8_linear_dev(torch, ops, c.vocabSize, c.hiddenSize,
+                                                              tensor_seed(40, next(idx))),
+                             layers=layers, finalNorm=ones, lmHead=lin(c.vocabSize, c.hiddenSize))
+    ctx = 2048
+    rng = np.random.default_rng(41)
+    eng = LlamaEngineQ8Resident.create(cfg, weights, torch.cuda.current_device())
+    try:
+        for l in range(c.numLayers):
+            k = rng.standard_normal(c.numKvHeads * ctx * c.headDim, dtype=np.float32)
+            v = rng.standard_normal(c.numKvHeads * ctx * c.headDim, dtype=np.float32)
+            eng.setKv(l, k, v, ctx)
+        first = int(rng.integers(0, c.vocabSize))
+        warm = 3
+        eng.greedySteps(first, warm)
+        es = torch.cuda.ExternalStream(eng.stream())
+        barrier()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(es)
+        toks = eng.greedySteps(first, args.decode_steps)
+        d1.record(es)
+        d1.synchronize()
+        ms = max_over_ranks(d0.elapsed_time(d1))
+        # host-API decode (forward(), logits copied to the host every token)
+        h0 = time.perf_counter()
+        n_host = 32
+        tok = int(toks[-1])
+        for _ in range(n_host):
+            (logits,) = eng.forward([tok])
+            tok = int(np.argmax(logits))
+        host_ms = max_over_ranks((time.perf_counter() - h0) * 1e3)
+        pos0 = ctx + warm
+        byts = sum(decode_bytes_per_token(cfg, pos0 + i) for i in range(args.decode_steps))
+        peak, src = measured_peaks()
+        tps = args.decode_steps / (ms / 1e3)
+        return {
+            "tokens_per_s": round(tps * world, 1),
+            "tokens_per_s_per_gpu": round(tps, 1),
+            "ms_per_token": round(ms / args.decode_steps, 4),
+            "config": "22 layers, hidden 2048, 32q/4kv heads, head_dim 64, FFN 5632, vocab 32000; context "
+                      f"{pos0}..{pos0 + args.decode_steps}; greedy; replicas on each GPU",
+            "bytes_per_token": byts // args.decode_steps,
+            "achieved_gbs": round(byts / (ms / 1e3) / 1e9, 1),
+            "roofline_frac": round(byts / (ms / 1e3) / 1e9 / peak, 4),
+            "gpu_launches_per_token": 5 * c.numLayers + 3,
+            "e2e_host_forward": {"tokens_per_s": round(n_host / (host_ms / 1e3) * world, 1),
+                                 "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * c.vocabSize},
+        }
+    finally:
+        eng.close()
+
+
+# ------------------------------------------------------- reference arm ---
+
+def run_reference(args, rank, world):
+    """The reference's CPU path for this workload: ops/matvec/reference.ts
+    `matvecQ8`, restated in C (oracle/), the TypeScript itself having no
+    runtime on this image; every host thread, on a bounded sample."""
+    if rank != 0:
+        return
+    import oracle.oracle as orc
+
+    K, R = COLS, ROWS  # one whole matrix of the stack per step
+    threads = os.cpu_count() or 1
+    w, s, x, how = reference_sample(R, K)
+    for _ in range(max(1, min(args.warmup, 3))):
+        orc.matvec_q8(w, s, x, R, K, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.matvec_q8(w, s, x, R, K, threads=threads)
+    el = time.perf_counter() - t0
+    value = algorithmic_bytes(R, K, 1) * args.steps / el / 1e9
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(el * 1e3 / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int8*f64 (reference.ts accumulates in f64)",
+        "data": "synthetic (seeded N(0, 0.02^2) weights quantized per row, x ~ N(0, 1))",
+        "config": {"workload": f"matvecQ8 stack: {args.matrices} x [{ROWS} x {COLS}] Q8 on one x; "
+                               f"each step one [{R} x {K}] matrix of it on the CPU",
+                   "matrices": args.matrices, "N": ROWS, "K": COLS, "parallelism": f"{threads} host threads"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"one [{R} x {K}] matrix per step ({how}), {args.steps} steps",
+                         "cpu": _cpu_model()},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference.ts cannot run here (no JavaScript runtime on the image); the C restatement of "
+                "ops/matvec/reference.ts:117-131 stands in",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def reference_sample(R, K):
+    """Matrix 0 of the stack: generated by the GPU when one is visible (as
+    our arm does), else by the host recipe (slower, identical values up to
+    one f32 ulp)."""
+    import oracle.oracle as orc
+    from xpuops.synth import fill_normal, tensor_seed
+
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            from xpuops import ops
+
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+            weights, scales, x, _ = build_stack(torch, ops, 0, 1, 1, torch.cuda.current_stream().cuda_stream)
+            return (weights.cpu().numpy().view(np.uint32), scales.cpu().numpy(), x.cpu().numpy(),
+                    "generated on the GPU, untimed")
+    except Exception:
+        pass
+    wf = fill_normal(R * K, tensor_seed(0, 0), 0.0, 0.02)
+    codes, sc = orc.quantize(wf, R, K)
+    return orc.pack_q8(codes, R, K), sc, fill_normal(K, tensor_seed(1, 0)), "generated on the host, untimed"
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -29,6 +29,12 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#if defined(__GNUC__)
+#define XPU_API __attribute__((visibility("default")))
+#else
+#define XPU_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -44,21 +50,21 @@ extern "C" {
 #define XPU_ENOMEM    7  /* device allocation failed                       */
 
 /* Message for the last failed call on this thread ("" if none). */
-const char* xpu_last_error(void);
+XPU_API const char* xpu_last_error(void);
 /* ABI version, bumped on any incompatible change. */
-int xpu_abi_version(void);
+XPU_API int xpu_abi_version(void);
 /* Number of visible CUDA devices (0 and XPU_OK on a machine without one). */
-int xpu_device_count(int* count);
+XPU_API int xpu_device_count(int* count);
 
 /* ---- device memory and streams (for hosts without an allocator) -------- */
-int xpu_malloc(void** ptr, size_t bytes);
-int xpu_free(void* ptr);
-int xpu_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
-int xpu_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
-int xpu_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
-int xpu_memset(void* dst, int value, size_t bytes, void* stream);
-int xpu_stream_sync(void* stream);
-int xpu_set_device(int device);
+XPU_API int xpu_malloc(void** ptr, size_t bytes);
+XPU_API int xpu_free(void* ptr);
+XPU_API int xpu_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+XPU_API int xpu_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+XPU_API int xpu_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+XPU_API int xpu_memset(void* dst, int value, size_t bytes, void* stream);
+XPU_API int xpu_stream_sync(void* stream);
+XPU_API int xpu_set_device(int device);
 
 /* ---- host-array ops: synchronous, caller-owned arrays, mirror the TS API --
  * Each copies its inputs to the current device, runs the sm_100a kernel and
@@ -66,31 +72,31 @@ int xpu_set_device(int device);
 
 /* ops/quantize/reference.ts:13-38 `quantize({input, N, D})`.
  * Bit-exact: f64 `127/absmax`, `Math.round` (ties toward +inf), clamp. */
-int xpu_quantize(const float* input, int64_t N, int64_t D,
+XPU_API int xpu_quantize(const float* input, int64_t N, int64_t D,
                  int32_t* output, float* scales);
 
 /* ops/matvec/reference.ts:267-283 `packQ8({codes, N, K})`. */
-int xpu_pack_q8(const int32_t* codes, int64_t N, int64_t K, uint32_t* packed);
+XPU_API int xpu_pack_q8(const int32_t* codes, int64_t N, int64_t K, uint32_t* packed);
 
 /* llm/weights-q8.ts:137-139 `packInt8Rows(codes, N, K)` (int8 codes). */
-int xpu_pack_int8_rows(const int8_t* codes, int64_t N, int64_t K, uint32_t* packed);
+XPU_API int xpu_pack_int8_rows(const int8_t* codes, int64_t N, int64_t K, uint32_t* packed);
 
 /* Fused `packQ8(quantize(w))`: ops/quantize/reference.ts:13-38 followed by
  * ops/matvec/reference.ts:267-283, in one pass.  Bit-exact. */
-int xpu_quantize_pack_q8(const float* w, int64_t N, int64_t K,
+XPU_API int xpu_quantize_pack_q8(const float* w, int64_t N, int64_t K,
                          uint32_t* packed, float* scales);
 
 /* ops/matvec/reference.ts:117-131 `matvecQ8({weight, scale, vector, N, K})`. */
-int xpu_matvec_q8(const uint32_t* weight, const float* scale, const float* vector,
+XPU_API int xpu_matvec_q8(const uint32_t* weight, const float* scale, const float* vector,
                   int64_t N, int64_t K, float* output);
 
 /* ops/matvec/reference.ts:196-207 `matvecQ8Ffn(...)`: silu(gate)*up. */
-int xpu_matvec_q8_ffn(const uint32_t* weight_gate, const float* scale_gate,
+XPU_API int xpu_matvec_q8_ffn(const uint32_t* weight_gate, const float* scale_gate,
                       const uint32_t* weight_up, const float* scale_up,
                       const float* vector, int64_t N, int64_t K, float* output);
 
 /* ops/matvec/reference.ts:235-242 `matvecQ8Residual(...)`: residual + W.x. */
-int xpu_matvec_q8_residual(const uint32_t* weight, const float* scale,
+XPU_API int xpu_matvec_q8_residual(const uint32_t* weight, const float* scale,
                            const float* vector, const float* residual,
                            int64_t N, int64_t K, float* output);
 
@@ -100,34 +106,46 @@ int xpu_matvec_q8_residual(const uint32_t* weight, const float* scale,
  * (TMA) streaming path, anything else the general vector path.           */
 
 /* Binding order of ops/matvec/wgsl/q8.wgsl:31-35: weight, scale, vector, out. */
-int xpu_matvec_q8_dev(const uint32_t* weight, const float* scale, const float* vector,
+XPU_API int xpu_matvec_q8_dev(const uint32_t* weight, const float* scale, const float* vector,
                       int64_t N, int64_t K, float* output, void* stream);
 /* ops/matvec/wgsl/q8_ffn.wgsl:29-35: wGate, sGate, wUp, sUp, vector, out. */
-int xpu_matvec_q8_ffn_dev(const uint32_t* weight_gate, const float* scale_gate,
+XPU_API int xpu_matvec_q8_ffn_dev(const uint32_t* weight_gate, const float* scale_gate,
                           const uint32_t* weight_up, const float* scale_up,
                           const float* vector, int64_t N, int64_t K, float* output,
                           void* stream);
 /* ops/matvec/wgsl/q8_residual.wgsl:30-35: weight, scale, vector, residual, out. */
-int xpu_matvec_q8_residual_dev(const uint32_t* weight, const float* scale,
+XPU_API int xpu_matvec_q8_residual_dev(const uint32_t* weight, const float* scale,
                                const float* vector, const float* residual,
                                int64_t N, int64_t K, float* output, void* stream);
+/* `count` matvecQ8 GEMVs on one vector (a stack of same-shaped matrices
+ * applied to the same x, e.g. every expert or layer slice of a model, or the
+ * row shard of each that one GPU holds): matrix m is `weights + m *
+ * weight_stride` (u32 words), its scales `scales + m * N`, its output
+ * `outputs + m * N`.  Consecutive launches overlap their weight streaming
+ * (programmatic dependent launch).  Same results as `count` calls of
+ * xpu_matvec_q8_dev. */
+XPU_API int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stride,
+                                    const float* scales, const float* vector, int64_t count,
+                                    int64_t N, int64_t K, float* outputs, void* stream);
 /* ops/quantize/wgsl/kernel.wgsl bindings (input, codes, scales), but with
  * reference.ts's rounding, so the codes are bit-exact. */
-int xpu_quantize_dev(const float* input, int64_t N, int64_t D,
+XPU_API int xpu_quantize_dev(const float* input, int64_t N, int64_t D,
                      int32_t* output, float* scales, void* stream);
-int xpu_pack_q8_dev(const int32_t* codes, int64_t N, int64_t K, uint32_t* packed,
+XPU_API int xpu_pack_q8_dev(const int32_t* codes, int64_t N, int64_t K, uint32_t* packed,
                     void* stream);
-int xpu_quantize_pack_q8_dev(const float* w, int64_t N, int64_t K,
+XPU_API int xpu_quantize_pack_q8_dev(const float* w, int64_t N, int64_t K,
                              uint32_t* packed, float* scales, void* stream);
 
 /* Seeded synthetic data (harness/roofline.ts:54-70 fills its probe buffer
  * with a hash; this is the normal-distribution counterpart used for every
- * synthetic config): element i = mean + std * z_i, z_i from Box-Muller on
- * two splitmix64(seed, i) uniforms; with probability `outlier_frac`
- * (decided by a third hash) the element is multiplied by `outlier_mul`. */
-int xpu_fill_normal_f32_dev(float* out, int64_t n, uint64_t seed, double mean,
-                            double std, double outlier_frac, double outlier_mul,
-                            void* stream);
+ * synthetic config): out[j] is element i = start + j of the stream
+ * mean + std * z_i, z_i from Box-Muller on two splitmix64(seed, i)
+ * uniforms; with probability `outlier_frac` (decided by a third hash) the
+ * element is multiplied by `outlier_mul`.  `start` lets a GPU generate just
+ * its shard of a tensor that is identical for any number of GPUs. */
+XPU_API int xpu_fill_normal_f32_dev(float* out, int64_t n, int64_t start, uint64_t seed,
+                                    double mean, double std, double outlier_frac,
+                                    double outlier_mul, void* stream);
 
 /* ---- the resident Q8 Llama engine (llm/engine-q8-resident.ts) ---------- */
 
@@ -178,7 +196,7 @@ typedef struct xpu_llama xpu_llama;
  * Checks shapes (llm/weights-q8.ts:68-96 `assertWeightShapesQ8`), packs every
  * linear on the device, allocates the KV cache and captures the decode step
  * into one CUDA graph.  Host weights may be freed after it returns. */
-int xpu_llama_create(const xpu_llama_config* config,
+XPU_API int xpu_llama_create(const xpu_llama_config* config,
                      const xpu_llama_weights_q8* weights, int device,
                      xpu_llama** engine);
 
@@ -188,7 +206,7 @@ int xpu_llama_create(const xpu_llama_config* config,
  * token (decode).  XPU_EINVAL for n == 0, XPU_ESTATE for n > 1 after prefill,
  * XPU_ERANGE when the position would pass maxSeqLen.  `logits` may be NULL
  * when only `argmax` (host, nullable) is wanted. */
-int xpu_llama_forward(xpu_llama* engine, const int32_t* tokens, int32_t n,
+XPU_API int xpu_llama_forward(xpu_llama* engine, const int32_t* tokens, int32_t n,
                       float* logits, int32_t* argmax);
 
 /* One decode step whose token id is read from device memory `token_dev`
@@ -196,30 +214,30 @@ int xpu_llama_forward(xpu_llama* engine, const int32_t* tokens, int32_t n,
  * written to device memory `next_dev`; logits stay on the device in the
  * engine's buffer (`xpu_llama_logits_dev`).  Async on the engine's stream;
  * advances the position.  For device-side generation loops. */
-int xpu_llama_decode_dev(xpu_llama* engine, const int32_t* token_dev, int32_t* next_dev);
+XPU_API int xpu_llama_decode_dev(xpu_llama* engine, const int32_t* token_dev, int32_t* next_dev);
 /* llm/engine.ts:240-256 `greedyGenerate`'s decode loop on the device: feeds
  * `first_token`, then `steps` decode steps, each step's argmax becoming the
  * next step's input with no host round trip.  `tokens_out` (host, nullable,
  * [steps]) receives each step's argmax.  Requires a prefilled engine. */
-int xpu_llama_greedy_steps(xpu_llama* engine, int32_t first_token, int32_t steps,
+XPU_API int xpu_llama_greedy_steps(xpu_llama* engine, int32_t first_token, int32_t steps,
                            int32_t* tokens_out);
-int xpu_llama_logits_dev(xpu_llama* engine, float** logits_dev);
-int xpu_llama_stream(xpu_llama* engine, void** stream);
+XPU_API int xpu_llama_logits_dev(xpu_llama* engine, float** logits_dev);
+XPU_API int xpu_llama_stream(xpu_llama* engine, void** stream);
 
 /* llm/engine-q8-resident.ts:993-996 `reset()`: position 0, next call is a
  * prefill; nothing is rebuilt and the KV cache is not cleared. */
-int xpu_llama_reset(xpu_llama* engine);
+XPU_API int xpu_llama_reset(xpu_llama* engine);
 /* llm/engine-q8-resident.ts:946-948 `position`. */
-int xpu_llama_position(const xpu_llama* engine, int32_t* position);
+XPU_API int xpu_llama_position(const xpu_llama* engine, int32_t* position);
 /* Fills positions [0, npos) of layer `layer`'s KV cache from host arrays
  * [numKvHeads, npos, headDim] and sets the position to npos, as if a prompt
  * of npos tokens had been prefilled (used to synthesize a long context). */
-int xpu_llama_set_kv(xpu_llama* engine, int32_t layer, const float* k,
+XPU_API int xpu_llama_set_kv(xpu_llama* engine, int32_t layer, const float* k,
                      const float* v, int32_t npos);
 /* Test hook, llm/engine-q8-resident.ts:1043-1050 `debugPoisonKVCache`:
  * every position of every layer's cache := value. */
-int xpu_llama_poison_kv(xpu_llama* engine, float value);
-int xpu_llama_destroy(xpu_llama* engine);
+XPU_API int xpu_llama_poison_kv(xpu_llama* engine, float value);
+XPU_API int xpu_llama_destroy(xpu_llama* engine);
 
 #ifdef __cplusplus
 }

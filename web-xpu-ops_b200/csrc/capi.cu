@@ -10,8 +10,8 @@ int quantize_dev(const float* in, int64_t N, int64_t D, int32_t* out, float* sca
 int pack_q8_dev_i32(const int32_t* codes, int64_t N, int64_t K, uint32_t* packed, cudaStream_t s);
 int pack_q8_dev_i8(const int8_t* codes, int64_t N, int64_t K, uint32_t* packed, cudaStream_t s);
 int quantize_pack_dev(const float* w, int64_t N, int64_t K, uint32_t* packed, float* scales, cudaStream_t s);
-int fill_normal_dev(float* out, int64_t n, uint64_t seed, double mean, double stdv, double frac, double mul,
-                    cudaStream_t s);
+int fill_normal_dev(float* out, int64_t n, int64_t start, uint64_t seed, double mean, double stdv, double frac,
+                    double mul, cudaStream_t s);
 
 namespace {
 
@@ -211,6 +211,30 @@ int xpu_matvec_q8_residual_dev(const uint32_t* weight, const float* scale, const
                     "matvecQ8Residual");
 }
 
+int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stride, const float* scales, const float* vector,
+                            int64_t count, int64_t N, int64_t K, float* outputs, void* stream) {
+  XPU_SHAPE(N, K, "matvecQ8 stack");
+  XPU_REQUIRE(count >= 0 && weight_stride >= N * ((K + 3) / 4), XPU_EINVAL,
+              "matvecQ8 stack: count must be >= 0 and the stride at least N*ceil(K/4) words");
+  if (N == 0 || count == 0) return XPU_OK;
+  XPU_REQUIRE(weights && scales && vector && outputs, XPU_EINVAL, "matvecQ8 stack: null pointer");
+  for (int64_t m = 0; m < count; ++m) {
+    MvParams p{};
+    p.w = weights + m * weight_stride;
+    p.s = scales + m * N;
+    p.x = vector;
+    p.y = outputs + m * N;
+    p.N = N;
+    p.K = K;
+    // The first launch follows whatever preceded it on the stream in full;
+    // later ones only read x (unchanged) and write their own outputs, so
+    // they may start while their predecessor drains.
+    int rc = run_matvec(p, EPI_PLAIN, PRO_PLAIN, LaunchOpts{(cudaStream_t)stream, m > 0});
+    if (rc) return rc;
+  }
+  return XPU_OK;
+}
+
 int xpu_quantize_dev(const float* input, int64_t N, int64_t D, int32_t* output, float* scales, void* stream) {
   XPU_SHAPE(N, D, "quantize");
   if (N == 0) return XPU_OK;
@@ -232,10 +256,10 @@ int xpu_quantize_pack_q8_dev(const float* w, int64_t N, int64_t K, uint32_t* pac
   return quantize_pack_dev(w, N, K, packed, scales, (cudaStream_t)stream);
 }
 
-int xpu_fill_normal_f32_dev(float* out, int64_t n, uint64_t seed, double mean, double std, double outlier_frac,
-                            double outlier_mul, void* stream) {
-  XPU_REQUIRE(n >= 0 && (out || n == 0), XPU_EINVAL, "fill_normal: bad arguments");
-  return fill_normal_dev(out, n, seed, mean, std, outlier_frac, outlier_mul, (cudaStream_t)stream);
+int xpu_fill_normal_f32_dev(float* out, int64_t n, int64_t start, uint64_t seed, double mean, double std,
+                            double outlier_frac, double outlier_mul, void* stream) {
+  XPU_REQUIRE(n >= 0 && start >= 0 && (out || n == 0), XPU_EINVAL, "fill_normal: bad arguments");
+  return fill_normal_dev(out, n, start, seed, mean, std, outlier_frac, outlier_mul, (cudaStream_t)stream);
 }
 
 }  // extern "C"

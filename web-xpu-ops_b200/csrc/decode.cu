@@ -549,6 +549,13 @@ int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, in
       cudaMallocHost(&e->h_logits, (size_t)c.vocab_size * 4) != cudaSuccess)
     return fail(cuda_status(cudaGetLastError(), "cudaMallocHost"));
   if (cudaDeviceSynchronize() != cudaSuccess) return fail(cuda_status(cudaGetLastError(), "create sync"));
+  // One eager step first, so every kernel is loaded and configured before
+  // stream capture; its only lasting effects (cache slot 0, the logits, the
+  // token and position words) are reset or overwritten by the first prefill.
+  if ((rc = record_step(e))) return fail(rc);
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess) return fail(cuda_status(cudaGetLastError(), "warm-up step"));
+  if ((rc = check_device_error())) return fail(rc);
+  if ((rc = set_device_pos(e, 0))) return fail(rc);
   if ((rc = build_graph(e))) return fail(rc);
   *out = e;
   return XPU_OK;

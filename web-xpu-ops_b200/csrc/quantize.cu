@@ -118,16 +118,17 @@ __device__ __forceinline__ uint64_t hash3(uint64_t seed, uint64_t i, uint64_t la
   return mix64(seed * 0x9E3779B97F4A7C15ull + (3 * i + lane + 1) * 0xD1B54A32D192ED03ull);
 }
 
-__global__ void fill_normal_kernel(float* out, int64_t n, uint64_t seed, double mean, double stdv, double frac,
-                                   double mul) {
+__global__ void fill_normal_kernel(float* out, int64_t n, int64_t start, uint64_t seed, double mean, double stdv,
+                                   double frac, double mul) {
   const double inv53 = 1.0 / 9007199254740992.0;  // 2^-53
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t i = (uint64_t)(start + j);
     double u1 = (double)((hash3(seed, i, 0) >> 11) + 1) * inv53;  // (0, 1]
     double u2 = (double)(hash3(seed, i, 1) >> 11) * inv53;        // [0, 1)
     double z = sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
     double v = mean + stdv * z;
     if (frac > 0.0 && (double)(hash3(seed, i, 2) >> 11) * inv53 < frac) v *= mul;
-    out[i] = (float)v;
+    out[j] = (float)v;
   }
 }
 
@@ -169,10 +170,10 @@ int quantize_pack_dev(const float* w, int64_t N, int64_t K, uint32_t* packed, fl
   return XPU_OK;
 }
 
-int fill_normal_dev(float* out, int64_t n, uint64_t seed, double mean, double stdv, double frac, double mul,
-                    cudaStream_t s) {
+int fill_normal_dev(float* out, int64_t n, int64_t start, uint64_t seed, double mean, double stdv, double frac,
+                    double mul, cudaStream_t s) {
   if (n == 0) return XPU_OK;
-  fill_normal_kernel<<<grid_for(n, 256), 256, 0, s>>>(out, n, seed, mean, stdv, frac, mul);
+  fill_normal_kernel<<<grid_for(n, 256), 256, 0, s>>>(out, n, start, seed, mean, stdv, frac, mul);
   XPU_TRY_CUDA(cudaGetLastError());
   return XPU_OK;
 }

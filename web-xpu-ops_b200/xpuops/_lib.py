@@ -108,7 +108,8 @@ SIGNATURES = {
     "xpu_quantize_dev": [P, I64, I64, P, P, P],
     "xpu_pack_q8_dev": [P, I64, I64, P, P],
     "xpu_quantize_pack_q8_dev": [P, I64, I64, P, P, P],
-    "xpu_fill_normal_f32_dev": [P, I64, C.c_uint64, C.c_double, C.c_double, C.c_double, C.c_double, P],
+    "xpu_fill_normal_f32_dev": [P, I64, I64, C.c_uint64, C.c_double, C.c_double, C.c_double, C.c_double, P],
+    "xpu_matvec_q8_stack_dev": [P, I64, P, P, I64, I64, I64, P, P],
     "xpu_llama_create": [C.POINTER(LlamaConfigC), C.POINTER(LlamaWeightsC), C.c_int, C.POINTER(P)],
     "xpu_llama_forward": [P, P, I32, P, P],
     "xpu_llama_decode_dev": [P, P, P],

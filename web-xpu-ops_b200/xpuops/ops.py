@@ -201,10 +201,18 @@ def quantizePackQ8_dev(input, N: int, K: int, packed, scales, stream=None) -> No
 
 
 def fill_normal_dev(output, n: int, seed: int, mean: float = 0.0, std: float = 1.0, outlier_frac: float = 0.0,
-                    outlier_mul: float = 1.0, stream=None) -> None:
-    """Seeded N(mean, std^2) f32 fill (see xpuops.synth for the exact recipe)."""
-    check(lib().xpu_fill_normal_f32_dev(_ptr(output), n, seed, mean, std, outlier_frac, outlier_mul,
+                    outlier_mul: float = 1.0, stream=None, start: int = 0) -> None:
+    """Elements [start, start + n) of the seeded N(mean, std^2) stream as f32
+    (see xpuops.synth for the exact recipe)."""
+    check(lib().xpu_fill_normal_f32_dev(_ptr(output), n, start, seed, mean, std, outlier_frac, outlier_mul,
                                         _ptr(stream) or None))
+
+
+def matvecQ8Stack_dev(weights, weight_stride: int, scales, vector, count: int, N: int, K: int, outputs,
+                      stream=None) -> None:
+    """`count` GEMVs of same-shaped matrices on one vector (xpu_matvec_q8_stack_dev)."""
+    check(lib().xpu_matvec_q8_stack_dev(_ptr(weights), weight_stride, _ptr(scales), _ptr(vector), count, N, K,
+                                        _ptr(outputs), _ptr(stream) or None))
 
 
 def stream_sync(stream=None) -> None:
