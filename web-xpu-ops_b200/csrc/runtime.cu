@@ -26,6 +26,7 @@ void clear_error() { t_last_error.clear(); }
 
 int cuda_status(cudaError_t e, const char* what) {
   set_error("CUDA error %s (%s) in %s", cudaGetErrorName(e), cudaGetErrorString(e), what);
+  cudaGetLastError();  // a non-sticky error must not surface again in a later call
   return e == cudaErrorMemoryAllocation ? XPU_ENOMEM : XPU_ECUDA;
 }
 
@@ -84,10 +85,14 @@ cudaError_t ensure_smem_attr(const void* kernel, size_t bytes) {
   std::lock_guard<std::mutex> lock(mu);
   size_t& have = done[kernel][dev];
   if (have >= bytes) return cudaSuccess;
-  // Raise to the device maximum once, so later, larger plans need no call.
-  size_t want = (size_t)device_info().max_smem_optin;
-  if (want < bytes) want = bytes;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
+  // Raise to the most this kernel can take (the device's opt-in limit less
+  // its static shared memory) once, so later, larger plans need no call.
+  cudaFuncAttributes fa{};
+  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return e;
+  size_t want = (size_t)device_info().max_smem_optin - fa.sharedSizeBytes;
+  if (want < bytes) return cudaErrorInvalidValue;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
   if (e == cudaSuccess) have = want;
   return e;
 }
