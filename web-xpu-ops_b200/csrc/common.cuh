@@ -91,12 +91,14 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
+// try_wait suspends the thread in hardware until the phase completes or the
+// hint (ns) passes, so a waiting warp does not spin through issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
@@ -134,6 +136,13 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
 // Named barrier among `count` threads (a multiple of 32), id 1..15.
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// 128-bit shared-memory load from a 32-bit shared-window address.
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
 }
 
 // 128-bit read-only global load that does not allocate in L1 (weights are
@@ -194,23 +203,47 @@ __device__ __forceinline__ f2 codes_pair(uint32_t wflip, int pair) {
   return c;
 }
 
-// acc[0..3] += codes(w) * x[0..15], w = 4 packed words (16 codes), x = 16
-// floats as 8 pairs.  Accumulator k collects word k.
-__device__ __forceinline__ void dot16(const uint4& w, const f2 (&x)[8], f2 (&acc)[4]) {
+// acc[k & 1] += codes(word k of w) . x[4k .. 4k+3] for the 16 codes of a
+// 16-byte slot, x held as 8 pairs: 4 LOP3 + 16 PRMT on the integer pipe and
+// 8 FADD2 + 8 FFMA2 (two f32 lanes each) on the FP pipe per slot.
+__device__ __forceinline__ void dot16(const uint4& w, const f2 (&x)[8], f2 (&acc)[2]) {
   const f2 negmagic = make_f2(-kMagic, -kMagic);
-  uint32_t ws[4] = {w.x ^ kSignFlip, w.y ^ kSignFlip, w.z ^ kSignFlip, w.w ^ kSignFlip};
+  const uint32_t ws[4] = {w.x ^ kSignFlip, w.y ^ kSignFlip, w.z ^ kSignFlip, w.w ^ kSignFlip};
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    f2 c0 = fadd2(codes_pair(ws[k], 0), negmagic);
-    f2 c1 = fadd2(codes_pair(ws[k], 1), negmagic);
-    acc[k] = ffma2(c0, x[2 * k], acc[k]);
-    acc[k] = ffma2(c1, x[2 * k + 1], acc[k]);
+    const f2 c0 = fadd2(codes_pair(ws[k], 0), negmagic);
+    const f2 c1 = fadd2(codes_pair(ws[k], 1), negmagic);
+    acc[k & 1] = ffma2(c0, x[2 * k], acc[k & 1]);
+    acc[k & 1] = ffma2(c1, x[2 * k + 1], acc[k & 1]);
   }
 }
 
-__device__ __forceinline__ float hsum4(const f2 (&acc)[4]) {
-  float2 a = unpack_f2(acc[0]), b = unpack_f2(acc[1]), c = unpack_f2(acc[2]), d = unpack_f2(acc[3]);
-  return ((a.x + a.y) + (b.x + b.y)) + ((c.x + c.y) + (d.x + d.y));
+__device__ __forceinline__ float hsum2(const f2 (&acc)[2]) {
+  const float2 t = unpack_f2(fadd2(acc[0], acc[1]));
+  return t.x + t.y;
+}
+
+// Sums RT per-lane values (one per row) over the 32 lanes of a warp.  The
+// first log2(RT) exchanges halve the values each lane holds (a lane keeps
+// one half and sends the other to its partner), the rest are plain
+// butterflies: RT - 1 + 5 - log2(RT) shuffles instead of 5 * RT.  Afterwards
+// lane l holds the warp total of row l / (32 / RT) in v[0].
+template <int RT>
+__device__ __forceinline__ float warp_reduce_rows(float (&v)[RT], int lane) {
+  int o = 16;
+#pragma unroll
+  for (int n = RT; n > 1; n /= 2, o /= 2) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int j = 0; j < n / 2; ++j) {
+      const float send = up ? v[j] : v[j + n / 2];
+      const float keep = up ? v[j + n / 2] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+#pragma unroll
+  for (; o >= 1; o /= 2) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+  return v[0];
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -7,7 +7,7 @@ namespace xpu {
 
 namespace {
 constexpr int kMaxStages = 8;
-constexpr int64_t kStageTargetBytes = 32768;  // one ring slot: a block of rows
+constexpr size_t kStageMaxBytes = 65536;  // one ring slot: a block of rows
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t round_up(size_t a, size_t b) { return (a + b - 1) / b * b; }
@@ -23,19 +23,22 @@ int plan_matvec(MvParams& p, int epi, int pro, MvPlan& plan) {
   const bool aligned = p.W > 0 && p.W % 4 == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0 &&
                        (nstream == 1 || reinterpret_cast<uintptr_t>(p.w2) % 16 == 0);
   if (aligned) {
+    // One 16-byte column slice per consumer thread where K allows (up to 16
+    // consumer warps), then the largest unit of rows whose per-thread
+    // accumulators and x registers fit (cpt <= cptmax) and whose stage ring
+    // keeps >= 2 stages in flight.
     const int64_t U = p.W / 4;
     const int64_t row_bytes = p.W * 4;
-    int rb = 8 / nstream;
-    while (rb > min_rb && rb * row_bytes * nstream > kStageTargetBytes) rb /= 2;
-    for (; rb >= min_rb; rb /= 2) {
-      const int rt = rb * nstream;
+    const int64_t ncw = std::clamp<int64_t>(ceil_div(U, 32), 1, 16);
+    const int64_t cpt = ceil_div(U, 32 * ncw);
+    for (int rt = 8; cpt <= 4 && rt >= min_rb * nstream; rt /= 2) {
+      const int rb = rt / nstream;
+      if (rb < min_rb || rb * nstream != rt) continue;
       const int cptmax = rt >= 8 ? 1 : (rt == 4 ? 2 : 4);
-      int64_t ncw = std::clamp<int64_t>(ceil_div(U, 32 * cptmax), 1, 16);
-      int64_t cpt = ceil_div(U, 32 * ncw);
       if (cpt > cptmax) continue;
       const size_t stage_bytes = (size_t)rb * row_bytes * nstream;
-      const size_t header = 16 * kMaxStages + 2 * 16 * rt * 4 + 16 * 8;
-      const size_t stage_off = round_up(header, 128);
+      if (stage_bytes > kStageMaxBytes && rt > min_rb * nstream) continue;
+      const size_t stage_off = round_up(mv_bulk_header_bytes(kMaxStages, rt), 128);
       const int64_t avail = (int64_t)di.max_smem_optin - (int64_t)stage_off - 1024;
       const int64_t S = std::min<int64_t>(kMaxStages, avail / (int64_t)stage_bytes);
       if (S < 2) continue;
@@ -47,7 +50,7 @@ int plan_matvec(MvParams& p, int epi, int pro, MvPlan& plan) {
       plan.smem = stage_off + (size_t)S * stage_bytes;
       const int64_t units = ceil_div(p.N, rb);
       plan.grid = dim3((unsigned)std::min<int64_t>(units, di.sm_count));
-      plan.block = dim3((unsigned)(32 * (ncw + 1)));
+      plan.block = dim3((unsigned)(32 * (ncw + 2)));
       p.ncw = (int)ncw;
       p.stages = (int)S;
       p.stage_off = (uint32_t)stage_off;

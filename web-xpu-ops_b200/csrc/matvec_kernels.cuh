@@ -174,24 +174,40 @@ __device__ __forceinline__ void load_x_cols(const MvParams& p, int tid, int nthr
 }
 
 // ------------------------------------------------------------ bulk kernel --
+// Warp roles: warps [0, ncw) consume, warp ncw produces (one thread issues
+// the bulk copies), warp ncw + 1 finishes rows (epilogue).  Consumers never
+// wait for each other: each publishes its per-row partial sums of a unit in
+// a ring of reduction slots and signals an mbarrier; the epilogue warp adds
+// the ncw partials of each row and writes the output.
+//
+// Shared memory: full[S] | empty[S] | rfull[RS] | rempty[RS] | red[RS][16][RT]
+// | red_d[16] (rmsnorm prologue) | ring of S stages (at p.stage_off).
+constexpr int kRedSlots = 4;
+
+__host__ __device__ constexpr size_t mv_bulk_header_bytes(int stages, int rt) {
+  return 8 * (2 * (size_t)stages + 2 * kRedSlots) + 4 * (size_t)kRedSlots * 16 * rt + 8 * 16;
+}
+
 // RT = rows per unit across all weight streams (FFN: RB gate + RB up rows).
-// Plans with RT >= 4 have at most 8 consumer warps (their stage size caps K);
-// RT <= 2 can use 16.
+// Plans use at most 16 consumer warps (18 warps in all).
 template <int RT, int CPT, int EPI, int PRO>
-__global__ void __launch_bounds__(RT >= 4 ? 288 : 544, 1) mv_bulk_kernel(MvParams p) {
+__global__ void __launch_bounds__(576, 1) mv_bulk_kernel(MvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int NSTREAM = EPI == EPI_FFN ? 2 : 1;
   constexpr int RB = RT / NSTREAM;
+  constexpr int RS = kRedSlots;
   const int ncw = p.ncw, nct = ncw * 32, S = p.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
-  float* red = reinterpret_cast<float*>(empty + S);            // [2][ncw][RT]
-  double* red_d = reinterpret_cast<double*>(red + 2 * 16 * RT);  // [16]
-  __shared__ int abort_flag;
+  uint64_t* rfull = empty + S;
+  uint64_t* rempty = rfull + RS;
+  float* red = reinterpret_cast<float*>(rempty + RS);              // [RS][16][RT]
+  double* red_d = reinterpret_cast<double*>(red + RS * 16 * RT);   // [16]
+  __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
   const int64_t units = (p.N + RB - 1) / RB;
-  const int64_t U = p.W / 4;  // uint4 per row
+  const int64_t U = p.W / 4;  // 16-byte slots per row
   const uint32_t row_bytes = (uint32_t)(p.W * 4);
 
   griddep_launch_dependents();
@@ -199,6 +215,10 @@ __global__ void __launch_bounds__(RT >= 4 ? 288 : 544, 1) mv_bulk_kernel(MvParam
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], ncw);
+    }
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&rfull[s], ncw);
+      mbar_init(&rempty[s], 1);
     }
     abort_flag = 0;
     fence_mbar_init();
@@ -209,10 +229,16 @@ __global__ void __launch_bounds__(RT >= 4 ? 288 : 544, 1) mv_bulk_kernel(MvParam
     // ---------------- producer: one thread streams row blocks ----------------
     if (lane != 0) return;
     const uint64_t policy = evict_first_policy();
+    // Stage index and phase advance incrementally (a 64-bit `% S` with a
+    // runtime S would cost a software division per unit).
     int64_t issued = 0;
-    for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++issued) {
-      const int s = (int)(issued % S);
-      if (issued >= S && !mbar_wait(&empty[s], (uint32_t)((issued / S - 1) & 1), p.err)) break;
+    int s = 0;
+    uint32_t ph = 0;  // parity of the round through the ring
+    for (int64_t u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++issued) {
+      if (issued >= S && !mbar_wait(&empty[s], ph ^ 1u, p.err)) {
+        abort_flag = 1;
+        break;
+      }
       const int64_t row0 = u * RB;
       const int rows = (int)(p.N - row0 < RB ? p.N - row0 : RB);
       const uint32_t bytes = rows * row_bytes;
@@ -220,61 +246,100 @@ __global__ void __launch_bounds__(RT >= 4 ? 288 : 544, 1) mv_bulk_kernel(MvParam
       mbar_arrive_expect_tx(&full[s], bytes * NSTREAM);
       bulk_g2s(dst, p.w + row0 * p.W, bytes, &full[s], policy);
       if constexpr (NSTREAM == 2) bulk_g2s(dst + (size_t)RB * row_bytes, p.w2 + row0 * p.W, bytes, &full[s], policy);
+      if (++s == S) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
-    // Every issued copy must land before the CTA may exit (error path).
+    // Every issued copy must land before the CTA may exit (error path): the
+    // last min(issued, S) copies, oldest first.
     for (int64_t i = (issued > S ? issued - S : 0); i < issued; ++i)
-      mbar_wait(&full[i % S], (uint32_t)((i / S) & 1), p.err);
+      mbar_wait(&full[(int)(i % S)], (uint32_t)((i / S) & 1), p.err);
+    return;
+  }
+
+  if (warp == ncw + 1) {
+    // ---------------- epilogue: finish the rows of every unit ----------------
+    griddep_wait();  // residual, position and outputs belong to predecessors
+    constexpr int OUTS = mv_outputs_per_unit<EPI, RB>();
+    int slot = 0;
+    uint32_t rph = 0;
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+      if (!mbar_wait(&rfull[slot], rph, p.err)) {
+        abort_flag = 1;
+        break;
+      }
+      if (abort_flag) break;
+      if (lane < OUTS) mv_epilogue<EPI, RB, RT>(p, u * RB, lane, red + slot * 16 * RT, ncw);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[slot]);
+      if (++slot == RS) {
+        slot = 0;
+        rph ^= 1u;
+      }
+    }
     return;
   }
 
   // ---------------- consumers ----------------
-  griddep_wait();  // x, gamma, residual and outputs belong to predecessors
+  griddep_wait();  // x and gamma belong to predecessors
   f2 xr[CPT][8];
   load_x_cols<CPT, PRO>(p, tid, nct, U, red_d, 1, xr);
-
   const f2 zero2 = make_f2(0.0f, 0.0f);
-  int64_t it = 0;
-  for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++it) {
-    const int s = (int)(it % S);
-    const bool ok = mbar_wait(&full[s], (uint32_t)((it / S) & 1), p.err);
-    if (!ok) abort_flag = 1;
+  int s = 0, slot = 0;
+  uint32_t ph = 0, rph = 0;
+  bool first_round = true;  // reduction slots are free on the first pass
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    if (abort_flag || !mbar_wait(&full[s], ph, p.err)) {
+      abort_flag = 1;
+      break;
+    }
     const int64_t row0 = u * RB;
     const int rows = (int)(p.N - row0 < RB ? p.N - row0 : RB);
-    const uint4* st = reinterpret_cast<const uint4*>(smem + p.stage_off + (size_t)s * p.stage_stride);
-
-    f2 acc[RT][4];
+    const uint32_t st = p.stage_off + (uint32_t)s * p.stage_stride;  // byte offset in smem
+    f2 acc[RT][2];
 #pragma unroll
-    for (int r = 0; r < RT; ++r)
+    for (int r = 0; r < RT; ++r) acc[r][0] = acc[r][1] = zero2;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) acc[r][k] = zero2;
-    if (ok) {
+    for (int j = 0; j < CPT; ++j) {
+      const uint32_t c = (uint32_t)tid + (uint32_t)j * (uint32_t)nct;
+      if (c < (uint32_t)U) {
+        const uint32_t col = st + 16u * c;
+        if (rows == RB) {  // every unit but possibly the last
 #pragma unroll
-      for (int j = 0; j < CPT; ++j) {
-        const int64_t c = tid + (int64_t)j * nct;
-        if (c < U) {
+          for (int r = 0; r < RT; ++r)
+            dot16(*reinterpret_cast<const uint4*>(smem + col + (uint32_t)r * row_bytes), xr[j], acc[r]);
+        } else {
 #pragma unroll
-          for (int r = 0; r < RT; ++r) {
-            if ((r % RB) < rows) {
-              uint4 w = st[r * U + c];
-              dot16(w, xr[j], acc[r]);
-            }
-          }
+          for (int r = 0; r < RT; ++r)
+            if ((r % RB) < rows)
+              dot16(*reinterpret_cast<const uint4*>(smem + col + (uint32_t)r * row_bytes), xr[j], acc[r]);
         }
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);  // stage may be refilled
+    if (lane == 0) mbar_arrive(&empty[s]);  // the stage may be refilled
 
-    float* rb = red + (it & 1) * 16 * RT;
+    float v[RT];
 #pragma unroll
-    for (int r = 0; r < RT; ++r) {
-      float v = warp_sum(hsum4(acc[r]));
-      if (lane == 0) rb[warp * RT + r] = v;
+    for (int r = 0; r < RT; ++r) v[r] = hsum2(acc[r]);
+    const float tot = warp_reduce_rows<RT>(v, lane);
+    if (!first_round && !mbar_wait(&rempty[slot], rph ^ 1u, p.err)) {
+      abort_flag = 1;
+      break;
     }
-    named_bar_sync(1, nct);
-    if (abort_flag) break;
-    constexpr int OUTS = mv_outputs_per_unit<EPI, RB>();
-    if (tid < OUTS) mv_epilogue<EPI, RB, RT>(p, row0, tid, rb, ncw);
+    if (lane % (32 / RT) == 0) red[(slot * 16 + warp) * RT + lane / (32 / RT)] = tot;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&rfull[slot]);
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
+    if (++slot == RS) {
+      slot = 0;
+      rph ^= 1u;
+      first_round = false;
+    }
   }
 }
 
@@ -321,15 +386,13 @@ __global__ void __launch_bounds__(256) mv_gen_kernel(MvParams p, int64_t off_wor
   }
   __syncthreads();
 
-  const f2 zero2 = make_f2(0.0f, 0.0f);
   int64_t it = 0;
   for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++it) {
     const int64_t row0 = u * RB;
-    f2 acc[RT][4];
+    const f2 zero2 = make_f2(0.0f, 0.0f);
+    f2 acc[RT][2];
 #pragma unroll
-    for (int r = 0; r < RT; ++r)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) acc[r][k] = zero2;
+    for (int r = 0; r < RT; ++r) acc[r][0] = acc[r][1] = zero2;
 #pragma unroll
     for (int r = 0; r < RT; ++r) {
       const int64_t row = row0 + (r % RB);
@@ -358,7 +421,7 @@ __global__ void __launch_bounds__(256) mv_gen_kernel(MvParams p, int64_t off_wor
         f2 xv[8];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float4 t = xp[e];
+          const float4 t = xp[e];
           xv[2 * e] = make_f2(t.x, t.y);
           xv[2 * e + 1] = make_f2(t.z, t.w);
         }
@@ -368,7 +431,7 @@ __global__ void __launch_bounds__(256) mv_gen_kernel(MvParams p, int64_t off_wor
     float* rb = &red[0][0];
 #pragma unroll
     for (int r = 0; r < RT; ++r) {
-      float v = warp_sum(hsum4(acc[r]));
+      float v = warp_sum(hsum2(acc[r]));
       if (lane == 0) red[warp][r] = v;
     }
     __syncthreads();
