@@ -127,6 +127,18 @@ XPU_API int xpu_matvec_q8_residual_dev(const uint32_t* weight, const float* scal
 XPU_API int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stride,
                                     const float* scales, const float* vector, int64_t count,
                                     int64_t N, int64_t K, float* outputs, void* stream);
+/* ops/gqa/reference.ts:203-303 `groupedAttention` for one decode query
+ * (B = 1, L = 1, causal, queryOffset = s_eff - 1, no mask), as the resident
+ * engine runs it each step (llm/engine-q8-resident.ts:1852-1853):
+ * out[h] = softmax(q[h] . K[g]^T * scale) . V[g] over positions [0, s_eff),
+ * g = h / (H / kv_heads).  q, out: [H, D]; k_cache, v_cache: [kv_heads, S, D]
+ * with S the position stride (maxSeqLen).  scale <= 0 means 1/sqrt(D).
+ * Positions are split over CTAs; the splits' softmax partials live in a
+ * workspace this call allocates and frees in stream order
+ * (cudaMallocAsync / cudaFreeAsync). */
+XPU_API int xpu_gqa_decode_dev(const float* q, const float* k_cache, const float* v_cache,
+                               int32_t H, int32_t kv_heads, int32_t D, int32_t S,
+                               int32_t s_eff, float scale, float* out, void* stream);
 /* ops/quantize/wgsl/kernel.wgsl bindings (input, codes, scales), but with
  * reference.ts's rounding, so the codes are bit-exact. */
 XPU_API int xpu_quantize_dev(const float* input, int64_t N, int64_t D,

@@ -1,0 +1,179 @@
+// attention.cu — the split-position decode attention kernel shared by the
+// engine's decode step and the C ABI (ops/gqa/reference.ts:203-303, decode
+// form), and its standalone entry point.
+#include <algorithm>
+
+#include "attention.cuh"
+#include "matvec_launch.cuh"
+
+namespace xpu {
+namespace {
+
+// One CTA per (kv head, position split): the G = H / kvH query heads that
+// share the kv head (ops/gqa/reference.ts:199-201) read each K/V row once.
+// Partial softmax statistics go to scratch; the last CTA of a kv head (an
+// atomic ticket, no waiting) merges the splits.
+__global__ void __launch_bounds__(256) attn_decode_kernel(AttnParams a) {
+  extern __shared__ float sm[];
+  const int g = blockIdx.x, sp = blockIdx.y;
+  const int G = a.H / a.kvH, hd = a.hd;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, nw = blockDim.x / 32;
+  float* q_s = sm;                   // [G][hd]
+  float* p_s = q_s + G * hd;         // [G][chunk_max]
+  float* stat = p_s + G * a.chunk_max;  // [G][2]
+  __shared__ unsigned int is_last;
+
+  griddep_launch_dependents();
+  griddep_wait();
+  const int L = a.pos ? *a.pos + 1 : a.s_eff;  // sEff: positions [0, L) are scanned
+  const int chunk = (L + a.nsplit - 1) / a.nsplit;
+  const int j0 = sp * chunk, j1 = min(L, j0 + chunk), n = max(0, j1 - j0);
+
+  for (int i = tid; i < G * hd; i += blockDim.x) q_s[i] = a.q[(g * G) * hd + i];
+  __syncthreads();
+
+  // scores: a warp per position, lanes across the head dimension
+  const float* kb = a.kcache + (int64_t)g * a.S * hd;
+  for (int j = j0 + warp; j < j1; j += nw) {
+    const float* kr = kb + (int64_t)j * hd;
+    for (int h = 0; h < G; ++h) {
+      float d = 0.0f;
+      for (int c = lane; c < hd; c += 32) d = fmaf(q_s[h * hd + c], kr[c], d);
+      d = warp_sum(d);
+      if (lane == 0) p_s[h * a.chunk_max + (j - j0)] = d * a.scale;
+    }
+  }
+  __syncthreads();
+  // per-head max and sum of exp over this split
+  for (int h = warp; h < G; h += nw) {
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, p_s[h * a.chunk_max + j]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.0f;
+    for (int j = lane; j < n; j += 32) {
+      float e = expf(p_s[h * a.chunk_max + j] - m);
+      p_s[h * a.chunk_max + j] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      stat[2 * h] = m;
+      stat[2 * h + 1] = l;
+    }
+  }
+  __syncthreads();
+  const float* vb = a.vcache + (int64_t)g * a.S * hd;
+  for (int i = tid; i < G * hd; i += blockDim.x) {
+    const int h = i / hd, c = i % hd;
+    float acc = 0.0f;
+    for (int j = 0; j < n; ++j) acc = fmaf(p_s[h * a.chunk_max + j], vb[(int64_t)(j0 + j) * hd + c], acc);
+    const int hh = g * G + h;
+    a.part_acc[((int64_t)hh * a.nsplit + sp) * hd + c] = acc;
+    if (c == 0) {
+      a.part_m[hh * a.nsplit + sp] = n > 0 ? stat[2 * h] : -INFINITY;
+      a.part_l[hh * a.nsplit + sp] = n > 0 ? stat[2 * h + 1] : 0.0f;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = atomicAdd(&a.counter[g], 1u) == (unsigned)(a.nsplit - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int i = tid; i < G * hd; i += blockDim.x) {
+    const int h = g * G + i / hd, c = i % hd;
+    float M = -INFINITY;
+    for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, __ldcg(&a.part_m[h * a.nsplit + s]));
+    float l = 0.0f, o = 0.0f;
+    for (int s = 0; s < a.nsplit; ++s) {
+      float m = __ldcg(&a.part_m[h * a.nsplit + s]);
+      if (m == -INFINITY) continue;
+      float w = expf(m - M);
+      l = fmaf(__ldcg(&a.part_l[h * a.nsplit + s]), w, l);
+      o = fmaf(__ldcg(&a.part_acc[((int64_t)h * a.nsplit + s) * hd + c]), w, o);
+    }
+    a.out[h * hd + c] = o / l;
+  }
+  if (tid == 0) a.counter[g] = 0;
+}
+
+
+}  // namespace
+
+void gqa_bind_workspace(AttnParams& a, float* ws) {
+  a.part_m = ws;
+  a.part_l = ws + (size_t)a.H * a.nsplit;
+  a.part_acc = ws + 2 * (size_t)a.H * a.nsplit;
+  a.counter = reinterpret_cast<unsigned int*>(ws + (size_t)a.H * a.nsplit * (a.hd + 2));
+}
+
+int gqa_default_splits(int kvH, int S) {
+  const int sms = device_info().sm_count;
+  return std::max(1, std::min((2 * sms + kvH - 1) / kvH, (S + 7) / 8));
+}
+
+int launch_gqa_decode(const AttnParams& a, const LaunchOpts& o) {
+  const int G = a.H / a.kvH;
+  const size_t smem = sizeof(float) * ((size_t)G * a.hd + (size_t)G * a.chunk_max + 2 * (size_t)G);
+  XPU_TRY_CUDA(ensure_smem_attr((const void*)attn_decode_kernel, smem));
+  XPU_TRY_CUDA(launch_ex(attn_decode_kernel, dim3(a.kvH, a.nsplit), dim3(256), smem, o, a));
+  return XPU_OK;
+}
+
+// Argument checks shared by the attention entry points
+// (ops/gqa/reference.ts:211-237 for the decode form).
+int gqa_check(const float* q, const float* k, const float* v, int H, int kvH, int D, int S, int s_eff,
+              const float* out) {
+  XPU_REQUIRE(q && k && v && out, XPU_EINVAL, "groupedAttention(): null pointer");
+  XPU_REQUIRE(kvH >= 1, XPU_EINVAL, "groupedAttention(): kvHeads must be a positive integer, got %d", kvH);
+  XPU_REQUIRE(H >= 1 && H % kvH == 0, XPU_EINVAL,
+              "groupedAttention(): kvHeads=%d must divide H=%d; a ragged split has no defensible grouping", kvH, H);
+  XPU_REQUIRE(D >= 1 && S >= 1, XPU_EINVAL, "groupedAttention(): D and S must be positive");
+  XPU_REQUIRE(s_eff >= 1 && s_eff <= S, XPU_EINVAL, "groupedAttention(): sEff must be an integer in [1, S=%d], got %d",
+              S, s_eff);
+  return XPU_OK;
+}
+
+AttnParams gqa_params(const float* q, const float* k, const float* v, int H, int kvH, int D, int S, int s_eff,
+                      float scale, float* out, int nsplit) {
+  AttnParams a{};
+  a.q = q;
+  a.kcache = k;
+  a.vcache = v;
+  a.pos = nullptr;
+  a.s_eff = s_eff;
+  a.out = out;
+  a.H = H;
+  a.kvH = kvH;
+  a.hd = D;
+  a.S = S;
+  a.nsplit = nsplit;
+  a.chunk_max = (s_eff + nsplit - 1) / nsplit;
+  a.scale = scale > 0.0f ? scale : (float)(1.0 / sqrt((double)D));
+  return a;
+}
+
+}  // namespace xpu
+
+using namespace xpu;
+
+extern "C" int xpu_gqa_decode_dev(const float* q, const float* k_cache, const float* v_cache, int32_t H,
+                                  int32_t kv_heads, int32_t D, int32_t S, int32_t s_eff, float scale, float* out,
+                                  void* stream) {
+  int rc = gqa_check(q, k_cache, v_cache, H, kv_heads, D, S, s_eff, out);
+  if (rc) return rc;
+  const int nsplit = std::min(gqa_default_splits(kv_heads, S), s_eff);
+  AttnParams a = gqa_params(q, k_cache, v_cache, H, kv_heads, D, S, s_eff, scale, out, nsplit);
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t bytes = gqa_workspace_floats(H, kv_heads, D, nsplit) * sizeof(float);
+  float* ws = nullptr;
+  XPU_TRY_CUDA(cudaMallocAsync((void**)&ws, bytes, st));
+  gqa_bind_workspace(a, ws);
+  cudaError_t e = cudaMemsetAsync(a.counter, 0, (size_t)kv_heads * sizeof(unsigned int), st);
+  if (e == cudaSuccess) rc = launch_gqa_decode(a, LaunchOpts{st, false});
+  else rc = cuda_status(e, "cudaMemsetAsync (attention counters)");
+  cudaError_t f = cudaFreeAsync(ws, st);
+  if (rc) return rc;
+  if (f != cudaSuccess) return cuda_status(f, "cudaFreeAsync (attention workspace)");
+  return XPU_OK;
+}

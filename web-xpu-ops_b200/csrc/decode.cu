@@ -19,6 +19,7 @@
 #include <algorithm>
 #include <vector>
 
+#include "attention.cuh"
 #include "matvec_launch.cuh"
 
 namespace xpu {
@@ -37,108 +38,6 @@ __global__ void embed_kernel(const int8_t* __restrict__ codes, const float* __re
   const double s = ok ? (double)scale[t] : 0.0;
   for (int c = threadIdx.x; c < hidden; c += blockDim.x)
     out[c] = ok ? (float)((double)codes[(int64_t)t * hidden + c] * s) : 0.0f;
-}
-
-struct AttnParams {
-  const float* q;  // [H * hd], roped
-  const float* kcache;
-  const float* vcache;  // [kvH, S, hd]
-  const int32_t* pos;
-  float* part_m;    // [H][nsplit]
-  float* part_l;    // [H][nsplit]
-  float* part_acc;  // [H][nsplit][hd]
-  unsigned int* counter;  // [kvH], zero between launches
-  float* out;             // [H * hd]
-  int H, kvH, hd, S, nsplit, chunk_max;
-  float scale;
-};
-
-// One CTA per (kv head, position split): the G = H / kvH query heads that
-// share the kv head (ops/gqa/reference.ts:199-201) read each K/V row once.
-// Partial softmax statistics go to scratch; the last CTA of a kv head (an
-// atomic ticket, no waiting) merges the splits.
-__global__ void __launch_bounds__(256) attn_decode_kernel(AttnParams a) {
-  extern __shared__ float sm[];
-  const int g = blockIdx.x, sp = blockIdx.y;
-  const int G = a.H / a.kvH, hd = a.hd;
-  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, nw = blockDim.x / 32;
-  float* q_s = sm;                   // [G][hd]
-  float* p_s = q_s + G * hd;         // [G][chunk_max]
-  float* stat = p_s + G * a.chunk_max;  // [G][2]
-  __shared__ unsigned int is_last;
-
-  griddep_launch_dependents();
-  griddep_wait();
-  const int L = *a.pos + 1;  // sEff: positions 0..pos are resident
-  const int chunk = (L + a.nsplit - 1) / a.nsplit;
-  const int j0 = sp * chunk, j1 = min(L, j0 + chunk), n = max(0, j1 - j0);
-
-  for (int i = tid; i < G * hd; i += blockDim.x) q_s[i] = a.q[(g * G) * hd + i];
-  __syncthreads();
-
-  // scores: a warp per position, lanes across the head dimension
-  const float* kb = a.kcache + (int64_t)g * a.S * hd;
-  for (int j = j0 + warp; j < j1; j += nw) {
-    const float* kr = kb + (int64_t)j * hd;
-    for (int h = 0; h < G; ++h) {
-      float d = 0.0f;
-      for (int c = lane; c < hd; c += 32) d = fmaf(q_s[h * hd + c], kr[c], d);
-      d = warp_sum(d);
-      if (lane == 0) p_s[h * a.chunk_max + (j - j0)] = d * a.scale;
-    }
-  }
-  __syncthreads();
-  // per-head max and sum of exp over this split
-  for (int h = warp; h < G; h += nw) {
-    float m = -INFINITY;
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, p_s[h * a.chunk_max + j]);
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.0f;
-    for (int j = lane; j < n; j += 32) {
-      float e = expf(p_s[h * a.chunk_max + j] - m);
-      p_s[h * a.chunk_max + j] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      stat[2 * h] = m;
-      stat[2 * h + 1] = l;
-    }
-  }
-  __syncthreads();
-  const float* vb = a.vcache + (int64_t)g * a.S * hd;
-  for (int i = tid; i < G * hd; i += blockDim.x) {
-    const int h = i / hd, c = i % hd;
-    float acc = 0.0f;
-    for (int j = 0; j < n; ++j) acc = fmaf(p_s[h * a.chunk_max + j], vb[(int64_t)(j0 + j) * hd + c], acc);
-    const int hh = g * G + h;
-    a.part_acc[((int64_t)hh * a.nsplit + sp) * hd + c] = acc;
-    if (c == 0) {
-      a.part_m[hh * a.nsplit + sp] = n > 0 ? stat[2 * h] : -INFINITY;
-      a.part_l[hh * a.nsplit + sp] = n > 0 ? stat[2 * h + 1] : 0.0f;
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = atomicAdd(&a.counter[g], 1u) == (unsigned)(a.nsplit - 1);
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  for (int i = tid; i < G * hd; i += blockDim.x) {
-    const int h = g * G + i / hd, c = i % hd;
-    float M = -INFINITY;
-    for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, __ldcg(&a.part_m[h * a.nsplit + s]));
-    float l = 0.0f, o = 0.0f;
-    for (int s = 0; s < a.nsplit; ++s) {
-      float m = __ldcg(&a.part_m[h * a.nsplit + s]);
-      if (m == -INFINITY) continue;
-      float w = expf(m - M);
-      l = fmaf(__ldcg(&a.part_l[h * a.nsplit + s]), w, l);
-      o = fmaf(__ldcg(&a.part_acc[((int64_t)h * a.nsplit + s) * hd + c]), w, o);
-    }
-    a.out[h * hd + c] = o / l;
-  }
-  if (tid == 0) a.counter[g] = 0;
 }
 
 // Greedy next token (llm/engine.ts:226-232: the first maximal index; values
@@ -333,9 +232,8 @@ int record_step(xpu_llama* e) {
     a.nsplit = e->nsplit;
     a.chunk_max = e->chunk_max;
     a.scale = (float)(1.0 / sqrt((double)hd));
-    const int G = c.num_heads / c.num_kv_heads;
-    size_t smem = sizeof(float) * ((size_t)G * hd + (size_t)G * e->chunk_max + 2 * G);
-    XPU_TRY_CUDA(launch_ex(attn_decode_kernel, dim3(c.num_kv_heads, e->nsplit), dim3(256), smem, dep, a));
+    a.s_eff = 0;
+    if ((rc = launch_gqa_decode(a, dep))) return rc;
     // o-proj + residual
     MvParams o{};
     o.err = err;
@@ -527,8 +425,7 @@ int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, in
 
   // Position splits for attention: about two CTAs per SM over all kv heads,
   // at least 8 positions per split.
-  const int sms = device_info().sm_count;
-  e->nsplit = std::max(1, std::min((2 * sms + c.num_kv_heads - 1) / c.num_kv_heads, (c.max_seq_len + 7) / 8));
+  e->nsplit = gqa_default_splits(c.num_kv_heads, c.max_seq_len);
   e->chunk_max = (c.max_seq_len + e->nsplit - 1) / e->nsplit;
   if ((rc = dev_alloc(e, &e->hidden_a, h)) || (rc = dev_alloc(e, &e->hidden_b, h)) || (rc = dev_alloc(e, &e->q, qd)) ||
       (rc = dev_alloc(e, &e->attn, qd)) || (rc = dev_alloc(e, &e->gated, c.ffn_hidden)) ||

@@ -29,8 +29,19 @@ int plan_matvec(MvParams& p, int epi, int pro, MvPlan& plan) {
     // keeps >= 2 stages in flight.
     const int64_t U = p.W / 4;
     const int64_t row_bytes = p.W * 4;
-    const int64_t ncw = std::clamp<int64_t>(ceil_div(U, 32), 1, 16);
+    // Fewest columns per thread first, then the consumer-warp count that
+    // leaves the fewest thread-columns idle (a stage is released only when
+    // its slowest warp is done), then more warps.
+    int64_t ncw = std::clamp<int64_t>(ceil_div(U, 32), 1, 16);
     const int64_t cpt = ceil_div(U, 32 * ncw);
+    for (int64_t w = ncw, best = cpt * 32 * ncw - U; w >= std::max<int64_t>(1, ncw / 2); --w) {
+      if (ceil_div(U, 32 * w) != cpt) break;
+      const int64_t waste = cpt * 32 * w - U;
+      if (waste < best) {
+        best = waste;
+        ncw = w;
+      }
+    }
     for (int rt = 8; cpt <= 4 && rt >= min_rb * nstream; rt /= 2) {
       const int rb = rt / nstream;
       if (rb < min_rb || rb * nstream != rt) continue;

@@ -217,3 +217,25 @@ def matvecQ8Stack_dev(weights, weight_stride: int, scales, vector, count: int, N
 
 def stream_sync(stream=None) -> None:
     check(lib().xpu_stream_sync(_ptr(stream) or None))
+
+
+def groupedAttentionDecode_dev(q, k_cache, v_cache, H: int, kvHeads: int, D: int, S: int, sEff: int, output,
+                               scale: float = 0.0, stream=None) -> None:
+    """ops/gqa/reference.ts:203-303 for one decode query (causal,
+    queryOffset = sEff - 1): device pointers, async on `stream`."""
+    check(lib().xpu_gqa_decode_dev(_ptr(q), _ptr(k_cache), _ptr(v_cache), H, kvHeads, D, S, sEff, scale,
+                                   _ptr(output), _ptr(stream) or None))
+
+
+def groupedAttentionDecode(q, k, v, H: int, kvHeads: int, D: int, S: int, sEff: int, scale: float = 0.0):
+    """Host-array form of groupedAttentionDecode_dev: returns out [H * D]."""
+    require_device()
+    qa, ka, va = _c(q, np.float32), _c(k, np.float32), _c(v, np.float32)
+    _need("groupedAttention: q", qa, H * D)
+    _need("groupedAttention: k", ka, kvHeads * S * D)
+    _need("groupedAttention: v", va, kvHeads * S * D)
+    dq, dk, dv = DeviceBuffer.from_numpy(qa[:H * D]), DeviceBuffer.from_numpy(ka), DeviceBuffer.from_numpy(va)
+    do = DeviceBuffer(4 * H * D)
+    groupedAttentionDecode_dev(dq, dk, dv, H, kvHeads, D, S, sEff, do, scale)
+    stream_sync()
+    return do.download(np.float32, H * D)
