@@ -139,6 +139,21 @@ XPU_API int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stri
 XPU_API int xpu_gqa_decode_dev(const float* q, const float* k_cache, const float* v_cache,
                                int32_t H, int32_t kv_heads, int32_t D, int32_t S,
                                int32_t s_eff, float scale, float* out, void* stream);
+/* No counterpart in the reference.  The same decode attention as
+ * xpu_gqa_decode_dev for callers that cannot allocate device memory: a host
+ * whose HBM is reserved by another allocator, a resident engine that creates
+ * every buffer up front, a latency-critical loop that must not enter the
+ * driver's allocator.  It calls no cudaMalloc or cudaFree: the split-softmax
+ * workspace is a fixed 1 MiB __device__ array in the library, held by every
+ * GPU that loads it until exit.  Shapes with H*(D+2) + kv_heads > 262144
+ * floats are rejected (XPU_EINVAL); shapes that fit fewer position splits
+ * than xpu_gqa_decode_dev uses run with fewer splits (equal up to f32
+ * summation order).  The first call on a device looks up the array's device
+ * address; make it before any stream capture.  All calls share the array, so
+ * calls whose kernels overlap on the GPU race. */
+XPU_API int xpu_gqa_decode_noalloc(const float* q, const float* k_cache, const float* v_cache,
+                                   int32_t H, int32_t kv_heads, int32_t D, int32_t S,
+                                   int32_t s_eff, float scale, float* out, void* stream);
 /* ops/quantize/wgsl/kernel.wgsl bindings (input, codes, scales), but with
  * reference.ts's rounding, so the codes are bit-exact. */
 XPU_API int xpu_quantize_dev(const float* input, int64_t N, int64_t D,
