@@ -11,47 +11,57 @@ namespace {
 
 // One CTA per (kv head, position split): the G = H / kvH query heads that
 // share the kv head (ops/gqa/reference.ts:199-201) read each K/V row once.
-// Partial softmax statistics go to scratch; the last CTA of a kv head (an
-// atomic ticket, no waiting) merges the splits.
-__global__ void __launch_bounds__(256) attn_decode_kernel(AttnParams a) {
+// Each split writes its softmax max, sum of exp and un-normalised output to
+// the workspace; the last CTA of a kv head (an atomic ticket, no waiting)
+// merges the splits.
+constexpr int kAttnThreads = 256;
+constexpr int kMaxHdPerLane = 4;  // head_dim <= 128
+
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnParams a) {
   extern __shared__ float sm[];
   const int g = blockIdx.x, sp = blockIdx.y;
-  const int G = a.H / a.kvH, hd = a.hd;
+  const int G = a.H / a.kvH, hd = a.hd, ns = a.nsplit;
   const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, nw = blockDim.x / 32;
-  float* q_s = sm;                   // [G][hd]
-  float* p_s = q_s + G * hd;         // [G][chunk_max]
-  float* stat = p_s + G * a.chunk_max;  // [G][2]
+  float* q_s = sm;                      // [G][hd]
+  float* p_s = q_s + G * hd;            // [G][chunk_max]
+  float* stat = p_s + G * a.chunk_max;  // [G][2], later [G][nsplit] merge weights
   __shared__ unsigned int is_last;
 
   griddep_launch_dependents();
   griddep_wait();
   const int L = a.pos ? *a.pos + 1 : a.s_eff;  // sEff: positions [0, L) are scanned
-  const int chunk = (L + a.nsplit - 1) / a.nsplit;
-  const int j0 = sp * chunk, j1 = min(L, j0 + chunk), n = max(0, j1 - j0);
+  const int chunk = (L + ns - 1) / ns;
+  const int j0 = min(L, sp * chunk), j1 = min(L, j0 + chunk), n = j1 - j0;
 
   for (int i = tid; i < G * hd; i += blockDim.x) q_s[i] = a.q[(g * G) * hd + i];
   __syncthreads();
 
-  // scores: a warp per position, lanes across the head dimension
+  // Scores: a warp per position; a lane holds its slice of the K row in
+  // registers and dots it with every query head of the group.
   const float* kb = a.kcache + (int64_t)g * a.S * hd;
   for (int j = j0 + warp; j < j1; j += nw) {
     const float* kr = kb + (int64_t)j * hd;
+    float kv[kMaxHdPerLane];
+#pragma unroll
+    for (int i = 0; i < kMaxHdPerLane; ++i) kv[i] = (lane + 32 * i < hd) ? kr[lane + 32 * i] : 0.0f;
     for (int h = 0; h < G; ++h) {
       float d = 0.0f;
-      for (int c = lane; c < hd; c += 32) d = fmaf(q_s[h * hd + c], kr[c], d);
+#pragma unroll
+      for (int i = 0; i < kMaxHdPerLane; ++i)
+        if (lane + 32 * i < hd) d = fmaf(q_s[h * hd + lane + 32 * i], kv[i], d);
       d = warp_sum(d);
       if (lane == 0) p_s[h * a.chunk_max + (j - j0)] = d * a.scale;
     }
   }
   __syncthreads();
-  // per-head max and sum of exp over this split
+  // Per-head max and sum of exp over this split.
   for (int h = warp; h < G; h += nw) {
     float m = -INFINITY;
     for (int j = lane; j < n; j += 32) m = fmaxf(m, p_s[h * a.chunk_max + j]);
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.0f;
     for (int j = lane; j < n; j += 32) {
-      float e = expf(p_s[h * a.chunk_max + j] - m);
+      const float e = expf(p_s[h * a.chunk_max + j] - m);
       p_s[h * a.chunk_max + j] = e;
       l += e;
     }
@@ -65,38 +75,65 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnParams a) {
   const float* vb = a.vcache + (int64_t)g * a.S * hd;
   for (int i = tid; i < G * hd; i += blockDim.x) {
     const int h = i / hd, c = i % hd;
-    float acc = 0.0f;
-    for (int j = 0; j < n; ++j) acc = fmaf(p_s[h * a.chunk_max + j], vb[(int64_t)(j0 + j) * hd + c], acc);
+    const float* pr = p_s + h * a.chunk_max;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    int j = 0;
+#pragma unroll 4
+    for (; j + 1 < n; j += 2) {
+      acc0 = fmaf(pr[j], vb[(int64_t)(j0 + j) * hd + c], acc0);
+      acc1 = fmaf(pr[j + 1], vb[(int64_t)(j0 + j + 1) * hd + c], acc1);
+    }
+    if (j < n) acc0 = fmaf(pr[j], vb[(int64_t)(j0 + j) * hd + c], acc0);
     const int hh = g * G + h;
-    a.part_acc[((int64_t)hh * a.nsplit + sp) * hd + c] = acc;
+    a.part_acc[((int64_t)hh * ns + sp) * hd + c] = acc0 + acc1;
     if (c == 0) {
-      a.part_m[hh * a.nsplit + sp] = n > 0 ? stat[2 * h] : -INFINITY;
-      a.part_l[hh * a.nsplit + sp] = n > 0 ? stat[2 * h + 1] : 0.0f;
+      a.part_m[hh * ns + sp] = n > 0 ? stat[2 * h] : -INFINITY;
+      a.part_l[hh * ns + sp] = n > 0 ? stat[2 * h + 1] : 0.0f;
     }
   }
   __threadfence();
   __syncthreads();
-  if (tid == 0) is_last = atomicAdd(&a.counter[g], 1u) == (unsigned)(a.nsplit - 1);
+  if (tid == 0) is_last = atomicAdd(&a.counter[g], 1u) == (unsigned)(ns - 1);
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  for (int i = tid; i < G * hd; i += blockDim.x) {
-    const int h = g * G + i / hd, c = i % hd;
+
+  // Merge: weights w[h][s] = exp(m_s - M) / sum_s' l_s' exp(m_s' - M), one
+  // warp per head, then each output is an independent weighted sum.
+  float* wts = p_s;  // reuse: [G][ns]; the launcher sizes p_s rows to max(chunk, nsplit)
+  for (int h = warp; h < G; h += nw) {
+    const int hh = g * G + h;
     float M = -INFINITY;
-    for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, __ldcg(&a.part_m[h * a.nsplit + s]));
-    float l = 0.0f, o = 0.0f;
-    for (int s = 0; s < a.nsplit; ++s) {
-      float m = __ldcg(&a.part_m[h * a.nsplit + s]);
-      if (m == -INFINITY) continue;
-      float w = expf(m - M);
-      l = fmaf(__ldcg(&a.part_l[h * a.nsplit + s]), w, l);
-      o = fmaf(__ldcg(&a.part_acc[((int64_t)h * a.nsplit + s) * hd + c]), w, o);
+    for (int s = lane; s < ns; s += 32) M = fmaxf(M, __ldcg(&a.part_m[hh * ns + s]));
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float l = 0.0f;
+    for (int s = lane; s < ns; s += 32) {
+      const float m = __ldcg(&a.part_m[hh * ns + s]);
+      const float w = m == -INFINITY ? 0.0f : expf(m - M);
+      wts[h * ns + s] = w;
+      l = fmaf(__ldcg(&a.part_l[hh * ns + s]), w, l);
     }
-    a.out[h * hd + c] = o / l;
+    l = warp_sum(l);
+    const float inv = 1.0f / l;
+    for (int s = lane; s < ns; s += 32) wts[h * ns + s] *= inv;
+  }
+  __syncthreads();
+  for (int i = tid; i < G * hd; i += blockDim.x) {
+    const int h = i / hd, c = i % hd, hh = g * G + h;
+    const float* src = a.part_acc + (int64_t)hh * ns * hd + c;
+    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
+    int s = 0;
+    for (; s + 3 < ns; s += 4) {
+      o0 = fmaf(wts[h * ns + s], __ldcg(src + (int64_t)s * hd), o0);
+      o1 = fmaf(wts[h * ns + s + 1], __ldcg(src + (int64_t)(s + 1) * hd), o1);
+      o2 = fmaf(wts[h * ns + s + 2], __ldcg(src + (int64_t)(s + 2) * hd), o2);
+      o3 = fmaf(wts[h * ns + s + 3], __ldcg(src + (int64_t)(s + 3) * hd), o3);
+    }
+    for (; s < ns; ++s) o0 = fmaf(wts[h * ns + s], __ldcg(src + (int64_t)s * hd), o0);
+    a.out[hh * hd + c] = (o0 + o1) + (o2 + o3);
   }
   if (tid == 0) a.counter[g] = 0;
 }
-
 
 }  // namespace
 
@@ -108,15 +145,23 @@ void gqa_bind_workspace(AttnParams& a, float* ws) {
 }
 
 int gqa_default_splits(int kvH, int S) {
+  // At most about one CTA per SM over all kv heads, and at least 64
+  // positions per split: the merge reads every split once per output.
   const int sms = device_info().sm_count;
-  return std::max(1, std::min((2 * sms + kvH - 1) / kvH, (S + 7) / 8));
+  return std::max(1, std::min((sms + kvH - 1) / kvH, (S + 63) / 64));
 }
 
 int launch_gqa_decode(const AttnParams& a, const LaunchOpts& o) {
   const int G = a.H / a.kvH;
-  const size_t smem = sizeof(float) * ((size_t)G * a.hd + (size_t)G * a.chunk_max + 2 * (size_t)G);
+  XPU_REQUIRE(a.hd <= 32 * kMaxHdPerLane, XPU_EINVAL, "groupedAttention: head dim %d exceeds %d", a.hd,
+              32 * kMaxHdPerLane);
+  // p_s doubles as the merge weights [G][nsplit]: size it for both.
+  const size_t ps = std::max<size_t>((size_t)a.chunk_max, (size_t)a.nsplit);
+  const size_t smem = sizeof(float) * ((size_t)G * a.hd + (size_t)G * ps + 2 * (size_t)G);
   XPU_TRY_CUDA(ensure_smem_attr((const void*)attn_decode_kernel, smem));
-  XPU_TRY_CUDA(launch_ex(attn_decode_kernel, dim3(a.kvH, a.nsplit), dim3(256), smem, o, a));
+  AttnParams b = a;
+  b.chunk_max = (int)ps;
+  XPU_TRY_CUDA(launch_ex(attn_decode_kernel, dim3(a.kvH, a.nsplit), dim3(kAttnThreads), smem, o, b));
   return XPU_OK;
 }
 
