@@ -146,9 +146,10 @@ XPU_API int xpu_gqa_decode_dev(const float* q, const float* k_cache, const float
  * driver's allocator.  It calls no cudaMalloc or cudaFree: the split-softmax
  * workspace is a fixed 1 MiB __device__ array in the library, held by every
  * GPU that loads it until exit.  Shapes with H*(D+2) + kv_heads > 262144
- * floats are rejected (XPU_EINVAL); shapes that fit fewer position splits
- * than xpu_gqa_decode_dev uses run with fewer splits (equal up to f32
- * summation order).  The first call on a device looks up the array's device
+ * floats, or contexts needing more position splits than that array holds
+ * (about 33,000 positions at H = 32, D = 64), are rejected (XPU_EINVAL);
+ * shapes that fit fewer position splits than xpu_gqa_decode_dev uses run
+ * with fewer splits (equal up to f32 summation order).  The first call on a device looks up the array's device
  * address; make it before any stream capture.  All calls share the array, so
  * calls whose kernels overlap on the GPU race. */
 XPU_API int xpu_gqa_decode_noalloc(const float* q, const float* k_cache, const float* v_cache,

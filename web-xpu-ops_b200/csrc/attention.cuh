@@ -20,6 +20,7 @@ struct AttnParams {
   float* out;             // [H * hd]
   int H, kvH, hd, S, nsplit, chunk_max;
   float scale;
+  unsigned int* err;  // device error word (bounded waits)
 };
 
 // Floats of workspace one call needs: part_m, part_l, part_acc, then kvH
@@ -29,8 +30,12 @@ inline size_t gqa_workspace_floats(int H, int kvH, int hd, int nsplit) {
 }
 // Points a's part_* and counter at a workspace of gqa_workspace_floats().
 void gqa_bind_workspace(AttnParams& a, float* ws);
-// About two CTAs per SM over all kv heads, at least 8 positions per split.
-int gqa_default_splits(int kvH, int S);
+// Position splits for a cache of S positions: about one CTA per SM over all
+// kv heads, at least 64 positions per split, and few enough positions per
+// split that the split's K and V fit in shared memory.
+int gqa_default_splits(int kvH, int S, int hd);
+// Smallest split count whose chunks fit in shared memory.
+int gqa_min_splits(int S, int hd);
 // Launches the split kernel (grid kvH x nsplit); a.nsplit and a.chunk_max set.
 int launch_gqa_decode(const AttnParams& a, const LaunchOpts& o);
 // Argument checks of the standalone entry points (ops/gqa/reference.ts:211-237).

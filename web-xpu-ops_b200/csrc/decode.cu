@@ -232,6 +232,7 @@ int record_step(xpu_llama* e) {
     a.nsplit = e->nsplit;
     a.chunk_max = e->chunk_max;
     a.scale = (float)(1.0 / sqrt((double)hd));
+    a.err = err;
     a.s_eff = 0;
     if ((rc = launch_gqa_decode(a, dep))) return rc;
     // o-proj + residual
@@ -425,7 +426,7 @@ int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, in
 
   // Position splits for attention: about two CTAs per SM over all kv heads,
   // at least 8 positions per split.
-  e->nsplit = gqa_default_splits(c.num_kv_heads, c.max_seq_len);
+  e->nsplit = gqa_default_splits(c.num_kv_heads, c.max_seq_len, c.head_dim);
   e->chunk_max = (c.max_seq_len + e->nsplit - 1) / e->nsplit;
   if ((rc = dev_alloc(e, &e->hidden_a, h)) || (rc = dev_alloc(e, &e->hidden_b, h)) || (rc = dev_alloc(e, &e->q, qd)) ||
       (rc = dev_alloc(e, &e->attn, qd)) || (rc = dev_alloc(e, &e->gated, c.ffn_hidden)) ||

@@ -71,7 +71,12 @@ extern "C" int xpu_gqa_decode_noalloc(const float* q, const float* k_cache, cons
               "(1 MiB); use xpu_gqa_decode_dev",
               per_split + (size_t)kv_heads, kScratchFloats);
   const int max_splits = (int)std::min<size_t>((kScratchFloats - (size_t)kv_heads) / per_split, 1 << 20);
-  const int nsplit = std::max(1, std::min({gqa_default_splits(kv_heads, S), (int)s_eff, max_splits}));
+  const int min_splits = gqa_min_splits(s_eff, D);
+  XPU_REQUIRE(min_splits <= max_splits, XPU_EINVAL,
+              "xpu_gqa_decode_noalloc: %d positions need %d splits, more than the static scratch holds (%d); "
+              "use xpu_gqa_decode_dev",
+              s_eff, min_splits, max_splits);
+  const int nsplit = std::max(min_splits, std::min({gqa_default_splits(kv_heads, S, D), (int)s_eff, max_splits}));
   float* ws = nullptr;
   if ((rc = scratch_address(&ws))) return rc;
   AttnParams a = gqa_params(q, k_cache, v_cache, H, kv_heads, D, S, s_eff, scale, out, nsplit);
