@@ -8,6 +8,7 @@ namespace xpu {
 namespace {
 constexpr int kMaxStages = 8;
 constexpr size_t kStageMaxBytes = 65536;  // one ring slot: a block of rows
+constexpr int64_t kRowGroupMinBytes = 32ll << 20;  // row groups only for matrices this large
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t round_up(size_t a, size_t b) { return (a + b - 1) / b * b; }
@@ -23,38 +24,76 @@ int plan_matvec(MvParams& p, int epi, int pro, MvPlan& plan) {
   const bool aligned = p.W > 0 && p.W % 4 == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0 &&
                        (nstream == 1 || reinterpret_cast<uintptr_t>(p.w2) % 16 == 0);
   if (aligned) {
-    // One 16-byte column slice per consumer thread where K allows (up to 16
-    // consumer warps), then the largest unit of rows whose per-thread
-    // accumulators and x registers fit (cpt <= cptmax) and whose stage ring
-    // keeps >= 2 stages in flight.
     const int64_t U = p.W / 4;
     const int64_t row_bytes = p.W * 4;
-    // Fewest columns per thread first, then the consumer-warp count that
-    // leaves the fewest thread-columns idle (a stage is released only when
-    // its slowest warp is done), then more warps.
-    int64_t ncw = std::clamp<int64_t>(ceil_div(U, 32), 1, 16);
-    const int64_t cpt = ceil_div(U, 32 * ncw);
-    for (int64_t w = ncw, best = cpt * 32 * ncw - U; w >= std::max<int64_t>(1, ncw / 2); --w) {
-      if (ceil_div(U, 32 * w) != cpt) break;
-      const int64_t waste = cpt * 32 * w - U;
-      if (waste < best) {
-        best = waste;
-        ncw = w;
+    int64_t ncw, cpt, rg = 1, wpg;
+    if (U % 32 == 0 && U < 512 && p.N * row_bytes >= kRowGroupMinBytes) {
+      // Short rows of a large matrix: one 16-byte column slice per thread,
+      // wpg warps per row, and rg row groups so that up to 16 consumer warps
+      // have work.  (Small matrices are latency-bound: more warps do not
+      // help them and larger units leave SMs idle.)
+      wpg = U / 32;
+      rg = std::min<int64_t>(16 / wpg, 8);
+      ncw = rg * wpg;
+      cpt = 1;
+    } else {
+      // Fewest columns per thread first, then the consumer-warp count that
+      // leaves the fewest thread-columns idle (a stage is released only when
+      // its slowest warp is done), then more warps.
+      ncw = std::clamp<int64_t>(ceil_div(U, 32), 1, 16);
+      cpt = ceil_div(U, 32 * ncw);
+      if (cpt >= 4) {  // 4 slices per thread: at most 14 consumer warps (launch bound)
+        ncw = 14;
+        cpt = ceil_div(U, 32 * ncw);
+      }
+      for (int64_t w = ncw, best = cpt * 32 * ncw - U; w >= std::max<int64_t>(1, ncw / 2); --w) {
+        if (ceil_div(U, 32 * w) != cpt) break;
+        const int64_t waste = cpt * 32 * w - U;
+        if (waste < best) {
+          best = waste;
+          ncw = w;
+        }
+      }
+      wpg = ncw;
+    }
+    // Rows per thread: the largest whose accumulators and x registers fit
+    // (rpt * cpt <= 8), whose unit fits one <= 64 KB stage with >= 2 stages
+    // in flight, and whose unit splits evenly over the weight streams (and
+    // into whole row pairs for QKV); with row groups, the largest that still
+    // gives every SM >= 2 units, else the one with the most units.
+    const size_t stage_off = round_up(mv_bulk_header_bytes(kMaxStages), 128);
+    int best = -1;
+    int64_t best_units = -1;
+    for (int rpt = 8; cpt <= 4 && rpt >= 1; rpt /= 2) {
+      const int cptmax = rpt >= 8 ? 1 : (rpt == 4 ? 2 : 4);
+      if (cpt > cptmax) continue;
+      const int64_t rt = rpt * rg;
+      if (rt % nstream) continue;
+      const int64_t rb = rt / nstream;
+      if (rb < min_rb || (epi == EPI_QKV && rb % 2)) continue;
+      const size_t stage_bytes = (size_t)rt * row_bytes;
+      if (stage_bytes > kStageMaxBytes && rpt > 1) continue;
+      const int64_t avail = (int64_t)di.max_smem_optin - (int64_t)stage_off - 1024;
+      if (avail / (int64_t)stage_bytes < 2) continue;
+      const int64_t units = ceil_div(p.N, rb);
+      if (rg == 1 || units >= 2 * (int64_t)di.sm_count) {
+        best = rpt;
+        break;
+      }
+      if (units > best_units) {
+        best_units = units;
+        best = rpt;
       }
     }
-    for (int rt = 8; cpt <= 4 && rt >= min_rb * nstream; rt /= 2) {
-      const int rb = rt / nstream;
-      if (rb < min_rb || rb * nstream != rt) continue;
-      const int cptmax = rt >= 8 ? 1 : (rt == 4 ? 2 : 4);
-      if (cpt > cptmax) continue;
-      const size_t stage_bytes = (size_t)rb * row_bytes * nstream;
-      if (stage_bytes > kStageMaxBytes && rt > min_rb * nstream) continue;
-      const size_t stage_off = round_up(mv_bulk_header_bytes(kMaxStages, rt), 128);
+    if (best > 0) {
+      const int rpt = best;
+      const int64_t rt = rpt * rg, rb = rt / nstream;
+      const size_t stage_bytes = (size_t)rt * row_bytes;
       const int64_t avail = (int64_t)di.max_smem_optin - (int64_t)stage_off - 1024;
       const int64_t S = std::min<int64_t>(kMaxStages, avail / (int64_t)stage_bytes);
-      if (S < 2) continue;
       plan.bulk = true;
-      plan.rt = rt;
+      plan.grouped = rg > 1;
+      plan.rt = rpt;
       plan.cpt = (int)cpt;
       plan.ncw = (int)ncw;
       plan.stages = (int)S;
@@ -63,6 +102,8 @@ int plan_matvec(MvParams& p, int epi, int pro, MvPlan& plan) {
       plan.grid = dim3((unsigned)std::min<int64_t>(units, di.sm_count));
       plan.block = dim3((unsigned)(32 * (ncw + 2)));
       p.ncw = (int)ncw;
+      p.rg = (int)rg;
+      p.wpg = (int)wpg;
       p.stages = (int)S;
       p.stage_off = (uint32_t)stage_off;
       p.stage_stride = (uint32_t)stage_bytes;

@@ -49,6 +49,8 @@ struct MvParams {
   float* vcache;
   // bulk kernel geometry
   int ncw;             // consumer warps
+  int rg;              // row groups: warps [g*wpg, (g+1)*wpg) take unit rows g, g+rg, ...
+  int wpg;             // warps per row group (one row's column slices)
   int stages;          // ring depth
   uint32_t stage_off;  // byte offset of the ring in dynamic shared memory
   uint32_t stage_stride;
@@ -62,16 +64,11 @@ __device__ __forceinline__ float silu_f32(float g) {
   return (float)(x / (1.0 + exp(-x)));
 }
 
-// Writes output row(s) of a unit from the per-warp partial sums in shared
-// memory (`rb[w * RT + r]`, w < nw): one call per output row, per row pair
-// for QKV (thread t handles unit rows 2t, 2t+1).
-template <int EPI, int RB, int RT>
-__device__ __forceinline__ void mv_epilogue(const MvParams& p, int64_t row0, int t, const float* rb, int nw) {
-  auto sum = [&](int r) {
-    float v = 0.0f;
-    for (int w = 0; w < nw; ++w) v += rb[w * RT + r];
-    return v;
-  };
+// Writes output row(s) of a unit given `sum(r)`, the finished dot product of
+// unit row r (gate rows [0, RB) and up rows [RB, 2RB) for FFN): one call per
+// output row, per row pair for QKV (call t handles unit rows 2t, 2t+1).
+template <int EPI, typename SumFn>
+__device__ __forceinline__ void mv_epilogue(const MvParams& p, int64_t row0, int t, int RB, SumFn sum) {
   if constexpr (EPI == EPI_PLAIN) {
     int64_t row = row0 + t;
     if (row < p.N) p.y[row] = __fmul_rn(sum(t), p.s[row]);
@@ -120,24 +117,26 @@ __device__ __forceinline__ void mv_epilogue(const MvParams& p, int64_t row0, int
   }
 }
 
-// Outputs written per unit: one thread per row, per pair for QKV.
-template <int EPI, int RB>
-__host__ __device__ constexpr int mv_outputs_per_unit() {
+// Outputs written per unit of RB rows (per stream): one per row, per pair for QKV.
+template <int EPI>
+__host__ __device__ constexpr int mv_outputs_per_unit(int RB) {
   return EPI == EPI_QKV ? RB / 2 : RB;
 }
 
 // x for the consumer thread's columns, 16 floats per column c (x[16c..16c+15],
-// zero past K).  With PRO_RMSNORM the CTA first reduces sum(x^2) in f64
-// (named barrier `bar` over `nthreads`), then applies
+// zero past K); the thread's columns are c = ti + j * nt (ti: its index in
+// its row group of nt threads).  With PRO_RMSNORM the CTA first reduces
+// sum(x^2) in f64 over the threads of row group 0 (each x[k] counted once),
+// with named barrier `bar` over all `nthreads` consumers, then applies
 // f32(x * (1/sqrt(ss/K + eps)) * gamma) as ops/rmsnorm/reference.ts:89-93.
 template <int CPT, int PRO>
-__device__ __forceinline__ void load_x_cols(const MvParams& p, int tid, int nthreads, int64_t U, double* red_d,
-                                            int bar, f2 (&xr)[CPT][8]) {
+__device__ __forceinline__ void load_x_cols(const MvParams& p, int tid, int nthreads, int ti, int nt, bool counts,
+                                            int64_t U, double* red_d, int bar, f2 (&xr)[CPT][8]) {
   float xv[CPT][16];
   double ss = 0.0;
 #pragma unroll
   for (int j = 0; j < CPT; ++j) {
-    int64_t c = tid + (int64_t)j * nthreads;
+    int64_t c = ti + (int64_t)j * nt;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       int64_t k = 16 * c + i;
@@ -147,9 +146,7 @@ __device__ __forceinline__ void load_x_cols(const MvParams& p, int tid, int nthr
     }
   }
   if constexpr (PRO == PRO_RMSNORM) {
-    // Columns beyond U (threads with no column) contribute 0.  Threads cover
-    // U*16 >= K entries, so every x[k] is counted exactly once.
-    double s = warp_sum_d(ss);
+    double s = warp_sum_d(counts ? ss : 0.0);
     int warp = tid / 32, lane = tid % 32, nw = nthreads / 32;
     if (lane == 0) red_d[warp] = s;
     named_bar_sync(bar, nthreads);
@@ -158,7 +155,7 @@ __device__ __forceinline__ void load_x_cols(const MvParams& p, int tid, int nthr
     double scale = 1.0 / sqrt(tot / (double)p.K + p.eps);
 #pragma unroll
     for (int j = 0; j < CPT; ++j) {
-      int64_t c = tid + (int64_t)j * nthreads;
+      int64_t c = ti + (int64_t)j * nt;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         int64_t k = 16 * c + i;
@@ -175,34 +172,41 @@ __device__ __forceinline__ void load_x_cols(const MvParams& p, int tid, int nthr
 
 // ------------------------------------------------------------ bulk kernel --
 // Warp roles: warps [0, ncw) consume, warp ncw produces (one thread issues
-// the bulk copies), warp ncw + 1 finishes rows (epilogue).  Consumers never
-// wait for each other: each publishes its per-row partial sums of a unit in
+// the bulk copies), warp ncw + 1 finishes rows (epilogue).  Consumers are
+// split into rg row groups of wpg warps; a group's threads own the 16-byte
+// column slices of a row (cpt each), and group g takes unit rows g, g + rg,
+// ... (RPT rows per thread).  A unit is RT = RPT * rg rows over all weight
+// streams (FFN: RT/2 gate rows then RT/2 up rows).  Consumers never wait for
+// each other: each warp publishes its RPT per-row partial sums of a unit in
 // a ring of reduction slots and signals an mbarrier; the epilogue warp adds
-// the ncw partials of each row and writes the output.
+// the partials of each row's group and writes the output.
 //
-// Shared memory: full[S] | empty[S] | rfull[RS] | rempty[RS] | red[RS][16][RT]
+// Shared memory: full[S] | empty[S] | rfull[RS] | rempty[RS] | red[RS][16][8]
 // | red_d[16] (rmsnorm prologue) | ring of S stages (at p.stage_off).
 constexpr int kRedSlots = 4;
 
-__host__ __device__ constexpr size_t mv_bulk_header_bytes(int stages, int rt) {
-  return 8 * (2 * (size_t)stages + 2 * kRedSlots) + 4 * (size_t)kRedSlots * 16 * rt + 8 * 16;
+__host__ __device__ constexpr size_t mv_bulk_header_bytes(int stages) {
+  return 8 * (2 * (size_t)stages + 2 * kRedSlots) + 4 * (size_t)kRedSlots * 16 * 8 + 8 * 16;
 }
 
-// RT = rows per unit across all weight streams (FFN: RB gate + RB up rows).
-// Plans use at most 16 consumer warps (18 warps in all).
-template <int RT, int CPT, int EPI, int PRO>
-__global__ void __launch_bounds__(576, 1) mv_bulk_kernel(MvParams p) {
+// Plans use at most 16 consumer warps (18 warps in all), 14 when each thread
+// holds 4 column slices (its x registers need the larger register budget).
+// GROUPED: row groups in use (rg > 1); otherwise rg = 1 is a compile-time
+// constant and the row arithmetic folds away.
+template <int RPT, int CPT, int EPI, int PRO, bool GROUPED>
+__global__ void __launch_bounds__(CPT >= 4 ? 512 : 576, 1) mv_bulk_kernel(MvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int NSTREAM = EPI == EPI_FFN ? 2 : 1;
-  constexpr int RB = RT / NSTREAM;
   constexpr int RS = kRedSlots;
   const int ncw = p.ncw, nct = ncw * 32, S = p.stages;
+  const int rg = GROUPED ? p.rg : 1, wpg = GROUPED ? p.wpg : ncw;
+  const int RT = RPT * rg, RB = RT / NSTREAM;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
   uint64_t* rfull = empty + S;
   uint64_t* rempty = rfull + RS;
-  float* red = reinterpret_cast<float*>(rempty + RS);              // [RS][16][RT]
-  double* red_d = reinterpret_cast<double*>(red + RS * 16 * RT);   // [16]
+  float* red = reinterpret_cast<float*>(rempty + RS);              // [RS][16][8]
+  double* red_d = reinterpret_cast<double*>(red + RS * 16 * 8);    // [16]
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
@@ -261,7 +265,7 @@ __global__ void __launch_bounds__(576, 1) mv_bulk_kernel(MvParams p) {
   if (warp == ncw + 1) {
     // ---------------- epilogue: finish the rows of every unit ----------------
     griddep_wait();  // residual, position and outputs belong to predecessors
-    constexpr int OUTS = mv_outputs_per_unit<EPI, RB>();
+    const int outs = mv_outputs_per_unit<EPI>(RB);
     int slot = 0;
     uint32_t rph = 0;
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
@@ -270,7 +274,15 @@ __global__ void __launch_bounds__(576, 1) mv_bulk_kernel(MvParams p) {
         break;
       }
       if (abort_flag) break;
-      if (lane < OUTS) mv_epilogue<EPI, RB, RT>(p, u * RB, lane, red + slot * 16 * RT, ncw);
+      const float* rb = red + slot * 16 * 8;
+      // Row r of the unit was summed by the warps of group r % rg, local row r / rg.
+      auto sum = [&](int r) {
+        const int g = r % rg, i = r / rg;
+        float v = 0.0f;
+        for (int w = g * wpg; w < (g + 1) * wpg; ++w) v += rb[w * 8 + i];
+        return v;
+      };
+      for (int t = lane; t < outs; t += 32) mv_epilogue<EPI>(p, u * RB, t, RB, sum);
       __syncwarp();
       if (lane == 0) mbar_arrive(&rempty[slot]);
       if (++slot == RS) {
@@ -283,8 +295,9 @@ __global__ void __launch_bounds__(576, 1) mv_bulk_kernel(MvParams p) {
 
   // ---------------- consumers ----------------
   griddep_wait();  // x and gamma belong to predecessors
+  const int group = warp / wpg, gt = wpg * 32, ti = (warp - group * wpg) * 32 + lane;
   f2 xr[CPT][8];
-  load_x_cols<CPT, PRO>(p, tid, nct, U, red_d, 1, xr);
+  load_x_cols<CPT, PRO>(p, tid, nct, ti, gt, group == 0, U, red_d, 1, xr);
   const f2 zero2 = make_f2(0.0f, 0.0f);
   int s = 0, slot = 0;
   uint32_t ph = 0, rph = 0;
@@ -297,38 +310,42 @@ __global__ void __launch_bounds__(576, 1) mv_bulk_kernel(MvParams p) {
     const int64_t row0 = u * RB;
     const int rows = (int)(p.N - row0 < RB ? p.N - row0 : RB);
     const uint32_t st = p.stage_off + (uint32_t)s * p.stage_stride;  // byte offset in smem
-    f2 acc[RT][2];
+    f2 acc[RPT][2];
 #pragma unroll
-    for (int r = 0; r < RT; ++r) acc[r][0] = acc[r][1] = zero2;
+    for (int r = 0; r < RPT; ++r) acc[r][0] = acc[r][1] = zero2;
 #pragma unroll
     for (int j = 0; j < CPT; ++j) {
-      const uint32_t c = (uint32_t)tid + (uint32_t)j * (uint32_t)nct;
+      const uint32_t c = (uint32_t)ti + (uint32_t)j * (uint32_t)gt;
       if (c < (uint32_t)U) {
         const uint32_t col = st + 16u * c;
         if (rows == RB) {  // every unit but possibly the last
 #pragma unroll
-          for (int r = 0; r < RT; ++r)
-            dot16(*reinterpret_cast<const uint4*>(smem + col + (uint32_t)r * row_bytes), xr[j], acc[r]);
+          for (int i = 0; i < RPT; ++i) {
+            const int r = group + rg * i;
+            dot16(*reinterpret_cast<const uint4*>(smem + col + (uint32_t)r * row_bytes), xr[j], acc[i]);
+          }
         } else {
 #pragma unroll
-          for (int r = 0; r < RT; ++r)
+          for (int i = 0; i < RPT; ++i) {
+            const int r = group + rg * i;
             if ((r % RB) < rows)
-              dot16(*reinterpret_cast<const uint4*>(smem + col + (uint32_t)r * row_bytes), xr[j], acc[r]);
+              dot16(*reinterpret_cast<const uint4*>(smem + col + (uint32_t)r * row_bytes), xr[j], acc[i]);
+          }
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // the stage may be refilled
 
-    float v[RT];
+    float v[RPT];
 #pragma unroll
-    for (int r = 0; r < RT; ++r) v[r] = hsum2(acc[r]);
-    const float tot = warp_reduce_rows<RT>(v, lane);
+    for (int i = 0; i < RPT; ++i) v[i] = hsum2(acc[i]);
+    const float tot = warp_reduce_rows<RPT>(v, lane);
     if (!first_round && !mbar_wait(&rempty[slot], rph ^ 1u, p.err)) {
       abort_flag = 1;
       break;
     }
-    if (lane % (32 / RT) == 0) red[(slot * 16 + warp) * RT + lane / (32 / RT)] = tot;
+    if (lane % (32 / RPT) == 0) red[(slot * 16 + warp) * 8 + lane / (32 / RPT)] = tot;
     __syncwarp();
     if (lane == 0) mbar_arrive(&rfull[slot]);
     if (++s == S) {
@@ -435,8 +452,13 @@ __global__ void __launch_bounds__(256) mv_gen_kernel(MvParams p, int64_t off_wor
       if (lane == 0) red[warp][r] = v;
     }
     __syncthreads();
-    constexpr int OUTS = mv_outputs_per_unit<EPI, RB>();
-    if (tid < OUTS) mv_epilogue<EPI, RB, RT>(p, row0, tid, rb, nt / 32);
+    constexpr int OUTS = mv_outputs_per_unit<EPI>(RB);
+    auto sum = [&](int r) {
+      float t = 0.0f;
+      for (int w = 0; w < nt / 32; ++w) t += rb[w * RT + r];
+      return t;
+    };
+    if (tid < OUTS) mv_epilogue<EPI>(p, row0, tid, RB, sum);
     __syncthreads();
   }
 }

@@ -11,7 +11,9 @@ namespace xpu {
 // Geometry chosen by plan_matvec().
 struct MvPlan {
   bool bulk = false;  // bulk-copy (TMA) kernel, else the general kernel
-  int rt = 0, cpt = 0, ncw = 0, stages = 0;
+  int rt = 0;         // bulk: rows per thread per unit; general: rows per unit
+  bool grouped = false;  // bulk: row groups in use
+  int cpt = 0, ncw = 0, stages = 0;
   dim3 grid, block;
   size_t smem = 0;
   int64_t off_words = 0;  // general kernel: words from the 16-byte grid to w
@@ -52,17 +54,19 @@ template <int EPI, int PRO>
 int launch_mv_impl(const MvParams& p, const MvPlan& plan, const LaunchOpts& o) {
   void (*k)(MvParams) = nullptr;
   if (plan.bulk) {
-#define XPU_MV_CASE(RT_, CPT_)                                      \
-  if (plan.rt == RT_ && plan.cpt == CPT_) k = mv_bulk_kernel<RT_, CPT_, EPI, PRO>;
-    if constexpr (EPI != EPI_FFN && EPI != EPI_QKV) {
-      XPU_MV_CASE(1, 1) XPU_MV_CASE(1, 2) XPU_MV_CASE(1, 3) XPU_MV_CASE(1, 4)
-    }
+#define XPU_MV_CASE(RT_, CPT_)                                                  \
+  if (!plan.grouped && plan.rt == RT_ && plan.cpt == CPT_) k = mv_bulk_kernel<RT_, CPT_, EPI, PRO, false>;
+#define XPU_MV_CASE_G(RT_)                                                      \
+  if (plan.grouped && plan.rt == RT_ && plan.cpt == 1) k = mv_bulk_kernel<RT_, 1, EPI, PRO, true>;
+    XPU_MV_CASE(1, 1) XPU_MV_CASE(1, 2) XPU_MV_CASE(1, 3) XPU_MV_CASE(1, 4)
     XPU_MV_CASE(2, 1) XPU_MV_CASE(2, 2) XPU_MV_CASE(2, 3) XPU_MV_CASE(2, 4)
     XPU_MV_CASE(4, 1) XPU_MV_CASE(4, 2)
     XPU_MV_CASE(8, 1)
+    XPU_MV_CASE_G(1) XPU_MV_CASE_G(2) XPU_MV_CASE_G(4) XPU_MV_CASE_G(8)
 #undef XPU_MV_CASE
+#undef XPU_MV_CASE_G
     if (!k) {
-      set_error("matvecQ8: no bulk kernel for rt=%d cpt=%d", plan.rt, plan.cpt);
+      set_error("matvecQ8: no bulk kernel for rpt=%d cpt=%d", plan.rt, plan.cpt);
       return XPU_EINVAL;
     }
     XPU_TRY_CUDA(ensure_smem_attr((const void*)k, plan.smem));
