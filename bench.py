@@ -412,7 +412,7 @@ def run_decode(args, torch, world, max_over_ranks, barrier):
         ms = max_over_ranks(d0.elapsed_time(d1))
         # host-API decode (forward(), logits copied to the host every token)
         h0 = time.perf_counter()
-        n_host = 32
+        n_host = min(32, args.decode_steps)
         tok = int(toks[-1])
         for _ in range(n_host):
             (logits,) = eng.forward([tok])
