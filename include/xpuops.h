@@ -121,9 +121,11 @@ XPU_API int xpu_matvec_q8_residual_dev(const uint32_t* weight, const float* scal
  * applied to the same x, e.g. every expert or layer slice of a model, or the
  * row shard of each that one GPU holds): matrix m is `weights + m *
  * weight_stride` (u32 words), its scales `scales + m * N`, its output
- * `outputs + m * N`.  Consecutive launches overlap their weight streaming
- * (programmatic dependent launch).  Same results as `count` calls of
- * xpu_matvec_q8_dev. */
+ * `outputs + m * N`.  Same results as `count` calls of xpu_matvec_q8_dev.
+ * A contiguous stack (weight_stride == N * ceil(K/4)) runs as one
+ * persistent launch over its count * N rows; otherwise one launch per
+ * matrix, consecutive launches overlapping their weight streaming
+ * (programmatic dependent launch). */
 XPU_API int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stride,
                                     const float* scales, const float* vector, int64_t count,
                                     int64_t N, int64_t K, float* outputs, void* stream);

@@ -350,3 +350,26 @@ def test_device_fill_matches_host_recipe():
     ulp = np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64))
     assert ulp.max() <= 1
     assert (ulp > 0).mean() < 1e-4
+
+
+@pytest.mark.parametrize("N,K", [(1024, 8192), (96, 2048), (40, 1028)])
+def test_stack_contiguous_and_strided_match_single_gemvs(N, K):
+    """xpu_matvec_q8_stack_dev: a contiguous stack (one launch over all rows)
+    and a strided one (a launch per matrix) give each matrix's matvecQ8."""
+    M, W = 3, (K + 3) // 4
+    mats = [_synth_q8(N, K, 7000 + m) for m in range(M)]
+    x = fill_normal(K, 7100)
+    contig = np.concatenate([m[1] for m in mats])
+    stride = N * W + 16
+    strided = np.zeros(M * stride, np.uint32)
+    for m in range(M):
+        strided[m * stride: m * stride + N * W] = mats[m][1]
+    scales = np.concatenate([m[2] for m in mats])
+    dx, ds = ops.DeviceBuffer.from_numpy(x), ops.DeviceBuffer.from_numpy(scales)
+    for w, st in ((contig, N * W), (strided, stride)):
+        dw, dy = ops.DeviceBuffer.from_numpy(w), ops.DeviceBuffer(4 * M * N)
+        ops.matvecQ8Stack_dev(dw, st, ds, dx, M, N, K, dy)
+        ops.stream_sync()
+        y = dy.download(np.float32, M * N).reshape(M, N)
+        for m in range(M):
+            check_matvec(y[m], mats[m][1], mats[m][2], x, N, K)

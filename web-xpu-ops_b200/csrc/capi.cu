@@ -218,6 +218,18 @@ int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stride, cons
               "matvecQ8 stack: count must be >= 0 and the stride at least N*ceil(K/4) words");
   if (N == 0 || count == 0) return XPU_OK;
   XPU_REQUIRE(weights && scales && vector && outputs, XPU_EINVAL, "matvecQ8 stack: null pointer");
+  if (weight_stride == N * ((K + 3) / 4)) {
+    // Contiguous stack: the matrices, their scales and their outputs are one
+    // [count * N, K] GEMV end to end; one persistent launch streams it all.
+    MvParams p{};
+    p.w = weights;
+    p.s = scales;
+    p.x = vector;
+    p.y = outputs;
+    p.N = count * N;
+    p.K = K;
+    return run_matvec(p, EPI_PLAIN, PRO_PLAIN, LaunchOpts{(cudaStream_t)stream, false});
+  }
   for (int64_t m = 0; m < count; ++m) {
     MvParams p{};
     p.w = weights + m * weight_stride;
