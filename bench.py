@@ -450,21 +450,45 @@ def run_decode(args, torch, world, max_over_ranks, barrier):
     rng = np.random.default_rng(41)
     eng = LlamaEngineQ8Resident.create(cfg, weights, torch.cuda.current_device())
     try:
+        kv0 = None
         for l in range(c.numLayers):
             k = rng.standard_normal(c.numKvHeads * ctx * c.headDim, dtype=np.float32)
             v = rng.standard_normal(c.numKvHeads * ctx * c.headDim, dtype=np.float32)
             eng.setKv(l, k, v, ctx)
+            if l == 0:
+                kv0 = (k, v)
         first = int(rng.integers(0, c.vocabSize))
         warm = 3
-        eng.greedySteps(first, warm)
         es = torch.cuda.ExternalStream(eng.stream())
-        barrier()
-        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        d0.record(es)
-        toks = eng.greedySteps(first, args.decode_steps)
-        d1.record(es)
-        d1.synchronize()
-        ms = max_over_ranks(d0.elapsed_time(d1))
+
+        def timed(path):
+            # setKv of one layer puts the position back to ctx; the other
+            # layers' rows >= ctx are rewritten before they are read.
+            eng.setDecodePath(path)
+            eng.setKv(0, kv0[0], kv0[1], ctx)
+            eng.greedySteps(first, warm)
+            barrier()
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            d0.record(es)
+            toks = eng.greedySteps(first, args.decode_steps)
+            d1.record(es)
+            d1.synchronize()
+            return max_over_ranks(d0.elapsed_time(d1)), toks
+
+        from xpuops import XpuInvalidArgument
+
+        default = eng.decodePath
+        GRAPH, PERSISTENT = LlamaEngineQ8Resident.DECODE_GRAPH, LlamaEngineQ8Resident.DECODE_PERSISTENT
+        paths = [default]
+        try:
+            other = PERSISTENT if default == GRAPH else GRAPH
+            eng.setDecodePath(other)
+            paths.append(other)
+        except XpuInvalidArgument:
+            pass
+        res = {pth: timed(pth) for pth in reversed(paths)}
+        eng.setDecodePath(default)
+        ms, toks = res[default]
         # host-API decode (forward(), logits copied to the host every token)
         h0 = time.perf_counter()
         n_host = min(32, args.decode_steps)
@@ -477,19 +501,28 @@ def run_decode(args, torch, world, max_over_ranks, barrier):
         byts = sum(decode_bytes_per_token(cfg, pos0 + i) for i in range(args.decode_steps))
         peak, src = measured_peaks()
         tps = args.decode_steps / (ms / 1e3)
-        return {
+        persistent = default == PERSISTENT
+        out = {
             "tokens_per_s": round(tps * world, 1),
             "tokens_per_s_per_gpu": round(tps, 1),
             "ms_per_token": round(ms / args.decode_steps, 4),
+            "path": "persistent (one cooperative launch per token)" if persistent else "graph (per-kernel)",
             "config": "22 layers, hidden 2048, 32q/4kv heads, head_dim 64, FFN 5632, vocab 32000; context "
                       f"{pos0}..{pos0 + args.decode_steps}; greedy; replicas on each GPU",
             "bytes_per_token": byts // args.decode_steps,
             "achieved_gbs": round(byts / (ms / 1e3) / 1e9, 1),
             "roofline_frac": round(byts / (ms / 1e3) / 1e9 / peak, 4),
-            "gpu_launches_per_token": 5 * c.numLayers + 3,
+            "gpu_launches_per_token": 1 if persistent else 5 * c.numLayers + 3,
             "e2e_host_forward": {"tokens_per_s": round(n_host / (host_ms / 1e3) * world, 1),
                                  "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * c.vocabSize},
         }
+        for pth in paths[1:]:
+            oms, otoks = res[pth]
+            out["persistent_path" if pth == PERSISTENT else "graph_path"] = {
+                "tokens_per_s_per_gpu": round(args.decode_steps / (oms / 1e3), 1),
+                "gpu_launches_per_token": 1 if pth == PERSISTENT else 5 * c.numLayers + 3,
+                "same_tokens": int(np.sum(np.asarray(otoks) == np.asarray(toks)))}
+        return out
     finally:
         eng.close()
 

@@ -224,8 +224,10 @@ typedef struct xpu_llama xpu_llama;
 
 /* llm/engine-q8-resident.ts:1052-1245 `LlamaEngineQ8Resident.create`.
  * Checks shapes (llm/weights-q8.ts:68-96 `assertWeightShapesQ8`), packs every
- * linear on the device, allocates the KV cache and captures the decode step
- * into one CUDA graph.  Host weights may be freed after it returns. */
+ * linear on the device, allocates the KV cache and prepares both decode-step
+ * paths: the per-kernel step captured as one CUDA graph, and the persistent
+ * step (one cooperative launch per token) where the shapes allow it.  Host
+ * weights may be freed after it returns. */
 XPU_API int xpu_llama_create(const xpu_llama_config* config,
                      const xpu_llama_weights_q8* weights, int device,
                      xpu_llama** engine);
@@ -238,6 +240,52 @@ XPU_API int xpu_llama_create(const xpu_llama_config* config,
  * when only `argmax` (host, nullable) is wanted. */
 XPU_API int xpu_llama_forward(xpu_llama* engine, const int32_t* tokens, int32_t n,
                       float* logits, int32_t* argmax);
+
+/* llm/engine-q8-resident.ts:33-152 `ForwardProfile`, the optional second
+ * argument of `forward(tokens, profile?)`.  `want_gpu_breakdown` is the
+ * caller's input (the reference's `wantGpuBreakdown`); every other field is
+ * written by xpu_llama_forward_profiled.  Times are host wall-clock except
+ * `entries`, which are device-timed phases of the call's LAST step when
+ * `want_gpu_breakdown` is set and the persistent step ran it
+ * (`gpu_timestamps_supported` = 1; the per-kernel graph path reports none,
+ * as the reference does without timestamp-query).  Entry labels follow the
+ * reference's "L<layer>:<kernel>" form: "L<l>:qkv", "L<l>:attn", "L<l>:o_proj",
+ * "L<l>:ffn", "L<l>:down", then "lm_head". */
+typedef struct xpu_profile_entry {
+  char   label[24];
+  double seconds;     /* latest CTA's phase end minus latest end of the phase before */
+  double wait_s;      /* mean over CTAs: grid-barrier wait before the phase          */
+  double input_s;     /* mean: staging the input vector (rmsnorm), or the query      */
+  double compute_s;   /* mean: dot products over the streamed weights, or the split  */
+  double epilogue_s;  /* mean: epilogue writes, or the split merge                   */
+} xpu_profile_entry;
+
+typedef struct xpu_forward_profile {
+  int32_t            want_gpu_breakdown;        /* input                             */
+  int32_t            gpu_timestamps_supported;  /* 1 when `entries` were measured     */
+  double             upload_ms;                 /* token uploads (enqueue)           */
+  int64_t            upload_bytes;
+  double             submit_to_done_ms;         /* first launch to stream completion */
+  double             readback_ms;               /* logits / argmax copies            */
+  double             total_ms;                  /* the whole call                    */
+  xpu_profile_entry* entries;                   /* caller-owned, `entries_cap` long  */
+  int32_t            entries_cap;
+  int32_t            n_entries;                 /* written (<= entries_cap)          */
+} xpu_forward_profile;
+
+/* xpu_llama_forward with a profile (NULL `profile` = xpu_llama_forward). */
+XPU_API int xpu_llama_forward_profiled(xpu_llama* engine, const int32_t* tokens, int32_t n,
+                               float* logits, int32_t* argmax, xpu_forward_profile* profile);
+
+/* The raw device timestamps behind the last profiled persistent step's
+ * entries (ns, %globaltimer): out[(phase * grid + cta) * events + e], phases
+ * in entry order, e as documented in the library's persistent-step source
+ * (0 phase start, 1 input staged, 2 dot products done, 3 epilogue done,
+ * 4 first weight stage ready, 5 total ns waited for weight stages, 6 / 7
+ * producer issued first / last stage; 0 = did not happen).  Writes min(cap, total) values and sets `n`
+ * to the total; XPU_ESTATE before any profiled persistent step. */
+XPU_API int xpu_llama_profile_trace(const xpu_llama* engine, uint64_t* out, int64_t cap, int64_t* n,
+                            int32_t* grid, int32_t* events);
 
 /* One decode step whose token id is read from device memory `token_dev`
  * (int32) and whose greedy next token (llm/engine.ts:226-232 `argmax`) is
@@ -267,6 +315,22 @@ XPU_API int xpu_llama_set_kv(xpu_llama* engine, int32_t layer, const float* k,
 /* Test hook, llm/engine-q8-resident.ts:1043-1050 `debugPoisonKVCache`:
  * every position of every layer's cache := value. */
 XPU_API int xpu_llama_poison_kv(xpu_llama* engine, float value);
+
+/* Decode-step paths.  No counterpart in the reference (its step is one
+ * WebGPU submit of ~300 dispatches): XPU_DECODE_GRAPH replays the captured
+ * per-kernel graph (113 launches per token for 22 layers);
+ * XPU_DECODE_PERSISTENT runs the whole step as one cooperative launch with
+ * grid barriers between its phases.  The persistent path applies when the
+ * shapes allow it (every GEMV row a whole number of 16-byte slots, head_dim
+ * <= 128 and a multiple of 4); the graph path is the default unless the
+ * environment sets XPUOPS_DECODE_PATH=persistent.
+ * Both paths compute the same step; sums are ordered differently, so logits
+ * agree to f32 rounding, not bit for bit.  Selecting XPU_DECODE_PERSISTENT
+ * where it does not apply gives XPU_EINVAL. */
+#define XPU_DECODE_GRAPH       0
+#define XPU_DECODE_PERSISTENT  1
+XPU_API int xpu_llama_set_decode_path(xpu_llama* engine, int32_t path);
+XPU_API int xpu_llama_decode_path(const xpu_llama* engine, int32_t* path);
 XPU_API int xpu_llama_destroy(xpu_llama* engine);
 
 #ifdef __cplusplus

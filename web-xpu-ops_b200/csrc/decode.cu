@@ -14,12 +14,16 @@
 // The token and the position live in device memory, so the captured graph is
 // replayed unchanged for every token.
 #include <math.h>
+#include <stdio.h>
 #include <string.h>
+
+#include <chrono>
 
 #include <algorithm>
 #include <vector>
 
 #include "attention.cuh"
+#include "decode_mk.cuh"
 #include "matvec_launch.cuh"
 
 namespace xpu {
@@ -133,6 +137,17 @@ struct xpu_llama {
   float* h_logits = nullptr;
   cudaGraphExec_t exec = nullptr;
   int32_t tokens_so_far = 0;
+  // persistent step (decode_mk.cu): one cooperative launch per token
+  int path = XPU_DECODE_GRAPH;
+  bool mk_ok = false;
+  xpu::MkParams mk{};
+  size_t mk_smem = 0;
+  int mk_grid = 0;
+  unsigned long long* mk_bar = nullptr;
+  unsigned int* mk_ticket = nullptr;
+  unsigned long long* mk_trace = nullptr;  // profile timestamps, allocated on first use
+  unsigned long long* h_trace = nullptr;
+  bool trace_valid = false;
 };
 
 namespace xpu {
@@ -315,6 +330,194 @@ int set_device_pos(xpu_llama* e, int32_t pos) {
   return XPU_OK;
 }
 
+// Zeroes the grid-barrier, ticket and attention counters (after a failed
+// step they may hold a partial count).
+int rearm_counters(xpu_llama* e) {
+  if (e->mk_bar) XPU_TRY_CUDA(cudaMemsetAsync(e->mk_bar, 0, 8, e->stream));
+  if (e->mk_ticket) XPU_TRY_CUDA(cudaMemsetAsync(e->mk_ticket, 0, 4, e->stream));
+  XPU_TRY_CUDA(cudaMemsetAsync(e->counter, 0, (size_t)e->c.num_kv_heads * 4, e->stream));
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  return XPU_OK;
+}
+
+// One decode step on e->stream with the selected path.
+int launch_step(xpu_llama* e) {
+  if (e->path == XPU_DECODE_PERSISTENT) return mk_launch(e->mk, e->mk_smem, e->mk_grid, e->stream);
+  XPU_TRY_CUDA(cudaGraphLaunch(e->exec, e->stream));
+  return XPU_OK;
+}
+
+// Reads and clears the device error word after a synchronised step; on an
+// error the counters are re-armed so the engine stays usable.
+int finish_steps(xpu_llama* e) {
+  int rc = check_device_error();
+  if (rc) rearm_counters(e);
+  return rc;
+}
+
+// Plans the persistent step (decode_mk.cu) for this engine's shapes.  When
+// the shapes do not fit it (rows that are not whole 16-byte slots, head_dim
+// > 128, shared memory), the engine keeps the per-kernel graph.  The graph
+// path stays the default unless XPUOPS_DECODE_PATH=persistent.
+int setup_persistent(xpu_llama* e) {
+  const xpu_llama_config& c = e->c;
+  const int64_t h = c.hidden_size, hd = c.head_dim;
+  const int64_t qd = (int64_t)c.num_heads * hd, kvd = (int64_t)c.num_kv_heads * hd;
+  const int L = c.num_layers;
+  std::vector<MkGemv> gh(4 * (size_t)L + 1);
+  std::vector<MkAttn> ah((size_t)std::max(L, 1));
+  for (int l = 0; l < L; ++l) {
+    Layer& Ly = e->layers[l];
+    MkGemv& q = gh[4 * l];
+    q = MkGemv{};
+    q.w = Ly.qkv.w;
+    q.s = Ly.qkv.s;
+    q.x = e->hidden_a;
+    q.gamma = Ly.attn_norm;
+    q.y = e->q;
+    q.kcache = Ly.kcache;
+    q.vcache = Ly.vcache;
+    q.N = (int)(qd + 2 * kvd);
+    q.K = (int)h;
+    q.epi = EPI_QKV;
+    q.embed = l == 0;
+    MkGemv& o = gh[4 * l + 1];
+    o = MkGemv{};
+    o.w = Ly.wo.w;
+    o.s = Ly.wo.s;
+    o.x = e->attn;
+    o.residual = e->hidden_a;
+    o.y = e->hidden_b;
+    o.N = (int)h;
+    o.K = (int)qd;
+    o.epi = EPI_RESID;
+    MkGemv& f = gh[4 * l + 2];
+    f = MkGemv{};
+    f.w = Ly.gate.w;
+    f.s = Ly.gate.s;
+    f.w2 = Ly.up.w;
+    f.s2 = Ly.up.s;
+    f.x = e->hidden_b;
+    f.gamma = Ly.ffn_norm;
+    f.y = e->gated;
+    f.N = c.ffn_hidden;
+    f.K = (int)h;
+    f.epi = EPI_FFN;
+    MkGemv& d = gh[4 * l + 3];
+    d = MkGemv{};
+    d.w = Ly.down.w;
+    d.s = Ly.down.s;
+    d.x = e->gated;
+    d.residual = e->hidden_b;
+    d.y = e->hidden_a;
+    d.N = (int)h;
+    d.K = c.ffn_hidden;
+    d.epi = EPI_RESID;
+    ah[l] = MkAttn{e->q, Ly.kcache, Ly.vcache, e->attn};
+  }
+  MkGemv& hd_ = gh[4 * (size_t)L];
+  hd_ = MkGemv{};
+  hd_.w = e->lm_head.w;
+  hd_.s = e->lm_head.s;
+  hd_.x = e->hidden_a;
+  hd_.gamma = e->final_norm;
+  hd_.y = e->logits;
+  hd_.N = c.vocab_size;
+  hd_.K = (int)h;
+  hd_.epi = EPI_PLAIN;
+  hd_.embed = L == 0;
+
+  MkParams& p = e->mk;
+  p = MkParams{};
+  p.layers = L;
+  p.embed_codes = e->embed_codes;
+  p.embed_scale = e->embed_scale;
+  p.vocab = c.vocab_size;
+  p.hidden = (int)h;
+  p.hidden0 = e->hidden_a;
+  p.eps = c.rms_norm_eps;
+  p.inv_freq = e->inv_freq;
+  p.q_rows = (int)qd;
+  p.kv_rows = (int)kvd;
+  p.head_dim = (int)hd;
+  p.max_seq = c.max_seq_len;
+  p.H = c.num_heads;
+  p.kvH = c.num_kv_heads;
+  p.attn_scale = (float)(1.0 / sqrt((double)hd));
+  p.part_m = e->part_m;
+  p.part_l = e->part_l;
+  p.part_acc = e->part_acc;
+  p.attn_counter = e->counter;
+  p.token = e->d_token;
+  p.pos = e->d_pos;
+  p.next = e->d_next;
+  p.gen = e->d_gen;
+  p.logits = e->logits;
+  p.err = device_error_word();
+  const int kmax = (int)std::max<int64_t>({h, qd, (int64_t)c.ffn_hidden});
+  int rc = mk_configure(p, gh.data(), (int)gh.size(), kmax, &e->mk_smem, &e->mk_grid);
+  if (rc == XPU_EINVAL) {  // shapes outside the persistent step: keep the graph
+    clear_error();
+    return XPU_OK;
+  }
+  if (rc) return rc;
+  MkGemv* d_gemv = nullptr;
+  MkAttn* d_attn = nullptr;
+  if ((rc = dev_alloc(e, &d_gemv, gh.size())) || (rc = dev_alloc(e, &d_attn, ah.size())) ||
+      (rc = dev_alloc(e, &e->mk_bar, 1)) || (rc = dev_alloc(e, &e->mk_ticket, 1)) ||
+      (rc = dev_alloc(e, &p.cand_v, (size_t)e->mk_grid)) || (rc = dev_alloc(e, &p.cand_i, (size_t)e->mk_grid)))
+    return rc;
+  XPU_TRY_CUDA(cudaMemcpy(d_gemv, gh.data(), gh.size() * sizeof(MkGemv), cudaMemcpyHostToDevice));
+  XPU_TRY_CUDA(cudaMemcpy(d_attn, ah.data(), ah.size() * sizeof(MkAttn), cudaMemcpyHostToDevice));
+  p.gemv = d_gemv;
+  p.attn = d_attn;
+  p.bar = e->mk_bar;
+  p.ticket = e->mk_ticket;
+  if ((rc = rearm_counters(e))) return rc;
+  // A first step, so the kernel is loaded before use; its effects (cache
+  // slot 0, logits, token and position words) are reset or overwritten.
+  if ((rc = mk_launch(p, e->mk_smem, e->mk_grid, e->stream))) return rc;
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess) return cuda_status(cudaGetLastError(), "persistent warm-up");
+  if ((rc = finish_steps(e))) return rc;
+  if ((rc = set_device_pos(e, 0))) return rc;
+  e->mk_ok = true;
+  const char* env = getenv("XPUOPS_DECODE_PATH");
+  e->path = (env && strcmp(env, "persistent") == 0) ? XPU_DECODE_PERSISTENT : XPU_DECODE_GRAPH;
+  return XPU_OK;
+}
+
+// Per-phase entries of the persistent step from the device timestamps of
+// its last launch (MkParams::trace layout).
+void fill_profile_entries(xpu_llama* e, xpu_forward_profile* prof) {
+  static const char* kNames[5] = {"qkv", "attn", "o_proj", "ffn", "down"};
+  const int G = e->mk_grid, L = e->c.num_layers, n_phase = 5 * L + 1;
+  const unsigned long long* tr = e->h_trace;
+  auto at = [&](int i, int b, int ev) { return (double)tr[((size_t)i * G + b) * kMkTraceEvents + ev]; };
+  double prev_end = at(0, 0, 0);
+  for (int b = 1; b < G; ++b) prev_end = std::min(prev_end, at(0, b, 0));
+  for (int i = 0; i < n_phase && prof->n_entries < prof->entries_cap; ++i) {
+    xpu_profile_entry& en = prof->entries[prof->n_entries++];
+    if (i < 5 * L)
+      snprintf(en.label, sizeof(en.label), "L%d:%s", i / 5, kNames[i % 5]);
+    else
+      snprintf(en.label, sizeof(en.label), "lm_head");
+    double end = 0, wait = 0, in = 0, comp = 0, epi = 0;
+    for (int b = 0; b < G; ++b) {
+      end = std::max(end, at(i, b, 3));
+      wait += i > 0 ? at(i, b, 0) - at(i - 1, b, 3) : 0.0;
+      in += at(i, b, 1) - at(i, b, 0);
+      comp += at(i, b, 2) - at(i, b, 1);
+      epi += at(i, b, 3) - at(i, b, 2);
+    }
+    en.seconds = (end - prev_end) * 1e-9;
+    en.wait_s = wait / G * 1e-9;
+    en.input_s = in / G * 1e-9;
+    en.compute_s = comp / G * 1e-9;
+    en.epilogue_s = epi / G * 1e-9;
+    prev_end = end;
+  }
+}
+
 void destroy_engine(xpu_llama* e) {
   if (!e) return;
   int prev = 0;
@@ -326,6 +529,7 @@ void destroy_engine(xpu_llama* e) {
   if (e->h_tokens) cudaFreeHost(e->h_tokens);
   if (e->h_misc) cudaFreeHost(e->h_misc);
   if (e->h_logits) cudaFreeHost(e->h_logits);
+  if (e->h_trace) cudaFreeHost(e->h_trace);
   if (e->stream) cudaStreamDestroy(e->stream);
   cudaSetDevice(prev);
   delete e;
@@ -428,12 +632,14 @@ int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, in
   // at least 8 positions per split.
   e->nsplit = gqa_default_splits(c.num_kv_heads, c.max_seq_len, c.head_dim);
   e->chunk_max = (c.max_seq_len + e->nsplit - 1) / e->nsplit;
+  // The persistent step uses up to one split per SM for each kv head.
+  const int ns_alloc = std::max(e->nsplit, device_info().sm_count);
   if ((rc = dev_alloc(e, &e->hidden_a, h)) || (rc = dev_alloc(e, &e->hidden_b, h)) || (rc = dev_alloc(e, &e->q, qd)) ||
       (rc = dev_alloc(e, &e->attn, qd)) || (rc = dev_alloc(e, &e->gated, c.ffn_hidden)) ||
       (rc = dev_alloc(e, &e->logits, c.vocab_size)) ||
-      (rc = dev_alloc(e, &e->part_m, (size_t)c.num_heads * e->nsplit)) ||
-      (rc = dev_alloc(e, &e->part_l, (size_t)c.num_heads * e->nsplit)) ||
-      (rc = dev_alloc(e, &e->part_acc, (size_t)c.num_heads * e->nsplit * hd)) ||
+      (rc = dev_alloc(e, &e->part_m, (size_t)c.num_heads * ns_alloc)) ||
+      (rc = dev_alloc(e, &e->part_l, (size_t)c.num_heads * ns_alloc)) ||
+      (rc = dev_alloc(e, &e->part_acc, (size_t)c.num_heads * ns_alloc * hd)) ||
       (rc = dev_alloc(e, &e->counter, c.num_kv_heads)) || (rc = dev_alloc(e, &e->d_token, 4)) ||
       (rc = dev_alloc(e, &e->d_next, 4)) || (rc = dev_alloc(e, &e->d_pos, 4)) ||
       (rc = dev_alloc(e, &e->d_gen, (size_t)c.max_seq_len)))
@@ -455,6 +661,7 @@ int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, in
   if ((rc = check_device_error())) return fail(rc);
   if ((rc = set_device_pos(e, 0))) return fail(rc);
   if ((rc = build_graph(e))) return fail(rc);
+  if ((rc = setup_persistent(e))) return fail(rc);
   *out = e;
   return XPU_OK;
 }
@@ -476,6 +683,14 @@ int xpu_llama_create(const xpu_llama_config* config, const xpu_llama_weights_q8*
 }
 
 int xpu_llama_forward(xpu_llama* e, const int32_t* tokens, int32_t n, float* logits, int32_t* argmax) {
+  return xpu_llama_forward_profiled(e, tokens, n, logits, argmax, nullptr);
+}
+
+int xpu_llama_forward_profiled(xpu_llama* e, const int32_t* tokens, int32_t n, float* logits, int32_t* argmax,
+                               xpu_forward_profile* prof) {
+  using clk = std::chrono::steady_clock;
+  const auto t_start = clk::now();
+  auto ms_since = [](clk::time_point a) { return std::chrono::duration<double, std::milli>(clk::now() - a).count(); };
   XPU_REQUIRE(e, XPU_EINVAL, "LlamaEngineQ8Resident.forward: null engine");
   XPU_REQUIRE(n > 0 && tokens, XPU_EINVAL, "LlamaEngineQ8Resident.forward: tokens must be non-empty");
   XPU_REQUIRE(e->tokens_so_far == 0 || n == 1, XPU_ESTATE,
@@ -483,22 +698,75 @@ int xpu_llama_forward(xpu_llama* e, const int32_t* tokens, int32_t n, float* log
   XPU_REQUIRE((int64_t)e->tokens_so_far + n <= e->c.max_seq_len, XPU_ERANGE,
               "LlamaEngineQ8Resident.forward: position %lld exceeds maxSeqLen=%d",
               (long long)e->tokens_so_far + n, e->c.max_seq_len);
+  XPU_REQUIRE(!prof || prof->entries_cap <= 0 || prof->entries, XPU_EINVAL,
+              "forward profile: entries_cap > 0 needs an entries array");
   XPU_TRY_CUDA(cudaSetDevice(e->device));
+  const bool breakdown = prof && prof->want_gpu_breakdown && e->path == XPU_DECODE_PERSISTENT;
+  const int n_phase = 5 * e->c.num_layers + 1;
+  const size_t trace_n = (size_t)n_phase * e->mk_grid * kMkTraceEvents;
+  if (breakdown && !e->mk_trace) {
+    int rc = dev_alloc(e, &e->mk_trace, trace_n);
+    if (rc) return rc;
+    XPU_TRY_CUDA(cudaMallocHost(&e->h_trace, trace_n * 8));
+  }
   const int32_t base = e->tokens_so_far;
   memcpy(e->h_tokens + base, tokens, (size_t)n * 4);
+  double upload_ms = 0.0;
+  const auto t_submit = clk::now();
   for (int32_t t = 0; t < n; ++t) {
+    const auto tu = clk::now();
     XPU_TRY_CUDA(cudaMemcpyAsync(e->d_token, e->h_tokens + base + t, 4, cudaMemcpyHostToDevice, e->stream));
-    XPU_TRY_CUDA(cudaGraphLaunch(e->exec, e->stream));
+    upload_ms += ms_since(tu);
+    int rc;
+    if (breakdown && t == n - 1) {
+      XPU_TRY_CUDA(cudaMemsetAsync(e->mk_trace, 0, trace_n * 8, e->stream));
+      e->trace_valid = true;
+      MkParams p = e->mk;
+      p.trace = e->mk_trace;
+      rc = mk_launch(p, e->mk_smem, e->mk_grid, e->stream);
+    } else {
+      rc = launch_step(e);
+    }
+    if (rc) return rc;
   }
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  const double submit_ms = ms_since(t_submit);
+  const auto t_read = clk::now();
   if (logits)
     XPU_TRY_CUDA(cudaMemcpyAsync(e->h_logits, e->logits, (size_t)e->c.vocab_size * 4, cudaMemcpyDeviceToHost, e->stream));
   XPU_TRY_CUDA(cudaMemcpyAsync(&e->h_misc[1], e->d_next, 4, cudaMemcpyDeviceToHost, e->stream));
+  if (breakdown)
+    XPU_TRY_CUDA(cudaMemcpyAsync(e->h_trace, e->mk_trace, trace_n * 8, cudaMemcpyDeviceToHost, e->stream));
   XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
-  int rc = check_device_error();
+  const double read_ms = ms_since(t_read);
+  int rc = finish_steps(e);
   if (rc) return rc;
   e->tokens_so_far = base + n;
   if (logits) memcpy(logits, e->h_logits, (size_t)e->c.vocab_size * 4);
   if (argmax) *argmax = e->h_misc[1];
+  if (prof) {
+    prof->upload_ms = upload_ms;
+    prof->upload_bytes = 4 * (int64_t)n;
+    prof->submit_to_done_ms = submit_ms;
+    prof->readback_ms = read_ms;
+    prof->gpu_timestamps_supported = breakdown ? 1 : 0;
+    prof->n_entries = 0;
+    if (breakdown) fill_profile_entries(e, prof);
+    prof->total_ms = ms_since(t_start);
+  }
+  return XPU_OK;
+}
+
+int xpu_llama_profile_trace(const xpu_llama* e, uint64_t* out, int64_t cap, int64_t* n, int32_t* grid,
+                            int32_t* events) {
+  XPU_REQUIRE(e && n && grid && events, XPU_EINVAL, "xpu_llama_profile_trace: null pointer");
+  XPU_REQUIRE(e->trace_valid && e->h_trace, XPU_ESTATE,
+              "xpu_llama_profile_trace: no profiled persistent step yet (forward with want_gpu_breakdown)");
+  const int64_t total = (int64_t)(5 * e->c.num_layers + 1) * e->mk_grid * kMkTraceEvents;
+  *n = total;
+  *grid = e->mk_grid;
+  *events = kMkTraceEvents;
+  if (out) memcpy(out, e->h_trace, (size_t)std::min(total, std::max<int64_t>(cap, 0)) * 8);
   return XPU_OK;
 }
 
@@ -510,7 +778,8 @@ int xpu_llama_decode_dev(xpu_llama* e, const int32_t* token_dev, int32_t* next_d
   XPU_TRY_CUDA(cudaSetDevice(e->device));
   if (token_dev != e->d_token)
     XPU_TRY_CUDA(cudaMemcpyAsync(e->d_token, token_dev, 4, cudaMemcpyDeviceToDevice, e->stream));
-  XPU_TRY_CUDA(cudaGraphLaunch(e->exec, e->stream));
+  int rc = launch_step(e);
+  if (rc) return rc;
   if (next_dev) XPU_TRY_CUDA(cudaMemcpyAsync(next_dev, e->d_next, 4, cudaMemcpyDeviceToDevice, e->stream));
   e->tokens_so_far += 1;
   return XPU_OK;
@@ -526,11 +795,14 @@ int xpu_llama_greedy_steps(xpu_llama* e, int32_t first_token, int32_t steps, int
   const int32_t base = e->tokens_so_far;
   e->h_tokens[base] = first_token;
   XPU_TRY_CUDA(cudaMemcpyAsync(e->d_token, e->h_tokens + base, 4, cudaMemcpyHostToDevice, e->stream));
-  for (int32_t s = 0; s < steps; ++s) XPU_TRY_CUDA(cudaGraphLaunch(e->exec, e->stream));
+  for (int32_t s = 0; s < steps; ++s) {
+    int rc = launch_step(e);
+    if (rc) return rc;
+  }
   if (tokens_out && steps > 0)
     XPU_TRY_CUDA(cudaMemcpyAsync(tokens_out, e->d_gen + base, (size_t)steps * 4, cudaMemcpyDeviceToHost, e->stream));
   XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
-  int rc = check_device_error();
+  int rc = finish_steps(e);
   if (rc) return rc;
   e->tokens_so_far = base + steps;
   return XPU_OK;
@@ -552,8 +824,9 @@ int xpu_llama_reset(xpu_llama* e) {
   XPU_REQUIRE(e, XPU_EINVAL, "xpu_llama_reset: null engine");
   XPU_TRY_CUDA(cudaSetDevice(e->device));
   XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
-  int rc = set_device_pos(e, 0);
+  int rc = rearm_counters(e);
   if (rc) return rc;
+  if ((rc = set_device_pos(e, 0))) return rc;
   e->tokens_so_far = 0;
   return XPU_OK;
 }
@@ -593,6 +866,24 @@ int xpu_llama_poison_kv(xpu_llama* e, float value) {
     XPU_TRY_CUDA(cudaMemcpy(L.kcache, buf.data(), n * 4, cudaMemcpyHostToDevice));
     XPU_TRY_CUDA(cudaMemcpy(L.vcache, buf.data(), n * 4, cudaMemcpyHostToDevice));
   }
+  return XPU_OK;
+}
+
+int xpu_llama_set_decode_path(xpu_llama* e, int32_t path) {
+  XPU_REQUIRE(e, XPU_EINVAL, "xpu_llama_set_decode_path: null engine");
+  XPU_REQUIRE(path == XPU_DECODE_GRAPH || path == XPU_DECODE_PERSISTENT, XPU_EINVAL,
+              "xpu_llama_set_decode_path: unknown path %d", path);
+  XPU_REQUIRE(path != XPU_DECODE_PERSISTENT || e->mk_ok, XPU_EINVAL,
+              "xpu_llama_set_decode_path: the persistent step does not apply to this engine's shapes");
+  XPU_TRY_CUDA(cudaSetDevice(e->device));
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  e->path = path;
+  return XPU_OK;
+}
+
+int xpu_llama_decode_path(const xpu_llama* e, int32_t* path) {
+  XPU_REQUIRE(e && path, XPU_EINVAL, "xpu_llama_decode_path: null pointer");
+  *path = e->path;
   return XPU_OK;
 }
 

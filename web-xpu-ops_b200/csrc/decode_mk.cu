@@ -1,0 +1,949 @@
+// decode_mk.cu — the persistent decode step (see decode_mk.cuh).
+//
+// Shares: GEMV phase rows are split over the CTAs in contiguous, balanced
+// ranges (whole row pairs for QKV, where RoPE rotates adjacent rows); CTA b
+// keeps the same share in every step.  A share is streamed as "pieces" of
+// at most one stage each (rows of the weight, then the same rows of the up
+// weight for FFN).
+//
+// Consumers, per GEMV phase:
+//  1. stage the input vector in shared memory (the embedding row for layer
+//     0), normalised by rmsnorm when the phase has a gain;
+//  2. load their 16-column slices of it into registers: warps form rg row
+//     groups of wpg warps, a group's threads own the columns of a row (cpt
+//     slices each), and group g takes rows g, g + rg, ... of every piece;
+//  3. for each piece: dot products over the stage, release it to the
+//     producer, reduce across the warp and park one partial per (warp of
+//     the group, share row) in shared memory;
+//  4. finish every share row (sum of the group's partials) with the phase's
+//     epilogue — the same arithmetic as the per-kernel path.
+// Attention: item (kv head, split) per CTA; splits write un-normalised
+// partials and the last CTA of a kv head (atomic ticket) merges them.
+// Grid barriers: a monotonically increasing arrival counter, zeroed by the
+// last CTA at the end of the step; every wait is bounded (a timeout sets
+// the device error word and the CTA finishes the step without waiting).
+#include <math.h>
+
+#include <algorithm>
+
+#include "decode_mk.cuh"
+#include "matvec_kernels.cuh"
+#include "matvec_launch.cuh"
+
+namespace xpu {
+namespace {
+
+constexpr int kMkSlots = 32;                 // pieces in flight at most
+constexpr uint32_t kMkPieceBytes = 32768;    // largest piece (one or two bulk copies)
+constexpr int kNct = 32 * kMkConsumerWarps;  // consumer threads
+// Attention's P.V reduction parks up to kNct * 8 floats in the partial area.
+constexpr int kMkRedMinFloats = kNct * 8;
+// float4 slots of the input vector each consumer thread stages per phase.
+constexpr int kMkVec = 4;
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Share of CTA b: units [u0, u1) of n over G CTAs.
+__host__ __device__ __forceinline__ void mk_share(int64_t n, int b, int G, int64_t& u0, int64_t& u1) {
+  u0 = n * b / G;
+  u1 = n * (b + 1) / G;
+}
+
+__host__ __device__ __forceinline__ int mk_granule(int epi) { return epi == EPI_QKV ? 2 : 1; }
+
+// Row pitch (in float4) of the staged input vector: >= U and = 2 mod 8, so
+// that 8 consecutive threads storing quarters e = 0..3 of two slots hit 8
+// different 16-byte bank groups.
+__host__ __device__ __forceinline__ int mk_xs_pitch(int U) { return U + ((10 - U % 8) % 8); }
+
+// Index into p.gemv of phase i (QKV, O, FFN, DOWN per layer, then HEAD);
+// -1 for attention.
+__device__ __forceinline__ int mk_gemv_index(int i, int layers) {
+  if (i >= 5 * layers) return 4 * layers;
+  const int l = i / 5, k = i % 5;
+  if (k == 1) return -1;
+  return 4 * l + (k == 0 ? 0 : k - 1);
+}
+
+// Profile timestamps (see MkParams::trace): mk_mark by thread 0 of the CTA,
+// mk_mark_any by the calling thread (the producer).
+__device__ __forceinline__ void mk_mark_any(const MkParams& p, int phase, int e) {
+  if (p.trace) p.trace[((size_t)phase * gridDim.x + blockIdx.x) * kMkTraceEvents + e] = global_timer_ns();
+}
+__device__ __forceinline__ void mk_mark(const MkParams& p, int phase, int e) {
+  if (threadIdx.x == 0) mk_mark_any(p, phase, e);
+}
+
+// Waits on an mbarrier unless the step was aborted; a timeout aborts it.
+__device__ __forceinline__ void mk_wait(uint64_t* bar, uint32_t parity, unsigned int* err, volatile int* abort_flag) {
+  if (*abort_flag) return;
+  if (!mbar_wait(bar, parity, err)) *abort_flag = 1;
+}
+
+// Grid barrier among the consumers of all CTAs: arrival `target / G`.
+__device__ __forceinline__ void mk_grid_sync(const MkParams& p, int prev_phase, unsigned long long target,
+                                             volatile int* abort_flag) {
+  unsigned long long* bar = p.bar;
+  unsigned int* err = p.err;
+  named_bar_sync(1, kNct);
+  mk_mark(p, prev_phase, 3);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(bar, 1ull);
+    if (!*abort_flag) {
+      const uint64_t t0 = global_timer_ns();
+      unsigned int n = 0;
+      while (ld_acquire_u64(bar) < target) {
+        if ((++n & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(err, 1u);
+          *abort_flag = 1;
+          break;
+        }
+      }
+      __threadfence();
+    }
+  }
+  named_bar_sync(1, kNct);
+}
+
+// ------------------------------------------------------------- producer --
+// Shared-memory ring: a circular byte buffer of p.ring_bytes; piece g (the
+// g-th issued, over the whole step) uses mbarrier slot g % kMkSlots and
+// starts at slot_off[slot].  Pieces are placed back to back (a piece that
+// would pass the end starts again at offset 0) and released by consumers in
+// any order; the producer reclaims space oldest-first.
+__device__ __forceinline__ void mk_wait_sleepy(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                               volatile int* abort_flag) {
+  if (*abort_flag || mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    __nanosleep(128);  // the producer waits off the consumers' issue slots
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(err, 1u);
+      *abort_flag = 1;
+      return;
+    }
+  }
+}
+
+// Attention item `it` (kv head g, position split sp) of a step whose query
+// sits at position L - 1: positions [j0, j1).
+struct MkItem {
+  int g, sp, j0, j1;
+};
+__device__ __forceinline__ MkItem mk_item(const MkParams& p, int it, int L) {
+  const int nsp = p.nsplit, chunk = (L + nsp - 1) / nsp;
+  MkItem m;
+  m.g = it / nsp;
+  m.sp = it - m.g * nsp;
+  m.j0 = min(L, m.sp * chunk);
+  m.j1 = min(L, m.j0 + chunk);
+  return m;
+}
+
+__device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                            uint32_t* slot_off, uint32_t* slot_len, volatile int* abort_flag) {
+  const int G = gridDim.x, b = blockIdx.x;
+  const int n_phase = 5 * p.layers + 1;
+  const uint32_t ring = p.ring_bytes;
+  const uint64_t policy = evict_first_policy();
+  const int pos = __ldcg(p.pos), L = pos + 1, hd = p.head_dim;
+  uint32_t head = 0;
+  int64_t issued = 0, oldest = 0;  // pieces [oldest, issued) may still be in use
+  // Places a piece of B bytes: waits (oldest first) until no piece in use
+  // overlaps it and a slot is free; returns its slot, or -1 on abort.
+  auto place = [&](uint32_t B, uint32_t& off) -> int {
+    off = head + B > ring ? 0u : head;
+    for (;;) {
+      bool blocked = issued - oldest >= kMkSlots;
+      for (int64_t k = oldest; k < issued && !blocked; ++k) {
+        const uint32_t so = slot_off[k % kMkSlots], sl = slot_len[k % kMkSlots];
+        blocked = so < off + B && off < so + sl;
+      }
+      if (!blocked || *abort_flag) break;
+      mk_wait_sleepy(&empty[oldest % kMkSlots], (uint32_t)((oldest / kMkSlots) & 1), p.err, abort_flag);
+      ++oldest;
+    }
+    if (*abort_flag) return -1;
+    const int slot = (int)(issued % kMkSlots);
+    slot_off[slot] = off;
+    slot_len[slot] = B;
+    ++issued;
+    head = off + B;
+    return slot;
+  };
+  for (int i = 0; i < n_phase && !*abort_flag; ++i) {
+    const int gi = mk_gemv_index(i, p.layers);
+    if (gi < 0) {
+      // Attention: the CTA's K and V rows of each item, positions before
+      // `pos` (the row at `pos` is written during this step, the consumers
+      // read it from the cache themselves).
+      const MkAttn* a = p.attn + i / 5;
+      for (int it = b; it < p.kvH * p.nsplit && !*abort_flag; it += G) {
+        const MkItem m = mk_item(p, it, L);
+        const int nn = m.j1 - m.j0;
+        if (nn == 0) continue;
+        const int jc = m.j1 < pos ? m.j1 : pos;
+        const uint32_t rb = 4u * hd, bytes = (uint32_t)(jc - m.j0) * rb;
+        uint32_t off;
+        const int slot = place(2u * nn * rb, off);
+        if (slot < 0) break;
+        uint8_t* dst = smem + p.off_ring + off;
+        mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+        if (bytes) {
+          const int64_t row = (int64_t)m.g * p.max_seq + m.j0;
+          bulk_g2s_plain(dst, a->kcache + row * hd, bytes, &full[slot]);
+          bulk_g2s_plain(dst + (size_t)nn * rb, a->vcache + row * hd, bytes, &full[slot]);
+        }
+      }
+      continue;
+    }
+    const MkGemv* g = p.gemv + gi;
+    const int gr = mk_granule(g->epi), P = g->piece_rows, ns = g->ns;
+    const int64_t W = g->W;
+    int64_t u0, u1;
+    mk_share(g->N / gr, b, G, u0, u1);
+    const int64_t r0 = u0 * gr, n = (u1 - u0) * gr;
+    const uint32_t row_bytes = (uint32_t)(4 * W);
+    for (int64_t base = 0; base < n && !*abort_flag; base += P) {
+      const int rows = (int)(n - base < P ? n - base : P);
+      const uint32_t bytes = (uint32_t)rows * row_bytes;
+      uint32_t off;
+      const int slot = place(bytes * ns, off);
+      if (slot < 0) break;
+      if (base == 0) mk_mark_any(p, i, 6);
+      uint8_t* dst = smem + p.off_ring + off;
+      mbar_arrive_expect_tx(&full[slot], bytes * ns);  // releases slot_off to the consumers
+      bulk_g2s(dst, g->w + (r0 + base) * W, bytes, &full[slot], policy);
+      if (ns == 2) bulk_g2s(dst + bytes, g->w2 + (r0 + base) * W, bytes, &full[slot], policy);
+      if (base + P >= n) mk_mark_any(p, i, 7);
+    }
+  }
+  // Every issued copy lands before the CTA exits.
+  for (int64_t k = (issued > kMkSlots ? issued - kMkSlots : 0); k < issued; ++k)
+    mbar_wait(&full[k % kMkSlots], (uint32_t)((k / kMkSlots) & 1), p.err);
+}
+
+// --------------------------------------------------------- GEMV phase --
+// One row's partial dot product over the thread's CPT column slices: all
+// slice loads first (a slice past the row end is clamped to the last slice,
+// whose x registers are zero there, so it adds exactly 0), then the math.
+template <int CPT>
+__device__ __forceinline__ void mk_row_dots(const uint8_t* rowp, const f2 (&xr)[4][8], f2 (&acc)[2], int ti, int gt,
+                                            int U) {
+  uint4 wv[CPT];
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = min(ti + j * gt, U - 1);
+    wv[j] = *reinterpret_cast<const uint4*>(rowp + 16 * (size_t)c);
+  }
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) dot16(wv[j], xr[j], acc);
+}
+
+// Returns, for the HEAD phase, the thread's first maximal logit of its rows.
+__device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, const MkGemv* g, uint8_t* smem,
+                                              uint64_t* full, uint64_t* empty, const uint32_t* slot_off,
+                                              int64_t& pbase, volatile int* abort_flag, int tok, int pos,
+                                              double* red_d, float& best, int& best_i) {
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int G = gridDim.x, b = blockIdx.x;
+  const int K = g->K, U = g->U, epi = g->epi, ns = g->ns, wpg = g->wpg, rg = g->rg, cpt = g->cpt;
+  const int P = g->piece_rows, RS = p.red_stride;
+  const int64_t W = g->W;
+  const uint32_t row_bytes = (uint32_t)(4 * W);
+  float* red = reinterpret_cast<float*>(smem + p.off_red);
+  float* xs = reinterpret_cast<float*>(smem + p.off_xs);
+  const int gr = mk_granule(epi);
+  int64_t u0, u1;
+  mk_share(g->N / gr, b, G, u0, u1);
+  const int64_t r0 = u0 * gr;
+  const int n = (int)((u1 - u0) * gr);
+
+  // 1. Input vector -> xs[0, 16U) (zero past K).  A thread issues all its
+  // loads (x and the rmsnorm gain, kMkVec float4 slots each) before using
+  // any, so staging costs one memory round trip.
+  const bool embed = g->embed != 0;
+  const float* gam = g->gamma;
+  const int nv = 4 * U;  // float4 slots of xs
+  float4 xv[kMkVec], gv[kMkVec];
+  if (embed) {
+    // gatherDequantRows (llm/weights-q8.ts:207-222): out-of-range ids give zeros.
+    const bool tok_ok = tok >= 0 && tok < p.vocab;
+    const double escale = tok_ok ? (double)p.embed_scale[tok] : 0.0;
+    int64_t e0, e1;
+    mk_share(K, b, G, e0, e1);
+#pragma unroll
+    for (int i = 0; i < kMkVec; ++i) {
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+      const int v = tid + i * kNct;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int k = 4 * v + e;
+        if (v < nv && k < K) {
+          t[e] = tok_ok ? (float)((double)p.embed_codes[(int64_t)tok * K + k] * escale) : 0.0f;
+          if (k >= e0 && k < e1) p.hidden0[k] = t[e];
+        }
+      }
+      xv[i] = make_float4(t[0], t[1], t[2], t[3]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kMkVec; ++i) {
+      const int v = tid + i * kNct, k = 4 * v;
+      xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (v < nv) {
+        if (k + 4 <= K) {
+          xv[i] = __ldcg(reinterpret_cast<const float4*>(g->x + k));
+        } else {
+          float t[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) t[e] = k + e < K ? __ldcg(g->x + k + e) : 0.0f;
+          xv[i] = make_float4(t[0], t[1], t[2], t[3]);
+        }
+      }
+    }
+  }
+  if (gam) {
+#pragma unroll
+    for (int i = 0; i < kMkVec; ++i) {
+      const int v = tid + i * kNct, k = 4 * v;
+      gv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (v < nv) {
+        if (k + 4 <= K) {
+          gv[i] = __ldg(reinterpret_cast<const float4*>(gam + k));
+        } else {
+          float t[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) t[e] = k + e < K ? __ldg(gam + k + e) : 0.0f;
+          gv[i] = make_float4(t[0], t[1], t[2], t[3]);
+        }
+      }
+    }
+    // ops/rmsnorm/reference.ts:80-96: scale = 1/sqrt(mean(x^2) + eps) in f64,
+    // out = f32(x * scale * gain).
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < kMkVec; ++i)
+      ss += (double)xv[i].x * xv[i].x + (double)xv[i].y * xv[i].y + (double)xv[i].z * xv[i].z +
+            (double)xv[i].w * xv[i].w;
+    const double sw = warp_sum_d(ss);
+    if (lane == 0) red_d[warp] = sw;
+    named_bar_sync(1, kNct);
+    double tot = 0.0;
+    for (int w = 0; w < kMkConsumerWarps; ++w) tot += red_d[w];
+    const double scale = 1.0 / sqrt(tot / (double)K + p.eps);
+#pragma unroll
+    for (int i = 0; i < kMkVec; ++i) {
+      xv[i].x = (float)((double)xv[i].x * scale * (double)gv[i].x);
+      xv[i].y = (float)((double)xv[i].y * scale * (double)gv[i].y);
+      xv[i].z = (float)((double)xv[i].z * scale * (double)gv[i].z);
+      xv[i].w = (float)((double)xv[i].w * scale * (double)gv[i].w);
+    }
+  }
+  // xs holds float4 (slot c, quarter e) = x[16c + 4e .. 16c + 4e + 3] at
+  // index e * UP + c (UP = mk_xs_pitch(U)): the register loads below read
+  // consecutive float4s across a warp and these stores spread over all
+  // bank groups, so neither side has bank conflicts.
+  const int UP = mk_xs_pitch(U);
+#pragma unroll
+  for (int i = 0; i < kMkVec; ++i) {
+    const int v = tid + i * kNct;
+    if (v < nv) reinterpret_cast<float4*>(xs)[(v & 3) * UP + (v >> 2)] = xv[i];
+  }
+  named_bar_sync(1, kNct);
+  mk_mark(p, phase, 1);
+
+  // Epilogue operands that do not depend on this phase's sums, loaded now so
+  // their latency hides behind the dot products: a thread finishes outputs
+  // tid, tid + kNct, ... and prefetches those of its first two.
+  const int outs = epi == EPI_QKV ? n / 2 : n;
+  float pa[2], pb[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int t = tid + q * kNct;
+    pa[q] = pb[q] = 0.0f;
+    if (t < outs) {
+      if (epi == EPI_QKV) {
+        pa[q] = g->s[r0 + 2 * t];
+        pb[q] = g->s[r0 + 2 * t + 1];
+      } else {
+        pa[q] = g->s[r0 + t];
+        if (epi == EPI_FFN) pb[q] = g->s2[r0 + t];
+        if (epi == EPI_RESID) pb[q] = __ldcg(g->residual + r0 + t);
+      }
+    }
+  }
+
+  // 2. The thread's column slices in registers.
+  const int group = warp / wpg, wi = warp - group * wpg, ti = wi * 32 + lane, gt = wpg * 32;
+  const bool active = group < rg;
+  f2 xr[4][8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = ti + j * gt;
+    const bool has = j < cpt && c < U;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float4 t = has ? reinterpret_cast<const float4*>(xs)[e * UP + c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      xr[j][2 * e] = make_f2(t.x, t.y);
+      xr[j][2 * e + 1] = make_f2(t.z, t.w);
+    }
+  }
+
+  // 3. Pieces of the share, in the producer's order: piece q holds rows
+  // [q P, q P + rows) of each stream; row r of the piece (stream 0 rows,
+  // then stream 1 rows) belongs to row group r % rg.
+  const f2 zero2 = make_f2(0.0f, 0.0f);
+  const int npieces = (n + P - 1) / P;
+  unsigned long long waited = 0, first_ready = 0;
+  for (int q = 0; q < npieces; ++q) {
+    const int64_t gidx = pbase + q;
+    const int slot = (int)(gidx % kMkSlots);
+    const uint32_t par = (uint32_t)((gidx / kMkSlots) & 1);
+    if (p.trace && tid == 0) {
+      const unsigned long long w0 = global_timer_ns();
+      mk_wait(&full[slot], par, p.err, abort_flag);
+      const unsigned long long w1 = global_timer_ns();
+      if (q == 0) first_ready = w1;
+      waited += w1 - w0;
+    } else {
+      mk_wait(&full[slot], par, p.err, abort_flag);
+    }
+    const int rows = n - q * P < P ? n - q * P : P;
+    const int R = ns * rows;
+    const uint8_t* st = smem + p.off_ring + slot_off[slot];
+    f2 acc[kMkRowsPerWarp][2];
+#pragma unroll
+    for (int t = 0; t < kMkRowsPerWarp; ++t) {
+      acc[t][0] = acc[t][1] = zero2;
+      const int r = group + rg * t;
+      if (active && r < R) {
+        const uint8_t* rowp = st + (size_t)r * row_bytes;
+        switch (cpt) {
+          case 1: mk_row_dots<1>(rowp, xr, acc[t], ti, gt, U); break;
+          case 2: mk_row_dots<2>(rowp, xr, acc[t], ti, gt, U); break;
+          case 3: mk_row_dots<3>(rowp, xr, acc[t], ti, gt, U); break;
+          default: mk_row_dots<4>(rowp, xr, acc[t], ti, gt, U); break;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    float v[kMkRowsPerWarp];
+#pragma unroll
+    for (int t = 0; t < kMkRowsPerWarp; ++t) v[t] = hsum2(acc[t]);
+    const float tot = warp_reduce_rows<kMkRowsPerWarp>(v, lane);
+    const int t = lane / (32 / kMkRowsPerWarp), r = group + rg * t;
+    if (active && lane % (32 / kMkRowsPerWarp) == 0 && r < R) {
+      const int stream = r / rows, local = r - stream * rows;
+      red[wi * RS + stream * n + q * P + local] = tot;
+    }
+  }
+  pbase += npieces;
+  if (p.trace && tid == 0) {
+    if (npieces > 0) p.trace[((size_t)phase * G + b) * kMkTraceEvents + 4] = first_ready;
+    p.trace[((size_t)phase * G + b) * kMkTraceEvents + 5] = waited;
+  }
+  named_bar_sync(1, kNct);
+  mk_mark(p, phase, 2);
+
+  // 4. Epilogue over the share rows (ops/matvec/reference.ts:117-131,
+  // :196-207, :235-242; RoPE and the KV write as the per-kernel path).
+  auto sum = [&](int r) {
+    float v = 0.0f;
+    for (int w = 0; w < wpg; ++w) v += red[w * RS + r];
+    return v;
+  };
+  if (epi == EPI_QKV) {
+    const int64_t qk_end = (int64_t)p.q_rows + p.kv_rows;
+    for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
+      const int64_t row = r0 + 2 * t;
+      const float sa = q < 2 ? (q == 0 ? pa[0] : pa[1]) : g->s[row];
+      const float sb = q < 2 ? (q == 0 ? pb[0] : pb[1]) : g->s[row + 1];
+      float a = __fmul_rn(sum(2 * t), sa);
+      float c = __fmul_rn(sum(2 * t + 1), sb);
+      if (row < qk_end) {
+        // RoPE on the adjacent pair (ops/rope/reference.ts:379-401), f64.
+        const int64_t local = row < p.q_rows ? row : row - p.q_rows;
+        const int pair = (int)((local % p.head_dim) / 2);
+        const double theta = (double)pos * p.inv_freq[pair];
+        double sn, cs;
+        sincos(theta, &sn, &cs);
+        const double x0 = a, x1 = c;
+        a = (float)(x0 * cs - x1 * sn);
+        c = (float)(x0 * sn + x1 * cs);
+      }
+      if (row < p.q_rows) {
+        g->y[row] = a;
+        g->y[row + 1] = c;
+      } else {
+        // KV cache slot `pos` (llm/engine-q8-resident.ts:1848-1851).
+        const bool is_k = row < qk_end;
+        const int64_t local = is_k ? row - p.q_rows : row - qk_end;
+        const int64_t h = local / p.head_dim, d = local % p.head_dim;
+        float* dst = (is_k ? g->kcache : g->vcache) + ((h * p.max_seq + pos) * p.head_dim + d);
+        dst[0] = a;
+        dst[1] = c;
+      }
+    }
+  } else if (epi == EPI_FFN) {
+    for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
+      const int64_t row = r0 + t;
+      const float sg = q < 2 ? (q == 0 ? pa[0] : pa[1]) : g->s[row];
+      const float su = q < 2 ? (q == 0 ? pb[0] : pb[1]) : g->s2[row];
+      const float gt_ = __fmul_rn(sum(t), sg);
+      const float up = __fmul_rn(sum(n + t), su);
+      g->y[row] = __fmul_rn(silu_f32(gt_), up);
+    }
+  } else if (epi == EPI_RESID) {
+    for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
+      const int64_t row = r0 + t;
+      const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : g->s[row];
+      const float res = q < 2 ? (q == 0 ? pb[0] : pb[1]) : __ldcg(g->residual + row);
+      g->y[row] = __fadd_rn(res, __fmul_rn(sum(t), sc));
+    }
+  } else {
+    constexpr int kNone = 0x7fffffff;
+    for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
+      const int64_t row = r0 + t;
+      const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : g->s[row];
+      const float v = __fmul_rn(sum(t), sc);
+      g->y[row] = v;
+      if (v == v && (best_i == kNone || v > best)) {  // ascending rows: ties keep the first
+        best = v;
+        best_i = (int)row;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------- attention phase --
+// Scores of one item for GT query heads per kv head (GT a power of two):
+// a warp takes PPI = 32 / GT positions at a time, each lane forms the 32
+// partial dot products (positions x heads) over its head_dim slice, and one
+// transpose reduction leaves lane l with (position l / GT, head l % GT).
+template <int GT>
+__device__ __forceinline__ void mk_scores(const float* q_s, const float* k_s, float* p_s, int nn, int hd, int cm,
+                                          float scale, int warp, int lane) {
+  constexpr int PPI = 32 / GT;
+  for (int jb = warp * PPI; jb < nn; jb += kMkConsumerWarps * PPI) {
+    float v[32];
+#pragma unroll
+    for (int pp = 0; pp < PPI; ++pp) {
+      const int j = jb + pp;
+      float kv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) kv[i] = (j < nn && lane + 32 * i < hd) ? k_s[j * hd + lane + 32 * i] : 0.0f;
+#pragma unroll
+      for (int h = 0; h < GT; ++h) {
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (lane + 32 * i < hd) d = fmaf(q_s[h * hd + lane + 32 * i], kv[i], d);
+        v[pp * GT + h] = d;
+      }
+    }
+    const float tot = warp_reduce_rows<32>(v, lane);
+    const int pp = lane / GT, h = lane % GT;
+    if (jb + pp < nn) p_s[h * cm + jb + pp] = tot * scale;
+  }
+}
+// Any head count: one warp reduction per (position, head).
+__device__ __forceinline__ void mk_scores_any(const float* q_s, const float* k_s, float* p_s, int Gq, int nn, int hd,
+                                              int cm, float scale, int warp, int lane) {
+  for (int j = warp; j < nn; j += kMkConsumerWarps) {
+    float kv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) kv[i] = lane + 32 * i < hd ? k_s[j * hd + lane + 32 * i] : 0.0f;
+    for (int h = 0; h < Gq; ++h) {
+      float d = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (lane + 32 * i < hd) d = fmaf(q_s[h * hd + lane + 32 * i], kv[i], d);
+      d = warp_sum(d);
+      if (lane == 0) p_s[h * cm + j] = d * scale;
+    }
+  }
+}
+
+constexpr int kMkMergeBatch = 40;  // split partials one thread loads per round trip
+
+// ops/gqa/reference.ts:203-303 for one decode query (sEff = pos + 1): item
+// (kv head g, split sp) scans positions [j0, j1) for the Gq heads of g, with
+// K and V rows streamed into the ring by the producer.
+__device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, const MkAttn* a, uint8_t* smem,
+                                              uint64_t* full, uint64_t* empty, const uint32_t* slot_off,
+                                              int64_t& pbase, volatile int* abort_flag, int pos, int* flag_s) {
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int G = gridDim.x, b = blockIdx.x;
+  const int Gq = p.H / p.kvH, hd = p.head_dim, nsp = p.nsplit, cm = p.cmax;
+  float* red = reinterpret_cast<float*>(smem + p.off_red);
+  float* q_s = reinterpret_cast<float*>(smem + p.off_xs);  // [Gq][hd]
+  float* p_s = q_s + Gq * hd;                               // [Gq][cm]
+  float* stat = p_s + Gq * cm;                              // [Gq][2]
+  const int L = pos + 1;
+  const int items = p.kvH * nsp;
+  mk_mark(p, phase, 1);  // CTAs without an item keep these
+  mk_mark(p, phase, 2);
+  for (int it = b; it < items; it += G) {
+    const MkItem m = mk_item(p, it, L);
+    const int g = m.g, sp = m.sp, j0 = m.j0, nn = m.j1 - m.j0;
+    for (int i = tid; i < Gq * hd; i += kNct) q_s[i] = __ldcg(a->q + (int64_t)g * Gq * hd + i);
+    const float* k_s = nullptr;
+    const float* v_s = nullptr;
+    int slot = -1;
+    if (nn > 0) {
+      const int64_t gidx = pbase++;
+      slot = (int)(gidx % kMkSlots);
+      mk_wait(&full[slot], (uint32_t)((gidx / kMkSlots) & 1), p.err, abort_flag);
+      float* kv = reinterpret_cast<float*>(smem + p.off_ring + slot_off[slot]);
+      k_s = kv;
+      v_s = kv + nn * hd;
+      if (pos >= j0 && pos < m.j1) {  // this step's row, written by the QKV phase
+        const int64_t row = ((int64_t)g * p.max_seq + pos) * hd;
+        for (int i = tid; i < hd; i += kNct) {
+          kv[(pos - j0) * hd + i] = __ldcg(a->kcache + row + i);
+          kv[(nn + pos - j0) * hd + i] = __ldcg(a->vcache + row + i);
+        }
+      }
+    }
+    named_bar_sync(1, kNct);
+    mk_mark(p, phase, 1);
+    switch (Gq) {
+      case 1: mk_scores<1>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
+      case 2: mk_scores<2>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
+      case 4: mk_scores<4>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
+      case 8: mk_scores<8>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
+      case 16: mk_scores<16>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
+      default: mk_scores_any(q_s, k_s, p_s, Gq, nn, hd, cm, p.attn_scale, warp, lane); break;
+    }
+    named_bar_sync(1, kNct);
+    // Max and sum of exp per head over this split.
+    for (int h = warp; h < Gq; h += kMkConsumerWarps) {
+      float mx = -INFINITY;
+      for (int j = lane; j < nn; j += 32) mx = fmaxf(mx, p_s[h * cm + j]);
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float l = 0.0f;
+      for (int j = lane; j < nn; j += 32) {
+        const float e = expf(p_s[h * cm + j] - mx);
+        p_s[h * cm + j] = e;
+        l += e;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        stat[2 * h] = mx;
+        stat[2 * h + 1] = l;
+      }
+    }
+    named_bar_sync(1, kNct);
+    // P.V: thread (jg, c) reads V[j][c] for j = jg, jg + jgN, ... and
+    // accumulates up to 8 heads; the jgN partials are added in order.
+    const int jgN = kNct / hd, c = tid % hd, jg = tid / hd;
+    for (int hb = 0; hb < Gq; hb += 8) {
+      const int hn = min(8, Gq - hb);
+      if (jg < jgN) {
+        float acc[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) acc[h] = 0.0f;
+        for (int j = jg; j < nn; j += jgN) {
+          const float v = v_s[j * hd + c];
+#pragma unroll
+          for (int h = 0; h < 8; ++h)
+            if (h < hn) acc[h] = fmaf(p_s[(hb + h) * cm + j], v, acc[h]);
+        }
+#pragma unroll
+        for (int h = 0; h < 8; ++h)
+          if (h < hn) red[(jg * 8 + h) * hd + c] = acc[h];
+      }
+      named_bar_sync(1, kNct);
+      for (int o = tid; o < hn * hd; o += kNct) {
+        const int h = o / hd, cc = o - h * hd;
+        float sacc = 0.0f;
+        for (int jj = 0; jj < jgN; ++jj) sacc += red[(jj * 8 + h) * hd + cc];
+        p.part_acc[((int64_t)(g * Gq + hb + h) * nsp + sp) * hd + cc] = sacc;
+      }
+      named_bar_sync(1, kNct);
+    }
+    if (slot >= 0 && lane == 0) mbar_arrive(&empty[slot]);  // K and V rows consumed
+    if (tid < Gq) {
+      const int hh = g * Gq + tid;
+      p.part_m[hh * nsp + sp] = nn > 0 ? stat[2 * tid] : -INFINITY;
+      p.part_l[hh * nsp + sp] = nn > 0 ? stat[2 * tid + 1] : 0.0f;
+    }
+    __threadfence();
+    named_bar_sync(1, kNct);
+    mk_mark(p, phase, 2);
+    if (tid == 0) *flag_s = atomicAdd(&p.attn_counter[g], 1u) == (unsigned)(nsp - 1);
+    named_bar_sync(1, kNct);
+    if (*flag_s) {
+      __threadfence();
+      // Merge: out = sum_s w[h][s] acc_s with w[h][s] = exp(m_s - M) /
+      // sum_s' l_s' exp(m_s' - M).  Each pass, a thread first issues the
+      // loads of its output's partials (kMkMergeBatch at a time), then the
+      // weights are formed while they are in flight.
+      float* wts = red;  // [Gq][nsp]
+      const int nout = Gq * hd;
+      for (int o0 = 0; o0 < nout; o0 += kNct) {
+        const int o = o0 + tid, h = o / hd, cc = o - h * hd;
+        const float* src = p.part_acc + (int64_t)(g * Gq + h) * nsp * hd + cc;
+        float av[kMkMergeBatch];
+#pragma unroll
+        for (int u = 0; u < kMkMergeBatch; ++u)
+          av[u] = (o < nout && u < nsp) ? __ldcg(src + (int64_t)u * hd) : 0.0f;
+        if (o0 == 0) {
+          for (int hh = warp; hh < Gq; hh += kMkConsumerWarps) {
+            const int head = g * Gq + hh;
+            float mv[8], lv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int sidx = lane + 32 * u;
+              mv[u] = sidx < nsp ? __ldcg(&p.part_m[head * nsp + sidx]) : -INFINITY;
+              lv[u] = sidx < nsp ? __ldcg(&p.part_l[head * nsp + sidx]) : 0.0f;
+            }
+            float M = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) M = fmaxf(M, mv[u]);
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            float l = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const float w = mv[u] == -INFINITY ? 0.0f : expf(mv[u] - M);
+              mv[u] = w;
+              l = fmaf(lv[u], w, l);
+            }
+            l = warp_sum(l);
+            const float inv = 1.0f / l;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              if (lane + 32 * u < nsp) wts[hh * nsp + lane + 32 * u] = mv[u] * inv;
+          }
+          named_bar_sync(1, kNct);
+        }
+        if (o < nout) {
+          const float* w = wts + h * nsp;
+          float o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int u = 0; u < kMkMergeBatch; ++u)
+            if (u < nsp) o4[u & 3] = fmaf(w[u], av[u], o4[u & 3]);
+          for (int s0 = kMkMergeBatch; s0 < nsp; ++s0) o4[s0 & 3] = fmaf(w[s0], __ldcg(src + (int64_t)s0 * hd), o4[s0 & 3]);
+          a->out[(int64_t)(g * Gq + h) * hd + cc] = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+        }
+      }
+      if (tid == 0) p.attn_counter[g] = 0;
+    }
+    named_bar_sync(1, kNct);
+  }
+}
+
+// ------------------------------------------------------------- kernel --
+__global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(MkParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kMkSlots];
+  __shared__ __align__(8) uint64_t empty[kMkSlots];
+  __shared__ uint32_t slot_off[kMkSlots];
+  __shared__ uint32_t slot_len[kMkSlots];
+  __shared__ double red_d[kMkConsumerWarps];
+  __shared__ float bv[kMkConsumerWarps];
+  __shared__ int bi[kMkConsumerWarps];
+  __shared__ int flag_s;
+  __shared__ volatile int abort_flag;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int G = gridDim.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < kMkSlots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kMkConsumerWarps);  // every consumer warp releases every piece
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kMkConsumerWarps) {
+    if (lane == 0) mk_producer(p, smem, full, empty, slot_off, slot_len, &abort_flag);
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int tok = __ldcg(p.token);
+  const int pos = __ldcg(p.pos);
+  const int n_phase = 5 * p.layers + 1;
+  int64_t pbase = 0;  // pieces issued before the current phase
+  unsigned long long target = 0;
+  constexpr int kNone = 0x7fffffff;
+  float best = -INFINITY;
+  int best_i = kNone;
+  for (int i = 0; i < n_phase; ++i) {
+    if (i > 0) {
+      target += (unsigned long long)G;
+      mk_grid_sync(p, i - 1, target, &abort_flag);
+    }
+    mk_mark(p, i, 0);
+    const int gi = mk_gemv_index(i, p.layers);
+    if (gi < 0)
+      mk_attn_phase(p, i, p.attn + i / 5, smem, full, empty, slot_off, pbase, &abort_flag, pos, &flag_s);
+    else
+      mk_gemv_phase(p, i, p.gemv + gi, smem, full, empty, slot_off, pbase, &abort_flag, tok, pos, red_d, best,
+                    best_i);
+  }
+
+  // Greedy argmax (llm/engine.ts:226-232): per-CTA candidate of its
+  // contiguous logit rows, then the last CTA picks the first maximal index.
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    if (ov > best || (ov == best && oi < best_i)) {
+      best = ov;
+      best_i = oi;
+    }
+  }
+  if (lane == 0) {
+    bv[warp] = best;
+    bi[warp] = best_i;
+  }
+  named_bar_sync(1, kNct);
+  mk_mark(p, n_phase - 1, 3);
+  if (tid == 0) {
+    for (int w = 1; w < kMkConsumerWarps; ++w)
+      if (bv[w] > best || (bv[w] == best && bi[w] < best_i)) {
+        best = bv[w];
+        best_i = bi[w];
+      }
+    p.cand_v[blockIdx.x] = best;
+    p.cand_i[blockIdx.x] = best_i;
+    __threadfence();
+    flag_s = atomicAdd(p.ticket, 1u) == (unsigned)(G - 1);
+  }
+  named_bar_sync(1, kNct);
+  if (!flag_s || warp != 0) return;
+  __threadfence();
+  best = -INFINITY;
+  best_i = kNone;
+  for (int c = lane; c < G; c += 32) {  // ascending CTAs hold ascending rows
+    const float v = __ldcg(p.cand_v + c);
+    const int ix = __ldcg(p.cand_i + c);
+    if (ix != kNone && (best_i == kNone || v > best)) {
+      best = v;
+      best_i = ix;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    if (ov > best || (ov == best && oi < best_i)) {
+      best = ov;
+      best_i = oi;
+    }
+  }
+  if (lane == 0) {
+    // A NaN at index 0 wins (nothing compares greater); all-NaN gives 0.
+    const float x0 = __ldcg(p.logits);
+    int idx = best_i;
+    if (idx == kNone || x0 != x0) idx = 0;
+    if (pos >= 0 && pos < p.max_seq) p.gen[pos] = idx;
+    *p.next = idx;
+    *p.token = idx;
+    *p.pos = pos + 1;
+    // Every CTA has passed its last barrier: re-arm the counters.
+    *p.bar = 0ull;
+    *p.ticket = 0u;
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ host --
+int mk_configure(MkParams& p, MkGemv* gh, int n_gemv, int kmax, size_t* smem_bytes, int* grid) {
+  const DeviceInfo& di = device_info();
+  int dev = 0, coop = 0;
+  XPU_TRY_CUDA(cudaGetDevice(&dev));
+  XPU_TRY_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+  XPU_REQUIRE(coop, XPU_EINVAL, "persistent decode: the device has no cooperative launch");
+  const int G = di.sm_count;
+  XPU_REQUIRE(p.head_dim <= 128, XPU_EINVAL, "persistent decode: head_dim %d > 128", p.head_dim);
+  int64_t red_stride = 0, piece_max = 0;
+  int max_wpg = 1;
+  int64_t max_u = 0;
+  for (int i = 0; i < n_gemv; ++i) {
+    MkGemv& g = gh[i];
+    g.W = (g.K + 3) / 4;
+    XPU_REQUIRE(g.W % 4 == 0, XPU_EINVAL, "persistent decode: rows of %d codes are not whole 16-byte slots", g.K);
+    g.U = g.W / 4;
+    g.ns = g.epi == EPI_FFN ? 2 : 1;
+    int wpg = 1;
+    while (wpg < kMkConsumerWarps && (g.U + 32 * wpg - 1) / (32 * wpg) > 4) ++wpg;
+    g.wpg = wpg;
+    g.cpt = (g.U + 32 * wpg - 1) / (32 * wpg);
+    XPU_REQUIRE(g.cpt <= 4 && 4 * g.U <= kMkVec * kNct, XPU_EINVAL, "persistent decode: K=%d too long", g.K);
+    g.rg = kMkConsumerWarps / wpg;
+    const int64_t row_bytes = 4 * (int64_t)g.W;
+    const int gr = mk_granule(g.epi);
+    const int64_t share_max = ((g.N / gr) + G - 1) / G * gr;
+    // Rows per piece (per stream): as many as fit kMkPieceBytes, at most
+    // kMkRowsPerWarp rows for every row group.
+    g.piece_rows = (int)std::min<int64_t>((int64_t)kMkPieceBytes / (g.ns * row_bytes),
+                                          (int64_t)g.rg * kMkRowsPerWarp / g.ns);
+    XPU_REQUIRE(g.piece_rows >= 1, XPU_EINVAL, "persistent decode: a row of K=%d does not fit a piece", g.K);
+    piece_max = std::max<int64_t>(piece_max, (int64_t)g.ns * g.piece_rows * row_bytes);
+    red_stride = std::max<int64_t>(red_stride, g.ns * share_max);
+    max_wpg = std::max(max_wpg, wpg);
+    max_u = std::max<int64_t>(max_u, g.U);
+    XPU_REQUIRE((int64_t)g.N % gr == 0, XPU_EINVAL, "persistent decode: QKV rows must pair");
+  }
+  // Attention: one item per CTA (kv head, split) where the heads allow.
+  const int Gq = p.H / p.kvH;
+  p.nsplit = std::max(1, G / p.kvH);
+  p.cmax = (p.max_seq + p.nsplit - 1) / p.nsplit;
+  const int64_t red_floats = std::max<int64_t>({(int64_t)kMkRedMinFloats, red_stride * max_wpg,
+                                                (int64_t)Gq * p.nsplit});
+  const int64_t xs_floats = std::max<int64_t>({16 * (int64_t)mk_xs_pitch((int)max_u), (int64_t)kmax,
+                                               (int64_t)Gq * p.head_dim + (int64_t)Gq * p.cmax + 2 * Gq});
+  auto up = [](size_t a) { return (a + 127) / 128 * 128; };
+  p.red_stride = (int)red_stride;
+  p.off_red = 0;
+  p.off_xs = (uint32_t)up(p.off_red + 4 * (size_t)red_floats);
+  p.off_ring = (uint32_t)up(p.off_xs + 4 * (size_t)xs_floats);
+  cudaFuncAttributes fa{};
+  XPU_TRY_CUDA(cudaFuncGetAttributes(&fa, decode_mk_kernel));
+  const size_t static_smem = fa.sharedSizeBytes;
+  const int64_t avail = ((int64_t)di.max_smem_optin - (int64_t)static_smem - (int64_t)p.off_ring) / 128 * 128;
+  const int64_t kv_piece = 2 * (int64_t)p.cmax * p.head_dim * 4;
+  XPU_REQUIRE(p.head_dim % 4 == 0, XPU_EINVAL, "persistent decode: head_dim %d is not a multiple of 4", p.head_dim);
+  XPU_REQUIRE(Gq * p.nsplit <= red_floats && p.nsplit <= 256, XPU_EINVAL, "persistent decode: too many splits");
+  XPU_REQUIRE(avail >= 3 * kv_piece, XPU_EINVAL,
+              "persistent decode: %lld positions per split do not fit the ring", (long long)p.cmax);
+  XPU_REQUIRE(avail >= 4 * piece_max, XPU_EINVAL,
+              "persistent decode: shared memory too small (%lld bytes of ring for %lld-byte pieces)",
+              (long long)avail, (long long)piece_max);
+  p.ring_bytes = (uint32_t)avail;
+  *smem_bytes = p.off_ring + (size_t)avail;
+  XPU_TRY_CUDA(ensure_smem_attr((const void*)decode_mk_kernel, *smem_bytes));
+  int per_sm = 0;
+  XPU_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mk_kernel, kMkThreads, *smem_bytes));
+  XPU_REQUIRE(per_sm >= 1, XPU_EINVAL, "persistent decode: the kernel does not fit on an SM");
+  *grid = G;
+  return XPU_OK;
+}
+
+int mk_launch(const MkParams& p, size_t smem_bytes, int grid, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kMkThreads);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  XPU_TRY_CUDA(cudaLaunchKernelEx(&cfg, decode_mk_kernel, p));
+  return XPU_OK;
+}
+
+}  // namespace xpu

@@ -1,0 +1,109 @@
+// decode_mk.cuh — the persistent decode step: one cooperative launch per
+// token runs the whole of llm/engine-q8-resident.ts `runDecodeStep`
+// (:1774-1892) on every SM at once.
+//
+// Each CTA (one per SM) holds a fixed share of the rows of every GEMV of the
+// step.  One producer thread per CTA streams its shares of all the step's
+// weights, phase after phase, through a ring of shared-memory stages with
+// cp.async.bulk; it never waits for the activations, so while the consumer
+// warps sit at a grid barrier the next phases' weights are already arriving.
+// Consumer warps run the phases in order:
+//   per layer  QKV  (rmsnorm prologue, RoPE + KV-cache write epilogue)
+//              ATTN (position splits over the CTAs, last-arriving CTA merges)
+//              O    (residual epilogue)
+//              FFN  (rmsnorm prologue, SiLU-gated epilogue)
+//              DOWN (residual epilogue)
+//   HEAD       lm_head (rmsnorm prologue) and the greedy argmax
+// with one grid barrier between consecutive phases (each reads a vector the
+// previous one wrote in full).
+#pragma once
+
+#include "common.cuh"
+
+namespace xpu {
+
+// One GEMV phase: rows [0, N) of `w` (and of `w2`, the up weight, for FFN)
+// times the phase's input vector.
+struct MkGemv {
+  const uint32_t* w;
+  const uint32_t* w2;
+  const float* s;
+  const float* s2;
+  const float* x;         // input vector (ignored when `embed` is set)
+  const float* gamma;     // rmsnorm gain, or null
+  const float* residual;  // residual epilogue
+  float* y;
+  float* kcache;  // QKV: the layer's caches
+  float* vcache;
+  int N, K, W, U;  // rows, columns, words per row, 16-byte slots per row
+  int epi;         // Epi (matvec_kernels.cuh)
+  int ns;          // weight streams (2 for FFN)
+  int wpg, rg, cpt;  // warps per row group, row groups, slots per thread
+  int piece_rows;    // rows per stream of one piece (one ring allocation)
+  int embed;         // x is the current token's embedding row
+};
+
+struct MkAttn {
+  const float* q;
+  const float* kcache;
+  const float* vcache;
+  float* out;
+};
+
+struct MkParams {
+  const MkGemv* gemv;  // [4 * layers + 1]: per layer QKV, O, FFN, DOWN; then HEAD
+  const MkAttn* attn;  // [layers]
+  int layers;
+  // embedding (layer 0 input) and its copy into the residual stream
+  const int8_t* embed_codes;
+  const float* embed_scale;
+  int vocab, hidden;
+  float* hidden0;  // the residual stream the embedding row is written to
+  double eps;
+  // RoPE / attention
+  const double* inv_freq;
+  int q_rows, kv_rows, head_dim, max_seq, H, kvH, nsplit, cmax;
+  float attn_scale;
+  float* part_m;
+  float* part_l;
+  float* part_acc;
+  unsigned int* attn_counter;  // [kvH], zero between steps
+  // step state
+  int32_t* token;
+  int32_t* pos;
+  int32_t* next;
+  int32_t* gen;
+  const float* logits;
+  // grid synchronisation, zero between steps
+  unsigned long long* bar;
+  unsigned int* ticket;
+  float* cand_v;  // [grid] per-CTA argmax candidates
+  int* cand_i;
+  unsigned int* err;
+  // Optional profile: when non-null, CTA b writes %globaltimer at
+  // trace[(phase * grid + b) * kMkTraceEvents + e]: thread 0 at e = 0 phase
+  // start (after the grid barrier), 1 input staged, 2 dot products done
+  // (all warps), 3 epilogue done, 4 its first weight stage ready, 5 the
+  // total ns it waited for weight stages in the phase; the producer at 6 / 7
+  // when it issued the phase's first / last stage.  The buffer is zeroed
+  // before a profiled step; events that did not happen stay 0.
+  unsigned long long* trace;
+  // shared-memory geometry
+  uint32_t ring_bytes;
+  uint32_t off_red, off_xs, off_ring;
+  int red_stride;  // floats per warp slot of the partial-sum area
+};
+
+constexpr int kMkConsumerWarps = 15;  // + 1 producer warp = 512 threads: 128 registers each
+constexpr int kMkThreads = 32 * (kMkConsumerWarps + 1);
+constexpr int kMkRowsPerWarp = 2;  // rows a row group takes from one piece
+constexpr int kMkTraceEvents = 8;
+
+// Decides whether the persistent step applies to this engine's shapes and
+// fills the geometry fields of `p` and of each MkGemv; XPU_OK, or XPU_EINVAL
+// with the reason (the caller then keeps the per-kernel graph).
+int mk_configure(MkParams& p, MkGemv* gemv_host, int n_gemv, int kmax, size_t* smem_bytes, int* grid);
+// One cooperative launch of the step on `stream`.
+int mk_launch(const MkParams& p, size_t smem_bytes, int grid, cudaStream_t stream);
+
+}  // namespace xpu

@@ -11,8 +11,8 @@ Public names mirror the reference's TypeScript exports:
 - llm/engine: argmax, greedyGenerate
 """
 from ._lib import XpuError, XpuInvalidArgument, XpuRangeError, XpuStateError, device_count
-from .llama import (LLAMA_1B_DECODE_CONFIG, SARASHINA_2_2_1B_CONFIG, TINY_FIXTURE_CONFIG, LlamaConfig,
-                    LlamaEngineQ8Resident, LlamaLayerWeightsQ8, LlamaWeightsQ8, QuantizedLinear, argmax,
+from .llama import (LLAMA_1B_DECODE_CONFIG, SARASHINA_2_2_1B_CONFIG, TINY_FIXTURE_CONFIG, ForwardProfile,
+                    LlamaConfig, LlamaEngineQ8Resident, createForwardProfile, LlamaLayerWeightsQ8, LlamaWeightsQ8, QuantizedLinear, argmax,
                     assertWeightShapesQ8, greedyGenerate)
 from .ops import (DeviceBuffer, matvecQ8, matvecQ8_dev, matvecQ8Ffn, matvecQ8Ffn_dev, matvecQ8Residual,
                   matvecQ8Residual_dev, packInt8Rows, packQ8, quantize, quantizePackQ8)

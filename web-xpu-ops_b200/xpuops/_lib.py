@@ -82,6 +82,23 @@ class LlamaWeightsC(C.Structure):
     ]
 
 
+class ProfileEntryC(C.Structure):
+    """include/xpuops.h `xpu_profile_entry`."""
+
+    _fields_ = [("label", C.c_char * 24), ("seconds", C.c_double), ("wait_s", C.c_double),
+                ("input_s", C.c_double), ("compute_s", C.c_double), ("epilogue_s", C.c_double)]
+
+
+class ForwardProfileC(C.Structure):
+    """include/xpuops.h `xpu_forward_profile`."""
+
+    _fields_ = [
+        ("want_gpu_breakdown", I32), ("gpu_timestamps_supported", I32), ("upload_ms", C.c_double),
+        ("upload_bytes", I64), ("submit_to_done_ms", C.c_double), ("readback_ms", C.c_double),
+        ("total_ms", C.c_double), ("entries", C.POINTER(ProfileEntryC)), ("entries_cap", I32), ("n_entries", I32),
+    ]
+
+
 # name -> (argtypes); every function returns int (status) unless listed in _RESTYPE.
 SIGNATURES = {
     "xpu_last_error": [],
@@ -114,6 +131,8 @@ SIGNATURES = {
     "xpu_gqa_decode_noalloc": [P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P],
     "xpu_llama_create": [C.POINTER(LlamaConfigC), C.POINTER(LlamaWeightsC), C.c_int, C.POINTER(P)],
     "xpu_llama_forward": [P, P, I32, P, P],
+    "xpu_llama_forward_profiled": [P, P, I32, P, P, C.POINTER(ForwardProfileC)],
+    "xpu_llama_profile_trace": [P, P, I64, C.POINTER(I64), C.POINTER(I32), C.POINTER(I32)],
     "xpu_llama_decode_dev": [P, P, P],
     "xpu_llama_greedy_steps": [P, I32, I32, P],
     "xpu_llama_logits_dev": [P, C.POINTER(P)],
@@ -122,6 +141,8 @@ SIGNATURES = {
     "xpu_llama_position": [P, C.POINTER(I32)],
     "xpu_llama_set_kv": [P, I32, P, P, I32],
     "xpu_llama_poison_kv": [P, C.c_float],
+    "xpu_llama_set_decode_path": [P, I32],
+    "xpu_llama_decode_path": [P, C.POINTER(I32)],
     "xpu_llama_destroy": [P],
 }
 _RESTYPE = {"xpu_last_error": C.c_char_p}

@@ -17,7 +17,8 @@ from typing import List, Optional
 
 import numpy as np
 
-from ._lib import (LlamaConfigC, LlamaLayerC, LlamaWeightsC, Q8LinearC, XpuInvalidArgument, check, lib,
+from ._lib import (ForwardProfileC, LlamaConfigC, LlamaLayerC, LlamaWeightsC, ProfileEntryC, Q8LinearC,
+                   XpuInvalidArgument, check, lib,
                    require_device)
 
 
@@ -175,14 +176,34 @@ class LlamaEngineQ8Resident:
             raise RuntimeError("LlamaEngineQ8Resident: engine is closed")
         return self._h
 
-    def forward(self, tokens) -> List[np.ndarray]:
-        """llm/engine-q8-resident.ts:1276-1283: ``[logits]`` of the last position."""
+    def forward(self, tokens, profile: Optional["ForwardProfile"] = None) -> List[np.ndarray]:
+        """llm/engine-q8-resident.ts:1276-1283: ``[logits]`` of the last position.
+        With ``profile`` (``createForwardProfile()``), its fields are filled as
+        the reference's ``forward(tokens, profile)`` does."""
         t = np.ascontiguousarray(tokens, dtype=np.int32)
         if t.size == 0:
             raise XpuInvalidArgument(1, "LlamaEngineQ8Resident.forward: tokens must be non-empty")
         logits = np.zeros(self.config.vocabSize, np.float32)
-        check(lib().xpu_llama_forward(self._handle(), t.ctypes.data_as(C.c_void_p), t.size,
-                                      logits.ctypes.data_as(C.c_void_p), None))
+        if profile is None:
+            check(lib().xpu_llama_forward(self._handle(), t.ctypes.data_as(C.c_void_p), t.size,
+                                          logits.ctypes.data_as(C.c_void_p), None))
+            return [logits]
+        cap = 5 * self.config.numLayers + 1
+        entries = (ProfileEntryC * cap)()
+        pc = ForwardProfileC(want_gpu_breakdown=int(bool(profile.wantGpuBreakdown)), entries=entries,
+                             entries_cap=cap)
+        check(lib().xpu_llama_forward_profiled(self._handle(), t.ctypes.data_as(C.c_void_p), t.size,
+                                               logits.ctypes.data_as(C.c_void_p), None, C.byref(pc)))
+        profile.uploadMs = pc.upload_ms
+        profile.uploadBytes = int(pc.upload_bytes)
+        profile.submitToDoneMs = pc.submit_to_done_ms
+        profile.readbackMs = pc.readback_ms
+        profile.totalMs = pc.total_ms
+        profile.gpuTimestampsSupported = bool(pc.gpu_timestamps_supported)
+        profile.gpuEntries = [
+            {"label": e.label.decode(), "seconds": e.seconds, "waitSeconds": e.wait_s, "inputSeconds": e.input_s,
+             "computeSeconds": e.compute_s, "epilogueSeconds": e.epilogue_s}
+            for e in entries[: pc.n_entries]]
         return [logits]
 
     def forward_argmax(self, tokens) -> int:
@@ -225,6 +246,32 @@ class LlamaEngineQ8Resident:
         """llm/engine-q8-resident.ts:1043-1050."""
         check(lib().xpu_llama_poison_kv(self._handle(), float(value)))
 
+    def profileTrace(self) -> np.ndarray:
+        """Raw device timestamps of the last profiled persistent step,
+        shaped [phases, CTAs, events] (include/xpuops.h xpu_llama_profile_trace)."""
+        n, g, ev = C.c_int64(0), C.c_int32(0), C.c_int32(0)
+        check(lib().xpu_llama_profile_trace(self._handle(), None, 0, C.byref(n), C.byref(g), C.byref(ev)))
+        out = np.zeros(n.value, np.uint64)
+        check(lib().xpu_llama_profile_trace(self._handle(), out.ctypes.data_as(C.c_void_p), n.value, C.byref(n),
+                                            C.byref(g), C.byref(ev)))
+        return out.reshape(-1, g.value, ev.value)
+
+    # Decode-step paths (include/xpuops.h XPU_DECODE_*); no reference counterpart.
+    DECODE_GRAPH = 0
+    DECODE_PERSISTENT = 1
+
+    @property
+    def decodePath(self) -> int:
+        """The decode-step path in use: DECODE_GRAPH or DECODE_PERSISTENT."""
+        p = C.c_int32(0)
+        check(lib().xpu_llama_decode_path(self._handle(), C.byref(p)))
+        return int(p.value)
+
+    def setDecodePath(self, path: int) -> None:
+        """Selects the decode-step path; XpuError (EINVAL) when the persistent
+        step does not apply to this engine's shapes."""
+        check(lib().xpu_llama_set_decode_path(self._handle(), int(path)))
+
     def stream(self) -> int:
         s = C.c_void_p()
         check(lib().xpu_llama_stream(self._handle(), C.byref(s)))
@@ -246,6 +293,29 @@ class LlamaEngineQ8Resident:
             self.close()
         except Exception:
             pass
+
+
+@dataclass
+class ForwardProfile:
+    """llm/engine-q8-resident.ts:33-152 `ForwardProfile`: `wantGpuBreakdown`
+    is the caller's input; the rest is written by ``forward(tokens, profile)``.
+    ``gpuEntries`` are the device-timed phases of the call's last step
+    (persistent decode path), each with the mean barrier wait / input /
+    compute / epilogue split over the CTAs."""
+
+    wantGpuBreakdown: bool = False
+    uploadMs: float = 0.0
+    uploadBytes: int = 0
+    submitToDoneMs: Optional[float] = None
+    readbackMs: Optional[float] = None
+    gpuEntries: list = field(default_factory=list)
+    gpuTimestampsSupported: bool = False
+    totalMs: float = 0.0
+
+
+def createForwardProfile() -> ForwardProfile:
+    """llm/engine-q8-resident.ts `createForwardProfile()`."""
+    return ForwardProfile()
 
 
 def argmax(logits) -> int:
