@@ -34,7 +34,7 @@ namespace xpu {
 namespace {
 
 constexpr int kMkSlots = 32;                 // pieces in flight at most
-constexpr uint32_t kMkPieceBytes = 32768;    // largest piece (one or two bulk copies)
+constexpr uint32_t kMkPieceBytes = 65536;    // largest piece (one or two bulk copies)
 constexpr int kNct = 32 * kMkConsumerWarps;  // consumer threads
 // Attention's P.V reduction parks up to kNct * 8 floats in the partial area.
 constexpr int kMkRedMinFloats = kNct * 8;
@@ -92,8 +92,9 @@ __device__ __forceinline__ void mk_grid_sync(const MkParams& p, int prev_phase, 
   named_bar_sync(1, kNct);
   mk_mark(p, prev_phase, 3);
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(bar, 1ull);
+    // Release: the CTA's writes (ordered before this thread by the named
+    // barrier) become visible to every CTA that acquires the count.
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(bar), "l"(1ull) : "memory");
     if (!*abort_flag) {
       const uint64_t t0 = global_timer_ns();
       unsigned int n = 0;
@@ -104,7 +105,6 @@ __device__ __forceinline__ void mk_grid_sync(const MkParams& p, int prev_phase, 
           break;
         }
       }
-      __threadfence();
     }
   }
   named_bar_sync(1, kNct);
@@ -229,30 +229,14 @@ __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, ui
 }
 
 // --------------------------------------------------------- GEMV phase --
-// One row's partial dot product over the thread's CPT column slices: all
-// slice loads first (a slice past the row end is clamped to the last slice,
-// whose x registers are zero there, so it adds exactly 0), then the math.
-template <int CPT>
-__device__ __forceinline__ void mk_row_dots(const uint8_t* rowp, const f2 (&xr)[4][8], f2 (&acc)[2], int ti, int gt,
-                                            int U) {
-  uint4 wv[CPT];
-#pragma unroll
-  for (int j = 0; j < CPT; ++j) {
-    const int c = min(ti + j * gt, U - 1);
-    wv[j] = *reinterpret_cast<const uint4*>(rowp + 16 * (size_t)c);
-  }
-#pragma unroll
-  for (int j = 0; j < CPT; ++j) dot16(wv[j], xr[j], acc);
-}
-
 // Returns, for the HEAD phase, the thread's first maximal logit of its rows.
 __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, const MkGemv* g, uint8_t* smem,
                                               uint64_t* full, uint64_t* empty, const uint32_t* slot_off,
                                               int64_t& pbase, volatile int* abort_flag, int tok, int pos,
-                                              double* red_d, float& best, int& best_i) {
+                                              double* red_d, const double* rope, float& best, int& best_i) {
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int G = gridDim.x, b = blockIdx.x;
-  const int K = g->K, U = g->U, epi = g->epi, ns = g->ns, wpg = g->wpg, rg = g->rg, cpt = g->cpt;
+  const int K = g->K, U = g->U, epi = g->epi, ns = g->ns, wpg = g->wpg, rg = g->rg;
   const int P = g->piece_rows, RS = p.red_stride;
   const int64_t W = g->W;
   const uint32_t row_bytes = (uint32_t)(4 * W);
@@ -379,20 +363,18 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
     }
   }
 
-  // 2. The thread's column slices in registers.
-  const int group = warp / wpg, wi = warp - group * wpg, ti = wi * 32 + lane, gt = wpg * 32;
+  // 2. The thread's 16-column slice in registers: a row group of wpg warps
+  // covers a row (thread ti of the group owns slice ti), and group g takes
+  // rows g, g + rg, ... of every piece.
+  const int group = warp / wpg, wi = warp - group * wpg, ti = wi * 32 + lane;
   const bool active = group < rg;
-  f2 xr[4][8];
+  const int cs = ti < U ? ti : U - 1;  // slice read (clamped; x is 0 past U)
+  f2 xr[8];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int c = ti + j * gt;
-    const bool has = j < cpt && c < U;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float4 t = has ? reinterpret_cast<const float4*>(xs)[e * UP + c] : make_float4(0.f, 0.f, 0.f, 0.f);
-      xr[j][2 * e] = make_f2(t.x, t.y);
-      xr[j][2 * e + 1] = make_f2(t.z, t.w);
-    }
+  for (int e = 0; e < 4; ++e) {
+    const float4 t = ti < U ? reinterpret_cast<const float4*>(xs)[e * UP + ti] : make_float4(0.f, 0.f, 0.f, 0.f);
+    xr[2 * e] = make_f2(t.x, t.y);
+    xr[2 * e + 1] = make_f2(t.z, t.w);
   }
 
   // 3. Pieces of the share, in the producer's order: piece q holds rows
@@ -417,20 +399,20 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
     const int rows = n - q * P < P ? n - q * P : P;
     const int R = ns * rows;
     const uint8_t* st = smem + p.off_ring + slot_off[slot];
+    // All of the warp's slice loads first, then the math: kMkRowsPerWarp
+    // independent rows.
+    uint4 wv[kMkRowsPerWarp];
+#pragma unroll
+    for (int t = 0; t < kMkRowsPerWarp; ++t) {
+      const int r = group + rg * t;
+      wv[t] = (active && r < R) ? *reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * (size_t)cs)
+                                : make_uint4(0u, 0u, 0u, 0u);
+    }
     f2 acc[kMkRowsPerWarp][2];
 #pragma unroll
     for (int t = 0; t < kMkRowsPerWarp; ++t) {
       acc[t][0] = acc[t][1] = zero2;
-      const int r = group + rg * t;
-      if (active && r < R) {
-        const uint8_t* rowp = st + (size_t)r * row_bytes;
-        switch (cpt) {
-          case 1: mk_row_dots<1>(rowp, xr, acc[t], ti, gt, U); break;
-          case 2: mk_row_dots<2>(rowp, xr, acc[t], ti, gt, U); break;
-          case 3: mk_row_dots<3>(rowp, xr, acc[t], ti, gt, U); break;
-          default: mk_row_dots<4>(rowp, xr, acc[t], ti, gt, U); break;
-        }
-      }
+      dot16(wv[t], xr, acc[t]);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
@@ -468,12 +450,11 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
       float a = __fmul_rn(sum(2 * t), sa);
       float c = __fmul_rn(sum(2 * t + 1), sb);
       if (row < qk_end) {
-        // RoPE on the adjacent pair (ops/rope/reference.ts:379-401), f64.
+        // RoPE on the adjacent pair (ops/rope/reference.ts:379-401), f64,
+        // with the step's cos/sin table.
         const int64_t local = row < p.q_rows ? row : row - p.q_rows;
         const int pair = (int)((local % p.head_dim) / 2);
-        const double theta = (double)pos * p.inv_freq[pair];
-        double sn, cs;
-        sincos(theta, &sn, &cs);
+        const double sn = rope[2 * pair], cs = rope[2 * pair + 1];
         const double x0 = a, x1 = c;
         a = (float)(x0 * cs - x1 * sn);
         c = (float)(x0 * sn + x1 * cs);
@@ -675,26 +656,35 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, cons
       p.part_m[hh * nsp + sp] = nn > 0 ? stat[2 * tid] : -INFINITY;
       p.part_l[hh * nsp + sp] = nn > 0 ? stat[2 * tid + 1] : 0.0f;
     }
-    __threadfence();
     named_bar_sync(1, kNct);
     mk_mark(p, phase, 2);
-    if (tid == 0) *flag_s = atomicAdd(&p.attn_counter[g], 1u) == (unsigned)(nsp - 1);
+    if (tid == 0) {
+      // Acquire-release ticket: publishes this split's partials and, for the
+      // last split, makes every other split's visible to this CTA.
+      unsigned int old;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.attn_counter + g) : "memory");
+      *flag_s = old == (unsigned)(nsp - 1);
+    }
     named_bar_sync(1, kNct);
     if (*flag_s) {
-      __threadfence();
       // Merge: out = sum_s w[h][s] acc_s with w[h][s] = exp(m_s - M) /
-      // sum_s' l_s' exp(m_s' - M).  Each pass, a thread first issues the
-      // loads of its output's partials (kMkMergeBatch at a time), then the
-      // weights are formed while they are in flight.
+      // sum_s' l_s' exp(m_s' - M).  A thread takes outputs tid and
+      // tid + kNct and issues the loads of both outputs' partials
+      // (kMkMergeBatch each) before the weights are formed, so the merge
+      // costs one round trip when nsplit <= kMkMergeBatch.
       float* wts = red;  // [Gq][nsp]
       const int nout = Gq * hd;
-      for (int o0 = 0; o0 < nout; o0 += kNct) {
-        const int o = o0 + tid, h = o / hd, cc = o - h * hd;
-        const float* src = p.part_acc + (int64_t)(g * Gq + h) * nsp * hd + cc;
-        float av[kMkMergeBatch];
+      for (int o0 = 0; o0 < nout; o0 += 2 * kNct) {
+        const int oa = o0 + tid, ob = oa + kNct;
+        const int ha = oa / hd, ca = oa - ha * hd, hb_ = ob / hd, cb = ob - hb_ * hd;
+        const float* srca = p.part_acc + (int64_t)(g * Gq + ha) * nsp * hd + ca;
+        const float* srcb = p.part_acc + (int64_t)(g * Gq + hb_) * nsp * hd + cb;
+        float av[kMkMergeBatch], bv[kMkMergeBatch];
 #pragma unroll
-        for (int u = 0; u < kMkMergeBatch; ++u)
-          av[u] = (o < nout && u < nsp) ? __ldcg(src + (int64_t)u * hd) : 0.0f;
+        for (int u = 0; u < kMkMergeBatch; ++u) {
+          av[u] = (oa < nout && u < nsp) ? __ldcg(srca + (int64_t)u * hd) : 0.0f;
+          bv[u] = (ob < nout && u < nsp) ? __ldcg(srcb + (int64_t)u * hd) : 0.0f;
+        }
         if (o0 == 0) {
           for (int hh = warp; hh < Gq; hh += kMkConsumerWarps) {
             const int head = g * Gq + hh;
@@ -724,15 +714,19 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, cons
           }
           named_bar_sync(1, kNct);
         }
-        if (o < nout) {
+        auto finish = [&](int o, int h, int cc, const float* src, const float (&v)[kMkMergeBatch]) {
+          if (o >= nout) return;
           const float* w = wts + h * nsp;
           float o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
           for (int u = 0; u < kMkMergeBatch; ++u)
-            if (u < nsp) o4[u & 3] = fmaf(w[u], av[u], o4[u & 3]);
-          for (int s0 = kMkMergeBatch; s0 < nsp; ++s0) o4[s0 & 3] = fmaf(w[s0], __ldcg(src + (int64_t)s0 * hd), o4[s0 & 3]);
+            if (u < nsp) o4[u & 3] = fmaf(w[u], v[u], o4[u & 3]);
+          for (int s0 = kMkMergeBatch; s0 < nsp; ++s0)
+            o4[s0 & 3] = fmaf(w[s0], __ldcg(src + (int64_t)s0 * hd), o4[s0 & 3]);
           a->out[(int64_t)(g * Gq + h) * hd + cc] = (o4[0] + o4[1]) + (o4[2] + o4[3]);
-        }
+        };
+        finish(oa, ha, ca, srca, av);
+        finish(ob, hb_, cb, srcb, bv);
       }
       if (tid == 0) p.attn_counter[g] = 0;
     }
@@ -748,6 +742,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(MkParams p) {
   __shared__ uint32_t slot_off[kMkSlots];
   __shared__ uint32_t slot_len[kMkSlots];
   __shared__ double red_d[kMkConsumerWarps];
+  __shared__ double rope[128];  // (sin, cos) per RoPE pair, head_dim <= 128
   __shared__ float bv[kMkConsumerWarps];
   __shared__ int bi[kMkConsumerWarps];
   __shared__ int flag_s;
@@ -773,6 +768,14 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(MkParams p) {
   // ---------------- consumers ----------------
   const int tok = __ldcg(p.token);
   const int pos = __ldcg(p.pos);
+  // RoPE angles of this step's position (ops/rope/reference.ts:226-244,
+  // :379-401): sin and cos of pos * invFreq[i] in f64, once per CTA.
+  for (int i = tid; i < p.head_dim / 2; i += kNct) {
+    double sn, cs;
+    sincos((double)pos * p.inv_freq[i], &sn, &cs);
+    rope[2 * i] = sn;
+    rope[2 * i + 1] = cs;
+  }
   const int n_phase = 5 * p.layers + 1;
   int64_t pbase = 0;  // pieces issued before the current phase
   unsigned long long target = 0;
@@ -789,8 +792,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(MkParams p) {
     if (gi < 0)
       mk_attn_phase(p, i, p.attn + i / 5, smem, full, empty, slot_off, pbase, &abort_flag, pos, &flag_s);
     else
-      mk_gemv_phase(p, i, p.gemv + gi, smem, full, empty, slot_off, pbase, &abort_flag, tok, pos, red_d, best,
-                    best_i);
+      mk_gemv_phase(p, i, p.gemv + gi, smem, full, empty, slot_off, pbase, &abort_flag, tok, pos, red_d, rope,
+                    best, best_i);
   }
 
   // Greedy argmax (llm/engine.ts:226-232): per-CTA candidate of its
@@ -876,11 +879,11 @@ int mk_configure(MkParams& p, MkGemv* gh, int n_gemv, int kmax, size_t* smem_byt
     XPU_REQUIRE(g.W % 4 == 0, XPU_EINVAL, "persistent decode: rows of %d codes are not whole 16-byte slots", g.K);
     g.U = g.W / 4;
     g.ns = g.epi == EPI_FFN ? 2 : 1;
-    int wpg = 1;
-    while (wpg < kMkConsumerWarps && (g.U + 32 * wpg - 1) / (32 * wpg) > 4) ++wpg;
+    const int wpg = (g.U + 31) / 32;  // one 16-byte slice per thread
+    XPU_REQUIRE(wpg <= kMkConsumerWarps && 4 * g.U <= kMkVec * kNct, XPU_EINVAL, "persistent decode: K=%d too long",
+                g.K);
     g.wpg = wpg;
-    g.cpt = (g.U + 32 * wpg - 1) / (32 * wpg);
-    XPU_REQUIRE(g.cpt <= 4 && 4 * g.U <= kMkVec * kNct, XPU_EINVAL, "persistent decode: K=%d too long", g.K);
+    g.cpt = 1;
     g.rg = kMkConsumerWarps / wpg;
     const int64_t row_bytes = 4 * (int64_t)g.W;
     const int gr = mk_granule(g.epi);
@@ -918,7 +921,7 @@ int mk_configure(MkParams& p, MkGemv* gh, int n_gemv, int kmax, size_t* smem_byt
   XPU_REQUIRE(Gq * p.nsplit <= red_floats && p.nsplit <= 256, XPU_EINVAL, "persistent decode: too many splits");
   XPU_REQUIRE(avail >= 3 * kv_piece, XPU_EINVAL,
               "persistent decode: %lld positions per split do not fit the ring", (long long)p.cmax);
-  XPU_REQUIRE(avail >= 4 * piece_max, XPU_EINVAL,
+  XPU_REQUIRE(avail >= 3 * piece_max, XPU_EINVAL,
               "persistent decode: shared memory too small (%lld bytes of ring for %lld-byte pieces)",
               (long long)avail, (long long)piece_max);
   p.ring_bytes = (uint32_t)avail;

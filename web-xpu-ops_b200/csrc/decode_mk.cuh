@@ -38,7 +38,7 @@ struct MkGemv {
   int N, K, W, U;  // rows, columns, words per row, 16-byte slots per row
   int epi;         // Epi (matvec_kernels.cuh)
   int ns;          // weight streams (2 for FFN)
-  int wpg, rg, cpt;  // warps per row group, row groups, slots per thread
+  int wpg, rg, cpt;  // warps per row group, row groups, 16-byte slices per thread (1)
   int piece_rows;    // rows per stream of one piece (one ring allocation)
   int embed;         // x is the current token's embedding row
 };
@@ -96,7 +96,7 @@ struct MkParams {
 
 constexpr int kMkConsumerWarps = 15;  // + 1 producer warp = 512 threads: 128 registers each
 constexpr int kMkThreads = 32 * (kMkConsumerWarps + 1);
-constexpr int kMkRowsPerWarp = 2;  // rows a row group takes from one piece
+constexpr int kMkRowsPerWarp = 8;  // rows a row group takes from one piece
 constexpr int kMkTraceEvents = 8;
 
 // Decides whether the persistent step applies to this engine's shapes and
