@@ -322,8 +322,8 @@ XPU_API int xpu_llama_poison_kv(xpu_llama* engine, float value);
  * XPU_DECODE_PERSISTENT runs the whole step as one cooperative launch with
  * grid barriers between its phases.  The persistent path applies when the
  * shapes allow it (every GEMV row a whole number of 16-byte slots, head_dim
- * <= 128 and a multiple of 4); the graph path is the default unless the
- * environment sets XPUOPS_DECODE_PATH=persistent.
+ * <= 128 and a multiple of 4, normalised inputs a multiple of 4 floats) and
+ * is then the default unless the environment sets XPUOPS_DECODE_PATH=graph.
  * Both paths compute the same step; sums are ordered differently, so logits
  * agree to f32 rounding, not bit for bit.  Selecting XPU_DECODE_PERSISTENT
  * where it does not apply gives XPU_EINVAL. */

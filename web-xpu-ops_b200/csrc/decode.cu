@@ -187,6 +187,24 @@ int upload_pack(xpu_llama* e, const xpu_q8_linear& src, uint32_t* dst_w, float* 
   return XPU_OK;
 }
 
+// One stacked allocation for a linear of every layer: layer i's [n, W] words
+// and [n] scales at i * n * W and i * n.
+int alloc_stacked(xpu_llama* e, std::vector<Layer>& layers, Linear Layer::*member, int64_t n, int64_t k) {
+  const int64_t W = (k + 3) / 4, L = (int64_t)layers.size();
+  uint32_t* w = nullptr;
+  float* sc = nullptr;
+  int rc = dev_alloc(e, &w, (size_t)(L * n * W));
+  if (rc || (rc = dev_alloc(e, &sc, (size_t)(L * n)))) return rc;
+  for (int64_t i = 0; i < L; ++i) {
+    Linear& l = layers[i].*member;
+    l.n = n;
+    l.k = k;
+    l.w = w + i * n * W;
+    l.s = sc + i * n;
+  }
+  return XPU_OK;
+}
+
 int alloc_linear(xpu_llama* e, Linear& l, int64_t n, int64_t k) {
   l.n = n;
   l.k = k;
@@ -357,78 +375,90 @@ int finish_steps(xpu_llama* e) {
 
 // Plans the persistent step (decode_mk.cu) for this engine's shapes.  When
 // the shapes do not fit it (rows that are not whole 16-byte slots, head_dim
-// > 128, shared memory), the engine keeps the per-kernel graph.  The graph
-// path stays the default unless XPUOPS_DECODE_PATH=persistent.
+// > 128, shared memory), the engine keeps the per-kernel graph.  The
+// persistent path is the default unless XPUOPS_DECODE_PATH=graph.
 int setup_persistent(xpu_llama* e) {
   const xpu_llama_config& c = e->c;
   const int64_t h = c.hidden_size, hd = c.head_dim;
   const int64_t qd = (int64_t)c.num_heads * hd, kvd = (int64_t)c.num_kv_heads * hd;
   const int L = c.num_layers;
-  std::vector<MkGemv> gh(4 * (size_t)L + 1);
-  std::vector<MkAttn> ah((size_t)std::max(L, 1));
-  for (int l = 0; l < L; ++l) {
-    Layer& Ly = e->layers[l];
-    MkGemv& q = gh[4 * l];
-    q = MkGemv{};
-    q.w = Ly.qkv.w;
-    q.s = Ly.qkv.s;
-    q.x = e->hidden_a;
-    q.gamma = Ly.attn_norm;
-    q.y = e->q;
-    q.kcache = Ly.kcache;
-    q.vcache = Ly.vcache;
-    q.N = (int)(qd + 2 * kvd);
-    q.K = (int)h;
-    q.epi = EPI_QKV;
-    q.embed = l == 0;
-    MkGemv& o = gh[4 * l + 1];
-    o = MkGemv{};
-    o.w = Ly.wo.w;
-    o.s = Ly.wo.s;
-    o.x = e->attn;
-    o.residual = e->hidden_a;
-    o.y = e->hidden_b;
-    o.N = (int)h;
-    o.K = (int)qd;
-    o.epi = EPI_RESID;
-    MkGemv& f = gh[4 * l + 2];
-    f = MkGemv{};
-    f.w = Ly.gate.w;
-    f.s = Ly.gate.s;
-    f.w2 = Ly.up.w;
-    f.s2 = Ly.up.s;
-    f.x = e->hidden_b;
-    f.gamma = Ly.ffn_norm;
-    f.y = e->gated;
-    f.N = c.ffn_hidden;
-    f.K = (int)h;
-    f.epi = EPI_FFN;
-    MkGemv& d = gh[4 * l + 3];
-    d = MkGemv{};
-    d.w = Ly.down.w;
-    d.s = Ly.down.s;
-    d.x = e->gated;
-    d.residual = e->hidden_b;
-    d.y = e->hidden_a;
-    d.N = (int)h;
-    d.K = c.ffn_hidden;
-    d.epi = EPI_RESID;
-    ah[l] = MkAttn{e->q, Ly.kcache, Ly.vcache, e->attn};
-  }
-  MkGemv& hd_ = gh[4 * (size_t)L];
-  hd_ = MkGemv{};
-  hd_.w = e->lm_head.w;
-  hd_.s = e->lm_head.s;
-  hd_.x = e->hidden_a;
-  hd_.gamma = e->final_norm;
-  hd_.y = e->logits;
-  hd_.N = c.vocab_size;
-  hd_.K = (int)h;
-  hd_.epi = EPI_PLAIN;
-  hd_.embed = L == 0;
-
   MkParams& p = e->mk;
   p = MkParams{};
+  // Per-kind descriptors: layer 0's buffers and the stride to the next
+  // layer's (the stacked allocations of create_engine).
+  auto stride_w = [&](Linear Layer::*m) { return L > 1 ? (int64_t)((e->layers[1].*m).w - (e->layers[0].*m).w) : 0; };
+  auto stride_s = [&](Linear Layer::*m) { return L > 1 ? (int64_t)((e->layers[1].*m).s - (e->layers[0].*m).s) : 0; };
+  const Layer* L0 = L > 0 ? &e->layers[0] : nullptr;
+  const int64_t gstride = L > 1 ? (int64_t)(e->layers[1].attn_norm - e->layers[0].attn_norm) : 0;
+  const int64_t kvstride = L > 1 ? (int64_t)(e->layers[1].kcache - e->layers[0].kcache) : 0;
+  MkGemv& q = p.kind[MK_QKV];
+  MkGemv& o = p.kind[MK_O];
+  MkGemv& f = p.kind[MK_FFN];
+  MkGemv& d = p.kind[MK_DOWN];
+  MkGemv& hg = p.kind[MK_HEAD];
+  if (L0) {
+    q.w = L0->qkv.w;
+    q.s = L0->qkv.s;
+    q.w_stride = stride_w(&Layer::qkv);
+    q.s_stride = stride_s(&Layer::qkv);
+    q.gamma = L0->attn_norm;
+    q.gamma_stride = gstride;
+    q.kcache = L0->kcache;
+    q.vcache = L0->vcache;
+    q.kv_stride = kvstride;
+    o.w = L0->wo.w;
+    o.s = L0->wo.s;
+    o.w_stride = stride_w(&Layer::wo);
+    o.s_stride = stride_s(&Layer::wo);
+    f.w = L0->gate.w;
+    f.s = L0->gate.s;
+    f.w2 = L0->up.w;
+    f.s2 = L0->up.s;
+    f.w_stride = stride_w(&Layer::gate);
+    f.s_stride = stride_s(&Layer::gate);
+    XPU_REQUIRE(stride_w(&Layer::up) == f.w_stride && stride_s(&Layer::up) == f.s_stride, XPU_EINVAL,
+                "persistent decode: gate and up stacks differ");
+    f.gamma = L0->ffn_norm;
+    f.gamma_stride = gstride;
+    d.w = L0->down.w;
+    d.s = L0->down.s;
+    d.w_stride = stride_w(&Layer::down);
+    d.s_stride = stride_s(&Layer::down);
+  }
+  q.x = e->hidden_a;
+  q.y = e->q;
+  q.N = (int)(qd + 2 * kvd);
+  q.K = (int)h;
+  q.epi = EPI_QKV;
+  o.x = e->attn;
+  o.residual = e->hidden_a;
+  o.y = e->hidden_b;
+  o.N = (int)h;
+  o.K = (int)qd;
+  o.epi = EPI_RESID;
+  f.x = e->hidden_b;
+  f.y = e->gated;
+  f.N = c.ffn_hidden;
+  f.K = (int)h;
+  f.epi = EPI_FFN;
+  d.x = e->gated;
+  d.residual = e->hidden_b;
+  d.y = e->hidden_a;
+  d.N = (int)h;
+  d.K = c.ffn_hidden;
+  d.epi = EPI_RESID;
+  hg.w = e->lm_head.w;
+  hg.s = e->lm_head.s;
+  hg.x = e->hidden_a;
+  hg.gamma = e->final_norm;
+  hg.y = e->logits;
+  hg.N = c.vocab_size;
+  hg.K = (int)h;
+  hg.epi = EPI_PLAIN;
+  p.attn_q = e->q;
+  p.attn_out = e->attn;
+
+
   p.layers = L;
   p.embed_codes = e->embed_codes;
   p.embed_scale = e->embed_scale;
@@ -455,22 +485,15 @@ int setup_persistent(xpu_llama* e) {
   p.logits = e->logits;
   p.err = device_error_word();
   const int kmax = (int)std::max<int64_t>({h, qd, (int64_t)c.ffn_hidden});
-  int rc = mk_configure(p, gh.data(), (int)gh.size(), kmax, &e->mk_smem, &e->mk_grid);
+  int rc = mk_configure(p, kmax, &e->mk_smem, &e->mk_grid);
   if (rc == XPU_EINVAL) {  // shapes outside the persistent step: keep the graph
     clear_error();
     return XPU_OK;
   }
   if (rc) return rc;
-  MkGemv* d_gemv = nullptr;
-  MkAttn* d_attn = nullptr;
-  if ((rc = dev_alloc(e, &d_gemv, gh.size())) || (rc = dev_alloc(e, &d_attn, ah.size())) ||
-      (rc = dev_alloc(e, &e->mk_bar, 1)) || (rc = dev_alloc(e, &e->mk_ticket, 1)) ||
+  if ((rc = dev_alloc(e, &e->mk_bar, 1)) || (rc = dev_alloc(e, &e->mk_ticket, 1)) ||
       (rc = dev_alloc(e, &p.cand_v, (size_t)e->mk_grid)) || (rc = dev_alloc(e, &p.cand_i, (size_t)e->mk_grid)))
     return rc;
-  XPU_TRY_CUDA(cudaMemcpy(d_gemv, gh.data(), gh.size() * sizeof(MkGemv), cudaMemcpyHostToDevice));
-  XPU_TRY_CUDA(cudaMemcpy(d_attn, ah.data(), ah.size() * sizeof(MkAttn), cudaMemcpyHostToDevice));
-  p.gemv = d_gemv;
-  p.attn = d_attn;
   p.bar = e->mk_bar;
   p.ticket = e->mk_ticket;
   if ((rc = rearm_counters(e))) return rc;
@@ -482,7 +505,7 @@ int setup_persistent(xpu_llama* e) {
   if ((rc = set_device_pos(e, 0))) return rc;
   e->mk_ok = true;
   const char* env = getenv("XPUOPS_DECODE_PATH");
-  e->path = (env && strcmp(env, "persistent") == 0) ? XPU_DECODE_PERSISTENT : XPU_DECODE_GRAPH;
+  e->path = (env && strcmp(env, "graph") == 0) ? XPU_DECODE_GRAPH : XPU_DECODE_PERSISTENT;
   return XPU_OK;
 }
 
@@ -579,30 +602,43 @@ int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, in
   int8_t* tmp = nullptr;
   if ((rc = dev_alloc(e, &tmp, (size_t)max_codes))) return fail(rc);
 
+  // Every per-layer tensor of one kind is stacked in one allocation (layer i
+  // at a fixed stride), which lets the persistent step address any layer
+  // from a single descriptor per kind.
   e->layers.resize(c.num_layers);
+  const int L = c.num_layers;
   const size_t cache = (size_t)c.num_kv_heads * c.max_seq_len * hd;
-  for (int i = 0; i < c.num_layers; ++i) {
+  float *norms = nullptr, *kcache = nullptr, *vcache = nullptr;
+  if ((rc = dev_alloc(e, &norms, 2 * (size_t)L * h)) || (rc = dev_alloc(e, &kcache, (size_t)L * cache)) ||
+      (rc = dev_alloc(e, &vcache, (size_t)L * cache)))
+    return fail(rc);
+  if ((rc = alloc_stacked(e, e->layers, &Layer::qkv, qd + 2 * kvd, h)) ||
+      (rc = alloc_stacked(e, e->layers, &Layer::wo, h, qd)) ||
+      (rc = alloc_stacked(e, e->layers, &Layer::gate, c.ffn_hidden, h)) ||
+      (rc = alloc_stacked(e, e->layers, &Layer::up, c.ffn_hidden, h)) ||
+      (rc = alloc_stacked(e, e->layers, &Layer::down, h, c.ffn_hidden)))
+    return fail(rc);
+  if (L > 0 && (cudaMemset(kcache, 0, (size_t)L * cache * 4) != cudaSuccess ||
+                cudaMemset(vcache, 0, (size_t)L * cache * 4) != cudaSuccess))
+    return fail(cuda_status(cudaGetLastError(), "cudaMemset cache"));
+  for (int i = 0; i < L; ++i) {
     const xpu_llama_layer_q8& S = w->layers[i];
-    Layer& L = e->layers[i];
-    if ((rc = dev_alloc(e, &L.attn_norm, h)) || (rc = dev_alloc(e, &L.ffn_norm, h))) return fail(rc);
-    if (cudaMemcpy(L.attn_norm, S.attn_norm, h * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(L.ffn_norm, S.ffn_norm, h * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    Layer& Ly = e->layers[i];
+    Ly.attn_norm = norms + (size_t)i * h;
+    Ly.ffn_norm = norms + (size_t)(L + i) * h;
+    Ly.kcache = kcache + (size_t)i * cache;
+    Ly.vcache = vcache + (size_t)i * cache;
+    if (cudaMemcpy(Ly.attn_norm, S.attn_norm, h * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(Ly.ffn_norm, S.ffn_norm, h * 4, cudaMemcpyHostToDevice) != cudaSuccess)
       return fail(cuda_status(cudaGetLastError(), "upload norms"));
-    if ((rc = alloc_linear(e, L.qkv, qd + 2 * kvd, h)) || (rc = alloc_linear(e, L.wo, h, qd)) ||
-        (rc = alloc_linear(e, L.gate, c.ffn_hidden, h)) || (rc = alloc_linear(e, L.up, c.ffn_hidden, h)) ||
-        (rc = alloc_linear(e, L.down, h, c.ffn_hidden)))
+    if ((rc = upload_pack(e, S.wq, Ly.qkv.w, Ly.qkv.s, 0, tmp)) ||
+        (rc = upload_pack(e, S.wk, Ly.qkv.w, Ly.qkv.s, qd, tmp)) ||
+        (rc = upload_pack(e, S.wv, Ly.qkv.w, Ly.qkv.s, qd + kvd, tmp)) ||
+        (rc = upload_pack(e, S.wo, Ly.wo.w, Ly.wo.s, 0, tmp)) ||
+        (rc = upload_pack(e, S.w_gate, Ly.gate.w, Ly.gate.s, 0, tmp)) ||
+        (rc = upload_pack(e, S.w_up, Ly.up.w, Ly.up.s, 0, tmp)) ||
+        (rc = upload_pack(e, S.w_down, Ly.down.w, Ly.down.s, 0, tmp)))
       return fail(rc);
-    if ((rc = upload_pack(e, S.wq, L.qkv.w, L.qkv.s, 0, tmp)) ||
-        (rc = upload_pack(e, S.wk, L.qkv.w, L.qkv.s, qd, tmp)) ||
-        (rc = upload_pack(e, S.wv, L.qkv.w, L.qkv.s, qd + kvd, tmp)) ||
-        (rc = upload_pack(e, S.wo, L.wo.w, L.wo.s, 0, tmp)) ||
-        (rc = upload_pack(e, S.w_gate, L.gate.w, L.gate.s, 0, tmp)) ||
-        (rc = upload_pack(e, S.w_up, L.up.w, L.up.s, 0, tmp)) ||
-        (rc = upload_pack(e, S.w_down, L.down.w, L.down.s, 0, tmp)))
-      return fail(rc);
-    if ((rc = dev_alloc(e, &L.kcache, cache)) || (rc = dev_alloc(e, &L.vcache, cache))) return fail(rc);
-    if (cudaMemset(L.kcache, 0, cache * 4) != cudaSuccess || cudaMemset(L.vcache, 0, cache * 4) != cudaSuccess)
-      return fail(cuda_status(cudaGetLastError(), "cudaMemset cache"));
   }
   if ((rc = alloc_linear(e, e->lm_head, c.vocab_size, h)) ||
       (rc = upload_pack(e, w->lm_head, e->lm_head.w, e->lm_head.s, 0, tmp)))

@@ -18,7 +18,8 @@
 //  4. finish every share row (sum of the group's partials) with the phase's
 //     epilogue — the same arithmetic as the per-kernel path.
 // Attention: item (kv head, split) per CTA; splits write un-normalised
-// partials and the last CTA of a kv head (atomic ticket) merges them.
+// partials, meet at a per-kv-head barrier, and each merges a share of the
+// kv head's outputs.
 // Grid barriers: a monotonically increasing arrival counter, zeroed by the
 // last CTA at the end of the step; every wait is bounded (a timeout sets
 // the device error word and the CTA finishes the step without waiting).
@@ -60,13 +61,38 @@ __host__ __device__ __forceinline__ int mk_granule(int epi) { return epi == EPI_
 // different 16-byte bank groups.
 __host__ __device__ __forceinline__ int mk_xs_pitch(int U) { return U + ((10 - U % 8) % 8); }
 
-// Index into p.gemv of phase i (QKV, O, FFN, DOWN per layer, then HEAD);
-// -1 for attention.
-__device__ __forceinline__ int mk_gemv_index(int i, int layers) {
-  if (i >= 5 * layers) return 4 * layers;
-  const int l = i / 5, k = i % 5;
-  if (k == 1) return -1;
-  return 4 * l + (k == 0 ? 0 : k - 1);
+// Kind of phase i (QKV, O, FFN, DOWN per layer, then HEAD); -1 for attention.
+__device__ __forceinline__ int mk_kind(int i, int layers) {
+  if (i >= 5 * layers) return MK_HEAD;
+  const int k = i % 5;
+  return k == 0 ? MK_QKV : (k == 1 ? -1 : k - 1);
+}
+
+// A GEMV phase: its kind's descriptor with layer l's stacked buffers.
+struct MkView {
+  const MkGemv* g;
+  const uint32_t* w;
+  const uint32_t* w2;
+  const float* s;
+  const float* s2;
+  const float* gamma;
+  float* kcache;
+  float* vcache;
+  bool embed;  // the input is the current token's embedding row
+};
+__device__ __forceinline__ MkView mk_view(const MkParams& p, int kind, int l) {
+  const MkGemv& g = p.kind[kind];
+  MkView v;
+  v.g = &g;
+  v.w = g.w + l * g.w_stride;
+  v.w2 = g.w2 ? g.w2 + l * g.w_stride : nullptr;
+  v.s = g.s + l * g.s_stride;
+  v.s2 = g.s2 ? g.s2 + l * g.s_stride : nullptr;
+  v.gamma = g.gamma ? g.gamma + l * g.gamma_stride : nullptr;
+  v.kcache = g.kcache ? g.kcache + l * g.kv_stride : nullptr;
+  v.vcache = g.vcache ? g.vcache + l * g.kv_stride : nullptr;
+  v.embed = (kind == MK_QKV && l == 0) || (kind == MK_HEAD && p.layers == 0);
+  return v;
 }
 
 // Profile timestamps (see MkParams::trace): mk_mark by thread 0 of the CTA,
@@ -177,12 +203,14 @@ __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, ui
     return slot;
   };
   for (int i = 0; i < n_phase && !*abort_flag; ++i) {
-    const int gi = mk_gemv_index(i, p.layers);
-    if (gi < 0) {
+    const int kind = mk_kind(i, p.layers);
+    if (kind < 0) {
       // Attention: the CTA's K and V rows of each item, positions before
       // `pos` (the row at `pos` is written during this step, the consumers
       // read it from the cache themselves).
-      const MkAttn* a = p.attn + i / 5;
+      const MkGemv& qk = p.kind[MK_QKV];
+      const float* kc = qk.kcache + (i / 5) * qk.kv_stride;
+      const float* vc = qk.vcache + (i / 5) * qk.kv_stride;
       for (int it = b; it < p.kvH * p.nsplit && !*abort_flag; it += G) {
         const MkItem m = mk_item(p, it, L);
         const int nn = m.j1 - m.j0;
@@ -196,14 +224,23 @@ __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, ui
         mbar_arrive_expect_tx(&full[slot], 2 * bytes);
         if (bytes) {
           const int64_t row = (int64_t)m.g * p.max_seq + m.j0;
-          bulk_g2s_plain(dst, a->kcache + row * hd, bytes, &full[slot]);
-          bulk_g2s_plain(dst + (size_t)nn * rb, a->vcache + row * hd, bytes, &full[slot]);
+          bulk_g2s_plain(dst, kc + row * hd, bytes, &full[slot]);
+          bulk_g2s_plain(dst + (size_t)nn * rb, vc + row * hd, bytes, &full[slot]);
         }
       }
       continue;
     }
-    const MkGemv* g = p.gemv + gi;
+    const MkView v = mk_view(p, kind, kind == MK_HEAD ? 0 : i / 5);
+    const MkGemv* g = v.g;
     const int gr = mk_granule(g->epi), P = g->piece_rows, ns = g->ns;
+    if (v.gamma) {  // the rmsnorm gain first (K floats, a multiple of 16 bytes)
+      uint32_t off;
+      const uint32_t B = 4u * (uint32_t)g->K;
+      const int slot = place(B, off);
+      if (slot < 0) break;
+      mbar_arrive_expect_tx(&full[slot], B);
+      bulk_g2s_plain(smem + p.off_ring + off, v.gamma, B, &full[slot]);
+    }
     const int64_t W = g->W;
     int64_t u0, u1;
     mk_share(g->N / gr, b, G, u0, u1);
@@ -218,8 +255,8 @@ __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, ui
       if (base == 0) mk_mark_any(p, i, 6);
       uint8_t* dst = smem + p.off_ring + off;
       mbar_arrive_expect_tx(&full[slot], bytes * ns);  // releases slot_off to the consumers
-      bulk_g2s(dst, g->w + (r0 + base) * W, bytes, &full[slot], policy);
-      if (ns == 2) bulk_g2s(dst + bytes, g->w2 + (r0 + base) * W, bytes, &full[slot], policy);
+      bulk_g2s(dst, v.w + (r0 + base) * W, bytes, &full[slot], policy);
+      if (ns == 2) bulk_g2s(dst + bytes, v.w2 + (r0 + base) * W, bytes, &full[slot], policy);
       if (base + P >= n) mk_mark_any(p, i, 7);
     }
   }
@@ -230,12 +267,13 @@ __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, ui
 
 // --------------------------------------------------------- GEMV phase --
 // Returns, for the HEAD phase, the thread's first maximal logit of its rows.
-__device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, const MkGemv* g, uint8_t* smem,
+__device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, const MkView& v, uint8_t* smem,
                                               uint64_t* full, uint64_t* empty, const uint32_t* slot_off,
                                               int64_t& pbase, volatile int* abort_flag, int tok, int pos,
                                               double* red_d, const double* rope, float& best, int& best_i) {
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int G = gridDim.x, b = blockIdx.x;
+  const MkGemv* g = v.g;
   const int K = g->K, U = g->U, epi = g->epi, ns = g->ns, wpg = g->wpg, rg = g->rg;
   const int P = g->piece_rows, RS = p.red_stride;
   const int64_t W = g->W;
@@ -251,8 +289,8 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
   // 1. Input vector -> xs[0, 16U) (zero past K).  A thread issues all its
   // loads (x and the rmsnorm gain, kMkVec float4 slots each) before using
   // any, so staging costs one memory round trip.
-  const bool embed = g->embed != 0;
-  const float* gam = g->gamma;
+  const bool embed = v.embed;
+  const float* gam = v.gamma;
   const int nv = 4 * U;  // float4 slots of xs
   float4 xv[kMkVec], gv[kMkVec];
   if (embed) {
@@ -292,21 +330,17 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
       }
     }
   }
+  int gslot = -1;
   if (gam) {
+    // The gain arrived in the ring as the phase's first piece (K floats).
+    const int64_t gidx = pbase++;
+    gslot = (int)(gidx % kMkSlots);
+    mk_wait(&full[gslot], (uint32_t)((gidx / kMkSlots) & 1), p.err, abort_flag);
+    const float* gs = reinterpret_cast<const float*>(smem + p.off_ring + slot_off[gslot]);
 #pragma unroll
     for (int i = 0; i < kMkVec; ++i) {
-      const int v = tid + i * kNct, k = 4 * v;
-      gv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (v < nv) {
-        if (k + 4 <= K) {
-          gv[i] = __ldg(reinterpret_cast<const float4*>(gam + k));
-        } else {
-          float t[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) t[e] = k + e < K ? __ldg(gam + k + e) : 0.0f;
-          gv[i] = make_float4(t[0], t[1], t[2], t[3]);
-        }
-      }
+      const int v = tid + i * kNct;
+      gv[i] = (4 * v < K) ? reinterpret_cast<const float4*>(gs)[v] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     // ops/rmsnorm/reference.ts:80-96: scale = 1/sqrt(mean(x^2) + eps) in f64,
     // out = f32(x * scale * gain).
@@ -339,6 +373,10 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
     const int v = tid + i * kNct;
     if (v < nv) reinterpret_cast<float4*>(xs)[(v & 3) * UP + (v >> 2)] = xv[i];
   }
+  if (gslot >= 0) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[gslot]);  // gain consumed
+  }
   named_bar_sync(1, kNct);
   mk_mark(p, phase, 1);
 
@@ -353,11 +391,11 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
     pa[q] = pb[q] = 0.0f;
     if (t < outs) {
       if (epi == EPI_QKV) {
-        pa[q] = g->s[r0 + 2 * t];
-        pb[q] = g->s[r0 + 2 * t + 1];
+        pa[q] = v.s[r0 + 2 * t];
+        pb[q] = v.s[r0 + 2 * t + 1];
       } else {
-        pa[q] = g->s[r0 + t];
-        if (epi == EPI_FFN) pb[q] = g->s2[r0 + t];
+        pa[q] = v.s[r0 + t];
+        if (epi == EPI_FFN) pb[q] = v.s2[r0 + t];
         if (epi == EPI_RESID) pb[q] = __ldcg(g->residual + r0 + t);
       }
     }
@@ -445,8 +483,8 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
     const int64_t qk_end = (int64_t)p.q_rows + p.kv_rows;
     for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
       const int64_t row = r0 + 2 * t;
-      const float sa = q < 2 ? (q == 0 ? pa[0] : pa[1]) : g->s[row];
-      const float sb = q < 2 ? (q == 0 ? pb[0] : pb[1]) : g->s[row + 1];
+      const float sa = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
+      const float sb = q < 2 ? (q == 0 ? pb[0] : pb[1]) : v.s[row + 1];
       float a = __fmul_rn(sum(2 * t), sa);
       float c = __fmul_rn(sum(2 * t + 1), sb);
       if (row < qk_end) {
@@ -467,7 +505,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
         const bool is_k = row < qk_end;
         const int64_t local = is_k ? row - p.q_rows : row - qk_end;
         const int64_t h = local / p.head_dim, d = local % p.head_dim;
-        float* dst = (is_k ? g->kcache : g->vcache) + ((h * p.max_seq + pos) * p.head_dim + d);
+        float* dst = (is_k ? v.kcache : v.vcache) + ((h * p.max_seq + pos) * p.head_dim + d);
         dst[0] = a;
         dst[1] = c;
       }
@@ -475,8 +513,8 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
   } else if (epi == EPI_FFN) {
     for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
       const int64_t row = r0 + t;
-      const float sg = q < 2 ? (q == 0 ? pa[0] : pa[1]) : g->s[row];
-      const float su = q < 2 ? (q == 0 ? pb[0] : pb[1]) : g->s2[row];
+      const float sg = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
+      const float su = q < 2 ? (q == 0 ? pb[0] : pb[1]) : v.s2[row];
       const float gt_ = __fmul_rn(sum(t), sg);
       const float up = __fmul_rn(sum(n + t), su);
       g->y[row] = __fmul_rn(silu_f32(gt_), up);
@@ -484,7 +522,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
   } else if (epi == EPI_RESID) {
     for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
       const int64_t row = r0 + t;
-      const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : g->s[row];
+      const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
       const float res = q < 2 ? (q == 0 ? pb[0] : pb[1]) : __ldcg(g->residual + row);
       g->y[row] = __fadd_rn(res, __fmul_rn(sum(t), sc));
     }
@@ -492,7 +530,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
     constexpr int kNone = 0x7fffffff;
     for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
       const int64_t row = r0 + t;
-      const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : g->s[row];
+      const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
       const float v = __fmul_rn(sum(t), sc);
       g->y[row] = v;
       if (v == v && (best_i == kNone || v > best)) {  // ascending rows: ties keep the first
@@ -552,14 +590,12 @@ __device__ __forceinline__ void mk_scores_any(const float* q_s, const float* k_s
   }
 }
 
-constexpr int kMkMergeBatch = 40;  // split partials one thread loads per round trip
-
 // ops/gqa/reference.ts:203-303 for one decode query (sEff = pos + 1): item
 // (kv head g, split sp) scans positions [j0, j1) for the Gq heads of g, with
 // K and V rows streamed into the ring by the producer.
-__device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, const MkAttn* a, uint8_t* smem,
+__device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, int layer, uint8_t* smem,
                                               uint64_t* full, uint64_t* empty, const uint32_t* slot_off,
-                                              int64_t& pbase, volatile int* abort_flag, int pos, int* flag_s) {
+                                              int64_t& pbase, volatile int* abort_flag, int pos) {
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int G = gridDim.x, b = blockIdx.x;
   const int Gq = p.H / p.kvH, hd = p.head_dim, nsp = p.nsplit, cm = p.cmax;
@@ -569,12 +605,14 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, cons
   float* stat = p_s + Gq * cm;                              // [Gq][2]
   const int L = pos + 1;
   const int items = p.kvH * nsp;
+  const float* kcache = p.kind[MK_QKV].kcache + layer * p.kind[MK_QKV].kv_stride;
+  const float* vcache = p.kind[MK_QKV].vcache + layer * p.kind[MK_QKV].kv_stride;
   mk_mark(p, phase, 1);  // CTAs without an item keep these
   mk_mark(p, phase, 2);
   for (int it = b; it < items; it += G) {
     const MkItem m = mk_item(p, it, L);
     const int g = m.g, sp = m.sp, j0 = m.j0, nn = m.j1 - m.j0;
-    for (int i = tid; i < Gq * hd; i += kNct) q_s[i] = __ldcg(a->q + (int64_t)g * Gq * hd + i);
+    for (int i = tid; i < Gq * hd; i += kNct) q_s[i] = __ldcg(p.attn_q + (int64_t)g * Gq * hd + i);
     const float* k_s = nullptr;
     const float* v_s = nullptr;
     int slot = -1;
@@ -588,8 +626,8 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, cons
       if (pos >= j0 && pos < m.j1) {  // this step's row, written by the QKV phase
         const int64_t row = ((int64_t)g * p.max_seq + pos) * hd;
         for (int i = tid; i < hd; i += kNct) {
-          kv[(pos - j0) * hd + i] = __ldcg(a->kcache + row + i);
-          kv[(nn + pos - j0) * hd + i] = __ldcg(a->vcache + row + i);
+          kv[(pos - j0) * hd + i] = __ldcg(kcache + row + i);
+          kv[(nn + pos - j0) * hd + i] = __ldcg(vcache + row + i);
         }
       }
     }
@@ -658,84 +696,58 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, cons
     }
     named_bar_sync(1, kNct);
     mk_mark(p, phase, 2);
+    // Group barrier of kv head g's splits (the count grows by nsplit per
+    // layer; the step's last CTA zeroes it), then each split merges its
+    // share of the group's outputs.
     if (tid == 0) {
-      // Acquire-release ticket: publishes this split's partials and, for the
-      // last split, makes every other split's visible to this CTA.
-      unsigned int old;
-      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.attn_counter + g) : "memory");
-      *flag_s = old == (unsigned)(nsp - 1);
-    }
-    named_bar_sync(1, kNct);
-    if (*flag_s) {
-      // Merge: out = sum_s w[h][s] acc_s with w[h][s] = exp(m_s - M) /
-      // sum_s' l_s' exp(m_s' - M).  A thread takes outputs tid and
-      // tid + kNct and issues the loads of both outputs' partials
-      // (kMkMergeBatch each) before the weights are formed, so the merge
-      // costs one round trip when nsplit <= kMkMergeBatch.
-      float* wts = red;  // [Gq][nsp]
-      const int nout = Gq * hd;
-      for (int o0 = 0; o0 < nout; o0 += 2 * kNct) {
-        const int oa = o0 + tid, ob = oa + kNct;
-        const int ha = oa / hd, ca = oa - ha * hd, hb_ = ob / hd, cb = ob - hb_ * hd;
-        const float* srca = p.part_acc + (int64_t)(g * Gq + ha) * nsp * hd + ca;
-        const float* srcb = p.part_acc + (int64_t)(g * Gq + hb_) * nsp * hd + cb;
-        float av[kMkMergeBatch], bv[kMkMergeBatch];
-#pragma unroll
-        for (int u = 0; u < kMkMergeBatch; ++u) {
-          av[u] = (oa < nout && u < nsp) ? __ldcg(srca + (int64_t)u * hd) : 0.0f;
-          bv[u] = (ob < nout && u < nsp) ? __ldcg(srcb + (int64_t)u * hd) : 0.0f;
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.attn_counter + g) : "memory");
+      const unsigned int target = (unsigned)((layer + 1) * nsp);
+      const uint64_t t0 = global_timer_ns();
+      unsigned int n = 0, c = 0;
+      while (!*abort_flag) {
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(c) : "l"(p.attn_counter + g) : "memory");
+        if (c >= target) break;
+        if ((++n & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.err, 1u);
+          *abort_flag = 1;
         }
-        if (o0 == 0) {
-          for (int hh = warp; hh < Gq; hh += kMkConsumerWarps) {
-            const int head = g * Gq + hh;
-            float mv[8], lv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int sidx = lane + 32 * u;
-              mv[u] = sidx < nsp ? __ldcg(&p.part_m[head * nsp + sidx]) : -INFINITY;
-              lv[u] = sidx < nsp ? __ldcg(&p.part_l[head * nsp + sidx]) : 0.0f;
-            }
-            float M = -INFINITY;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) M = fmaxf(M, mv[u]);
-            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-            float l = 0.0f;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const float w = mv[u] == -INFINITY ? 0.0f : expf(mv[u] - M);
-              mv[u] = w;
-              l = fmaf(lv[u], w, l);
-            }
-            l = warp_sum(l);
-            const float inv = 1.0f / l;
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              if (lane + 32 * u < nsp) wts[hh * nsp + lane + 32 * u] = mv[u] * inv;
-          }
-          named_bar_sync(1, kNct);
-        }
-        auto finish = [&](int o, int h, int cc, const float* src, const float (&v)[kMkMergeBatch]) {
-          if (o >= nout) return;
-          const float* w = wts + h * nsp;
-          float o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-          for (int u = 0; u < kMkMergeBatch; ++u)
-            if (u < nsp) o4[u & 3] = fmaf(w[u], v[u], o4[u & 3]);
-          for (int s0 = kMkMergeBatch; s0 < nsp; ++s0)
-            o4[s0 & 3] = fmaf(w[s0], __ldcg(src + (int64_t)s0 * hd), o4[s0 & 3]);
-          a->out[(int64_t)(g * Gq + h) * hd + cc] = (o4[0] + o4[1]) + (o4[2] + o4[3]);
-        };
-        finish(oa, ha, ca, srca, av);
-        finish(ob, hb_, cb, srcb, bv);
       }
-      if (tid == 0) p.attn_counter[g] = 0;
     }
     named_bar_sync(1, kNct);
+    // Merge (one warp per output, lanes over splits): with M = max_s m_s and
+    // w_s = exp(m_s - M), out = (sum_s w_s acc_s) / (sum_s w_s l_s).
+    const int nout = Gq * hd, o0 = (int)((int64_t)nout * sp / nsp), o1 = (int)((int64_t)nout * (sp + 1) / nsp);
+    for (int o = o0 + warp; o < o1; o += kMkConsumerWarps) {
+      const int h = o / hd, cc = o - h * hd, hh = g * Gq + h;
+      float mv[8], lv[8], av[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int si = lane + 32 * u;
+        const bool ok = si < nsp;
+        mv[u] = ok ? __ldcg(&p.part_m[hh * nsp + si]) : -INFINITY;
+        lv[u] = ok ? __ldcg(&p.part_l[hh * nsp + si]) : 0.0f;
+        av[u] = ok ? __ldcg(&p.part_acc[((int64_t)hh * nsp + si) * hd + cc]) : 0.0f;
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) M = fmaxf(M, mv[u]);
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      float l = 0.0f, acc = 0.0f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = mv[u] == -INFINITY ? 0.0f : expf(mv[u] - M);
+        l = fmaf(lv[u], w, l);
+        acc = fmaf(av[u], w, acc);
+      }
+      l = warp_sum(l);
+      acc = warp_sum(acc);
+      if (lane == 0) p.attn_out[(int64_t)hh * hd + cc] = acc / l;
+    }
   }
 }
 
 // ------------------------------------------------------------- kernel --
-__global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(MkParams p) {
+__global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_constant__ MkParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kMkSlots];
   __shared__ __align__(8) uint64_t empty[kMkSlots];
@@ -788,11 +800,11 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(MkParams p) {
       mk_grid_sync(p, i - 1, target, &abort_flag);
     }
     mk_mark(p, i, 0);
-    const int gi = mk_gemv_index(i, p.layers);
-    if (gi < 0)
-      mk_attn_phase(p, i, p.attn + i / 5, smem, full, empty, slot_off, pbase, &abort_flag, pos, &flag_s);
+    const int kind = mk_kind(i, p.layers);
+    if (kind < 0)
+      mk_attn_phase(p, i, i / 5, smem, full, empty, slot_off, pbase, &abort_flag, pos);
     else
-      mk_gemv_phase(p, i, p.gemv + gi, smem, full, empty, slot_off, pbase, &abort_flag, tok, pos, red_d, rope,
+      mk_gemv_phase(p, i, mk_view(p, kind, kind == MK_HEAD ? 0 : i / 5), smem, full, empty, slot_off, pbase, &abort_flag, tok, pos, red_d, rope,
                     best, best_i);
   }
 
@@ -856,13 +868,14 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(MkParams p) {
     // Every CTA has passed its last barrier: re-arm the counters.
     *p.bar = 0ull;
     *p.ticket = 0u;
+    for (int gg = 0; gg < p.kvH; ++gg) p.attn_counter[gg] = 0u;
   }
 }
 
 }  // namespace
 
 // ------------------------------------------------------------------ host --
-int mk_configure(MkParams& p, MkGemv* gh, int n_gemv, int kmax, size_t* smem_bytes, int* grid) {
+int mk_configure(MkParams& p, int kmax, size_t* smem_bytes, int* grid) {
   const DeviceInfo& di = device_info();
   int dev = 0, coop = 0;
   XPU_TRY_CUDA(cudaGetDevice(&dev));
@@ -873,12 +886,14 @@ int mk_configure(MkParams& p, MkGemv* gh, int n_gemv, int kmax, size_t* smem_byt
   int64_t red_stride = 0, piece_max = 0;
   int max_wpg = 1;
   int64_t max_u = 0;
-  for (int i = 0; i < n_gemv; ++i) {
-    MkGemv& g = gh[i];
+  for (int i = 0; i < MK_KINDS; ++i) {
+    MkGemv& g = p.kind[i];
     g.W = (g.K + 3) / 4;
     XPU_REQUIRE(g.W % 4 == 0, XPU_EINVAL, "persistent decode: rows of %d codes are not whole 16-byte slots", g.K);
     g.U = g.W / 4;
     g.ns = g.epi == EPI_FFN ? 2 : 1;
+    XPU_REQUIRE(!g.gamma || g.K % 4 == 0, XPU_EINVAL,
+                "persistent decode: a normalised input of %d floats is not whole 16-byte slots", g.K);
     const int wpg = (g.U + 31) / 32;  // one 16-byte slice per thread
     XPU_REQUIRE(wpg <= kMkConsumerWarps && 4 * g.U <= kMkVec * kNct, XPU_EINVAL, "persistent decode: K=%d too long",
                 g.K);
@@ -918,7 +933,7 @@ int mk_configure(MkParams& p, MkGemv* gh, int n_gemv, int kmax, size_t* smem_byt
   const int64_t avail = ((int64_t)di.max_smem_optin - (int64_t)static_smem - (int64_t)p.off_ring) / 128 * 128;
   const int64_t kv_piece = 2 * (int64_t)p.cmax * p.head_dim * 4;
   XPU_REQUIRE(p.head_dim % 4 == 0, XPU_EINVAL, "persistent decode: head_dim %d is not a multiple of 4", p.head_dim);
-  XPU_REQUIRE(Gq * p.nsplit <= red_floats && p.nsplit <= 256, XPU_EINVAL, "persistent decode: too many splits");
+  XPU_REQUIRE(p.nsplit <= 256, XPU_EINVAL, "persistent decode: too many splits");
   XPU_REQUIRE(avail >= 3 * kv_piece, XPU_EINVAL,
               "persistent decode: %lld positions per split do not fit the ring", (long long)p.cmax);
   XPU_REQUIRE(avail >= 3 * piece_max, XPU_EINVAL,

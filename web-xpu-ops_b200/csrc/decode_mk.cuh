@@ -22,37 +22,38 @@
 
 namespace xpu {
 
-// One GEMV phase: rows [0, N) of `w` (and of `w2`, the up weight, for FFN)
-// times the phase's input vector.
+// One kind of GEMV phase (QKV, O, FFN, DOWN, HEAD): rows [0, N) of `w` (and
+// of `w2`, the up weight, for FFN) times the phase's input vector.  The
+// per-layer weights, scales, gains and caches of a kind are stacked: layer
+// l's are at base + l * stride.  Activation buffers are shared by all layers.
 struct MkGemv {
   const uint32_t* w;
   const uint32_t* w2;
+  int64_t w_stride;  // words
   const float* s;
   const float* s2;
-  const float* x;         // input vector (ignored when `embed` is set)
+  int64_t s_stride;  // floats
+  const float* x;         // input vector (the embedding row for QKV of layer 0)
   const float* gamma;     // rmsnorm gain, or null
+  int64_t gamma_stride;   // floats
   const float* residual;  // residual epilogue
   float* y;
-  float* kcache;  // QKV: the layer's caches
+  float* kcache;  // QKV: the caches
   float* vcache;
+  int64_t kv_stride;  // floats
   int N, K, W, U;  // rows, columns, words per row, 16-byte slots per row
   int epi;         // Epi (matvec_kernels.cuh)
   int ns;          // weight streams (2 for FFN)
   int wpg, rg, cpt;  // warps per row group, row groups, 16-byte slices per thread (1)
   int piece_rows;    // rows per stream of one piece (one ring allocation)
-  int embed;         // x is the current token's embedding row
 };
 
-struct MkAttn {
-  const float* q;
-  const float* kcache;
-  const float* vcache;
-  float* out;
-};
+enum MkKind : int { MK_QKV = 0, MK_O = 1, MK_FFN = 2, MK_DOWN = 3, MK_HEAD = 4, MK_KINDS = 5 };
 
 struct MkParams {
-  const MkGemv* gemv;  // [4 * layers + 1]: per layer QKV, O, FFN, DOWN; then HEAD
-  const MkAttn* attn;  // [layers]
+  MkGemv kind[MK_KINDS];
+  const float* attn_q;  // attention input (QKV output) and output
+  float* attn_out;
   int layers;
   // embedding (layer 0 input) and its copy into the residual stream
   const int8_t* embed_codes;
@@ -102,7 +103,7 @@ constexpr int kMkTraceEvents = 8;
 // Decides whether the persistent step applies to this engine's shapes and
 // fills the geometry fields of `p` and of each MkGemv; XPU_OK, or XPU_EINVAL
 // with the reason (the caller then keeps the per-kernel graph).
-int mk_configure(MkParams& p, MkGemv* gemv_host, int n_gemv, int kmax, size_t* smem_bytes, int* grid);
+int mk_configure(MkParams& p, int kmax, size_t* smem_bytes, int* grid);
 // One cooperative launch of the step on `stream`.
 int mk_launch(const MkParams& p, size_t smem_bytes, int grid, cudaStream_t stream);
 
