@@ -281,8 +281,8 @@ XPU_API int xpu_llama_forward_profiled(xpu_llama* engine, const int32_t* tokens,
  * entries (ns, %globaltimer): out[(phase * grid + cta) * events + e], phases
  * in entry order, e as documented in the library's persistent-step source
  * (0 phase start, 1 input staged, 2 dot products done, 3 epilogue done,
- * 4 first weight stage ready, 5 total ns waited for weight stages, 6 / 7
- * producer issued first / last stage; 0 = did not happen).  Writes min(cap, total) values and sets `n`
+ * 4 first weight stage ready, 5 total ns waited for weight stages, 7
+ * producer issued the last weight piece, 6 unused; 0 = did not happen).  Writes min(cap, total) values and sets `n`
  * to the total; XPU_ESTATE before any profiled persistent step. */
 XPU_API int xpu_llama_profile_trace(const xpu_llama* engine, uint64_t* out, int64_t cap, int64_t* n,
                             int32_t* grid, int32_t* events);

@@ -36,6 +36,7 @@ namespace {
 
 constexpr int kMkSlots = 32;                 // pieces in flight at most
 constexpr uint32_t kMkPieceBytes = 65536;    // largest piece (one or two bulk copies)
+constexpr int64_t kMkPrefetchAhead = 384 * 1024;  // L2 prefetch distance of a CTA's stream
 constexpr int kNct = 32 * kMkConsumerWarps;  // consumer threads
 // Attention's P.V reduction parks up to kNct * 8 floats in the partial area.
 constexpr int kMkRedMinFloats = kNct * 8;
@@ -171,13 +172,83 @@ __device__ __forceinline__ MkItem mk_item(const MkParams& p, int it, int L) {
   return m;
 }
 
+// The q-th piece this CTA streams for phase i, in the order the consumers
+// take them: for a GEMV phase its rmsnorm gain (if any), then its weight
+// rows P at a time (rows of w, then the same rows of w2); for attention one
+// piece per item with the K and V rows before `pos`.  Returns false past
+// the phase's last piece; B = 0 marks an item with no positions (no piece).
+struct MkPiece {
+  const void* src0;
+  const void* src1;
+  uint32_t bytes0, bytes1, off1, B;
+  bool weights;  // streamed once: L2 evict-first
+};
+__device__ __forceinline__ bool mk_piece(const MkParams& p, int b, int G, int pos, int i, int q, MkPiece& pc) {
+  pc.src1 = nullptr;
+  pc.bytes1 = 0;
+  pc.off1 = 0;
+  const int kind = mk_kind(i, p.layers);
+  if (kind < 0) {
+    const int it = b + q * G;
+    if (it >= p.kvH * p.nsplit) return false;
+    const MkItem m = mk_item(p, it, pos + 1);
+    const int nn = m.j1 - m.j0, hd = p.head_dim;
+    const int jc = m.j1 < pos ? m.j1 : pos;  // the row at `pos` is written during the step
+    const uint32_t rb = 4u * hd;
+    const MkGemv& qk = p.kind[MK_QKV];
+    const int64_t row = (int64_t)(i / 5) * qk.kv_stride + ((int64_t)m.g * p.max_seq + m.j0) * hd;
+    pc.src0 = qk.kcache + row;
+    pc.src1 = qk.vcache + row;
+    pc.bytes0 = pc.bytes1 = nn > 0 ? (uint32_t)(jc - m.j0) * rb : 0u;
+    pc.off1 = (uint32_t)nn * rb;
+    pc.B = 2u * nn * rb;
+    pc.weights = false;
+    return true;
+  }
+  const MkView v = mk_view(p, kind, kind == MK_HEAD ? 0 : i / 5);
+  const MkGemv* g = v.g;
+  if (v.gamma) {
+    if (q == 0) {
+      pc.src0 = v.gamma;
+      pc.bytes0 = pc.B = 4u * (uint32_t)g->K;
+      pc.weights = false;
+      return true;
+    }
+    --q;
+  }
+  const int gr = mk_granule(g->epi), P = g->piece_rows;
+  int64_t u0, u1;
+  mk_share(g->N / gr, b, G, u0, u1);
+  const int64_t r0 = u0 * gr, n = (u1 - u0) * gr, base = (int64_t)q * P;
+  if (base >= n) return false;
+  const int rows = (int)(n - base < P ? n - base : P);
+  const uint32_t bytes = (uint32_t)rows * (uint32_t)(4 * g->W);
+  pc.src0 = v.w + (r0 + base) * g->W;
+  pc.bytes0 = bytes;
+  if (g->ns == 2) {
+    pc.src1 = v.w2 + (r0 + base) * g->W;
+    pc.bytes1 = bytes;
+    pc.off1 = bytes;
+  }
+  pc.B = bytes * g->ns;
+  pc.weights = true;
+  return true;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// One thread streams the step's pieces into the ring and, kMkPrefetchAhead
+// bytes further along the same sequence, asks L2 to prefetch them from HBM,
+// so that ring refills read L2 even when the ring itself cannot run ahead.
 __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                             uint32_t* slot_off, uint32_t* slot_len, volatile int* abort_flag) {
   const int G = gridDim.x, b = blockIdx.x;
   const int n_phase = 5 * p.layers + 1;
   const uint32_t ring = p.ring_bytes;
   const uint64_t policy = evict_first_policy();
-  const int pos = __ldcg(p.pos), L = pos + 1, hd = p.head_dim;
+  const int pos = __ldcg(p.pos);
   uint32_t head = 0;
   int64_t issued = 0, oldest = 0;  // pieces [oldest, issued) may still be in use
   // Places a piece of B bytes: waits (oldest first) until no piece in use
@@ -202,62 +273,44 @@ __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, ui
     head = off + B;
     return slot;
   };
-  for (int i = 0; i < n_phase && !*abort_flag; ++i) {
-    const int kind = mk_kind(i, p.layers);
-    if (kind < 0) {
-      // Attention: the CTA's K and V rows of each item, positions before
-      // `pos` (the row at `pos` is written during this step, the consumers
-      // read it from the cache themselves).
-      const MkGemv& qk = p.kind[MK_QKV];
-      const float* kc = qk.kcache + (i / 5) * qk.kv_stride;
-      const float* vc = qk.vcache + (i / 5) * qk.kv_stride;
-      for (int it = b; it < p.kvH * p.nsplit && !*abort_flag; it += G) {
-        const MkItem m = mk_item(p, it, L);
-        const int nn = m.j1 - m.j0;
-        if (nn == 0) continue;
-        const int jc = m.j1 < pos ? m.j1 : pos;
-        const uint32_t rb = 4u * hd, bytes = (uint32_t)(jc - m.j0) * rb;
-        uint32_t off;
-        const int slot = place(2u * nn * rb, off);
-        if (slot < 0) break;
-        uint8_t* dst = smem + p.off_ring + off;
-        mbar_arrive_expect_tx(&full[slot], 2 * bytes);
-        if (bytes) {
-          const int64_t row = (int64_t)m.g * p.max_seq + m.j0;
-          bulk_g2s_plain(dst, kc + row * hd, bytes, &full[slot]);
-          bulk_g2s_plain(dst + (size_t)nn * rb, vc + row * hd, bytes, &full[slot]);
-        }
+  // L2 prefetch cursor: phase pf_i, piece pf_q; pf_bytes streamed so far.
+  int pf_i = 0, pf_q = 0;
+  int64_t pf_bytes = 0, sent_bytes = 0;
+  auto prefetch_to = [&](int64_t limit) {
+    while (pf_i < n_phase && pf_bytes < limit) {
+      MkPiece pc;
+      if (!mk_piece(p, b, G, pos, pf_i, pf_q, pc)) {
+        ++pf_i;
+        pf_q = 0;
+        continue;
       }
-      continue;
+      ++pf_q;
+      if (pc.bytes0) prefetch_l2(pc.src0, pc.bytes0);
+      if (pc.bytes1) prefetch_l2(pc.src1, pc.bytes1);
+      pf_bytes += pc.B;
     }
-    const MkView v = mk_view(p, kind, kind == MK_HEAD ? 0 : i / 5);
-    const MkGemv* g = v.g;
-    const int gr = mk_granule(g->epi), P = g->piece_rows, ns = g->ns;
-    if (v.gamma) {  // the rmsnorm gain first (K floats, a multiple of 16 bytes)
+  };
+  prefetch_to(kMkPrefetchAhead);
+  for (int i = 0; i < n_phase && !*abort_flag; ++i) {
+    for (int q = 0; !*abort_flag; ++q) {
+      MkPiece pc;
+      if (!mk_piece(p, b, G, pos, i, q, pc)) break;
+      if (pc.B == 0) continue;
       uint32_t off;
-      const uint32_t B = 4u * (uint32_t)g->K;
-      const int slot = place(B, off);
+      const int slot = place(pc.B, off);
       if (slot < 0) break;
-      mbar_arrive_expect_tx(&full[slot], B);
-      bulk_g2s_plain(smem + p.off_ring + off, v.gamma, B, &full[slot]);
-    }
-    const int64_t W = g->W;
-    int64_t u0, u1;
-    mk_share(g->N / gr, b, G, u0, u1);
-    const int64_t r0 = u0 * gr, n = (u1 - u0) * gr;
-    const uint32_t row_bytes = (uint32_t)(4 * W);
-    for (int64_t base = 0; base < n && !*abort_flag; base += P) {
-      const int rows = (int)(n - base < P ? n - base : P);
-      const uint32_t bytes = (uint32_t)rows * row_bytes;
-      uint32_t off;
-      const int slot = place(bytes * ns, off);
-      if (slot < 0) break;
-      if (base == 0) mk_mark_any(p, i, 6);
       uint8_t* dst = smem + p.off_ring + off;
-      mbar_arrive_expect_tx(&full[slot], bytes * ns);  // releases slot_off to the consumers
-      bulk_g2s(dst, v.w + (r0 + base) * W, bytes, &full[slot], policy);
-      if (ns == 2) bulk_g2s(dst + bytes, v.w2 + (r0 + base) * W, bytes, &full[slot], policy);
-      if (base + P >= n) mk_mark_any(p, i, 7);
+      mbar_arrive_expect_tx(&full[slot], pc.bytes0 + pc.bytes1);  // releases slot_off to the consumers
+      if (pc.weights) {
+        mk_mark_any(p, i, 7);
+        bulk_g2s(dst, pc.src0, pc.bytes0, &full[slot], policy);
+        if (pc.bytes1) bulk_g2s(dst + pc.off1, pc.src1, pc.bytes1, &full[slot], policy);
+      } else {
+        if (pc.bytes0) bulk_g2s_plain(dst, pc.src0, pc.bytes0, &full[slot]);
+        if (pc.bytes1) bulk_g2s_plain(dst + pc.off1, pc.src1, pc.bytes1, &full[slot]);
+      }
+      sent_bytes += pc.B;
+      prefetch_to(sent_bytes + kMkPrefetchAhead);
     }
   }
   // Every issued copy lands before the CTA exits.

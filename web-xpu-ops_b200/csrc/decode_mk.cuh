@@ -85,8 +85,8 @@ struct MkParams {
   // trace[(phase * grid + b) * kMkTraceEvents + e]: thread 0 at e = 0 phase
   // start (after the grid barrier), 1 input staged, 2 dot products done
   // (all warps), 3 epilogue done, 4 its first weight stage ready, 5 the
-  // total ns it waited for weight stages in the phase; the producer at 6 / 7
-  // when it issued the phase's first / last stage.  The buffer is zeroed
+  // total ns it waited for weight stages in the phase; the producer at 7
+  // when it issued the phase's last weight piece (6 unused).  The buffer is zeroed
   // before a profiled step; events that did not happen stay 0.
   unsigned long long* trace;
   // shared-memory geometry
