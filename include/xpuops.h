@@ -179,6 +179,23 @@ XPU_API int xpu_fill_normal_f32_dev(float* out, int64_t n, int64_t start, uint64
 
 /* ---- the resident Q8 Llama engine (llm/engine-q8-resident.ts) ---------- */
 
+/* ops/matmul/reference.ts:87-137 `matmulQ8({a, weight, scale, N, M, K})`:
+ * out[t, m] = sum_k a[t, k] * (code[m, k] * scale[m]) with `a` [N, K] f32,
+ * `weight` [M, ceil(K/4)] u32 in matvecQ8's packed layout, `scale` [M] and
+ * `out` [N, M] f32 (ops/matmul/index.ts).  Empty K gives zeros.  Computed on
+ * the tensor cores (tcgen05 kind::i8): each row of `a` is split into four
+ * exact int8 limbs (a rounded to 30 bits below its row maximum) and the
+ * int32 products are recombined in f64; a row of `a` holding NaN or Inf
+ * gives NaN outputs.  Within the reference's tolerance {rel 1e-4, abs 6e-4}.
+ * Host arrays, blocking. */
+XPU_API int xpu_matmul_q8(const float* a, const uint32_t* weight, const float* scale, int64_t N, int64_t M,
+                  int64_t K, float* out);
+/* Device pointers, asynchronous on `stream`.  Rows of `weight` that are whole
+ * 16-byte slots on a 16-byte aligned base take the tensor-core path; other
+ * rows fall back to one matvecQ8 per row of `a`. */
+XPU_API int xpu_matmul_q8_dev(const float* a, const uint32_t* weight, const float* scale, int64_t N, int64_t M,
+                      int64_t K, float* out, void* stream);
+
 /* llm/config.ts:16-56 `LlamaConfig`, field for field (JS numbers -> double). */
 typedef struct xpu_llama_config {
   int32_t num_layers;

@@ -48,6 +48,7 @@ def _declare(L):
     L.or_pack_q8.argtypes = [P, I64, I64, P]
     L.or_pack_int8_rows.argtypes = [P, I64, I64, P]
     L.or_matvec_q8.argtypes = [P, P, P, I64, I64, P]
+    L.or_matmul_q8.argtypes = [P, P, P, I64, I64, I64, P]
     L.or_matvec_q8_rows.argtypes = [P, P, P, I64, I64, I64, I64, P]
     L.or_matvec_q8_mt.argtypes = [P, P, P, I64, I64, P, C.c_int]
     L.or_matvec_q8_absbound.argtypes = [P, P, P, I64, I64, P]
@@ -119,6 +120,14 @@ def matvec_q8(weight, scale, vector, N: int, K: int, threads: int = 1) -> np.nda
     else:
         lib().or_matvec_q8(_p(w), _p(s), _p(x), N, K, _p(y))
     return y
+
+
+def matmul_q8(a, weight, scale, N: int, M: int, K: int) -> np.ndarray:
+    """ops/matmul/reference.ts:87-137 matmulQ8: ``[N, M]`` f32."""
+    av, w, s = _c(a, np.float32), _c(weight, np.uint32), _c(scale, np.float32)
+    out = np.zeros(N * M, np.float32)
+    lib().or_matmul_q8(_p(av), _p(w), _p(s), N, M, K, _p(out))
+    return out.reshape(N, M)
 
 
 def matvec_q8_rows(weight, scale, vector, N: int, K: int, row_begin: int, row_end: int) -> np.ndarray:

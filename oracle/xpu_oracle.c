@@ -116,6 +116,31 @@ void or_matvec_q8(const uint32_t* weight, const float* scale, const float* vecto
   or_matvec_q8_rows(weight, scale, vector, N, K, 0, N, output);
 }
 
+/* ops/matmul/reference.ts:87-137: the weight dequantized into matmul's
+ * [K, M] operand (each element f32(code * scale), :127-131), then the naive
+ * f64-accumulated triple loop of matmul (:34-45). */
+void or_matmul_q8(const float* a, const uint32_t* weight, const float* scale, int64_t N, int64_t M, int64_t K,
+                  float* out) {
+  int64_t words_per_row = (K + 3) / 4;
+  float* b = (float*)malloc((size_t)(K * M > 0 ? K * M : 1) * sizeof(float));
+  for (int64_t row = 0; row < M; ++row) {
+    const double s = (double)scale[row];
+    const uint32_t* w = weight + row * words_per_row;
+    for (int64_t k = 0; k < K; ++k) {
+      uint32_t byte = (w[k >> 2] >> ((k & 3) * 8)) & 0xffu;
+      b[k * M + row] = f32((double)unpack_i8(byte) * s);
+    }
+  }
+  for (int64_t t = 0; t < N; ++t) {
+    for (int64_t col = 0; col < M; ++col) {
+      double sum = 0.0;
+      for (int64_t k = 0; k < K; ++k) sum += (double)a[t * K + k] * (double)b[k * M + col];
+      out[t * M + col] = f32(sum);
+    }
+  }
+  free(b);
+}
+
 typedef struct {
   const uint32_t* w; const float* s; const float* x; int64_t N, K, b, e; float* y;
 } mv_job;

@@ -56,6 +56,12 @@ void or_matvec_q8_ffn(const uint32_t* wg, const float* sg, const uint32_t* wu, c
 void or_matvec_q8_residual(const uint32_t* w, const float* s, const float* vector,
                            const float* residual, int64_t N, int64_t K, float* output);
 /* ops/activation/reference.ts:78-92 (silu only) */
+/* ops/matmul/reference.ts:87-137 matmulQ8: b[k][m] = f32(code[m][k] * scale[m])
+ * (the dequantized-transposed operand), then matmul (:34-45): out[t][m] =
+ * f32(sum_k a[t][k] * b[k][m]) summed in f64, a [N, K], out [N, M]. */
+void or_matmul_q8(const float* a, const uint32_t* weight, const float* scale, int64_t N, int64_t M, int64_t K,
+                  float* out);
+
 void or_silu(const float* input, int64_t n, float* output);
 /* ops/rmsnorm/reference.ts:80-96 */
 void or_rmsnorm(const float* input, const float* weight, int64_t N, int64_t D, double eps,

@@ -255,3 +255,22 @@ def test_tiny_fixture_prefill_then_decode_contract(fixture):
     eng.reset()
     again = eng.forward(fixture["promptTokens"])
     np.testing.assert_array_equal(again, logits)
+
+
+def test_oracle_matmul_q8_definition():
+    """ops/matmul/reference.ts:87-137: b = f32(code * scale) per element, then
+    the f64-accumulated matmul; checked against numpy in f64, plus the empty
+    K case (zeros) and the one-element case."""
+    rng = np.random.default_rng(3)
+    N, M, K = 5, 7, 19
+    a = rng.standard_normal(N * K).astype(np.float32)
+    codes = rng.integers(-127, 128, M * K).astype(np.int32)
+    s = rng.uniform(0.01, 0.2, M).astype(np.float32)
+    w = orc.pack_q8(codes, M, K)
+    b = (codes.reshape(M, K).astype(np.float64) * s.astype(np.float64)[:, None]).astype(np.float32)
+    want = (a.reshape(N, K).astype(np.float64) @ b.T.astype(np.float64)).astype(np.float32)
+    np.testing.assert_array_equal(orc.matmul_q8(a, w, s, N, M, K), want)
+    assert np.all(orc.matmul_q8(np.zeros(0, np.float32), np.zeros(0, np.uint32), s[:5], 3, 5, 0) == 0)
+    one = orc.matmul_q8(np.array([2.0], np.float32), orc.pack_q8(np.array([-3], np.int32), 1, 1),
+                        np.array([0.5], np.float32), 1, 1, 1)
+    assert one.tolist() == [[-3.0]]

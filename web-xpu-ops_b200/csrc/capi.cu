@@ -12,6 +12,8 @@ int pack_q8_dev_i8(const int8_t* codes, int64_t N, int64_t K, uint32_t* packed, 
 int quantize_pack_dev(const float* w, int64_t N, int64_t K, uint32_t* packed, float* scales, cudaStream_t s);
 int fill_normal_dev(float* out, int64_t n, int64_t start, uint64_t seed, double mean, double stdv, double frac,
                     double mul, cudaStream_t s);
+int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s, int64_t N, int64_t M, int64_t K,
+                  float* out, cudaStream_t st);
 
 namespace {
 
@@ -272,6 +274,41 @@ int xpu_fill_normal_f32_dev(float* out, int64_t n, int64_t start, uint64_t seed,
                             double outlier_frac, double outlier_mul, void* stream) {
   XPU_REQUIRE(n >= 0 && start >= 0 && (out || n == 0), XPU_EINVAL, "fill_normal: bad arguments");
   return fill_normal_dev(out, n, start, seed, mean, std, outlier_frac, outlier_mul, (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------------- matmulQ8 --
+int xpu_matmul_q8(const float* a, const uint32_t* weight, const float* scale, int64_t N, int64_t M, int64_t K,
+                  float* out) {
+  XPU_REQUIRE(N >= 0 && M >= 0 && K >= 0, XPU_EINVAL, "matmulQ8: N, M and K must be non-negative, got %lld %lld %lld",
+              (long long)N, (long long)M, (long long)K);
+  if (N == 0 || M == 0) return XPU_OK;
+  XPU_REQUIRE(out && (K == 0 || (a && weight && scale)), XPU_EINVAL, "matmulQ8: null pointer");
+  const int64_t W = (K + 3) / 4, Wp = (W + 3) / 4 * 4;  // rows padded to 16 bytes for the tensor-core path
+  Scratch sc;
+  float *da = nullptr, *ds = nullptr, *dout = nullptr;
+  uint32_t* dw = nullptr;
+  int rc;
+  if ((rc = sc.upload(&da, a, (size_t)(N * K))) || (rc = sc.alloc(&dw, (size_t)(M * Wp))) ||
+      (rc = sc.upload(&ds, scale, (size_t)M)) || (rc = sc.alloc(&dout, (size_t)(N * M))))
+    return rc;
+  if (W > 0) {
+    XPU_TRY_CUDA(cudaMemset(dw, 0, (size_t)(M * Wp) * 4));
+    XPU_TRY_CUDA(cudaMemcpy2D(dw, (size_t)Wp * 4, weight, (size_t)W * 4, (size_t)W * 4, (size_t)M, cudaMemcpyHostToDevice));
+  }
+  if ((rc = matmul_q8_dev(da, dw, Wp, ds, N, M, K, dout, nullptr))) return rc;
+  if ((rc = finish())) return rc;
+  XPU_TRY_CUDA(cudaMemcpy(out, dout, (size_t)(N * M) * 4, cudaMemcpyDeviceToHost));
+  return XPU_OK;
+}
+
+int xpu_matmul_q8_dev(const float* a, const uint32_t* weight, const float* scale, int64_t N, int64_t M, int64_t K,
+                      float* out, void* stream) {
+  XPU_REQUIRE(N >= 0 && M >= 0 && K >= 0, XPU_EINVAL, "matmulQ8: N, M and K must be non-negative, got %lld %lld %lld",
+              (long long)N, (long long)M, (long long)K);
+  if (N == 0 || M == 0) return XPU_OK;
+  XPU_REQUIRE(out && (K == 0 || (a && weight && scale)), XPU_EINVAL, "matmulQ8: null pointer");
+  XPU_REQUIRE(reinterpret_cast<uintptr_t>(weight) % 4 == 0, XPU_EINVAL, "matmulQ8: weight must be 4-byte aligned");
+  return matmul_q8_dev(a, weight, (K + 3) / 4, scale, N, M, K, out, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -1,0 +1,402 @@
+// matmul_q8.cu — matmulQ8 (ops/matmul/reference.ts:87-137) on the 5th-
+// generation tensor cores: out[t, m] = sum_k a[t, k] * (code[m, k] * s[m]),
+// a [N, K] f32, codes [M, ceil(K/4)] u32 (matvecQ8's packed layout, which is
+// byte for byte an int8 [M, 4 ceil(K/4)] matrix), out [N, M] f32.
+//
+// The activations are split, per row t, into four int8 "limbs": with E the
+// exponent of max_k |a[t, k]| (frexp), X = round(a * 2^(30 - E)) is a signed
+// integer below 2^30 in magnitude and X = d0 + 256 d1 + 65536 d2 + 2^24 d3
+// with balanced base-256 digits d_j in [-128, 127].  The products
+// code . d_j are then exact int8 x int8 sums with int32 accumulation —
+// `tcgen05.mma.kind::i8`, D[m, 4 t + j] in TMEM — and the epilogue forms
+// s[m] * 2^(E - 30) * sum_j 256^j D[m, 4 t + j] in f64.  Against the
+// reference (f64 sum of a * f32(code * s)) the only differences are the
+// rounding of a to 30 bits below its row maximum and of code * s to f32,
+// both far inside the reference's own tolerance {rel 1e-4, abs 6e-4}
+// (ops/matmul/q8.wgsl.test.ts).
+//
+// GEMM kernel: one CTA per (128 weight rows, BN limb rows) tile.  Warp 0
+// streams 128-byte K slices of both operands with 2-D TMA (128-byte
+// swizzle) into a 4-stage ring, warp 1 allocates the TMEM accumulator and
+// issues four MMAs (K = 32 bytes each) per stage, and warps 2-5 read the
+// accumulator back (tcgen05.ld) and write the outputs.  Every wait is
+// bounded; after a timeout the CTA still releases its TMEM and drains its
+// copies before it exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <limits.h>
+#include <math.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "matvec_launch.cuh"
+
+namespace xpu {
+namespace {
+
+constexpr int kMmBM = 128;      // weight rows per tile (the MMA's M)
+constexpr int kMmBK = 128;      // K bytes per stage: one 128-byte swizzle row
+constexpr int kMmStages = 4;
+constexpr int kMmLimbs = 4;
+constexpr int kMmThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
+constexpr int kMmNonFinite = INT_MIN;
+
+// ------------------------------------------------------------------ limbs --
+// One CTA per activation row: the row's exponent and its four digit rows
+// limbs[4 t + j][0, Kpad) (zero past K).  A row holding NaN or Inf gets the
+// exponent kMmNonFinite and zero digits; its outputs are NaN.
+__global__ void __launch_bounds__(256) mm_limbs_kernel(const float* __restrict__ a, int64_t K, int64_t Kpad,
+                                                        int8_t* __restrict__ limbs, int* __restrict__ expo) {
+  __shared__ float smax[8];
+  __shared__ int sbad[8];
+  const int64_t t = blockIdx.x;
+  const float* row = a + t * K;
+  float mx = 0.0f;
+  int bad = 0;
+  for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = row[k];
+    bad |= !isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) {
+    smax[warp] = mx;
+    sbad[warp] = bad;
+  }
+  __syncthreads();
+  mx = 0.0f;
+  bad = 0;
+  for (int w = 0; w < (int)blockDim.x / 32; ++w) {
+    mx = fmaxf(mx, smax[w]);
+    bad |= sbad[w];
+  }
+  int E = 0;
+  if (mx > 0.0f) frexp((double)mx, &E);  // mx = f * 2^E, f in [0.5, 1)
+  const double sc = ldexp(1.0, 30 - E);
+  int8_t* d0 = limbs + 4 * t * Kpad;
+  for (int64_t k = threadIdx.x; k < Kpad; k += blockDim.x) {
+    long long X = (!bad && k < K) ? __double2ll_rn((double)row[k] * sc) : 0;
+#pragma unroll
+    for (int j = 0; j < kMmLimbs; ++j) {
+      long long d = X & 255;
+      if (d >= 128) d -= 256;
+      d0[j * Kpad + k] = (int8_t)d;
+      X = (X - d) >> 8;
+    }
+  }
+  if (threadIdx.x == 0) expo[t] = bad ? kMmNonFinite : E;
+}
+
+// ------------------------------------------------------------ tcgen05 GEMM --
+struct MmArgs {
+  const float* scale;
+  const int* expo;
+  float* out;
+  int M, N, nkb, BN;
+  uint32_t idesc, tmem_cols;
+  unsigned int* err;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile written by TMA
+// with 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart
+// (stride byte offset), descriptor version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset
+  d |= (uint64_t)1 << 46;             // version
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kMmThreads, 1)
+    mm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, MmArgs g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kMmStages];
+  __shared__ __align__(8) uint64_t empty[kMmStages];
+  __shared__ __align__(8) uint64_t done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = blockIdx.x * kMmBM, n0 = blockIdx.y * g.BN;
+  const uint32_t a_bytes = kMmBM * kMmBK, stage_bytes = a_bytes + (uint32_t)g.BN * kMmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kMmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                 "r"(g.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int kb = 0;
+      for (; kb < g.nkb && !abort_flag; ++kb) {
+        const int s = kb % kMmStages;
+        if (kb >= kMmStages && !mbar_wait(&empty[s], (uint32_t)(((kb / kMmStages) + 1) & 1), g.err)) {
+          abort_flag = 1;
+          break;
+        }
+        uint8_t* st = smem + (size_t)s * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        tma_load_2d(st, &tmA, kb * kMmBK, m0, &full[s]);
+        tma_load_2d(st + a_bytes, &tmB, kb * kMmBK, n0, &full[s]);
+      }
+      // Every issued copy lands before the CTA moves on.
+      for (int i = (kb > kMmStages ? kb - kMmStages : 0); i < kb; ++i)
+        mbar_wait(&full[i % kMmStages], (uint32_t)((i / kMmStages) & 1), g.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int issued = 0;
+      for (int kb = 0; kb < g.nkb; ++kb) {
+        const int s = kb % kMmStages;
+        if (abort_flag || !mbar_wait(&full[s], (uint32_t)((kb / kMmStages) & 1), g.err)) {
+          abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_addr(smem + (size_t)s * stage_bytes), sb = sa + a_bytes;
+#pragma unroll
+        for (int k4 = 0; k4 < kMmBK / 32; ++k4)
+          tc_mma_i8(tmem, sw128_desc(sa + 32 * k4), sw128_desc(sb + 32 * k4), g.idesc, (kb | k4) != 0);
+        tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        ++issued;
+      }
+      tc_commit(&done);  // arrives when every issued MMA has completed
+      (void)issued;
+    }
+  } else {
+    // ---------------- epilogue: warps 2-5, TMEM lane quarter warp % 4 ----------------
+    const bool ok = mbar_wait(&done, 0, g.err);
+    tc_fence_after();
+    const int q = warp % 4;
+    const int row = m0 + q * 32 + lane;
+    const float s = row < g.M ? g.scale[row] : 0.0f;
+    for (int c0 = 0; c0 < g.BN; c0 += 16) {
+      uint32_t r[16];
+      tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
+      if (!ok || abort_flag) continue;
+#pragma unroll
+      for (int tt = 0; tt < 16 / kMmLimbs; ++tt) {
+        const int t = (n0 + c0) / kMmLimbs + tt;
+        if (t >= g.N || row >= g.M) continue;
+        const int e = g.expo[t];
+        float y;
+        if (e == kMmNonFinite) {
+          y = __int_as_float(0x7fffffff);
+        } else {
+          const double v = (double)(int)r[4 * tt] + 256.0 * (double)(int)r[4 * tt + 1] +
+                           65536.0 * (double)(int)r[4 * tt + 2] + 16777216.0 * (double)(int)r[4 * tt + 3];
+          y = (float)((double)s * ldexp(v, e - 30));
+        }
+        g.out[(int64_t)t * g.M + row] = y;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    // Every MMA has completed before the accumulator is released (the
+    // epilogue saw it already unless its wait timed out).
+    if (lane == 0) mbar_wait(&done, 0, g.err);
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(g.tmem_cols) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------- host --
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// 2-D int8 tensor map over rows x cols bytes (row pitch `pitch`), boxes of
+// box_rows x 128 bytes with 128-byte swizzle; reads past the edges give 0.
+int encode_i8_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t pitch, int box_rows) {
+  auto enc = tensor_map_encoder();
+  XPU_REQUIRE(enc, XPU_ECUDA, "matmulQ8: cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)pitch};
+  const cuuint32_t box[2] = {(cuuint32_t)kMmBK, (cuuint32_t)box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  XPU_REQUIRE(r == CUDA_SUCCESS, XPU_ECUDA, "matmulQ8: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return XPU_OK;
+}
+
+int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+
+// Per-row GEMV fallback for weights whose rows are not whole 16-byte
+// slots (no TMA on such rows): out[t, :] = matvecQ8(a[t, :]) for each t.
+int matmul_q8_rows(const float* a, const uint32_t* w, const float* s, int64_t N, int64_t M, int64_t K, float* out,
+                   cudaStream_t st) {
+  for (int64_t t = 0; t < N; ++t) {
+    MvParams p{};
+    p.w = w;
+    p.s = s;
+    p.x = a + t * K;
+    p.y = out + t * M;
+    p.N = M;
+    p.K = K;
+    int rc = run_matvec(p, EPI_PLAIN, PRO_PLAIN, LaunchOpts{st, false});
+    if (rc) return rc;
+  }
+  return XPU_OK;
+}
+
+}  // namespace
+
+// matmulQ8 with device pointers; weight row m starts at word m * ldw
+// (ldw >= ceil(K/4), words past ceil(K/4) zero).  Rows that are whole
+// 16-byte slots (ldw % 4 == 0) on a 16-byte aligned base take the tensor
+// cores; otherwise ldw must equal ceil(K/4) (matvecQ8's layout) for the
+// per-row path.
+int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s, int64_t N, int64_t M, int64_t K,
+                  float* out, cudaStream_t st) {
+  if (N == 0 || M == 0) return XPU_OK;
+  if (K == 0) {  // the empty sum
+    XPU_TRY_CUDA(cudaMemsetAsync(out, 0, (size_t)(N * M) * 4, st));
+    return XPU_OK;
+  }
+  const int64_t W = ldw;
+  const bool tma_ok = W % 4 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
+  if (!tma_ok) {
+    XPU_REQUIRE(ldw == (K + 3) / 4, XPU_EINVAL, "matmulQ8: rows of %lld words need a 16-byte multiple pitch",
+                (long long)ldw);
+    return matmul_q8_rows(a, w, s, N, M, K, out, st);
+  }
+  XPU_REQUIRE(N <= (INT_MAX / kMmLimbs) && M <= INT_MAX, XPU_EINVAL, "matmulQ8: N=%lld or M=%lld too large",
+              (long long)N, (long long)M);
+  const DeviceInfo& di = device_info();
+  const int64_t N4 = kMmLimbs * N, Kpad = round_up(K, 16);
+  // Limb rows per tile: the largest power-of-two multiple of 16 up to 256
+  // that covers N4, halved while that leaves SMs idle.
+  int BN = 16;
+  while (BN < 256 && BN < N4) BN *= 2;
+  const int64_t mt = (M + kMmBM - 1) / kMmBM;
+  while (BN > 32 && mt * ((N4 + BN - 1) / BN) < di.sm_count) BN /= 2;
+  const int64_t nt = (N4 + BN - 1) / BN;
+
+  int8_t* limbs = nullptr;
+  int* expo = nullptr;
+  XPU_TRY_CUDA(cudaMallocAsync(&limbs, (size_t)(N4 * Kpad), st));
+  cudaError_t ce = cudaMallocAsync(&expo, (size_t)N * sizeof(int), st);
+  if (ce != cudaSuccess) {
+    cudaFreeAsync(limbs, st);
+    return cuda_status(ce, "cudaMallocAsync");
+  }
+  int rc = XPU_OK;
+  CUtensorMap ta, tb;
+  mm_limbs_kernel<<<(unsigned)N, 256, 0, st>>>(a, K, Kpad, limbs, expo);
+  ce = cudaGetLastError();
+  if (ce != cudaSuccess) rc = cuda_status(ce, "mm_limbs_kernel");
+  bool use_tc = false;
+  if (!rc) {
+    // Both maps span whole padded rows (4W and Kpad bytes, multiples of 16):
+    // the bytes past K are zero in both operands, and a row width that is
+    // not a multiple of 16 bytes gave wrong tiles.
+    use_tc = encode_i8_map(&ta, w, M, 4 * W, 4 * W, kMmBM) == XPU_OK &&
+             encode_i8_map(&tb, limbs, N4, Kpad, Kpad, BN) == XPU_OK;
+    if (!use_tc) {  // a shape the tensor-map encoder refuses: the per-row path
+      clear_error();
+      rc = ldw == (K + 3) / 4 ? matmul_q8_rows(a, w, s, N, M, K, out, st)
+                               : (set_error("matmulQ8: tensor map refused for K=%lld", (long long)K), XPU_EINVAL);
+    }
+  }
+  if (!rc && use_tc) {
+    MmArgs g{};
+    g.scale = s;
+    g.expo = expo;
+    g.out = out;
+    g.M = (int)M;
+    g.N = (int)N;
+    g.nkb = (int)((Kpad + kMmBK - 1) / kMmBK);
+    g.BN = BN;
+    // kind::i8 instruction descriptor: int32 accumulator, signed int8 A and
+    // B, both K-major, M = 128, N = BN.
+    g.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kMmBM >> 4) << 24);
+    g.tmem_cols = (uint32_t)std::max(32, BN);
+    g.err = device_error_word();
+    const size_t smem = (size_t)kMmStages * ((size_t)kMmBM * kMmBK + (size_t)BN * kMmBK) + 1024;
+    ce = ensure_smem_attr((const void*)mm_q8_tc_kernel, smem);
+    if (ce == cudaSuccess) {
+      mm_q8_tc_kernel<<<dim3((unsigned)mt, (unsigned)nt), kMmThreads, smem, st>>>(ta, tb, g);
+      ce = cudaGetLastError();
+    }
+    if (ce != cudaSuccess) rc = cuda_status(ce, "mm_q8_tc_kernel");
+  }
+  cudaFreeAsync(expo, st);
+  cudaFreeAsync(limbs, st);
+  return rc;
+}
+
+}  // namespace xpu

@@ -14,7 +14,7 @@ from ._lib import XpuError, XpuInvalidArgument, XpuRangeError, XpuStateError, de
 from .llama import (LLAMA_1B_DECODE_CONFIG, SARASHINA_2_2_1B_CONFIG, TINY_FIXTURE_CONFIG, ForwardProfile,
                     LlamaConfig, LlamaEngineQ8Resident, createForwardProfile, LlamaLayerWeightsQ8, LlamaWeightsQ8, QuantizedLinear, argmax,
                     assertWeightShapesQ8, greedyGenerate)
-from .ops import (DeviceBuffer, matvecQ8, matvecQ8_dev, matvecQ8Ffn, matvecQ8Ffn_dev, matvecQ8Residual,
+from .ops import (DeviceBuffer, matmulQ8, matmulQ8_dev, matvecQ8, matvecQ8_dev, matvecQ8Ffn, matvecQ8Ffn_dev, matvecQ8Residual,
                   matvecQ8Residual_dev, packInt8Rows, packQ8, quantize, quantizePackQ8)
 from .weights_io import buildLlamaWeightsQ8, llamaConfigFromManifest
 

@@ -120,6 +120,8 @@ SIGNATURES = {
     "xpu_matvec_q8_ffn": [P, P, P, P, P, I64, I64, P],
     "xpu_matvec_q8_residual": [P, P, P, P, I64, I64, P],
     "xpu_matvec_q8_dev": [P, P, P, I64, I64, P, P],
+    "xpu_matmul_q8": [P, P, P, I64, I64, I64, P],
+    "xpu_matmul_q8_dev": [P, P, P, I64, I64, I64, P, P],
     "xpu_matvec_q8_ffn_dev": [P, P, P, P, P, I64, I64, P, P],
     "xpu_matvec_q8_residual_dev": [P, P, P, P, I64, I64, P, P],
     "xpu_quantize_dev": [P, I64, I64, P, P, P],

@@ -95,6 +95,25 @@ def matvecQ8(weight, scale, vector, N: int, K: int) -> np.ndarray:
     return y
 
 
+def matmulQ8(a, weight, scale, N: int, M: int, K: int) -> np.ndarray:
+    """ops/matmul/reference.ts:87-137 (ops/matmul/index.ts ``matmulQ8``):
+    ``a`` [N, K] f32 times the packed Q8 weight [M, ceil(K/4)] with per-row
+    ``scale`` [M]; returns ``[N * M]`` f32 (row-major [N, M])."""
+    require_device()
+    av, w, s = _c(a, np.float32), _c(weight, np.uint32), _c(scale, np.float32)
+    _need("matmulQ8: a", av, N * K)
+    _need("matmulQ8: weight", w, M * _words(K))
+    _need("matmulQ8: scale", s, M)
+    out = np.zeros(N * M, np.float32)
+    check(lib().xpu_matmul_q8(_p(av), _p(w), _p(s), N, M, K, _p(out)))
+    return out
+
+
+def matmulQ8_dev(a, weight, scale, N: int, M: int, K: int, out, stream=None) -> None:
+    """Device-pointer form (torch tensors or DeviceBuffer): asynchronous."""
+    check(lib().xpu_matmul_q8_dev(_ptr(a), _ptr(weight), _ptr(scale), N, M, K, _ptr(out), _ptr(stream) or None))
+
+
 def matvecQ8Ffn(weightGate, scaleGate, weightUp, scaleUp, vector, N: int, K: int) -> np.ndarray:
     """ops/matvec/reference.ts:196-207: ``silu(gate) * up``."""
     require_device()
