@@ -13,7 +13,7 @@ int quantize_pack_dev(const float* w, int64_t N, int64_t K, uint32_t* packed, fl
 int fill_normal_dev(float* out, int64_t n, int64_t start, uint64_t seed, double mean, double stdv, double frac,
                     double mul, cudaStream_t s);
 int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s, int64_t N, int64_t M, int64_t K,
-                  float* out, cudaStream_t st);
+                  float* out, const float* residual, cudaStream_t st);
 
 namespace {
 
@@ -295,7 +295,7 @@ int xpu_matmul_q8(const float* a, const uint32_t* weight, const float* scale, in
     XPU_TRY_CUDA(cudaMemset(dw, 0, (size_t)(M * Wp) * 4));
     XPU_TRY_CUDA(cudaMemcpy2D(dw, (size_t)Wp * 4, weight, (size_t)W * 4, (size_t)W * 4, (size_t)M, cudaMemcpyHostToDevice));
   }
-  if ((rc = matmul_q8_dev(da, dw, Wp, ds, N, M, K, dout, nullptr))) return rc;
+  if ((rc = matmul_q8_dev(da, dw, Wp, ds, N, M, K, dout, nullptr, nullptr))) return rc;
   if ((rc = finish())) return rc;
   XPU_TRY_CUDA(cudaMemcpy(out, dout, (size_t)(N * M) * 4, cudaMemcpyDeviceToHost));
   return XPU_OK;
@@ -308,7 +308,7 @@ int xpu_matmul_q8_dev(const float* a, const uint32_t* weight, const float* scale
   if (N == 0 || M == 0) return XPU_OK;
   XPU_REQUIRE(out && (K == 0 || (a && weight && scale)), XPU_EINVAL, "matmulQ8: null pointer");
   XPU_REQUIRE(reinterpret_cast<uintptr_t>(weight) % 4 == 0, XPU_EINVAL, "matmulQ8: weight must be 4-byte aligned");
-  return matmul_q8_dev(a, weight, (K + 3) / 4, scale, N, M, K, out, (cudaStream_t)stream);
+  return matmul_q8_dev(a, weight, (K + 3) / 4, scale, N, M, K, out, nullptr, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -25,6 +25,7 @@
 #include "attention.cuh"
 #include "decode_mk.cuh"
 #include "matvec_launch.cuh"
+#include "prefill.cuh"
 
 namespace xpu {
 
@@ -148,6 +149,12 @@ struct xpu_llama {
   unsigned long long* mk_trace = nullptr;  // profile timestamps, allocated on first use
   unsigned long long* h_trace = nullptr;
   bool trace_valid = false;
+  // batched prefill (prefill.cu): chunks of up to pf_cap prompt tokens
+  bool pf_ok = false;
+  int pf_cap = 0;
+  std::vector<xpu::PrefillLayer> pf_layers;
+  xpu::PrefillArgs pf{};
+  int32_t* pf_tokens = nullptr;
 };
 
 namespace xpu {
@@ -509,6 +516,103 @@ int setup_persistent(xpu_llama* e) {
   return XPU_OK;
 }
 
+// Prepares the batched prefill: per-layer weight views and activation
+// buffers for chunks of up to kPrefillChunk tokens.  Shapes the attention
+// kernel does not take keep the token-by-token prefill.
+constexpr int kPrefillChunk = 512;
+
+int setup_prefill(xpu_llama* e) {
+  const xpu_llama_config& c = e->c;
+  if (prefill_check(c.num_heads, c.num_kv_heads, c.head_dim) != XPU_OK) {
+    clear_error();
+    return XPU_OK;
+  }
+  const int64_t h = c.hidden_size, hd = c.head_dim;
+  const int64_t qd = (int64_t)c.num_heads * hd, kvd = (int64_t)c.num_kv_heads * hd;
+  e->pf_layers.resize(c.num_layers);
+  for (int l = 0; l < c.num_layers; ++l) {
+    const Layer& L = e->layers[l];
+    PrefillLayer& P = e->pf_layers[l];
+    P.attn_norm = L.attn_norm;
+    P.ffn_norm = L.ffn_norm;
+    P.wqkv = L.qkv.w;
+    P.sqkv = L.qkv.s;
+    P.wo = L.wo.w;
+    P.so = L.wo.s;
+    P.wg = L.gate.w;
+    P.sg = L.gate.s;
+    P.wu = L.up.w;
+    P.su = L.up.s;
+    P.wd = L.down.w;
+    P.sd = L.down.s;
+    P.ldw_h = (h + 3) / 4;
+    P.ldw_qd = (qd + 3) / 4;
+    P.ldw_f = ((int64_t)c.ffn_hidden + 3) / 4;
+    P.kcache = L.kcache;
+    P.vcache = L.vcache;
+  }
+  const int cap = std::min(kPrefillChunk, c.max_seq_len);
+  PrefillArgs& a = e->pf;
+  a = PrefillArgs{};
+  a.layer = e->pf_layers.data();
+  a.layers = c.num_layers;
+  a.hidden = (int)h;
+  a.H = c.num_heads;
+  a.kvH = c.num_kv_heads;
+  a.hd = (int)hd;
+  a.ffn = c.ffn_hidden;
+  a.vocab = c.vocab_size;
+  a.S = c.max_seq_len;
+  a.eps = c.rms_norm_eps;
+  a.attn_scale = (float)(1.0 / sqrt((double)hd));
+  a.embed_codes = e->embed_codes;
+  a.embed_scale = e->embed_scale;
+  a.inv_freq = e->inv_freq;
+  const size_t rows = (size_t)cap;
+  int rc;
+  if ((rc = dev_alloc(e, &a.hid, rows * h)) || (rc = dev_alloc(e, &a.hid2, rows * h)) ||
+      (rc = dev_alloc(e, &a.xn, rows * h)) || (rc = dev_alloc(e, &a.qkv, rows * (qd + 2 * kvd))) ||
+      (rc = dev_alloc(e, &a.q, rows * qd)) || (rc = dev_alloc(e, &a.attn, rows * qd)) ||
+      (rc = dev_alloc(e, &a.gate, rows * c.ffn_hidden)) || (rc = dev_alloc(e, &a.up, rows * c.ffn_hidden)) ||
+      (rc = dev_alloc(e, &e->pf_tokens, rows)))
+    return rc;
+  e->pf_cap = cap;
+  e->pf_ok = true;
+  return XPU_OK;
+}
+
+// The prompt tokens[0, n) at positions [base, base + n) in chunks, then
+// the final position's lm_head and argmax (the step's bookkeeping: the next
+// token, gen[base + n - 1], the position base + n).
+int run_prefill(xpu_llama* e, int32_t base, int32_t n) {
+  const xpu_llama_config& c = e->c;
+  int rc;
+  int T = 0;
+  for (int32_t c0 = 0; c0 < n; c0 += e->pf_cap) {
+    T = std::min(e->pf_cap, n - c0);
+    XPU_TRY_CUDA(cudaMemcpyAsync(e->pf_tokens, e->h_tokens + base + c0, (size_t)T * 4, cudaMemcpyHostToDevice,
+                                 e->stream));
+    if ((rc = prefill_chunk(e->pf, e->pf_tokens, T, base + c0, e->stream))) return rc;
+  }
+  MvParams hp{};
+  hp.err = device_error_word();
+  hp.w = e->lm_head.w;
+  hp.s = e->lm_head.s;
+  hp.x = e->pf.hid + (size_t)(T - 1) * c.hidden_size;
+  hp.gamma = e->final_norm;
+  hp.eps = c.rms_norm_eps;
+  hp.y = e->logits;
+  hp.N = c.vocab_size;
+  hp.K = c.hidden_size;
+  if ((rc = run_matvec(hp, EPI_PLAIN, PRO_RMSNORM, LaunchOpts{e->stream, false}))) return rc;
+  e->h_misc[2] = base + n - 1;
+  XPU_TRY_CUDA(cudaMemcpyAsync(e->d_pos, &e->h_misc[2], 4, cudaMemcpyHostToDevice, e->stream));
+  XPU_TRY_CUDA(launch_ex(argmax_kernel, dim3(1), dim3(1024), 0, LaunchOpts{e->stream, false},
+                         (const float*)e->logits, c.vocab_size, e->d_next, e->d_token, e->d_pos, e->d_gen,
+                         c.max_seq_len));
+  return XPU_OK;
+}
+
 // Per-phase entries of the persistent step from the device timestamps of
 // its last launch (MkParams::trace layout).
 void fill_profile_entries(xpu_llama* e, xpu_forward_profile* prof) {
@@ -698,6 +802,7 @@ int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, in
   if ((rc = set_device_pos(e, 0))) return fail(rc);
   if ((rc = build_graph(e))) return fail(rc);
   if ((rc = setup_persistent(e))) return fail(rc);
+  if ((rc = setup_prefill(e))) return fail(rc);
   *out = e;
   return XPU_OK;
 }
@@ -737,7 +842,10 @@ int xpu_llama_forward_profiled(xpu_llama* e, const int32_t* tokens, int32_t n, f
   XPU_REQUIRE(!prof || prof->entries_cap <= 0 || prof->entries, XPU_EINVAL,
               "forward profile: entries_cap > 0 needs an entries array");
   XPU_TRY_CUDA(cudaSetDevice(e->device));
-  const bool breakdown = prof && prof->want_gpu_breakdown && e->path == XPU_DECODE_PERSISTENT;
+  // A multi-token first call is the resident prefill (llm/engine-q8-resident.ts
+  // runPrefillResident): every layer over the whole prompt at once.
+  const bool prefill = e->tokens_so_far == 0 && n > 1 && e->pf_ok;
+  const bool breakdown = prof && prof->want_gpu_breakdown && e->path == XPU_DECODE_PERSISTENT && !prefill;
   const int n_phase = 5 * e->c.num_layers + 1;
   const size_t trace_n = (size_t)n_phase * e->mk_grid * kMkTraceEvents;
   if (breakdown && !e->mk_trace) {
@@ -749,7 +857,11 @@ int xpu_llama_forward_profiled(xpu_llama* e, const int32_t* tokens, int32_t n, f
   memcpy(e->h_tokens + base, tokens, (size_t)n * 4);
   double upload_ms = 0.0;
   const auto t_submit = clk::now();
-  for (int32_t t = 0; t < n; ++t) {
+  if (prefill) {
+    int rc = run_prefill(e, base, n);
+    if (rc) return rc;
+  }
+  for (int32_t t = 0; t < n && !prefill; ++t) {
     const auto tu = clk::now();
     XPU_TRY_CUDA(cudaMemcpyAsync(e->d_token, e->h_tokens + base + t, 4, cudaMemcpyHostToDevice, e->stream));
     upload_ms += ms_since(tu);

@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(256) mm_limbs_kernel(const float* __restrict__
 struct MmArgs {
   const float* scale;
   const int* expo;
+  const float* residual;  // optional [N, M]: out = f32(residual + y)
   float* out;
   int M, N, nkb, BN;
   uint32_t idesc, tmem_cols;
@@ -246,7 +247,8 @@ __global__ void __launch_bounds__(kMmThreads, 1)
                            65536.0 * (double)(int)r[4 * tt + 2] + 16777216.0 * (double)(int)r[4 * tt + 3];
           y = (float)((double)s * ldexp(v, e - 30));
         }
-        g.out[(int64_t)t * g.M + row] = y;
+        const int64_t o = (int64_t)t * g.M + row;
+        g.out[o] = g.residual ? __fadd_rn(g.residual[o], y) : y;
       }
     }
   }
@@ -298,16 +300,17 @@ int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 // Per-row GEMV fallback for weights whose rows are not whole 16-byte
 // slots (no TMA on such rows): out[t, :] = matvecQ8(a[t, :]) for each t.
 int matmul_q8_rows(const float* a, const uint32_t* w, const float* s, int64_t N, int64_t M, int64_t K, float* out,
-                   cudaStream_t st) {
+                   const float* residual, cudaStream_t st) {
   for (int64_t t = 0; t < N; ++t) {
     MvParams p{};
     p.w = w;
     p.s = s;
     p.x = a + t * K;
     p.y = out + t * M;
+    p.residual = residual ? residual + t * M : nullptr;
     p.N = M;
     p.K = K;
-    int rc = run_matvec(p, EPI_PLAIN, PRO_PLAIN, LaunchOpts{st, false});
+    int rc = run_matvec(p, residual ? EPI_RESID : EPI_PLAIN, PRO_PLAIN, LaunchOpts{st, false});
     if (rc) return rc;
   }
   return XPU_OK;
@@ -315,16 +318,20 @@ int matmul_q8_rows(const float* a, const uint32_t* w, const float* s, int64_t N,
 
 }  // namespace
 
-// matmulQ8 with device pointers; weight row m starts at word m * ldw
+// matmulQ8 with device pointers (out = residual + matmulQ8 when `residual`
+// is given); weight row m starts at word m * ldw
 // (ldw >= ceil(K/4), words past ceil(K/4) zero).  Rows that are whole
 // 16-byte slots (ldw % 4 == 0) on a 16-byte aligned base take the tensor
 // cores; otherwise ldw must equal ceil(K/4) (matvecQ8's layout) for the
 // per-row path.
 int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s, int64_t N, int64_t M, int64_t K,
-                  float* out, cudaStream_t st) {
+                  float* out, const float* residual, cudaStream_t st) {
   if (N == 0 || M == 0) return XPU_OK;
   if (K == 0) {  // the empty sum
-    XPU_TRY_CUDA(cudaMemsetAsync(out, 0, (size_t)(N * M) * 4, st));
+    if (residual)
+      XPU_TRY_CUDA(cudaMemcpyAsync(out, residual, (size_t)(N * M) * 4, cudaMemcpyDeviceToDevice, st));
+    else
+      XPU_TRY_CUDA(cudaMemsetAsync(out, 0, (size_t)(N * M) * 4, st));
     return XPU_OK;
   }
   const int64_t W = ldw;
@@ -332,7 +339,7 @@ int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s
   if (!tma_ok) {
     XPU_REQUIRE(ldw == (K + 3) / 4, XPU_EINVAL, "matmulQ8: rows of %lld words need a 16-byte multiple pitch",
                 (long long)ldw);
-    return matmul_q8_rows(a, w, s, N, M, K, out, st);
+    return matmul_q8_rows(a, w, s, N, M, K, out, residual, st);
   }
   XPU_REQUIRE(N <= (INT_MAX / kMmLimbs) && M <= INT_MAX, XPU_EINVAL, "matmulQ8: N=%lld or M=%lld too large",
               (long long)N, (long long)M);
@@ -368,7 +375,7 @@ int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s
              encode_i8_map(&tb, limbs, N4, Kpad, Kpad, BN) == XPU_OK;
     if (!use_tc) {  // a shape the tensor-map encoder refuses: the per-row path
       clear_error();
-      rc = ldw == (K + 3) / 4 ? matmul_q8_rows(a, w, s, N, M, K, out, st)
+      rc = ldw == (K + 3) / 4 ? matmul_q8_rows(a, w, s, N, M, K, out, residual, st)
                                : (set_error("matmulQ8: tensor map refused for K=%lld", (long long)K), XPU_EINVAL);
     }
   }
@@ -376,6 +383,7 @@ int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s
     MmArgs g{};
     g.scale = s;
     g.expo = expo;
+    g.residual = residual;
     g.out = out;
     g.M = (int)M;
     g.N = (int)N;
