@@ -516,6 +516,34 @@ def run_decode(args, torch, world, max_over_ranks, barrier):
             "e2e_host_forward": {"tokens_per_s": round(n_host / (host_ms / 1e3) * world, 1),
                                  "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * c.vocabSize},
         }
+        # Prefill: a 512-token prompt through the batched prefill (tensor-core
+        # matmulQ8 GEMMs), measured on the engine stream; forward() also
+        # returns the final logits to the host.
+        n_prompt = min(512, c.maxSeqLen)
+        prompt = np.random.default_rng(43).integers(0, c.vocabSize, n_prompt).tolist()
+        eng.reset()
+        eng.forward(prompt)  # warm-up (workspace, modules)
+        p_ms, p_wall = [], []
+        for _ in range(3):
+            eng.reset()
+            barrier()
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            w0 = time.perf_counter()
+            d0.record(es)
+            eng.forward(prompt)
+            d1.record(es)
+            d1.synchronize()
+            p_wall.append((time.perf_counter() - w0) * 1e3)
+            p_ms.append(d0.elapsed_time(d1))
+        pms = max_over_ranks(float(np.mean(p_ms)))
+        pwall = max_over_ranks(float(np.mean(p_wall)))
+        out["prefill"] = {
+            "prompt_tokens": n_prompt,
+            "ms": round(pms, 3),
+            "tokens_per_s": round(n_prompt / (pms / 1e3) * world, 1),
+            "e2e_ms": round(pwall, 3),
+            "path": "batched prefill: tcgen05 matmulQ8 GEMMs (int8 weights x int8 activation limbs)",
+        }
         for pth in paths[1:]:
             oms, otoks = res[pth]
             out["persistent_path" if pth == PERSISTENT else "graph_path"] = {
