@@ -84,6 +84,15 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def tensor_cores_serve(torch, M, R, K):
+    """Whether XPU_MATVEC_AUTO sends this stack to the tensor cores: rows of
+    whole 16-byte slots, K <= 65536, and at least eight 128-row tiles per SM
+    (the library's rule; the torch allocation is 16-byte aligned)."""
+    W = (K + 3) // 4
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return W % 4 == 0 and (R * W) % 4 == 0 and K <= 65536 and M * (-(-R // 128)) >= 8 * sms
+
+
 def ncu_traffic(kernel_key: str):
     p = ROOT / "profiles" / "ncu_traffic.json"
     if not p.exists():
@@ -234,11 +243,35 @@ def run_ours(args, rank, world, local):
     bytes_rank = algorithmic_bytes(R, K, M)
     bytes_job = bytes_rank * world
     value = bytes_job * args.steps / (total_ms / 1e3) / 1e9
-    # The contiguous stack runs as one persistent launch per step.
+    # One persistent launch per step over the stack (on the tensor-core path
+    # preceded by the one-CTA limb split, inside the same events).
     avg_launch_s = gemv_ms / 1e3 / args.steps
     achieved = bytes_rank / avg_launch_s / 1e9
     peak, peak_src = measured_peaks()
-    traffic = ncu_traffic(f"mv_bulk_kernel_{R}x{K}")
+    on_tc = tensor_cores_serve(torch, M, R, K)
+    kname = "mv_tc_kernel" if on_tc else "mv_bulk_kernel"
+    traffic = ncu_traffic(f"{kname}_{R}x{K}")
+    launches_per_step = 2 if on_tc else 1
+
+    # The other matvecQ8 path, pinned, on the same stack (comparison only).
+    ops.setMatvecPath(ops.MATVEC_CUDA_CORES if on_tc else ops.MATVEC_TENSOR_CORES)
+    try:
+        for _ in range(2):
+            ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
+        barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        alt_steps = max(3, args.steps // 2)
+        a0.record(stream)
+        for _ in range(alt_steps):
+            ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
+        a1.record(stream)
+        barrier()
+        alt_ms = max_over_ranks(a0.elapsed_time(a1)) / alt_steps
+    finally:
+        ops.setMatvecPath(ops.MATVEC_AUTO)
+    alt = {"path": "cuda_cores (mv_bulk_kernel)" if on_tc else "tensor_cores (mv_tc_kernel)",
+           "value": round(bytes_job / (alt_ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(alt_ms, 4),
+           "steps": alt_steps}
 
     # e2e: host x in, host y out, through the C ABI, per step
     x_host = torch.empty(K, dtype=torch.float32).pin_memory()
@@ -298,12 +331,16 @@ def run_ours(args, rank, world, local):
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                         "traffic": traffic, "kernel": "mv_bulk_kernel (matvecQ8, bulk-copy path): one launch per step over the contiguous stack",
+                         "traffic": traffic,
+                         "kernel": ("mv_tc_kernel (matvecQ8 on tcgen05 tensor cores, x in 8 int8 limbs): one persistent "
+                                    "launch per step over the stack, after mv_limbs8_kernel" if on_tc else
+                                    "mv_bulk_kernel (matvecQ8, bulk-copy path): one launch per step over the contiguous stack"),
                          "launch_ms": round(avg_launch_s * 1e3, 5)},
+            "other_path": alt,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": K * 4,
                     "d2h_bytes_per_step": world * M * R * 4, "ms_per_step": round(e2e_ms / e2e_steps, 4)},
-            "gpu_launches": args.steps * world,
-            "gpu_launches_per_rank": args.steps,
+            "gpu_launches": args.steps * world * launches_per_step,
+            "gpu_launches_per_rank": args.steps * launches_per_step,
             "target_gemv": target,
             "clocks": clocks,
             "cpu_baseline": cpu,

@@ -121,14 +121,35 @@ XPU_API int xpu_matvec_q8_residual_dev(const uint32_t* weight, const float* scal
  * applied to the same x, e.g. every expert or layer slice of a model, or the
  * row shard of each that one GPU holds): matrix m is `weights + m *
  * weight_stride` (u32 words), its scales `scales + m * N`, its output
- * `outputs + m * N`.  Same results as `count` calls of xpu_matvec_q8_dev.
- * A contiguous stack (weight_stride == N * ceil(K/4)) runs as one
- * persistent launch over its count * N rows; otherwise one launch per
- * matrix, consecutive launches overlapping their weight streaming
- * (programmatic dependent launch). */
+ * `outputs + m * N`.  With the CUDA-core path, the same results as `count`
+ * calls of xpu_matvec_q8_dev; a contiguous stack (weight_stride == N *
+ * ceil(K/4)) runs as one persistent launch over its count * N rows, a
+ * strided one as one launch per matrix, consecutive launches overlapping
+ * their weight streaming (programmatic dependent launch).  The tensor-core
+ * path (below) runs any stack it applies to as one persistent launch. */
 XPU_API int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stride,
                                     const float* scales, const float* vector, int64_t count,
                                     int64_t N, int64_t K, float* outputs, void* stream);
+/* matvecQ8 paths of xpu_matvec_q8, xpu_matvec_q8_dev and
+ * xpu_matvec_q8_stack_dev (process-wide; the fused FFN and residual forms
+ * always use the CUDA cores).  No counterpart in the reference, whose
+ * single WGSL kernel sums code * x in f64 per row.
+ *   XPU_MATVEC_CUDA_CORES: f32 partial sums per 16-byte slice, combined in
+ *     f64; within 1e-5 * |scale| * sum|code * x| of the f64 sum.
+ *   XPU_MATVEC_TENSOR_CORES: x split into eight exact int8 limbs (62-bit
+ *     fixed point below its largest magnitude), int8 x int8 MMAs into int32,
+ *     recombined in f64: the f64 sum to within f64 rounding, so the f32
+ *     outputs equal the reference's but for rare ties of the last rounding.
+ *     Used where the weights start on 16 bytes, rows and the stack stride
+ *     are whole 16-byte slots, K <= 65536 and count * N < 2^31; elsewhere
+ *     the CUDA cores serve the call.
+ *   XPU_MATVEC_AUTO (initial): the tensor cores where they apply and the
+ *     call has at least eight 128-row tiles per SM, else the CUDA cores. */
+#define XPU_MATVEC_AUTO          0
+#define XPU_MATVEC_CUDA_CORES    1
+#define XPU_MATVEC_TENSOR_CORES  2
+XPU_API int xpu_set_matvec_path(int32_t path);
+XPU_API int xpu_matvec_path(int32_t* path);
 /* ops/gqa/reference.ts:203-303 `groupedAttention` for one decode query
  * (B = 1, L = 1, causal, queryOffset = s_eff - 1, no mask), as the resident
  * engine runs it each step (llm/engine-q8-resident.ts:1852-1853):

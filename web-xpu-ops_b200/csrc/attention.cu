@@ -291,13 +291,13 @@ extern "C" int xpu_gqa_decode_dev(const float* q, const float* k_cache, const fl
   cudaStream_t st = (cudaStream_t)stream;
   const size_t bytes = gqa_workspace_floats(H, kv_heads, D, nsplit) * sizeof(float);
   float* ws = nullptr;
-  XPU_TRY_CUDA(cudaMallocAsync((void**)&ws, bytes, st));
+  XPU_TRY_CUDA(scratch_alloc((void**)&ws, bytes, st));
   gqa_bind_workspace(a, ws);
   cudaError_t e = cudaMemsetAsync(a.counter, 0, (size_t)kv_heads * sizeof(unsigned int), st);
   if (e == cudaSuccess) rc = launch_gqa_decode(a, LaunchOpts{st, false});
   else rc = cuda_status(e, "cudaMemsetAsync (attention counters)");
-  cudaError_t f = cudaFreeAsync(ws, st);
+  cudaError_t f = scratch_free(ws, st);
   if (rc) return rc;
-  if (f != cudaSuccess) return cuda_status(f, "cudaFreeAsync (attention workspace)");
+  if (f != cudaSuccess) return cuda_status(f, "scratch_free (attention workspace)");
   return XPU_OK;
 }

@@ -151,7 +151,10 @@ static int matvec_host(int epi, const uint32_t* w, const float* sc, const uint32
   p.y = dy;
   p.N = N;
   p.K = K;
-  if ((rc = run_matvec(p, epi, PRO_PLAIN, LaunchOpts{})) || (rc = finish())) return rc;
+  rc = (epi == EPI_PLAIN && matvec_tc_applies(dw, N * W, 1, N, K))
+           ? matvec_tc_dev(dw, N * W, ds, dx, 1, N, K, dy, nullptr)
+           : run_matvec(p, epi, PRO_PLAIN, LaunchOpts{});
+  if (rc || (rc = finish())) return rc;
   XPU_TRY_CUDA(cudaMemcpy(out, dy, (size_t)N * 4, cudaMemcpyDeviceToHost));
   return XPU_OK;
 }
@@ -182,6 +185,8 @@ static int matvec_dev(int epi, const uint32_t* w, const float* sc, const uint32_
   XPU_REQUIRE((w || N * W == 0) && sc && (x || K == 0) && out, XPU_EINVAL, "%s: null pointer", who);
   XPU_REQUIRE(epi != EPI_FFN || ((w2 || N * W == 0) && sc2), XPU_EINVAL, "%s: null pointer", who);
   XPU_REQUIRE(epi != EPI_RESID || residual, XPU_EINVAL, "%s: null residual", who);
+  if (epi == EPI_PLAIN && matvec_tc_applies(w, N * W, 1, N, K))
+    return matvec_tc_dev(w, N * W, sc, x, 1, N, K, out, (cudaStream_t)stream);
   MvParams p{};
   p.w = w;
   p.w2 = w2;
@@ -220,6 +225,9 @@ int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stride, cons
               "matvecQ8 stack: count must be >= 0 and the stride at least N*ceil(K/4) words");
   if (N == 0 || count == 0) return XPU_OK;
   XPU_REQUIRE(weights && scales && vector && outputs, XPU_EINVAL, "matvecQ8 stack: null pointer");
+  // Many 128-row tiles: one persistent tensor-core launch over the stack.
+  if (matvec_tc_applies(weights, weight_stride, count, N, K))
+    return matvec_tc_dev(weights, weight_stride, scales, vector, count, N, K, outputs, (cudaStream_t)stream);
   if (weight_stride == N * ((K + 3) / 4)) {
     // Contiguous stack: the matrices, their scales and their outputs are one
     // [count * N, K] GEMV end to end; one persistent launch streams it all.
@@ -246,6 +254,14 @@ int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stride, cons
     int rc = run_matvec(p, EPI_PLAIN, PRO_PLAIN, LaunchOpts{(cudaStream_t)stream, m > 0});
     if (rc) return rc;
   }
+  return XPU_OK;
+}
+
+int xpu_set_matvec_path(int32_t path) { return set_matvec_path(path); }
+
+int xpu_matvec_path(int32_t* path) {
+  XPU_REQUIRE(path, XPU_EINVAL, "matvec path: null pointer");
+  *path = matvec_path();
   return XPU_OK;
 }
 

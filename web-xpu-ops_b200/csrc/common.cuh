@@ -45,6 +45,13 @@ struct DeviceInfo {
 };
 const DeviceInfo& device_info();  // of the current device (cached per device)
 
+// Stream-ordered scratch for per-call workspaces (limb splits, attention
+// partials): a memory pool of the library's own per device whose freed
+// blocks stay mapped for the next call, so a call after a synchronize does
+// not map fresh memory.  scratch_free() is stream-ordered like cudaFreeAsync.
+cudaError_t scratch_alloc(void** ptr, size_t bytes, cudaStream_t st);
+cudaError_t scratch_free(void* ptr, cudaStream_t st);
+
 // Launch knob shared by every kernel: whether to attach the programmatic
 // stream serialization attribute (PDL) so the kernel may start before its
 // predecessor finishes; kernels call griddep_wait() before reading any

@@ -355,12 +355,11 @@ int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s
 
   int8_t* limbs = nullptr;
   int* expo = nullptr;
-  XPU_TRY_CUDA(cudaMallocAsync(&limbs, (size_t)(N4 * Kpad), st));
-  cudaError_t ce = cudaMallocAsync(&expo, (size_t)N * sizeof(int), st);
-  if (ce != cudaSuccess) {
-    cudaFreeAsync(limbs, st);
-    return cuda_status(ce, "cudaMallocAsync");
-  }
+  // One scratch block: the limb rows (N4 * Kpad bytes, a multiple of 16),
+  // then the row exponents.
+  XPU_TRY_CUDA(scratch_alloc((void**)&limbs, (size_t)(N4 * Kpad) + (size_t)N * sizeof(int), st));
+  expo = reinterpret_cast<int*>(limbs + N4 * Kpad);
+  cudaError_t ce;
   int rc = XPU_OK;
   CUtensorMap ta, tb;
   mm_limbs_kernel<<<(unsigned)N, 256, 0, st>>>(a, K, Kpad, limbs, expo);
@@ -402,8 +401,7 @@ int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s
     }
     if (ce != cudaSuccess) rc = cuda_status(ce, "mm_q8_tc_kernel");
   }
-  cudaFreeAsync(expo, st);
-  cudaFreeAsync(limbs, st);
+  scratch_free(limbs, st);
   return rc;
 }
 

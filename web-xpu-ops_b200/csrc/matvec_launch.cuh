@@ -29,6 +29,18 @@ int launch_mv(const MvParams& p, const MvPlan& plan, const LaunchOpts& o);
 // Plans and launches; the single entry used by the C ABI and the engine.
 int run_matvec(MvParams p, int epi, int pro, const LaunchOpts& o);
 
+// Tensor-core matvecQ8 over `count` same-shaped matrices (matvec_tc.cu).
+// matvec_tc_applies(): the shape and alignment suit it and the process-wide
+// path (set_matvec_path, XPU_MATVEC_*) asks for the tensor cores, or is AUTO
+// and the stack has at least 8 row tiles of 128 per SM.  matvec_tc_dev():
+// matrix m at w + m * mat_stride words, its scales at s + m * N, its outputs
+// at y + m * N.
+int set_matvec_path(int path);
+int matvec_path();
+bool matvec_tc_applies(const uint32_t* w, int64_t mat_stride, int64_t count, int64_t N, int64_t K);
+int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const float* x, int64_t count, int64_t N,
+                  int64_t K, float* y, cudaStream_t st);
+
 // Launch helper: cudaLaunchKernelEx with the PDL attribute when requested.
 template <typename... Args>
 cudaError_t launch_ex(void (*kernel)(Args...), dim3 grid, dim3 block, size_t smem, const LaunchOpts& o,

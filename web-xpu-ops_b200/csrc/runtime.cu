@@ -76,6 +76,43 @@ const DeviceInfo& device_info() {
   return cache.emplace(dev, di).first->second;
 }
 
+static cudaError_t scratch_pool(cudaMemPool_t* pool) {
+  static std::mutex mu;
+  static std::unordered_map<int, cudaMemPool_t> pools;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = pools.find(dev);
+  if (it != pools.end()) {
+    *pool = it->second;
+    return cudaSuccess;
+  }
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = dev;
+  cudaMemPool_t p = nullptr;
+  if ((e = cudaMemPoolCreate(&p, &props)) != cudaSuccess) return e;
+  uint64_t keep = UINT64_MAX;  // never hand freed blocks back at a synchronize
+  if ((e = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep)) != cudaSuccess) {
+    cudaMemPoolDestroy(p);
+    return e;
+  }
+  pools.emplace(dev, p);
+  *pool = p;
+  return cudaSuccess;
+}
+
+cudaError_t scratch_alloc(void** ptr, size_t bytes, cudaStream_t st) {
+  cudaMemPool_t pool;
+  cudaError_t e = scratch_pool(&pool);
+  if (e != cudaSuccess) return e;
+  return cudaMallocFromPoolAsync(ptr, bytes ? bytes : 16, pool, st);
+}
+
+cudaError_t scratch_free(void* ptr, cudaStream_t st) { return ptr ? cudaFreeAsync(ptr, st) : cudaSuccess; }
+
 cudaError_t ensure_smem_attr(const void* kernel, size_t bytes) {
   if (bytes <= 48 * 1024) return cudaSuccess;
   static std::mutex mu;

@@ -14,8 +14,9 @@ from ._lib import XpuError, XpuInvalidArgument, XpuRangeError, XpuStateError, de
 from .llama import (LLAMA_1B_DECODE_CONFIG, SARASHINA_2_2_1B_CONFIG, TINY_FIXTURE_CONFIG, ForwardProfile,
                     LlamaConfig, LlamaEngineQ8Resident, createForwardProfile, LlamaLayerWeightsQ8, LlamaWeightsQ8, QuantizedLinear, argmax,
                     assertWeightShapesQ8, greedyGenerate)
-from .ops import (DeviceBuffer, matmulQ8, matmulQ8_dev, matvecQ8, matvecQ8_dev, matvecQ8Ffn, matvecQ8Ffn_dev, matvecQ8Residual,
-                  matvecQ8Residual_dev, packInt8Rows, packQ8, quantize, quantizePackQ8)
+from .ops import (MATVEC_AUTO, MATVEC_CUDA_CORES, MATVEC_TENSOR_CORES, DeviceBuffer, matmulQ8, matmulQ8_dev, matvecPath,
+                  matvecQ8, matvecQ8_dev, matvecQ8Ffn, matvecQ8Ffn_dev, matvecQ8Residual, matvecQ8Residual_dev,
+                  packInt8Rows, packQ8, quantize, quantizePackQ8, setMatvecPath)
 from .weights_io import buildLlamaWeightsQ8, llamaConfigFromManifest
 
 __all__ = [n for n in dir() if not n.startswith("_")]

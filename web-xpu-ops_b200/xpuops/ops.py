@@ -234,6 +234,28 @@ def matvecQ8Stack_dev(weights, weight_stride: int, scales, vector, count: int, N
                                         _ptr(outputs), _ptr(stream) or None))
 
 
+MATVEC_AUTO = 0
+MATVEC_CUDA_CORES = 1
+MATVEC_TENSOR_CORES = 2
+
+
+def setMatvecPath(path: int) -> None:
+    """Process-wide matvecQ8 path (xpu_set_matvec_path): MATVEC_AUTO, or
+    MATVEC_CUDA_CORES / MATVEC_TENSOR_CORES to pin one where it applies."""
+    check(lib().xpu_set_matvec_path(path))
+
+
+def matvecPath() -> int:
+    out = C.c_int32()
+    check(lib().xpu_matvec_path(C.byref(out)))
+    return out.value
+
+
+def copy_dev(dst, src, nbytes: int, stream=None) -> None:
+    """Device-to-device copy of `nbytes` (xpu_memcpy_d2d)."""
+    check(lib().xpu_memcpy_d2d(_ptr(dst), _ptr(src), nbytes, _ptr(stream) or None))
+
+
 def stream_sync(stream=None) -> None:
     check(lib().xpu_stream_sync(_ptr(stream) or None))
 
