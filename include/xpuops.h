@@ -136,15 +136,17 @@ XPU_API int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stri
  * single WGSL kernel sums code * x in f64 per row.
  *   XPU_MATVEC_CUDA_CORES: f32 partial sums per 16-byte slice, combined in
  *     f64; within 1e-5 * |scale| * sum|code * x| of the f64 sum.
- *   XPU_MATVEC_TENSOR_CORES: x split into eight exact int8 limbs (62-bit
- *     fixed point below its largest magnitude), int8 x int8 MMAs into int32,
- *     recombined in f64: the f64 sum to within f64 rounding, so the f32
- *     outputs equal the reference's but for rare ties of the last rounding.
- *     Used where the weights start on 16 bytes, rows and the stack stride
- *     are whole 16-byte slots, K <= 65536 and count * N < 2^31; elsewhere
- *     the CUDA cores serve the call.
+ *   XPU_MATVEC_TENSOR_CORES: x written exactly as two levels of eight int8
+ *     limbs (every element within 2^100 of the largest), int8 x int8 MMAs
+ *     into int32, recombined in f64: the f64 sum to within f64 rounding, so
+ *     the f32 outputs equal the reference's but for rare ties of the last
+ *     rounding; a vector with NaN/Inf or a wider range takes the
+ *     reference's own f64 loop.  Used where the weights start on 16 bytes,
+ *     rows and the stack stride are whole 16-byte slots and K <= 65536;
+ *     elsewhere the CUDA cores serve the call.
  *   XPU_MATVEC_AUTO (initial): the tensor cores where they apply and the
- *     call has at least eight 128-row tiles per SM, else the CUDA cores. */
+ *     call streams at least 512 MiB of weights, or at least 64 MiB with
+ *     K >= 16384; else the CUDA cores. */
 #define XPU_MATVEC_AUTO          0
 #define XPU_MATVEC_CUDA_CORES    1
 #define XPU_MATVEC_TENSOR_CORES  2

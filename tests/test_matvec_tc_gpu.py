@@ -1,11 +1,14 @@
 """matvecQ8 on the tensor cores (XPU_MATVEC_TENSOR_CORES) against the oracle.
 
-The vector is split into eight exact int8 limbs and the dot products are
-exact int32 MMAs recombined in f64, so the outputs are the reference's f64 sum
+The vector is written exactly as two levels of eight int8 limbs (any element
+within 2^100 of the largest) and the dot products are exact int32 MMAs
+recombined in f64, so the outputs are the reference's f64 sum
 (ops/matvec/reference.ts:117-131) to f64 rounding: within 1e-9 * |scale| *
 sum|code * x| plus one f32 rounding of the result, NaN and Inf where the
 reference has them, and equal to the oracle's f32 output in all but rare
-last-rounding ties.
+last-rounding ties.  Vectors beyond that range (or non-finite) take the
+reference's own f64 loop and equal the oracle bit for bit.  Work is split
+stream-K, so small shapes here split every row tile across many CTAs.
 """
 import numpy as np
 import pytest
@@ -60,11 +63,12 @@ def _stack(mats, x, N, K, stride):
 
 
 @pytest.mark.parametrize("N,K", [(128, 16), (5, 1024), (64, 8192), (200, 112), (129, 2048), (1000, 4096),
-                                 (3, 65536)])
+                                 (3, 65536), (256, 65536), (1000, 2048), (20000, 528)])
 def test_single_gemv_shapes(tc, N, K):
     """Partial row tiles (N < 128, N % 128 != 0), K from one 16-byte slot to
     the largest the int32 accumulator takes, K not a multiple of the 128-byte
-    stage."""
+    slice or the 4-slice stage; few tiles (each split over up to 148 CTAs,
+    combined by ticket) and many."""
     w, s = _synth(N, K, 40 + K, outlier_frac=0.001)
     x = fill_normal(K, 41 + K)
     dw, ds, dx = ops.DeviceBuffer.from_numpy(w), ops.DeviceBuffer.from_numpy(s), ops.DeviceBuffer.from_numpy(x)
@@ -127,6 +131,35 @@ def test_full_code_range_at_max_k(tc):
     w = orc.pack_q8(codes, N, K)
     s = fill_normal(N, 6, 0.0, 0.01)
     tc_check(xpuops.matvecQ8(w, s, x, N, K), w, s, x, N, K)
+
+
+def test_large_elements_against_zero_codes(tc):
+    """Elements 2^40 .. 2^90 above the rest meet zero codes: the result is
+    carried by the small elements, which only the second limb level holds
+    exactly (one 62-bit level would round them away)."""
+    N, K = 512, 4096
+    rng = np.random.default_rng(21)
+    codes = rng.integers(-127, 128, (N, K)).astype(np.int32)
+    big = rng.choice(K, 64, replace=False)
+    codes[:, big] = 0
+    w = orc.pack_q8(codes.ravel(), N, K)
+    s = fill_normal(N, 22, 0.0, 0.01)
+    for span in (40.0, 70.0, 90.0):
+        x = fill_normal(K, 23)
+        x[big] = (2.0 ** span * rng.choice([-1.0, 1.0], big.size)).astype(np.float32)
+        tc_check(xpuops.matvecQ8(w, s, x, N, K), w, s, x, N, K)
+
+
+def test_dynamic_range_beyond_two_levels_takes_the_reference_loop(tc):
+    """An element more than 2^100 below the largest: every row takes the
+    reference's f64 loop, bit-identical to the oracle."""
+    N, K = 300, 1024
+    w, s = _synth(N, K, 24)
+    x = fill_normal(K, 25)
+    x[7] = np.float32(2.0 ** 80)
+    x[9] = np.float32(2.0 ** -30)
+    y = xpuops.matvecQ8(w, s, x, N, K)
+    np.testing.assert_array_equal(y, orc.matvec_q8(w, s, x, N, K))
 
 
 def test_nonfinite_vector_propagates_like_the_reference(tc):
@@ -197,12 +230,9 @@ def test_unaligned_weights_take_the_cuda_cores(tc):
 
 
 def test_path_switch_and_auto_policy():
-    """XPU_MATVEC_AUTO keeps small calls on the CUDA cores and sends stacks of
-    at least eight 128-row tiles per SM to the tensor cores (bit-identical to
-    the pinned paths); unknown paths are refused."""
-    import torch
-
-    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    """XPU_MATVEC_AUTO keeps small calls on the CUDA cores and sends large
+    ones (here 96 MiB of rows of 16384 codes) to the tensor cores,
+    bit-identical to the pinned paths; unknown paths are refused."""
     assert ops.matvecPath() == ops.MATVEC_AUTO
     with pytest.raises(xpuops.XpuInvalidArgument, match="unknown path"):
         ops.setMatvecPath(3)
@@ -216,18 +246,30 @@ def test_path_switch_and_auto_policy():
             out[p] = xpuops.matvecQ8(w, s, x, N, K)
         np.testing.assert_array_equal(out[ops.MATVEC_AUTO], out[ops.MATVEC_CUDA_CORES])
         assert not np.array_equal(out[ops.MATVEC_TENSOR_CORES], out[ops.MATVEC_CUDA_CORES])
-        tiles_per_mat = 125
-        M = -(-8 * sms // tiles_per_mat)
-        N2, K2 = 128 * tiles_per_mat, 64
-        mats = [_synth(N2, K2, 600 + m) for m in range(M)]
-        x2 = fill_normal(K2, 699)
+        M, N2, K2 = 3, 2048, 16384  # 96 MiB of weights, long rows
+        W2 = K2 // 4
+        dw, ds = ops.DeviceBuffer(4 * M * N2 * W2), ops.DeviceBuffer(4 * M * N2)
+        f = ops.DeviceBuffer(4 * N2 * K2)
+        for m in range(M):
+            ops.fill_normal_dev(f, N2 * K2, 800 + m, 0.0, 0.02)
+            ops.quantizePackQ8_dev(f, N2, K2, dw.ptr + 4 * m * N2 * W2, ds.ptr + 4 * m * N2)
+        f.free()
+        x2 = fill_normal(K2, 899)
+        dx, dy = ops.DeviceBuffer.from_numpy(x2), ops.DeviceBuffer(4 * M * N2)
         stack = {}
         for p in (ops.MATVEC_AUTO, ops.MATVEC_CUDA_CORES, ops.MATVEC_TENSOR_CORES):
             ops.setMatvecPath(p)
-            stack[p] = _stack(mats, x2, N2, K2, N2 * K2 // 4)
+            ops.matvecQ8Stack_dev(dw, N2 * W2, ds, dx, M, N2, K2, dy)
+            ops.stream_sync()
+            stack[p] = dy.download(np.float32, M * N2)
         np.testing.assert_array_equal(stack[ops.MATVEC_AUTO], stack[ops.MATVEC_TENSOR_CORES])
+        all_w, all_s = dw.download(np.uint32, M * N2 * W2), ds.download(np.float32, M * N2)
         for m in (0, M - 1):
-            tc_check(stack[ops.MATVEC_AUTO][m], mats[m][0], mats[m][1], x2, N2, K2)
+            wm, sm = all_w[m * N2 * W2:(m + 1) * N2 * W2], all_s[m * N2:(m + 1) * N2]
+            tc_check(stack[ops.MATVEC_AUTO][m * N2:(m + 1) * N2], wm, sm, x2, N2, K2)
+            assert matvec_within_bound(stack[ops.MATVEC_CUDA_CORES][m * N2:(m + 1) * N2],
+                                       stack[ops.MATVEC_TENSOR_CORES][m * N2:(m + 1) * N2],
+                                       orc.matvec_q8_bound(wm, sm, x2, N2, K2)) is None
     finally:
         ops.setMatvecPath(ops.MATVEC_AUTO)
 

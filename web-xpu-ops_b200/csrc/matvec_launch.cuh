@@ -32,7 +32,8 @@ int run_matvec(MvParams p, int epi, int pro, const LaunchOpts& o);
 // Tensor-core matvecQ8 over `count` same-shaped matrices (matvec_tc.cu).
 // matvec_tc_applies(): the shape and alignment suit it and the process-wide
 // path (set_matvec_path, XPU_MATVEC_*) asks for the tensor cores, or is AUTO
-// and the stack has at least 8 row tiles of 128 per SM.  matvec_tc_dev():
+// and the call is large (512 MiB of weights, or 64 MiB with K >= 16384).
+// matvec_tc_dev():
 // matrix m at w + m * mat_stride words, its scales at s + m * N, its outputs
 // at y + m * N.
 int set_matvec_path(int path);

@@ -1,27 +1,39 @@
 // matvec_tc.cu — matvecQ8 (ops/matvec/reference.ts:117-131) on the 5th-
-// generation tensor cores, for GEMVs and stacks of GEMVs with many 128-row
-// tiles (the benchmark's 80 x [28672 x 8192] stack).
+// generation tensor cores: single GEMVs and stacks of GEMVs on one vector.
 //
-// y[n] = f32((sum_k code[n, k] x[k]) * scale[n]).  The vector is split into
-// eight int8 limbs: with E the frexp exponent of max_k |x[k]|,
-// X = round(x * 2^(62 - E)) (exact for every x within 2^-38 of the maximum)
-// = sum_j 256^j d_j with balanced digits d_j in [-128, 127].  The packed
-// weight is an int8 [N, 4W] K-major matrix, so one `tcgen05.mma.kind::i8`
-// with M = 128 weight rows and N = 8 limb rows gives D[n, j] =
-// sum_k code[n, k] d_j[k] exactly in int32, and the epilogue forms
-// sum_j 256^j D[n, j] * 2^(E - 62) in f64: the dot product to f64 precision
-// (the reference sums in f64), then one multiply by the scale and one f32
-// rounding.  A vector holding NaN or Inf makes every row take the
-// reference's own f64 loop, so 0 * Inf = NaN propagates as it does there.
+// y[n] = f32((sum_k code[n, k] x[k]) * scale[n]).  The vector is written as
+// exact integers in two levels of eight int8 limbs.  With E the frexp
+// exponent of max_k |x[k]|, level one holds X1 = round(x * 2^(62 - E)) and
+// level two the remainder exactly, X2 = (x * 2^(62 - E) - X1) * 2^62, so
+//   x = 2^(E - 62) * (X1 + 2^-62 * X2)
+// for every x whose frexp exponent is at least E - 100 (a 24-bit mantissa
+// then has no bits below 2^(E - 124)).  X1 and X2 each split into balanced
+// base-256 digits d_j in [-128, 127]: the bytes of (X + 0x80..80) with their
+// top bits flipped.  The packed weight is an int8 [N, 4W] K-major matrix, so
+// one `tcgen05.mma.kind::i8` with M = 128 weight rows and N = 16 limb rows
+// gives D[n, j] = sum_k code[n, k] d_j[k] exactly in int32 (|D| <= 2^30 for
+// K <= 65536), and the epilogue forms
+//   2^(E - 62) * (sum_j 256^j D[n, j] + 2^-62 * sum_j 256^j D[n, 8 + j])
+// in f64: the exact dot product to f64 rounding (the reference sums in f64),
+// then one multiply by the scale and one f32 rounding.  A vector holding NaN
+// or Inf, or an element more than 2^100 below the largest, makes every row
+// take the reference's own f64 loop instead (0 * Inf = NaN as there).
 //
-// Kernel: persistent, one CTA per SM; tile = 128 rows of one matrix over the
-// whole K.  Warp 0 streams the tile through a ring of stages, each holding G
-// consecutive 128-byte K slices of its 128 rows (TMA boxes of the 3-D weight
-// stack, 128-byte swizzle) and the matching slices of the limbs, so every row
-// is read G * 128 contiguous bytes at a time; warp 1 issues four MMAs per
-// slice into one of two TMEM accumulators; warps 2-5 read a finished
-// accumulator (tcgen05.ld), free it, and write the tile's outputs,
-// overlapping the next tile's MMAs.  Every wait is bounded.
+// Kernel (persistent, one CTA per SM, 192 threads):
+//   warp 0      TMA producer: 128-row x 128-byte weight slices (3-D box of
+//               the weight stack, 128-byte swizzle), four slices per stage,
+//               so every row is read 512 contiguous bytes at a time;
+//   warp 1      TMEM owner and MMA issuer: four MMAs per slice into one of
+//               two accumulators (double-buffered across segments);
+//   warps 2-5   compute the stage's limb slices from x straight into shared
+//               memory in the swizzled K-major layout, and run the epilogue:
+//               read a finished accumulator (tcgen05.ld), free it, write y.
+// Work is split stream-K: the (tile, slice) units of all tiles are divided
+// evenly over the CTAs, so a CTA's range is a sequence of segments (slices
+// [lo, hi) of one 128-row tile).  A tile split between CTAs combines the
+// exact int32 partial accumulators of its contributors: each writes its
+// partial to global memory and takes a ticket; the last arrival sums them
+// (in CTA order) and writes the outputs.  Every wait is bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <limits.h>
@@ -36,94 +48,77 @@
 namespace xpu {
 namespace {
 
-constexpr int kTcBM = 128;
-constexpr int kTcBK = 128;
-constexpr int kTcLimbs = 8;
-constexpr int kTcThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
-constexpr int kTcNonFinite = INT_MIN;
-constexpr uint32_t kTcSliceA = kTcBM * kTcBK;     // 16 KB of weights per slice
-constexpr uint32_t kTcSliceB = kTcLimbs * kTcBK;  // 1 KB of limbs per slice
-constexpr uint32_t kTcRingBytes = 12 * (kTcSliceA + kTcSliceB);  // 204 KB
-constexpr uint32_t kTcTmemCols = 32;  // two accumulators of 8 columns, 16 apart
-constexpr int kTcMaxStages = 12;
+constexpr int kTcBM = 128;                 // weight rows per tile (MMA M)
+constexpr int kTcBK = 128;                 // bytes (codes) per slice
+constexpr int kTcLimbs = 16;               // two levels of eight limbs (MMA N)
+constexpr int kTcG = 4;                    // slices per stage
+constexpr int kTcStages = 3;
+constexpr int kTcThreads = 192;
+constexpr int kTcWriters = 128;            // warps 2-5
+constexpr uint32_t kTcSliceA = kTcBM * kTcBK;      // 16 KB
+constexpr uint32_t kTcSliceB = kTcLimbs * kTcBK;   // 2 KB
+constexpr uint32_t kTcStageA = kTcG * kTcSliceA;   // weights of a stage
+constexpr uint32_t kTcStageBytes = kTcG * (kTcSliceA + kTcSliceB);  // 72 KB
+constexpr uint32_t kTcTmemCols = 32;       // two accumulators of 16 columns
+constexpr int kTcBarWriters = 1;           // named barrier of warps 2-5
+constexpr int kTcFlagNonFinite = 1;
+constexpr int kTcFlagInexact = 2;
+constexpr uint64_t kDigitBias = 0x8080808080808080ull;
+constexpr int64_t kTcMinUnits = 8;       // slices per CTA at least (small GEMVs)
 
-// Stage geometry for G slices per stage: A slices [G][128 rows][128 B], then
-// B slices [G][8 limbs][128 B], every slice 1024-byte aligned.
-template <int G>
-struct TcStage {
-  static constexpr uint32_t kBytes = G * (kTcSliceA + kTcSliceB);
-  static constexpr int kStages = (int)(kTcRingBytes / kBytes);
-  static_assert(kStages >= 2 && kStages <= kTcMaxStages, "ring of at least two stages");
-};
-
-// ------------------------------------------------------------------ limbs --
-// One CTA: the vector's exponent (or kTcNonFinite) and its eight digit rows
-// limbs[j][0, Kpad) (zero past K).
-__global__ void __launch_bounds__(1024) mv_limbs8_kernel(const float* __restrict__ x, int64_t K, int64_t Kpad,
-                                                         int8_t* __restrict__ limbs, int* __restrict__ expo) {
-  __shared__ float smax[32];
-  __shared__ int sbad[32];
-  griddep_launch_dependents();  // the GEMV may start streaming weights now
-  float mx = 0.0f;
-  int bad = 0;
-  for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-    const float v = x[k];
-    bad |= !isfinite(v);
-    mx = fmaxf(mx, fabsf(v));
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
-  }
-  if (threadIdx.x % 32 == 0) {
-    smax[threadIdx.x / 32] = mx;
-    sbad[threadIdx.x / 32] = bad;
-  }
-  __syncthreads();
-  mx = 0.0f;
-  bad = 0;
-  for (int w = 0; w < (int)blockDim.x / 32; ++w) {
-    mx = fmaxf(mx, smax[w]);
-    bad |= sbad[w];
-  }
-  int E = 0;
-  if (mx > 0.0f) frexp((double)mx, &E);
-  const double sc = ldexp(1.0, 62 - E);
-  for (int64_t k = threadIdx.x; k < Kpad; k += blockDim.x) {
-    long long X = (!bad && k < K) ? __double2ll_rn((double)x[k] * sc) : 0;
-#pragma unroll
-    for (int j = 0; j < kTcLimbs; ++j) {
-      long long d = X & 255;
-      if (d >= 128) d -= 256;
-      limbs[j * Kpad + k] = (int8_t)d;
-      X = (X - d) >> 8;
-    }
-  }
-  if (threadIdx.x == 0) *expo = bad ? kTcNonFinite : E;
-}
-
-// ------------------------------------------------------------------ GEMV --
 struct TcArgs {
-  const uint32_t* w;  // for the reference loop of a non-finite vector
+  const uint32_t* w;
   const float* x;
   const float* s;
-  const int* expo;
   float* y;
+  int4* part;            // [grid][2][128 rows][4 x int4]: split-tile partials
+  unsigned int* ticket;  // [grid], zeroed by mv_xstat_kernel
+  const float4* stats;   // [nstats] per-block (max |x|, min nonzero |x|, non-finite, -)
   int64_t ldw, mat_stride, s_stride, y_stride;
-  int N, K, count, tiles_per_mat, n_tiles;
-  int nkb;     // stages per tile
-  int slices;  // 128-byte slices per row, ceil(4W / 128)
+  int64_t total;  // n_tiles * S units
+  int N, K, tiles_per_mat, S, nstats;
   uint32_t idesc;
   unsigned int* err;
 };
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
-      : "memory");
+// ----------------------------------------------------------- stream-K map --
+// CTA b owns units [first_unit(b), first_unit(b + 1)); unit u is slice
+// u % S of tile u / S.
+__device__ __forceinline__ int64_t first_unit(int64_t b, int64_t total, int64_t grid) { return b * total / grid; }
+// The CTA whose range holds unit u.
+__device__ __forceinline__ int64_t owner_of(int64_t u, int64_t total, int64_t grid) {
+  return ((u + 1) * grid + total - 1) / total - 1;
 }
+
+struct Seg {
+  int64_t tile;
+  int lo, hi;  // slices of the tile
+  bool whole;
+};
+struct SegCursor {
+  int64_t u0, u1, t0, nseg;
+  int S;
+  __device__ void init(const TcArgs& g) {
+    const int64_t grid = gridDim.x;
+    u0 = first_unit(blockIdx.x, g.total, grid);
+    u1 = first_unit(blockIdx.x + 1, g.total, grid);
+    S = g.S;
+    t0 = u0 / S;
+    nseg = u1 > u0 ? (u1 - 1) / S - t0 + 1 : 0;
+  }
+  __device__ Seg get(int64_t j) const {
+    Seg s;
+    s.tile = t0 + j;
+    const int64_t base = s.tile * S;
+    s.lo = (int)(max(u0, base) - base);
+    s.hi = (int)(min(u1, base + S) - base);
+    s.whole = s.lo == 0 && s.hi == S;
+    return s;
+  }
+};
+__device__ __forceinline__ int seg_stages(const Seg& s) { return (s.hi - s.lo + kTcG - 1) / kTcG; }
+
+// ------------------------------------------------------------------- PTX --
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
@@ -131,8 +126,10 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
-
-// K-major SW128 shared-memory descriptor (see matmul_q8.cu).
+// K-major, 128-byte-swizzled shared-memory matrix descriptor: rows of 128
+// bytes, 8-row groups 1024 bytes apart (start address in 16-byte units,
+// leading offset 1 (unused when swizzled), stride offset 1024 bytes,
+// descriptor version 1, layout SWIZZLE_128B).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)1 << 16;
@@ -155,37 +152,135 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                : "memory");
 }
-__device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, int (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// Generic-proxy shared-memory writes made visible to the tensor cores.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-template <int G>
+// ---------------------------------------------------------------- limbs --
+// The two 8-digit limb words of one vector element (digit j in byte j).
+struct LimbPair {
+  uint64_t l1, l2;
+};
+__device__ __forceinline__ LimbPair limbs_of(float x, double sc1) {
+  const double y = (double)x * sc1;  // exact: a power-of-two scaling, |y| < 2^62
+  const long long X1 = __double2ll_rn(y);
+  const double r = y - (double)X1;   // exact, |r| <= 1/2
+  const long long X2 = __double2ll_rn(r * 4611686018427387904.0);  // r * 2^62
+  LimbPair p;
+  p.l1 = ((uint64_t)X1 + kDigitBias) ^ kDigitBias;
+  p.l2 = ((uint64_t)X2 + kDigitBias) ^ kDigitBias;
+  return p;
+}
+// Byte j (0..3) of four words, as one word (byte i from word i).
+__device__ __forceinline__ uint32_t gather_byte(uint32_t a, uint32_t b, uint32_t c, uint32_t d, int j) {
+  const uint32_t sel = (uint32_t)j | ((uint32_t)(4 + j) << 4);
+  return __byte_perm(__byte_perm(a, b, sel), __byte_perm(c, d, sel), 0x5410u);
+}
+__device__ __forceinline__ uint32_t half_word(uint64_t v, int j) { return j < 4 ? (uint32_t)v : (uint32_t)(v >> 32); }
+
+// Writes the 16 limb rows of columns [4 * lane, 4 * lane + 4) of one slice
+// (vector elements k0 .. k0 + 3, zero past K) into the slice's K-major SW128
+// tile: byte (row r, column c) at (r / 8) * 1024 + (r % 8) * 128 +
+// ((c / 16) ^ (r % 8)) * 16 + c % 16.
+__device__ __forceinline__ void write_limb_columns(uint8_t* tile, const float* __restrict__ x, int64_t k0, int K,
+                                                   double sc1, int lane) {
+  LimbPair p[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = limbs_of(k0 + i < K ? x[k0 + i] : 0.0f, sc1);
+  const uint32_t chunk = (uint32_t)lane >> 2, within = ((uint32_t)lane & 3u) * 4u;
+#pragma unroll
+  for (int r = 0; r < kTcLimbs; ++r) {
+    const int j = r & 7;
+    const uint64_t v0 = r < 8 ? p[0].l1 : p[0].l2, v1 = r < 8 ? p[1].l1 : p[1].l2;
+    const uint64_t v2 = r < 8 ? p[2].l1 : p[2].l2, v3 = r < 8 ? p[3].l1 : p[3].l2;
+    const uint32_t word =
+        gather_byte(half_word(v0, j), half_word(v1, j), half_word(v2, j), half_word(v3, j), j & 3);
+    const uint32_t off =
+        (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u + ((chunk ^ (uint32_t)(r & 7)) << 4) + within;
+    *reinterpret_cast<uint32_t*>(tile + off) = word;
+  }
+}
+
+// ----------------------------------------------------------- vector stats --
+// Block b of `gridDim.x`: the largest and smallest nonzero magnitudes and
+// the finiteness of its share of x, into stats[b]; block 0 also zeroes the
+// GEMV's tickets.  The GEMV (a programmatic dependent launch) starts
+// streaming weights meanwhile and reads these after griddepcontrol.wait.
+constexpr int kStatThreads = 256;
+__global__ void __launch_bounds__(kStatThreads) mv_xstat_kernel(const float* __restrict__ x, int K,
+                                                                float4* __restrict__ stats,
+                                                                unsigned int* __restrict__ ticket, int nticket) {
+  griddep_launch_dependents();
+  __shared__ float smx[kStatThreads / 32], smn[kStatThreads / 32];
+  __shared__ int sbad[kStatThreads / 32];
+  const int64_t k0 = (int64_t)blockIdx.x * K / gridDim.x, k1 = (int64_t)(blockIdx.x + 1) * K / gridDim.x;
+  float mx = 0.0f, mn = INFINITY;
+  int bad = 0;
+  for (int64_t k = k0 + threadIdx.x; k < k1; k += kStatThreads) {
+    const float v = x[k];
+    bad |= !isfinite(v);
+    const float a = fabsf(v);
+    mx = fmaxf(mx, a);
+    if (a > 0.0f) mn = fminf(mn, a);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+  }
+  if (threadIdx.x % 32 == 0) {
+    smx[threadIdx.x / 32] = mx;
+    smn[threadIdx.x / 32] = mn;
+    sbad[threadIdx.x / 32] = bad;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kStatThreads / 32; ++w) {
+      mx = fmaxf(mx, smx[w]);
+      mn = fminf(mn, smn[w]);
+      bad |= sbad[w];
+    }
+    stats[blockIdx.x] = make_float4(mx, mn, bad ? 1.0f : 0.0f, 0.0f);
+  }
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nticket; i += kStatThreads) ticket[i] = 0u;
+}
+
+// ---------------------------------------------------------------- kernel --
 __global__ void __launch_bounds__(kTcThreads, 1)
-    mv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcArgs g) {
-  constexpr int kStages = TcStage<G>::kStages;
-  constexpr uint32_t kStageBytes = TcStage<G>::kBytes;
+    mv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ TcArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t full[kStages];
-  __shared__ __align__(8) uint64_t empty[kStages];
+  __shared__ __align__(8) uint64_t full[kTcStages];    // weights landed (TMA)
+  __shared__ __align__(8) uint64_t bready[kTcStages];  // limbs written (4 warps)
+  __shared__ __align__(8) uint64_t empty[kTcStages];   // stage consumed (MMA commit)
   __shared__ __align__(8) uint64_t tfull[2];
   __shared__ __align__(8) uint64_t tempty[2];
   __shared__ __align__(8) uint64_t done;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
+  __shared__ float red_max[4], red_min[4];
+  __shared__ int red_bad[4];
+  __shared__ volatile int s_flag;  // warps 2-5: one thread's result for all
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&bready[s], 4);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&tempty[b], 4);
     }
     mbar_init(&done, 1);
     abort_flag = 0;
@@ -201,129 +296,256 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  SegCursor cur;
+  cur.init(g);
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      // The weight slices of the first ring of stages go out at once; their
-      // limb slices, written by the preceding limb kernel (programmatic
-      // dependent launch), after griddepcontrol.wait.
-      int pend_kb[kStages], pend_n[kStages];
-      int npend = 0;
-      bool limbs_ready = false;
-      auto load_limbs = [&](int s, int kb, int n) {
-        uint8_t* sb = smem + (size_t)s * kStageBytes + G * kTcSliceA;
-        for (int j = 0; j < n; ++j) tma_load_2d(sb + j * kTcSliceB, &tmB, (kb * G + j) * kTcBK, 0, &full[s]);
-      };
-      auto flush = [&]() {
-        griddep_wait();
-        for (int i = 0; i < npend; ++i) load_limbs(i, pend_kb[i], pend_n[i]);
-        limbs_ready = true;
-      };
+      // ---------------- TMA producer: weights ----------------
       int64_t it = 0;
-      for (int t = blockIdx.x; t < g.n_tiles && !abort_flag; t += gridDim.x) {
-        const int mi = t / g.tiles_per_mat, rt = t - mi * g.tiles_per_mat;
-        for (int kb = 0; kb < g.nkb && !abort_flag; ++kb, ++it) {
-          const int s = (int)(it % kStages);
-          if (it >= kStages && !mbar_wait(&empty[s], (uint32_t)(((it / kStages) + 1) & 1), g.err)) {
+      for (int64_t j = 0; j < cur.nseg && !abort_flag; ++j) {
+        const Seg sg = cur.get(j);
+        const int mi = (int)(sg.tile / g.tiles_per_mat), rt = (int)(sg.tile % g.tiles_per_mat);
+        bool ok = true;
+        for (int c = sg.lo; c < sg.hi; c += kTcG, ++it) {
+          const int s = (int)(it % kTcStages);
+          if (it >= kTcStages && !mbar_wait(&empty[s], (uint32_t)(((it / kTcStages) + 1) & 1), g.err)) {
             abort_flag = 1;
+            ok = false;
             break;
           }
-          // Only slices that start inside the row are loaded (and multiplied).
-          const int n = min(G, g.slices - kb * G);
-          uint8_t* st = smem + (size_t)s * kStageBytes;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)n * (kTcSliceA + kTcSliceB));
-          for (int j = 0; j < n; ++j) tma_load_3d(st + j * kTcSliceA, &tmA, (kb * G + j) * kTcBK, rt * kTcBM, mi, &full[s]);
-          if (limbs_ready) {
-            load_limbs(s, kb, n);
-          } else {  // it == s while the first ring fills
-            pend_kb[s] = kb;
-            pend_n[s] = n;
-            if (++npend == kStages) flush();
-          }
+          const int n = min(kTcG, sg.hi - c);
+          uint8_t* st = smem + (size_t)s * kTcStageBytes;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)n * kTcSliceA);
+          for (int q = 0; q < n; ++q) tma_load_3d(st + q * kTcSliceA, &tmA, (c + q) * kTcBK, rt * kTcBM, mi, &full[s]);
         }
+        if (!ok) break;
       }
-      if (!limbs_ready) flush();
-      for (int64_t i = (it > kStages ? it - kStages : 0); i < it; ++i)
-        mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1), g.err);
+      // Land every copy still in flight before the CTA may exit.
+      for (int64_t i = (it > kTcStages ? it - kTcStages : 0); i < it; ++i)
+        mbar_wait(&full[i % kTcStages], (uint32_t)((i / kTcStages) & 1), g.err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       int64_t it = 0;
-      int tc = 0;
-      for (int t = blockIdx.x; t < g.n_tiles && !abort_flag; t += gridDim.x, ++tc) {
-        const int b = tc & 1;
-        if (tc >= 2 && !mbar_wait(&tempty[b], (uint32_t)(((tc / 2) + 1) & 1), g.err)) {
+      for (int64_t j = 0; j < cur.nseg && !abort_flag; ++j) {
+        const Seg sg = cur.get(j);
+        const int b = (int)(j & 1);
+        if (j >= 2 && !mbar_wait(&tempty[b], (uint32_t)(((j / 2) + 1) & 1), g.err)) {
           abort_flag = 1;
           break;
         }
         tc_fence_after();
         const uint32_t acc = tmem + 16u * (uint32_t)b;
-        for (int kb = 0; kb < g.nkb; ++kb, ++it) {
-          const int s = (int)(it % kStages);
-          if (abort_flag || !mbar_wait(&full[s], (uint32_t)((it / kStages) & 1), g.err)) {
+        bool first = true, ok = true;
+        for (int c = sg.lo; c < sg.hi; c += kTcG, ++it) {
+          const int s = (int)(it % kTcStages);
+          const uint32_t par = (uint32_t)((it / kTcStages) & 1);
+          if (abort_flag || !mbar_wait(&full[s], par, g.err) || !mbar_wait(&bready[s], par, g.err)) {
             abort_flag = 1;
+            ok = false;
             break;
           }
           tc_fence_after();
-          const int n = min(G, g.slices - kb * G);
-          const uint32_t sa = smem_addr(smem + (size_t)s * kStageBytes), sb = sa + G * kTcSliceA;
+          const int n = min(kTcG, sg.hi - c);
+          const uint32_t sa = smem_addr(smem + (size_t)s * kTcStageBytes), sb = sa + kTcStageA;
+          for (int q = 0; q < n; ++q) {
 #pragma unroll
-          for (int j = 0; j < G; ++j) {
-            if (j < n) {
-#pragma unroll
-              for (int k4 = 0; k4 < kTcBK / 32; ++k4)
-                tc_mma_i8(acc, sw128_desc(sa + j * kTcSliceA + 32 * k4), sw128_desc(sb + j * kTcSliceB + 32 * k4),
-                          g.idesc, (kb | j | k4) != 0);
+            for (int k4 = 0; k4 < kTcBK / 32; ++k4) {
+              tc_mma_i8(acc, sw128_desc(sa + q * kTcSliceA + 32 * k4), sw128_desc(sb + q * kTcSliceB + 32 * k4),
+                        g.idesc, (first && q == 0 && k4 == 0) ? 0u : 1u);
             }
           }
+          first = false;
           tc_commit(&empty[s]);
         }
+        if (!ok) break;
         tc_commit(&tfull[b]);
       }
       tc_commit(&done);
     }
   } else {
-    // ---------------- epilogue: warps 2-5, TMEM lane quarter warp % 4 ----------------
-    const int q = warp % 4;
-    griddep_wait();  // the exponent, written by the limb kernel
-    const int E = *g.expo;
-    int tc = 0;
-    for (int t = blockIdx.x; t < g.n_tiles; t += gridDim.x, ++tc) {
-      const int b = tc & 1;
-      bool ok = !abort_flag && mbar_wait(&tfull[b], (uint32_t)((tc / 2) & 1), g.err);
-      ok = __all_sync(0xffffffffu, ok);  // the TMEM load below is warp-collective
-      if (!ok) abort_flag = 1;
-      tc_fence_after();
-      uint32_t r[8];
-      tc_ld8(tmem + ((uint32_t)(q * 32) << 16) + 16u * (uint32_t)b, r);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
-      if (!ok) break;
-      const int mi = t / g.tiles_per_mat, rt = t - mi * g.tiles_per_mat;
-      const int row = rt * kTcBM + q * 32 + lane;
-      if (row >= g.N) continue;
-      const double sc = (double)g.s[mi * g.s_stride + row];
+    // ---------------- warps 2-5: limbs and epilogue ----------------
+    const int tid = threadIdx.x - 64;  // 0..127
+    const int q = warp % 4;            // TMEM lane quarter of this warp
+    const int wl = warp - 2;           // slice of a stage this warp writes
+
+    // The vector's largest and smallest nonzero magnitudes and finiteness,
+    // from the per-block stats of mv_xstat_kernel (which also zeroed the
+    // tickets): the first reads of anything the preceding kernel wrote.
+    griddep_wait();
+    float mx = 0.0f, mn = INFINITY;
+    int bad = 0;
+    for (int i = tid; i < g.nstats; i += kTcWriters) {
+      const float4 st = __ldcg(g.stats + i);
+      mx = fmaxf(mx, st.x);
+      mn = fminf(mn, st.y);
+      bad |= st.z != 0.0f;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    if (lane == 0) {
+      red_max[wl] = mx;
+      red_min[wl] = mn;
+      red_bad[wl] = bad;
+    }
+    named_bar_sync(kTcBarWriters, kTcWriters);
+    mx = fmaxf(fmaxf(red_max[0], red_max[1]), fmaxf(red_max[2], red_max[3]));
+    mn = fminf(fminf(red_min[0], red_min[1]), fminf(red_min[2], red_min[3]));
+    bad = red_bad[0] | red_bad[1] | red_bad[2] | red_bad[3];
+    int E = 0, Emin = 0;
+    if (mx > 0.0f && !bad) {
+      frexp((double)mx, &E);
+      frexp((double)mn, &Emin);
+    }
+    const int flags = bad ? kTcFlagNonFinite : (mx > 0.0f && Emin < E - 100 ? kTcFlagInexact : 0);
+    const double sc1 = ldexp(1.0, 62 - E);
+
+    // Finishes row `row` of tile `tile` from its 16 accumulators.
+    auto finish_row = [&](int64_t tile, int row, const int (&D)[16]) {
+      const int64_t mi = tile / g.tiles_per_mat;
+      const int64_t grow = (tile % g.tiles_per_mat) * kTcBM + row;
+      if (grow >= g.N) return;
+      const double sc = (double)g.s[mi * g.s_stride + grow];
       double v;
-      if (E != kTcNonFinite) {
-        v = 0.0;
+      if (!flags) {
+        double v1 = 0.0, v2 = 0.0;
 #pragma unroll
-        for (int j = kTcLimbs - 1; j >= 0; --j) v = v * 256.0 + (double)(int)r[j];
-        v = ldexp(v, E - 62);
+        for (int j = 7; j >= 0; --j) {
+          v1 = v1 * 256.0 + (double)D[j];
+          v2 = v2 * 256.0 + (double)D[8 + j];
+        }
+        v = ldexp(v1, E - 62) + ldexp(v2, E - 124);
       } else {
-        // ops/matvec/reference.ts:117-131 as written: f64 sum, NaN and Inf
-        // propagate (0 * Inf = NaN).
-        const uint32_t* wr = g.w + mi * g.mat_stride + (int64_t)row * g.ldw;
+        // ops/matvec/reference.ts:117-131 as written: f64 sum in k order,
+        // NaN and Inf propagate (0 * Inf = NaN).
+        const uint32_t* wr = g.w + mi * g.mat_stride + grow * g.ldw;
         v = 0.0;
         for (int k = 0; k < g.K; ++k) {
           const int code = (int)(int8_t)((wr[k >> 2] >> ((k & 3) * 8)) & 0xffu);
           v += (double)code * (double)g.x[k];
         }
       }
-      g.y[mi * g.y_stride + row] = (float)(v * sc);
+      g.y[mi * g.y_stride + grow] = (float)(v * sc);
+    };
+
+    // Epilogue of segment j (its accumulator is in buffer j & 1).  Returns
+    // false when the wait for the accumulator gave up.
+    auto finish_segment = [&](int64_t j) -> bool {
+      const Seg sg = cur.get(j);
+      const int b = (int)(j & 1);
+      if (tid == 0) s_flag = !abort_flag && mbar_wait(&tfull[b], (uint32_t)((j / 2) & 1), g.err);
+      named_bar_sync(kTcBarWriters, kTcWriters);
+      const bool ready = s_flag;
+      named_bar_sync(kTcBarWriters, kTcWriters);  // s_flag is reused below
+      if (!ready) return false;
+      tc_fence_after();
+      int D[16];
+      tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + 16u * (uint32_t)b, D);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+      const int row = q * 32 + lane;
+      if (sg.whole) {
+        finish_row(sg.tile, row, D);
+        return true;
+      }
+      // Split tile: publish this CTA's partial, take a ticket.
+      const int64_t grid = gridDim.x;
+      const int which = sg.tile == cur.t0 ? 0 : 1;
+      int4* mine = g.part + ((int64_t)(blockIdx.x * 2 + which) * kTcBM + row) * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) __stcg(mine + i, make_int4(D[4 * i], D[4 * i + 1], D[4 * i + 2], D[4 * i + 3]));
+      // The barrier orders every writer's stores before thread 0's fence
+      // (cumulativity), which orders them before its ticket increment; the
+      // last arrival's fence orders the ticket before the partial loads.
+      named_bar_sync(kTcBarWriters, kTcWriters);
+      const int64_t base = sg.tile * g.S;
+      const int64_t b_lo = owner_of(base, g.total, grid), b_hi = owner_of(base + g.S - 1, g.total, grid);
+      if (tid == 0) {
+        const unsigned int n = (unsigned int)(sg.hi - sg.lo);
+        __threadfence();
+        const bool last = atomicAdd(&g.ticket[b_lo], n) + n == (unsigned int)g.S;
+        if (last) __threadfence();
+        s_flag = last;
+      }
+      named_bar_sync(kTcBarWriters, kTcWriters);
+      const bool last = s_flag;
+      named_bar_sync(kTcBarWriters, kTcWriters);
+      if (last) {
+        int sum[16] = {};
+        // Contributors four at a time: their loads are independent.
+        for (int64_t c0 = b_lo; c0 <= b_hi; c0 += 4) {
+          int4 v[4][4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int64_t c = c0 + u;
+            if (c <= b_hi) {
+              const int wc = sg.tile == first_unit(c, g.total, grid) / g.S ? 0 : 1;
+              const int4* src = g.part + ((c * 2 + wc) * kTcBM + row) * 4;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) v[u][i] = __ldcg(src + i);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) v[u][i] = make_int4(0, 0, 0, 0);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              sum[4 * i] += v[u][i].x;
+              sum[4 * i + 1] += v[u][i].y;
+              sum[4 * i + 2] += v[u][i].z;
+              sum[4 * i + 3] += v[u][i].w;
+            }
+        }
+        finish_row(sg.tile, row, sum);
+      }
+      return true;
+    };
+
+    int64_t it = 0, ep = 0, ep_last = -1;  // next segment to finish, its last stage
+    bool ok = true;
+    if (cur.nseg > 0) ep_last = seg_stages(cur.get(0)) - 1;
+    for (int64_t j = 0; j < cur.nseg && ok; ++j) {
+      const Seg sg = cur.get(j);
+      for (int c = sg.lo; c < sg.hi; c += kTcG, ++it) {
+        const int s = (int)(it % kTcStages);
+        if (it >= kTcStages) {
+          if (tid == 0) s_flag = !abort_flag && mbar_wait(&empty[s], (uint32_t)(((it / kTcStages) + 1) & 1), g.err);
+          named_bar_sync(kTcBarWriters, kTcWriters);
+          ok = s_flag;
+          named_bar_sync(kTcBarWriters, kTcWriters);
+          if (!ok) break;
+        }
+        const int n = min(kTcG, sg.hi - c);
+        if (wl < n) {
+          uint8_t* tile = smem + (size_t)s * kTcStageBytes + kTcStageA + wl * kTcSliceB;
+          write_limb_columns(tile, g.x, (int64_t)(c + wl) * kTcBK + 4 * lane, g.K, sc1, lane);
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bready[s]);
+        // A segment whose last stage lies kTcStages - 1 stages back has all
+        // its MMAs issued; finishing it here keeps the MMA fed meanwhile.
+        while (ok && ep < cur.nseg && ep_last + (kTcStages - 1) <= it) {
+          ok = finish_segment(ep);
+          ++ep;
+          if (ep < cur.nseg) ep_last += seg_stages(cur.get(ep));
+        }
+        if (!ok) break;
+      }
     }
+    while (ok && ep < cur.nseg) {
+      ok = finish_segment(ep);
+      ++ep;
+    }
+    if (!ok) abort_flag = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -350,23 +572,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return fn;
 }
 
-// 128-byte slices of each row per ring stage, and the L2 promotion of the
-// TMA reads.
-constexpr int kTcSlicesPerStage = 4;
-constexpr CUtensorMapL2promotion kTcPromotion = CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
-
-template <int G>
-cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcArgs& g, cudaStream_t st) {
-  const size_t smem = (size_t)TcStage<G>::kStages * TcStage<G>::kBytes + 1024;
-  cudaError_t ce = ensure_smem_attr((const void*)mv_tc_kernel<G>, smem);
-  if (ce != cudaSuccess) return ce;
-  const int grid = std::min(g.n_tiles, device_info().sm_count);
-  return launch_ex(mv_tc_kernel<G>, dim3(grid), dim3(kTcThreads), smem, LaunchOpts{st, true}, ta, tb, g);
-}
+std::atomic<int> g_matvec_path{XPU_MATVEC_AUTO};
 
 }  // namespace
-
-std::atomic<int> g_matvec_path{XPU_MATVEC_AUTO};
 
 int set_matvec_path(int path) {
   XPU_REQUIRE(path == XPU_MATVEC_AUTO || path == XPU_MATVEC_CUDA_CORES || path == XPU_MATVEC_TENSOR_CORES, XPU_EINVAL,
@@ -376,21 +584,65 @@ int set_matvec_path(int path) {
 }
 int matvec_path() { return g_matvec_path.load(); }
 
-// Minimum 128-row tiles for the tensor-core GEMV: with fewer, the persistent
-// grid would leave SMs idle for a whole tile (the f32 path balances rows).
-constexpr int64_t kTcMinTilesPerSm = 8;
+// XPU_MATVEC_AUTO: the tensor cores serve calls streaming at least 512 MiB of
+// weights, and calls of at least 64 MiB whose rows are 16384 codes or more
+// (there the CUDA-core kernel runs 4 slices per thread on 14 warps); the
+// CUDA-core kernels' shorter start wins below.
+constexpr int64_t kTcMinBytes = 512ll << 20;
+constexpr int64_t kTcMinBytesLongRows = 64ll << 20;
+constexpr int64_t kTcLongRows = 16384;
 
 bool matvec_tc_applies(const uint32_t* w, int64_t mat_stride, int64_t count, int64_t N, int64_t K) {
   const int64_t W = (K + 3) / 4;
   // K <= 65536 keeps |D| <= 128 * 128 * K within int32.
   if (N <= 0 || K <= 0 || count <= 0 || K > 65536 || W % 4 || mat_stride % 4) return false;
   if (reinterpret_cast<uintptr_t>(w) % 16) return false;
-  if (count * N > (int64_t)INT_MAX || count > 65535) return false;
+  if (count > 65535 || N > (int64_t)INT_MAX - kTcBM) return false;
   const int path = g_matvec_path.load(std::memory_order_relaxed);
   if (path == XPU_MATVEC_CUDA_CORES) return false;
   if (path == XPU_MATVEC_TENSOR_CORES) return true;
-  const int64_t tiles = count * ((N + kTcBM - 1) / kTcBM);
-  return tiles >= kTcMinTilesPerSm * device_info().sm_count;
+  const int64_t bytes = count * N * W * 4;
+  return bytes >= kTcMinBytes || (K >= kTcLongRows && bytes >= kTcMinBytesLongRows);
+}
+
+// The weight tensor map of one (pointer, shape, stride), cached: encoding is
+// a pure function of these, so a hit is always valid.
+struct TcMapKey {
+  const void* w;
+  int64_t W, N, count, mat_stride;
+  bool operator==(const TcMapKey& o) const {
+    return w == o.w && W == o.W && N == o.N && count == o.count && mat_stride == o.mat_stride;
+  }
+};
+static int weight_map(const TcMapKey& key, CUtensorMap* out) {
+  static std::mutex mu;
+  static TcMapKey keys[16];
+  static CUtensorMap maps[16];
+  static int used = 0, next = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (keys[i] == key) {
+        *out = maps[i];
+        return XPU_OK;
+      }
+  }
+  auto enc = encoder();
+  XPU_REQUIRE(enc, XPU_ECUDA, "matvecQ8: cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[3] = {(cuuint64_t)(4 * key.W), (cuuint64_t)key.N, (cuuint64_t)key.count};
+  const cuuint64_t strides[2] = {(cuuint64_t)(4 * key.W), (cuuint64_t)(4 * key.mat_stride)};
+  const cuuint32_t box[3] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM, 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(key.w), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  XPU_REQUIRE(r == CUDA_SUCCESS, XPU_ECUDA, "matvecQ8: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  std::lock_guard<std::mutex> lock(mu);
+  keys[next] = key;
+  maps[next] = *out;
+  next = (next + 1) % 16;
+  used = std::max(used, next == 0 ? 16 : next);
+  return XPU_OK;
 }
 
 // y[m][n] = matvecQ8 of matrix m (words at w + m * mat_stride, scales at
@@ -398,62 +650,57 @@ bool matvec_tc_applies(const uint32_t* w, int64_t mat_stride, int64_t count, int
 // matvec_tc_applies().
 int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const float* x, int64_t count, int64_t N,
                   int64_t K, float* y, cudaStream_t st) {
-  const int64_t W = (K + 3) / 4, Kpad = (K + 15) / 16 * 16;
-  auto enc = encoder();
-  XPU_REQUIRE(enc, XPU_ECUDA, "matvecQ8: cuTensorMapEncodeTiled is not available");
-  int8_t* limbs = nullptr;
-  int* expo = nullptr;
-  XPU_TRY_CUDA(scratch_alloc((void**)&limbs, (size_t)(kTcLimbs * Kpad) + 16, st));
-  expo = reinterpret_cast<int*>(limbs + kTcLimbs * Kpad);
-  int rc = XPU_OK;
-  mv_limbs8_kernel<<<1, 1024, 0, st>>>(x, K, Kpad, limbs, expo);
+  const int64_t W = (K + 3) / 4;
+  const DeviceInfo& di = device_info();
+  const int tiles_per_mat = (int)((N + kTcBM - 1) / kTcBM);
+  const int S = (int)((4 * W + kTcBK - 1) / kTcBK);
+  const int64_t total = count * tiles_per_mat * (int64_t)S;
+  // At least kTcMinUnits slices per CTA: a split tile's finisher sums one
+  // partial per contributor, so small GEMVs run on fewer, fuller CTAs.
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(total / kTcMinUnits, di.sm_count));
+  const int nstats = (int)std::max<int64_t>(1, std::min<int64_t>(di.sm_count, K / kStatThreads));
+  CUtensorMap ta;
+  int rc = weight_map(TcMapKey{w, W, N, count, mat_stride}, &ta);
+  if (rc) return rc;
+
+  // Scratch: the split-tile partials (written before they are read), the
+  // tickets (zeroed by the stats kernel) and the vector stats.
+  const size_t part_bytes = (size_t)grid * 2 * kTcBM * kTcLimbs * sizeof(int);
+  const size_t ticket_bytes = ((size_t)grid * sizeof(unsigned int) + 15) / 16 * 16;
+  const size_t stat_bytes = (size_t)nstats * sizeof(float4);
+  uint8_t* scratch = nullptr;
+  XPU_TRY_CUDA(scratch_alloc((void**)&scratch, part_bytes + ticket_bytes + stat_bytes, st));
+  TcArgs g{};
+  g.w = w;
+  g.x = x;
+  g.s = s;
+  g.y = y;
+  g.part = reinterpret_cast<int4*>(scratch);
+  g.ticket = reinterpret_cast<unsigned int*>(scratch + part_bytes);
+  g.stats = reinterpret_cast<const float4*>(scratch + part_bytes + ticket_bytes);
+  g.ldw = W;
+  g.mat_stride = mat_stride;
+  g.s_stride = N;
+  g.y_stride = N;
+  g.total = total;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.tiles_per_mat = tiles_per_mat;
+  g.S = S;
+  g.nstats = nstats;
+  // kind::i8: int32 accumulator, signed A and B, K-major, M = 128, N = 16.
+  g.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcLimbs >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
+  g.err = device_error_word();
+  mv_xstat_kernel<<<nstats, kStatThreads, 0, st>>>(x, (int)K, const_cast<float4*>(g.stats), g.ticket, grid);
   cudaError_t ce = cudaGetLastError();
-  if (ce != cudaSuccess) rc = cuda_status(ce, "mv_limbs8_kernel");
-  CUtensorMap ta, tb;
-  if (!rc) {
-    const cuuint64_t dims[3] = {(cuuint64_t)(4 * W), (cuuint64_t)N, (cuuint64_t)count};
-    const cuuint64_t strides[2] = {(cuuint64_t)(4 * W), (cuuint64_t)(4 * mat_stride)};
-    const cuuint32_t box[3] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM, 1};
-    const cuuint32_t es[3] = {1, 1, 1};
-    CUresult r = enc(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint32_t*>(w), dims, strides, box, es,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, kTcPromotion,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    const cuuint64_t bdims[2] = {(cuuint64_t)Kpad, (cuuint64_t)kTcLimbs};
-    const cuuint64_t bstrides[1] = {(cuuint64_t)Kpad};
-    const cuuint32_t bbox[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcLimbs};
-    if (r == CUDA_SUCCESS)
-      r = enc(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, limbs, bdims, bstrides, bbox, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, kTcPromotion, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      set_error("matvecQ8: cuTensorMapEncodeTiled failed (%d)", (int)r);
-      rc = XPU_ECUDA;
-    }
+  if (ce == cudaSuccess) {
+    const size_t smem = (size_t)kTcStages * kTcStageBytes + 1024;
+    ce = ensure_smem_attr((const void*)mv_tc_kernel, smem);
+    if (ce == cudaSuccess)
+      ce = launch_ex(mv_tc_kernel, dim3(grid), dim3(kTcThreads), smem, LaunchOpts{st, true}, ta, g);
   }
-  if (!rc) {
-    TcArgs g{};
-    g.w = w;
-    g.x = x;
-    g.s = s;
-    g.expo = expo;
-    g.y = y;
-    g.ldw = W;
-    g.mat_stride = mat_stride;
-    g.s_stride = N;
-    g.y_stride = N;
-    g.N = (int)N;
-    g.K = (int)K;
-    g.count = (int)count;
-    g.tiles_per_mat = (int)((N + kTcBM - 1) / kTcBM);
-    g.n_tiles = g.count * g.tiles_per_mat;
-    g.slices = (int)((4 * W + kTcBK - 1) / kTcBK);
-    g.nkb = (g.slices + kTcSlicesPerStage - 1) / kTcSlicesPerStage;
-    // kind::i8: int32 accumulator, signed A and B, K-major, M = 128, N = 8.
-    g.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcLimbs >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
-    g.err = device_error_word();
-    ce = launch_tc<kTcSlicesPerStage>(ta, tb, g, st);
-    if (ce != cudaSuccess) rc = cuda_status(ce, "mv_tc_kernel");
-  }
-  scratch_free(limbs, st);
+  if (ce != cudaSuccess) rc = cuda_status(ce, "mv_tc_kernel");
+  scratch_free(scratch, st);
   return rc;
 }
 
