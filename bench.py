@@ -94,12 +94,18 @@ def tensor_cores_serve(M, R, K):
     return W % 4 == 0 and (R * W) % 4 == 0 and K <= 65536 and (b >= 512 << 20 or (K >= 16384 and b >= 64 << 20))
 
 
-def ncu_traffic(kernel_key: str):
+def ncu_traffic(kernel: str, rows: int, cols: int):
+    """DRAM bytes (read + write) of one launch over this rank's rows, from
+    the ncu capture summarised in profiles/ncu_traffic.json (taken on one
+    GPU over all 28672 rows; traffic scales with the rows streamed), and
+    the capture's command.  (None, None) when there is no capture."""
     p = ROOT / "profiles" / "ncu_traffic.json"
     if not p.exists():
-        return None
-    d = json.loads(p.read_text())
-    return d.get(kernel_key)
+        return None, None
+    e = json.loads(p.read_text()).get(f"{kernel}_{ROWS}x{cols}")
+    if not e:
+        return None, None
+    return round(e["bytes_per_launch"] * rows / ROWS), e["command"]
 
 
 class ClockSampler:
@@ -251,7 +257,7 @@ def run_ours(args, rank, world, local):
     peak, peak_src = measured_peaks()
     on_tc = tensor_cores_serve(M, R, K)
     kname = "mv_tc_kernel" if on_tc else "mv_bulk_kernel"
-    traffic = ncu_traffic(f"{kname}_{R}x{K}")
+    traffic, traffic_cmd = ncu_traffic(kname, R, K)
     launches_per_step = 1
 
     # The other matvecQ8 path, pinned, on the same stack (comparison only).
@@ -332,7 +338,7 @@ def run_ours(args, rank, world, local):
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                         "traffic": traffic,
+                         "traffic": traffic, "traffic_source": traffic_cmd,
                          "kernel": ("mv_tc_kernel (matvecQ8 on tcgen05 tensor cores, x as exact int8 limbs): one "
                                     "persistent stream-K launch per step over the stack" if on_tc else
                                     "mv_bulk_kernel (matvecQ8, bulk-copy path): one launch per step over the contiguous stack"),
