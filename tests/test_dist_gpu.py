@@ -1,8 +1,10 @@
 """The row-sharded matvecQ8 stack on 2 GPUs: one process per GPU over NCCL,
 each computes its row shard (generated on its own GPU from the seeded
 stream's offset), the slices are all-gathered, and the result must equal
-the unsharded GEMV on one GPU bit for bit (a row's summation order depends
-on K only, not on which GPU holds the row).  Skipped with fewer than 2 GPUs."""
+the unsharded GEMV on one GPU bit for bit, on both matvecQ8 paths (a row's
+CUDA-core summation order depends on K only; the tensor-core sums are exact
+integers, whichever CTAs and GPU compute them).  Skipped with fewer than 2
+GPUs."""
 import os
 import socket
 
@@ -43,13 +45,15 @@ def _stack(rank_rows, first_row):
     return y
 
 
-def _rank(rank, world, port, out):
-    import sys
+def _rank(rank, world, port, out, path):
     from datetime import timedelta
 
     import torch.distributed as dist
 
+    from xpuops import ops
     from xpuops.dist import gathered_to_rows, shard_rows
+
+    ops.setMatvecPath(path)
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -65,11 +69,19 @@ def _rank(rank, world, port, out):
     dist.destroy_process_group()
 
 
-def test_two_gpu_row_shard_equals_one_gpu(tmp_path):
+@pytest.mark.parametrize("path", ["cuda_cores", "tensor_cores"])
+def test_two_gpu_row_shard_equals_one_gpu(tmp_path, path):
+    from xpuops import ops
+
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    code = {"cuda_cores": ops.MATVEC_CUDA_CORES, "tensor_cores": ops.MATVEC_TENSOR_CORES}[path]
     out = tmp_path / "y.npy"
-    mp.start_processes(_rank, args=(2, _port(), str(out)), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_rank, args=(2, _port(), str(out), code), nprocs=2, start_method="spawn", join=True)
     torch.cuda.set_device(0)
-    single = _stack(N, 0).cpu().numpy().reshape(M, N)
+    ops.setMatvecPath(code)
+    try:
+        single = _stack(N, 0).cpu().numpy().reshape(M, N)
+    finally:
+        ops.setMatvecPath(ops.MATVEC_AUTO)
     np.testing.assert_array_equal(np.load(out), single)
