@@ -86,16 +86,30 @@ def test_neighbouring_scale_matters():
     assert not np.allclose(got[:, 0], got[:, 1])
 
 
-def test_nonfinite_row_gives_nan_row_only():
-    N, M, K = 3, 200, 256
+def test_nonfinite_rows_and_scales_follow_the_reference():
+    """A NaN or Inf activation (its row) and a NaN or Inf scale (its column)
+    take the reference's own loop: Inf where the reference has Inf, NaN for
+    NaN and for 0 * Inf (ops/matmul/reference.ts:123-137); the other outputs
+    are untouched."""
+    N, M, K = 4, 200, 256
     rng = np.random.default_rng(5)
     a = rng.standard_normal(N * K).astype(np.float32)
     a[K + 7] = np.nan
-    w, s = _packed(M, K, seed=9)
+    a[2 * K + 9] = np.inf
+    codes = rng.integers(-127, 128, (M, K)).astype(np.int32)
+    codes[:100, 9] = 0  # 0 * Inf = NaN in these columns of row 2
+    w = orc.pack_q8(codes.ravel(), M, K)
+    s = np.abs(rng.standard_normal(M)).astype(np.float32) * 0.01
+    s[5] = np.inf
+    s[6] = np.nan
     got = matmulQ8(a, w, s, N, M, K).reshape(N, M)
-    assert np.all(np.isnan(got[1]))
     want = orc.matmul_q8(a, w, s, N, M, K)
-    assert agree(got[[0, 2]], want[[0, 2]], **TOL) is None
+    odd = np.zeros((N, M), bool)
+    odd[[1, 2]] = True
+    odd[:, [5, 6]] = True
+    np.testing.assert_array_equal(got[odd], want[odd])
+    assert np.isnan(got[1]).all() and np.isnan(got[2, :100]).all() and np.isinf(got[2, 100:]).all()
+    assert agree(got[~odd], want[~odd], **TOL) is None
 
 
 def test_device_api_both_paths_and_determinism():

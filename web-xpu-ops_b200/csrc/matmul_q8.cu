@@ -11,9 +11,13 @@
 // `tcgen05.mma.kind::i8`, D[m, 4 t + j] in TMEM — and the epilogue forms
 // s[m] * 2^(E - 30) * sum_j 256^j D[m, 4 t + j] in f64.  Against the
 // reference (f64 sum of a * f32(code * s)) the only differences are the
-// rounding of a to 30 bits below its row maximum and of code * s to f32,
-// both far inside the reference's own tolerance {rel 1e-4, abs 6e-4}
-// (ops/matmul/q8.wgsl.test.ts).
+// rounding of a to 30 bits below its row maximum and of code * s to f32.
+// Per output that is at most 2^-31 * max_k |a[t, k]| * sum_k |code * s|
+// plus 2^-24 of each term, far inside the reference's own tolerance
+// {rel 1e-4, abs 6e-4} (ops/matmul/q8.wgsl.test.ts) unless a row spans
+// ~2^30 and its largest elements meet zero codes.  An activation row with
+// NaN or Inf, or a weight row with a non-finite scale, is computed by the
+// reference's own loop instead, so Inf, NaN and 0 * Inf come out as there.
 //
 // GEMM kernel: one CTA per (128 weight rows, BN limb rows) tile.  Warp 0
 // streams 128-byte K slices of both operands with 2-D TMA (128-byte
@@ -45,7 +49,8 @@ constexpr int kMmNonFinite = INT_MIN;
 // ------------------------------------------------------------------ limbs --
 // One CTA per activation row: the row's exponent and its four digit rows
 // limbs[4 t + j][0, Kpad) (zero past K).  A row holding NaN or Inf gets the
-// exponent kMmNonFinite and zero digits; its outputs are NaN.
+// exponent kMmNonFinite and zero digits; the epilogue computes its outputs
+// with the reference's loop.
 __global__ void __launch_bounds__(256) mm_limbs_kernel(const float* __restrict__ a, int64_t K, int64_t Kpad,
                                                         int8_t* __restrict__ limbs, int* __restrict__ expo) {
   __shared__ float smax[8];
@@ -98,7 +103,10 @@ struct MmArgs {
   const int* expo;
   const float* residual;  // optional [N, M]: out = f32(residual + y)
   float* out;
-  int M, N, nkb, BN;
+  const float* a;     // the activations and weights, for the reference loop
+  const uint32_t* w;  // of non-finite rows and scales
+  int64_t ldw;
+  int M, N, K, nkb, BN;
   uint32_t idesc, tmem_cols;
   unsigned int* err;
 };
@@ -240,8 +248,17 @@ __global__ void __launch_bounds__(kMmThreads, 1)
         if (t >= g.N || row >= g.M) continue;
         const int e = g.expo[t];
         float y;
-        if (e == kMmNonFinite) {
-          y = __int_as_float(0x7fffffff);
+        if (e == kMmNonFinite || !isfinite(s)) {
+          // ops/matmul/reference.ts:123-137 as written: b = f32(code * s),
+          // then an f64 sum of a * b in k order.
+          const float* ar = g.a + (int64_t)t * g.K;
+          const uint32_t* wr = g.w + (int64_t)row * g.ldw;
+          double v = 0.0;
+          for (int k = 0; k < g.K; ++k) {
+            const int code = (int)(int8_t)((wr[k >> 2] >> ((k & 3) * 8)) & 0xffu);
+            v += (double)ar[k] * (double)(float)((double)code * (double)s);
+          }
+          y = (float)v;
         } else {
           const double v = (double)(int)r[4 * tt] + 256.0 * (double)(int)r[4 * tt + 1] +
                            65536.0 * (double)(int)r[4 * tt + 2] + 16777216.0 * (double)(int)r[4 * tt + 3];
@@ -384,8 +401,12 @@ int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s
     g.expo = expo;
     g.residual = residual;
     g.out = out;
+    g.a = a;
+    g.w = w;
+    g.ldw = ldw;
     g.M = (int)M;
     g.N = (int)N;
+    g.K = (int)K;
     g.nkb = (int)((Kpad + kMmBK - 1) / kMmBK);
     g.BN = BN;
     // kind::i8 instruction descriptor: int32 accumulator, signed int8 A and

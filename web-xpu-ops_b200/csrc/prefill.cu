@@ -16,6 +16,7 @@
 
 #include <algorithm>
 
+#include "matvec_launch.cuh"
 #include "prefill.cuh"
 
 namespace xpu {
@@ -180,6 +181,179 @@ __global__ void __launch_bounds__(kPfThreads) pf_attn_kernel(const float* __rest
   }
 }
 
+// Causal grouped attention over a block of query rows at a time: the G query
+// heads of kv head g for BT = 64 / G consecutive tokens (64 rows, row r =
+// token r / G, head r % G) against K/V tiles of 64 positions staged in
+// shared memory.  Per tile: scores S = Q K^T (each thread 2 rows x 8
+// positions, float4 loads), scale and causal mask, an online softmax whose
+// row statistics the 8 lanes sharing a row reduce by shuffles, then
+// O += P V (each thread 2 rows x HD / 8 dims).  Each CTA takes query block
+// i and block nb - 1 - i so that the causal work is even.  Arithmetic as
+// pf_attn_kernel: f32 dot products times the scale, expf, f32 sums.
+constexpr int kAtRows = 64;
+constexpr int kAtPos = 64;
+template <int HD>
+struct AttnTile {
+  static constexpr int kLd = HD + 4;       // padded row (conflict-free float4 reads)
+  static constexpr int kPLd = kAtPos + 4;
+  static constexpr int kDims = HD / 8;     // output dims per thread
+  static constexpr size_t kSmem = sizeof(float) * (3 * (size_t)kAtRows * kLd + (size_t)kAtRows * kPLd);
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kPfThreads, 1) pf_attn_tiled_kernel(const float* __restrict__ q, const float* kcache,
+                                                                   const float* vcache, int T, int H, int kvH, int S,
+                                                                   int p0, float scale, float* __restrict__ out) {
+  using A = AttnTile<HD>;
+  extern __shared__ float4 sm4[];
+  float* Qs = reinterpret_cast<float*>(sm4);
+  float* Ks = Qs + kAtRows * A::kLd;
+  float* Vs = Ks + kAtRows * A::kLd;
+  float* Ps = Vs + kAtRows * A::kLd;
+  const int g = blockIdx.y, G = H / kvH, BT = kAtRows / G;
+  const int nb = (T + BT - 1) / BT;
+  const int tid = threadIdx.x, tr = tid >> 3, tc = tid & 7;
+  const float* kb = kcache + (int64_t)g * S * HD;
+  const float* vb = vcache + (int64_t)g * S * HD;
+  for (int pass = 0; pass < 2; ++pass) {
+    const int blk = pass == 0 ? (int)blockIdx.x : nb - 1 - (int)blockIdx.x;
+    if (blk < 0 || blk >= nb || (pass == 1 && blk == (int)blockIdx.x)) break;
+    const int t0 = blk * BT, t1 = min(t0 + BT, T);
+    __syncthreads();  // the previous block's readers of Qs are done
+    for (int i = tid; i < kAtRows * (HD / 4); i += kPfThreads) {
+      const int r = i / (HD / 4), c = (i % (HD / 4)) * 4, t = t0 + r / G;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t < t1) v = *reinterpret_cast<const float4*>(q + ((int64_t)t * H + g * G + r % G) * HD + c);
+      *reinterpret_cast<float4*>(Qs + r * A::kLd + c) = v;
+    }
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    float o[2][A::kDims];
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+      for (int d = 0; d < A::kDims; ++d) o[rr][d] = 0.f;
+    int tq[2];  // absolute position of each of this thread's rows (-1: no row)
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int t = t0 + (2 * tr + rr) / G;
+      tq[rr] = t < t1 ? p0 + t : -1;
+    }
+    const int last = p0 + t1 - 1;  // the block's last query position
+    for (int pb = 0; pb <= last; pb += kAtPos) {
+      __syncthreads();  // previous tile's readers of Ks/Vs/Ps are done
+      for (int i = tid; i < kAtPos * (HD / 4); i += kPfThreads) {
+        const int r = i / (HD / 4), c = (i % (HD / 4)) * 4, p = pb + r;
+        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+        if (p <= last) {
+          kv = *reinterpret_cast<const float4*>(kb + (int64_t)p * HD + c);
+          vv = *reinterpret_cast<const float4*>(vb + (int64_t)p * HD + c);
+        }
+        *reinterpret_cast<float4*>(Ks + r * A::kLd + c) = kv;
+        *reinterpret_cast<float4*>(Vs + r * A::kLd + c) = vv;
+      }
+      __syncthreads();
+      float sc[2][8];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sc[rr][i] = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < HD; d += 4) {
+        const float4 qa = *reinterpret_cast<const float4*>(Qs + (2 * tr) * A::kLd + d);
+        const float4 qb = *reinterpret_cast<const float4*>(Qs + (2 * tr + 1) * A::kLd + d);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 k = *reinterpret_cast<const float4*>(Ks + (tc * 8 + i) * A::kLd + d);
+          sc[0][i] = fmaf(qa.x, k.x, sc[0][i]);
+          sc[0][i] = fmaf(qa.y, k.y, sc[0][i]);
+          sc[0][i] = fmaf(qa.z, k.z, sc[0][i]);
+          sc[0][i] = fmaf(qa.w, k.w, sc[0][i]);
+          sc[1][i] = fmaf(qb.x, k.x, sc[1][i]);
+          sc[1][i] = fmaf(qb.y, k.y, sc[1][i]);
+          sc[1][i] = fmaf(qb.z, k.z, sc[1][i]);
+          sc[1][i] = fmaf(qb.w, k.w, sc[1][i]);
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int p = pb + tc * 8 + i;
+          sc[rr][i] = p <= tq[rr] ? sc[rr][i] * scale : -INFINITY;
+          mx = fmaxf(mx, sc[rr][i]);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        const float mnew = fmaxf(m[rr], mx);
+        const float corr = m[rr] == -INFINITY ? 0.f : expf(m[rr] - mnew);
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float e = sc[rr][i] == -INFINITY ? 0.f : expf(sc[rr][i] - mnew);
+          sc[rr][i] = e;
+          sum += e;
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        l[rr] = l[rr] * corr + sum;
+        m[rr] = mnew;
+#pragma unroll
+        for (int d = 0; d < A::kDims; ++d) o[rr][d] *= corr;
+        float* prow = Ps + (2 * tr + rr) * A::kPLd + tc * 8;
+        *reinterpret_cast<float4*>(prow) = make_float4(sc[rr][0], sc[rr][1], sc[rr][2], sc[rr][3]);
+        *reinterpret_cast<float4*>(prow + 4) = make_float4(sc[rr][4], sc[rr][5], sc[rr][6], sc[rr][7]);
+      }
+      __syncthreads();
+#pragma unroll 2
+      for (int p = 0; p < kAtPos; p += 4) {
+        const float4 pa = *reinterpret_cast<const float4*>(Ps + (2 * tr) * A::kPLd + p);
+        const float4 pq = *reinterpret_cast<const float4*>(Ps + (2 * tr + 1) * A::kPLd + p);
+        const float wa[4] = {pa.x, pa.y, pa.z, pa.w}, wq[4] = {pq.x, pq.y, pq.z, pq.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float* vrow = Vs + (p + j) * A::kLd + tc * A::kDims;
+#pragma unroll
+          for (int d = 0; d < A::kDims; d += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(vrow + d);
+            o[0][d] = fmaf(wa[j], v.x, o[0][d]);
+            o[0][d + 1] = fmaf(wa[j], v.y, o[0][d + 1]);
+            o[0][d + 2] = fmaf(wa[j], v.z, o[0][d + 2]);
+            o[0][d + 3] = fmaf(wa[j], v.w, o[0][d + 3]);
+            o[1][d] = fmaf(wq[j], v.x, o[1][d]);
+            o[1][d + 1] = fmaf(wq[j], v.y, o[1][d + 1]);
+            o[1][d + 2] = fmaf(wq[j], v.z, o[1][d + 2]);
+            o[1][d + 3] = fmaf(wq[j], v.w, o[1][d + 3]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      if (tq[rr] < 0) continue;
+      const int r = 2 * tr + rr, t = t0 + r / G;
+      float* dst = out + ((int64_t)t * H + g * G + r % G) * HD + tc * A::kDims;
+#pragma unroll
+      for (int d = 0; d < A::kDims; d += 4)
+        *reinterpret_cast<float4*>(dst + d) =
+            make_float4(o[rr][d] / l[rr], o[rr][d + 1] / l[rr], o[rr][d + 2] / l[rr], o[rr][d + 3] / l[rr]);
+    }
+  }
+}
+
+template <int HD>
+int launch_attn_tiled(const PrefillArgs& a, const float* kc, const float* vc, int T, int p0, cudaStream_t st) {
+  const int G = a.H / a.kvH, BT = kAtRows / G, nb = (T + BT - 1) / BT;
+  const size_t smem = AttnTile<HD>::kSmem;
+  XPU_TRY_CUDA(ensure_smem_attr((const void*)pf_attn_tiled_kernel<HD>, smem));
+  pf_attn_tiled_kernel<HD><<<dim3((nb + 1) / 2, a.kvH), kPfThreads, smem, st>>>(a.q, kc, vc, T, a.H, a.kvH, a.S, p0,
+                                                                                a.attn_scale, a.attn);
+  XPU_TRY_CUDA(cudaGetLastError());
+  return XPU_OK;
+}
+
 // matvecQ8Ffn's epilogue (ops/matvec/reference.ts:196-207) elementwise:
 // out = f32(silu(gate) * up) with silu in f64.
 __global__ void __launch_bounds__(kPfThreads) pf_silu_mul_kernel(const float* gate, const float* __restrict__ up,
@@ -205,6 +379,9 @@ int prefill_chunk(const PrefillArgs& a, const int32_t* d_tokens, int T, int p0, 
   pf_embed_kernel<<<T, kPfThreads, 0, st>>>(a.embed_codes, a.embed_scale, a.vocab, (int)h, d_tokens, a.hid);
   XPU_TRY_CUDA(cudaGetLastError());
   const size_t attn_smem = sizeof(float) * ((size_t)G * a.hd + (size_t)G * kPfChunk + 3 * (size_t)G);
+  // The tiled attention takes head_dim 32, 64 or 128 with the G query heads
+  // of a kv head dividing its 64-row block; other shapes keep pf_attn_kernel.
+  const bool tiled = (a.hd == 32 || a.hd == 64 || a.hd == 128) && G <= kAtRows && kAtRows % G == 0;
   int rc;
   for (int l = 0; l < a.layers; ++l) {
     const PrefillLayer& L = a.layer[l];
@@ -214,9 +391,16 @@ int prefill_chunk(const PrefillArgs& a, const int32_t* d_tokens, int T, int p0, 
     pf_rope_kv_kernel<<<T, kPfThreads, 0, st>>>(a.qkv, (int)qd, (int)kvd, a.hd, a.S, p0, a.inv_freq, a.q, L.kcache,
                                                 L.vcache);
     XPU_TRY_CUDA(cudaGetLastError());
-    pf_attn_kernel<<<dim3(T, a.kvH), kPfThreads, attn_smem, st>>>(a.q, L.kcache, L.vcache, a.H, a.kvH, a.S, a.hd, p0,
-                                                                  a.attn_scale, a.attn);
-    XPU_TRY_CUDA(cudaGetLastError());
+    if (tiled) {
+      rc = a.hd == 32    ? launch_attn_tiled<32>(a, L.kcache, L.vcache, T, p0, st)
+           : a.hd == 64  ? launch_attn_tiled<64>(a, L.kcache, L.vcache, T, p0, st)
+                         : launch_attn_tiled<128>(a, L.kcache, L.vcache, T, p0, st);
+      if (rc) return rc;
+    } else {
+      pf_attn_kernel<<<dim3(T, a.kvH), kPfThreads, attn_smem, st>>>(a.q, L.kcache, L.vcache, a.H, a.kvH, a.S, a.hd,
+                                                                    p0, a.attn_scale, a.attn);
+      XPU_TRY_CUDA(cudaGetLastError());
+    }
     if ((rc = matmul_q8_dev(a.attn, L.wo, L.ldw_qd, L.so, T, h, qd, a.hid2, a.hid, st))) return rc;
     pf_rmsnorm_kernel<<<T, kPfThreads, 0, st>>>(a.hid2, L.ffn_norm, (int)h, a.eps, a.xn);
     XPU_TRY_CUDA(cudaGetLastError());
