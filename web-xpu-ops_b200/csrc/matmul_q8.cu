@@ -41,10 +41,12 @@ namespace {
 
 constexpr int kMmBM = 128;      // weight rows per tile (the MMA's M)
 constexpr int kMmBK = 128;      // K bytes per stage: one 128-byte swizzle row
-constexpr int kMmStages = 4;
+constexpr int kMmMaxStages = 6;
+constexpr size_t kMmSmemPerCta = 110 * 1024;  // two CTAs per SM: one's epilogue overlaps the other's MMAs
 constexpr int kMmLimbs = 4;
 constexpr int kMmThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
 constexpr int kMmNonFinite = INT_MIN;
+constexpr uint32_t kDigitBias32 = 0x80808080u;
 
 // ------------------------------------------------------------------ limbs --
 // One CTA per activation row: the row's exponent and its four digit rows
@@ -84,14 +86,22 @@ __global__ void __launch_bounds__(256) mm_limbs_kernel(const float* __restrict__
   if (mx > 0.0f) frexp((double)mx, &E);  // mx = f * 2^E, f in [0.5, 1)
   const double sc = ldexp(1.0, 30 - E);
   int8_t* d0 = limbs + 4 * t * Kpad;
-  for (int64_t k = threadIdx.x; k < Kpad; k += blockDim.x) {
-    long long X = (!bad && k < K) ? __double2ll_rn((double)row[k] * sc) : 0;
+  // |X| <= 2^30, so X + 0x80808080 fits in 32 bits and its bytes, top bits
+  // flipped, are the balanced digits d_0..d_3.  Four consecutive elements
+  // per thread: each limb row gets one 32-bit word (bytes transposed).
+  for (int64_t k4 = 4 * (int64_t)threadIdx.x; k4 < Kpad; k4 += 4 * (int64_t)blockDim.x) {
+    uint32_t u[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t k = k4 + i;
+      const int X = (!bad && k < K) ? (int)__double2ll_rn((double)row[k] * sc) : 0;
+      u[i] = ((uint32_t)X + kDigitBias32) ^ kDigitBias32;
+    }
 #pragma unroll
     for (int j = 0; j < kMmLimbs; ++j) {
-      long long d = X & 255;
-      if (d >= 128) d -= 256;
-      d0[j * Kpad + k] = (int8_t)d;
-      X = (X - d) >> 8;
+      const uint32_t sel = (uint32_t)j | ((uint32_t)(4 + j) << 4);
+      const uint32_t word = __byte_perm(__byte_perm(u[0], u[1], sel), __byte_perm(u[2], u[3], sel), 0x5410u);
+      *reinterpret_cast<uint32_t*>(d0 + j * Kpad + k4) = word;
     }
   }
   if (threadIdx.x == 0) expo[t] = bad ? kMmNonFinite : E;
@@ -106,7 +116,7 @@ struct MmArgs {
   const float* a;     // the activations and weights, for the reference loop
   const uint32_t* w;  // of non-finite rows and scales
   int64_t ldw;
-  int M, N, K, nkb, BN;
+  int M, N, K, nkb, BN, stages;
   uint32_t idesc, tmem_cols;
   unsigned int* err;
 };
@@ -162,8 +172,10 @@ __global__ void __launch_bounds__(kMmThreads, 1)
     mm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, MmArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t full[kMmStages];
-  __shared__ __align__(8) uint64_t empty[kMmStages];
+  __shared__ __align__(8) uint64_t full[kMmMaxStages];
+  __shared__ __align__(8) uint64_t empty[kMmMaxStages];
+  __shared__ int s_expo[256 / kMmLimbs];     // exponents of this tile's activation rows
+  __shared__ double s_pow[256 / kMmLimbs];   // 2^(exponent - 30), exact
   __shared__ __align__(8) uint64_t done;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
@@ -172,7 +184,7 @@ __global__ void __launch_bounds__(kMmThreads, 1)
   const uint32_t a_bytes = kMmBM * kMmBK, stage_bytes = a_bytes + (uint32_t)g.BN * kMmBK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kMmStages; ++s) {
+    for (int s = 0; s < g.stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -196,8 +208,8 @@ __global__ void __launch_bounds__(kMmThreads, 1)
       // ---------------- TMA producer ----------------
       int kb = 0;
       for (; kb < g.nkb && !abort_flag; ++kb) {
-        const int s = kb % kMmStages;
-        if (kb >= kMmStages && !mbar_wait(&empty[s], (uint32_t)(((kb / kMmStages) + 1) & 1), g.err)) {
+        const int s = kb % g.stages;
+        if (kb >= g.stages && !mbar_wait(&empty[s], (uint32_t)(((kb / g.stages) + 1) & 1), g.err)) {
           abort_flag = 1;
           break;
         }
@@ -207,16 +219,16 @@ __global__ void __launch_bounds__(kMmThreads, 1)
         tma_load_2d(st + a_bytes, &tmB, kb * kMmBK, n0, &full[s]);
       }
       // Every issued copy lands before the CTA moves on.
-      for (int i = (kb > kMmStages ? kb - kMmStages : 0); i < kb; ++i)
-        mbar_wait(&full[i % kMmStages], (uint32_t)((i / kMmStages) & 1), g.err);
+      for (int i = (kb > g.stages ? kb - g.stages : 0); i < kb; ++i)
+        mbar_wait(&full[i % g.stages], (uint32_t)((i / g.stages) & 1), g.err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       int issued = 0;
       for (int kb = 0; kb < g.nkb; ++kb) {
-        const int s = kb % kMmStages;
-        if (abort_flag || !mbar_wait(&full[s], (uint32_t)((kb / kMmStages) & 1), g.err)) {
+        const int s = kb % g.stages;
+        if (abort_flag || !mbar_wait(&full[s], (uint32_t)((kb / g.stages) & 1), g.err)) {
           abort_flag = 1;
           break;
         }
@@ -233,11 +245,18 @@ __global__ void __launch_bounds__(kMmThreads, 1)
     }
   } else {
     // ---------------- epilogue: warps 2-5, TMEM lane quarter warp % 4 ----------------
-    const bool ok = mbar_wait(&done, 0, g.err);
-    tc_fence_after();
     const int q = warp % 4;
     const int row = m0 + q * 32 + lane;
     const float s = row < g.M ? g.scale[row] : 0.0f;
+    for (int i = threadIdx.x - 64; i < g.BN / kMmLimbs; i += 128) {
+      const int t = n0 / kMmLimbs + i;
+      const int e = t < g.N ? g.expo[t] : 0;
+      s_expo[i] = e;
+      s_pow[i] = e == kMmNonFinite ? 0.0 : ldexp(1.0, e - 30);
+    }
+    named_bar_sync(1, 128);
+    const bool ok = mbar_wait(&done, 0, g.err);
+    tc_fence_after();
     for (int c0 = 0; c0 < g.BN; c0 += 16) {
       uint32_t r[16];
       tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
@@ -246,7 +265,7 @@ __global__ void __launch_bounds__(kMmThreads, 1)
       for (int tt = 0; tt < 16 / kMmLimbs; ++tt) {
         const int t = (n0 + c0) / kMmLimbs + tt;
         if (t >= g.N || row >= g.M) continue;
-        const int e = g.expo[t];
+        const int e = s_expo[c0 / kMmLimbs + tt];
         float y;
         if (e == kMmNonFinite || !isfinite(s)) {
           // ops/matmul/reference.ts:123-137 as written: b = f32(code * s),
@@ -262,7 +281,7 @@ __global__ void __launch_bounds__(kMmThreads, 1)
         } else {
           const double v = (double)(int)r[4 * tt] + 256.0 * (double)(int)r[4 * tt + 1] +
                            65536.0 * (double)(int)r[4 * tt + 2] + 16777216.0 * (double)(int)r[4 * tt + 3];
-          y = (float)((double)s * ldexp(v, e - 30));
+          y = (float)((double)s * (v * s_pow[c0 / kMmLimbs + tt]));
         }
         const int64_t o = (int64_t)t * g.M + row;
         g.out[o] = g.residual ? __fadd_rn(g.residual[o], y) : y;
@@ -341,27 +360,28 @@ int matmul_q8_rows(const float* a, const uint32_t* w, const float* s, int64_t N,
 // 16-byte slots (ldw % 4 == 0) on a 16-byte aligned base take the tensor
 // cores; otherwise ldw must equal ceil(K/4) (matvecQ8's layout) for the
 // per-row path.
-int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s, int64_t N, int64_t M, int64_t K,
-                  float* out, const float* residual, cudaStream_t st) {
-  if (N == 0 || M == 0) return XPU_OK;
-  if (K == 0) {  // the empty sum
-    if (residual)
-      XPU_TRY_CUDA(cudaMemcpyAsync(out, residual, (size_t)(N * M) * 4, cudaMemcpyDeviceToDevice, st));
-    else
-      XPU_TRY_CUDA(cudaMemsetAsync(out, 0, (size_t)(N * M) * 4, st));
-    return XPU_OK;
+namespace {
+
+// The limb rows (kMmLimbs * N rows of Kpad bytes) and row exponents of a,
+// in one scratch block; freed by the caller with scratch_free(*limbs).
+int mm_make_limbs(const float* a, int64_t N, int64_t K, int8_t** limbs, int** expo, cudaStream_t st) {
+  const int64_t Kpad = round_up(K, 16);
+  XPU_TRY_CUDA(scratch_alloc((void**)limbs, (size_t)(kMmLimbs * N * Kpad) + (size_t)N * sizeof(int), st));
+  *expo = reinterpret_cast<int*>(*limbs + kMmLimbs * N * Kpad);
+  mm_limbs_kernel<<<(unsigned)N, 256, 0, st>>>(a, K, Kpad, *limbs, *expo);
+  const cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) {
+    scratch_free(*limbs, st);
+    return cuda_status(ce, "mm_limbs_kernel");
   }
-  const int64_t W = ldw;
-  const bool tma_ok = W % 4 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
-  if (!tma_ok) {
-    XPU_REQUIRE(ldw == (K + 3) / 4, XPU_EINVAL, "matmulQ8: rows of %lld words need a 16-byte multiple pitch",
-                (long long)ldw);
-    return matmul_q8_rows(a, w, s, N, M, K, out, residual, st);
-  }
-  XPU_REQUIRE(N <= (INT_MAX / kMmLimbs) && M <= INT_MAX, XPU_EINVAL, "matmulQ8: N=%lld or M=%lld too large",
-              (long long)N, (long long)M);
+  return XPU_OK;
+}
+
+// One GEMM on precomputed limbs (mm_make_limbs of the same a).
+int mm_launch(const int8_t* limbs, const int* expo, const float* a, const uint32_t* w, int64_t ldw, const float* s,
+              int64_t N, int64_t M, int64_t K, float* out, const float* residual, cudaStream_t st) {
   const DeviceInfo& di = device_info();
-  const int64_t N4 = kMmLimbs * N, Kpad = round_up(K, 16);
+  const int64_t W = ldw, N4 = kMmLimbs * N, Kpad = round_up(K, 16);
   // Limb rows per tile: the largest power-of-two multiple of 16 up to 256
   // that covers N4, halved while that leaves SMs idle.
   int BN = 16;
@@ -369,59 +389,104 @@ int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s
   const int64_t mt = (M + kMmBM - 1) / kMmBM;
   while (BN > 32 && mt * ((N4 + BN - 1) / BN) < di.sm_count) BN /= 2;
   const int64_t nt = (N4 + BN - 1) / BN;
-
-  int8_t* limbs = nullptr;
-  int* expo = nullptr;
-  // One scratch block: the limb rows (N4 * Kpad bytes, a multiple of 16),
-  // then the row exponents.
-  XPU_TRY_CUDA(scratch_alloc((void**)&limbs, (size_t)(N4 * Kpad) + (size_t)N * sizeof(int), st));
-  expo = reinterpret_cast<int*>(limbs + N4 * Kpad);
-  cudaError_t ce;
-  int rc = XPU_OK;
   CUtensorMap ta, tb;
-  mm_limbs_kernel<<<(unsigned)N, 256, 0, st>>>(a, K, Kpad, limbs, expo);
-  ce = cudaGetLastError();
-  if (ce != cudaSuccess) rc = cuda_status(ce, "mm_limbs_kernel");
-  bool use_tc = false;
-  if (!rc) {
-    // Both maps span whole padded rows (4W and Kpad bytes, multiples of 16):
-    // the bytes past K are zero in both operands, and a row width that is
-    // not a multiple of 16 bytes gave wrong tiles.
-    use_tc = encode_i8_map(&ta, w, M, 4 * W, 4 * W, kMmBM) == XPU_OK &&
-             encode_i8_map(&tb, limbs, N4, Kpad, Kpad, BN) == XPU_OK;
-    if (!use_tc) {  // a shape the tensor-map encoder refuses: the per-row path
-      clear_error();
-      rc = ldw == (K + 3) / 4 ? matmul_q8_rows(a, w, s, N, M, K, out, residual, st)
-                               : (set_error("matmulQ8: tensor map refused for K=%lld", (long long)K), XPU_EINVAL);
-    }
+  // Both maps span whole padded rows (4W and Kpad bytes, multiples of 16):
+  // the bytes past K are zero in both operands, and a row width that is not
+  // a multiple of 16 bytes gave wrong tiles.
+  if (encode_i8_map(&ta, w, M, 4 * W, 4 * W, kMmBM) != XPU_OK ||
+      encode_i8_map(&tb, limbs, N4, Kpad, Kpad, BN) != XPU_OK) {
+    // A shape the tensor-map encoder refuses: the per-row path.
+    clear_error();
+    if (ldw == (K + 3) / 4) return matmul_q8_rows(a, w, s, N, M, K, out, residual, st);
+    set_error("matmulQ8: tensor map refused for K=%lld", (long long)K);
+    return XPU_EINVAL;
   }
-  if (!rc && use_tc) {
-    MmArgs g{};
-    g.scale = s;
-    g.expo = expo;
-    g.residual = residual;
-    g.out = out;
-    g.a = a;
-    g.w = w;
-    g.ldw = ldw;
-    g.M = (int)M;
-    g.N = (int)N;
-    g.K = (int)K;
-    g.nkb = (int)((Kpad + kMmBK - 1) / kMmBK);
-    g.BN = BN;
-    // kind::i8 instruction descriptor: int32 accumulator, signed int8 A and
-    // B, both K-major, M = 128, N = BN.
-    g.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kMmBM >> 4) << 24);
-    g.tmem_cols = (uint32_t)std::max(32, BN);
-    g.err = device_error_word();
-    const size_t smem = (size_t)kMmStages * ((size_t)kMmBM * kMmBK + (size_t)BN * kMmBK) + 1024;
-    ce = ensure_smem_attr((const void*)mm_q8_tc_kernel, smem);
-    if (ce == cudaSuccess) {
-      mm_q8_tc_kernel<<<dim3((unsigned)mt, (unsigned)nt), kMmThreads, smem, st>>>(ta, tb, g);
-      ce = cudaGetLastError();
-    }
-    if (ce != cudaSuccess) rc = cuda_status(ce, "mm_q8_tc_kernel");
+  MmArgs g{};
+  g.scale = s;
+  g.expo = expo;
+  g.residual = residual;
+  g.out = out;
+  g.a = a;
+  g.w = w;
+  g.ldw = ldw;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.nkb = (int)((Kpad + kMmBK - 1) / kMmBK);
+  g.BN = BN;
+  // kind::i8 instruction descriptor: int32 accumulator, signed int8 A and
+  // B, both K-major, M = 128, N = BN.
+  g.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kMmBM >> 4) << 24);
+  g.tmem_cols = (uint32_t)std::max(32, BN);
+  g.err = device_error_word();
+  const size_t stage_bytes = (size_t)kMmBM * kMmBK + (size_t)BN * kMmBK;
+  g.stages = (int)std::clamp<size_t>((kMmSmemPerCta - 1024) / stage_bytes, 2, kMmMaxStages);
+  const size_t smem = (size_t)g.stages * stage_bytes + 1024;
+  cudaError_t ce = ensure_smem_attr((const void*)mm_q8_tc_kernel, smem);
+  if (ce == cudaSuccess) {
+    mm_q8_tc_kernel<<<dim3((unsigned)mt, (unsigned)nt), kMmThreads, smem, st>>>(ta, tb, g);
+    ce = cudaGetLastError();
   }
+  return ce == cudaSuccess ? XPU_OK : cuda_status(ce, "mm_q8_tc_kernel");
+}
+
+// The tensor-core path applies (16-byte rows); else the per-row path runs.
+int mm_check(const uint32_t* w, int64_t ldw, int64_t N, int64_t M, int64_t K, bool* rows) {
+  *rows = !(ldw % 4 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0);
+  if (*rows)
+    XPU_REQUIRE(ldw == (K + 3) / 4, XPU_EINVAL, "matmulQ8: rows of %lld words need a 16-byte multiple pitch",
+                (long long)ldw);
+  XPU_REQUIRE(N <= (INT_MAX / kMmLimbs) && M <= INT_MAX, XPU_EINVAL, "matmulQ8: N=%lld or M=%lld too large",
+              (long long)N, (long long)M);
+  return XPU_OK;
+}
+
+int mm_empty(int64_t N, int64_t M, float* out, const float* residual, cudaStream_t st) {
+  if (residual)
+    XPU_TRY_CUDA(cudaMemcpyAsync(out, residual, (size_t)(N * M) * 4, cudaMemcpyDeviceToDevice, st));
+  else
+    XPU_TRY_CUDA(cudaMemsetAsync(out, 0, (size_t)(N * M) * 4, st));
+  return XPU_OK;
+}
+
+}  // namespace
+
+int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s, int64_t N, int64_t M, int64_t K,
+                  float* out, const float* residual, cudaStream_t st) {
+  if (N == 0 || M == 0) return XPU_OK;
+  if (K == 0) return mm_empty(N, M, out, residual, st);  // the empty sum
+  bool rows;
+  int rc = mm_check(w, ldw, N, M, K, &rows);
+  if (rc) return rc;
+  if (rows) return matmul_q8_rows(a, w, s, N, M, K, out, residual, st);
+  int8_t* limbs;
+  int* expo;
+  if ((rc = mm_make_limbs(a, N, K, &limbs, &expo, st))) return rc;
+  rc = mm_launch(limbs, expo, a, w, ldw, s, N, M, K, out, residual, st);
+  scratch_free(limbs, st);
+  return rc;
+}
+
+int matmul_q8_pair_dev(const float* a, const uint32_t* w1, const float* s1, float* out1, const uint32_t* w2,
+                       const float* s2, float* out2, int64_t ldw, int64_t N, int64_t M, int64_t K, cudaStream_t st) {
+  if (N == 0 || M == 0) return XPU_OK;
+  if (K == 0) {
+    int rc = mm_empty(N, M, out1, nullptr, st);
+    return rc ? rc : mm_empty(N, M, out2, nullptr, st);
+  }
+  bool rows1, rows2;
+  int rc = mm_check(w1, ldw, N, M, K, &rows1);
+  if (!rc) rc = mm_check(w2, ldw, N, M, K, &rows2);
+  if (rc) return rc;
+  if (rows1 || rows2) {
+    rc = matmul_q8_dev(a, w1, ldw, s1, N, M, K, out1, nullptr, st);
+    return rc ? rc : matmul_q8_dev(a, w2, ldw, s2, N, M, K, out2, nullptr, st);
+  }
+  int8_t* limbs;
+  int* expo;
+  if ((rc = mm_make_limbs(a, N, K, &limbs, &expo, st))) return rc;
+  rc = mm_launch(limbs, expo, a, w1, ldw, s1, N, M, K, out1, nullptr, st);
+  if (!rc) rc = mm_launch(limbs, expo, a, w2, ldw, s2, N, M, K, out2, nullptr, st);
   scratch_free(limbs, st);
   return rc;
 }

@@ -23,6 +23,9 @@ namespace xpu {
 
 int matmul_q8_dev(const float* a, const uint32_t* w, int64_t ldw, const float* s, int64_t N, int64_t M, int64_t K,
                   float* out, const float* residual, cudaStream_t st);
+// Two matmulQ8 of the same activations (gate and up): the limbs once.
+int matmul_q8_pair_dev(const float* a, const uint32_t* w1, const float* s1, float* out1, const uint32_t* w2,
+                       const float* s2, float* out2, int64_t ldw, int64_t N, int64_t M, int64_t K, cudaStream_t st);
 
 namespace {
 
@@ -182,49 +185,86 @@ __global__ void __launch_bounds__(kPfThreads) pf_attn_kernel(const float* __rest
 }
 
 // Causal grouped attention over a block of query rows at a time: the G query
-// heads of kv head g for BT = 64 / G consecutive tokens (64 rows, row r =
-// token r / G, head r % G) against K/V tiles of 64 positions staged in
-// shared memory.  Per tile: scores S = Q K^T (each thread 2 rows x 8
-// positions, float4 loads), scale and causal mask, an online softmax whose
-// row statistics the 8 lanes sharing a row reduce by shuffles, then
-// O += P V (each thread 2 rows x HD / 8 dims).  Each CTA takes query block
-// i and block nb - 1 - i so that the causal work is even.  Arithmetic as
-// pf_attn_kernel: f32 dot products times the scale, expf, f32 sums.
-constexpr int kAtRows = 64;
+// heads of kv head g for BT = R / G consecutive tokens (R rows, row r =
+// token r / G, head r % G) against K/V tiles of 64 positions.  The tiles are
+// double-buffered in shared memory: warp 0 brings tile i + 1 in with one
+// 1-D bulk copy (TMA) per K or V row into the padded rows, completing on an
+// mbarrier, while the CTA computes tile i.  Per tile: scores S = Q K^T (each
+// thread 2 rows x 8 positions tc + 8 i, float4 loads: the 8 lanes of a row
+// read 8 consecutive padded K rows, one bank quad each), scale and causal
+// mask, an online softmax whose row statistics the 8 lanes sharing a row
+// reduce by shuffles, then O += P V (each thread 2 rows x HD / 8 dims, in
+// quads tc * 4 + 32 j so that the 8 lanes of a row cover all 32 banks).
+// Each CTA takes query block i and block nb - 1 - i so that the causal
+// work is even.  Arithmetic as pf_attn_kernel: f32 dot products times the
+// scale, expf, f32 sums.
 constexpr int kAtPos = 64;
-template <int HD>
+template <int HD, int R>
 struct AttnTile {
+  static constexpr int kThreads = 4 * R;   // 2 rows x (8 positions | HD / 8 dims) each
   static constexpr int kLd = HD + 4;       // padded row (conflict-free float4 reads)
   static constexpr int kPLd = kAtPos + 4;
   static constexpr int kDims = HD / 8;     // output dims per thread
-  static constexpr size_t kSmem = sizeof(float) * (3 * (size_t)kAtRows * kLd + (size_t)kAtRows * kPLd);
+  static constexpr int kKV = kAtPos * kLd;  // floats of one K or V buffer
+  static constexpr size_t kSmem = sizeof(float) * ((size_t)R * kLd + 4 * (size_t)kKV + (size_t)R * kPLd);
 };
 
-template <int HD>
-__global__ void __launch_bounds__(kPfThreads, 1) pf_attn_tiled_kernel(const float* __restrict__ q, const float* kcache,
-                                                                   const float* vcache, int T, int H, int kvH, int S,
-                                                                   int p0, float scale, float* __restrict__ out) {
-  using A = AttnTile<HD>;
+template <int HD, int R>
+__global__ void __launch_bounds__(AttnTile<HD, R>::kThreads, 1)
+    pf_attn_tiled_kernel(const float* __restrict__ q, const float* kcache, const float* vcache, int T, int H, int kvH,
+                         int S, int p0, float scale, float* __restrict__ out, unsigned int* err) {
+  using A = AttnTile<HD, R>;
+  constexpr int NT = A::kThreads;
   extern __shared__ float4 sm4[];
+  __shared__ __align__(8) uint64_t bars[2];  // buffer b's tile has landed
   float* Qs = reinterpret_cast<float*>(sm4);
-  float* Ks = Qs + kAtRows * A::kLd;
-  float* Vs = Ks + kAtRows * A::kLd;
-  float* Ps = Vs + kAtRows * A::kLd;
-  const int g = blockIdx.y, G = H / kvH, BT = kAtRows / G;
+  float* KV = Qs + R * A::kLd;              // K0, V0, K1, V1
+  float* Ps = KV + 4 * A::kKV;
+  const int g = blockIdx.y, G = H / kvH, BT = R / G;
   const int nb = (T + BT - 1) / BT;
-  const int tid = threadIdx.x, tr = tid >> 3, tc = tid & 7;
+  const int tid = threadIdx.x, tr = tid >> 3, tc = tid & 7, warp = tid / 32, lane = tid % 32;
   const float* kb = kcache + (int64_t)g * S * HD;
   const float* vb = vcache + (int64_t)g * S * HD;
-  for (int pass = 0; pass < 2; ++pass) {
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // Tile c (positions [pb, pb + 64), rows up to `last`) into buffer c & 1;
+  // rows past `last` of its V buffer are zeroed (their weight is 0, and
+  // 0 * stale bits must not make NaN).
+  auto fill = [&](int64_t c, int pb, int last) {
+    float* Kb = KV + (c & 1) * 2 * A::kKV;
+    float* Vb = Kb + A::kKV;
+    const int nrows = min(kAtPos, last - pb + 1);
+    if (warp == 0) {
+      if (lane == 0) mbar_arrive_expect_tx(&bars[c & 1], (uint32_t)(2 * nrows * HD * sizeof(float)));
+      __syncwarp();
+      for (int r = lane; r < nrows; r += 32) {
+        bulk_g2s_plain(Kb + r * A::kLd, kb + (int64_t)(pb + r) * HD, HD * sizeof(float), &bars[c & 1]);
+        bulk_g2s_plain(Vb + r * A::kLd, vb + (int64_t)(pb + r) * HD, HD * sizeof(float), &bars[c & 1]);
+      }
+    }
+    for (int i = tid; i < (kAtPos - nrows) * (HD / 4); i += NT) {
+      const int r = nrows + i / (HD / 4), cc = (i % (HD / 4)) * 4;
+      *reinterpret_cast<float4*>(Vb + r * A::kLd + cc) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  int64_t c = 0;  // tiles consumed by this CTA
+  bool ok = true;
+  for (int pass = 0; pass < 2 && ok; ++pass) {
     const int blk = pass == 0 ? (int)blockIdx.x : nb - 1 - (int)blockIdx.x;
     if (blk < 0 || blk >= nb || (pass == 1 && blk == (int)blockIdx.x)) break;
     const int t0 = blk * BT, t1 = min(t0 + BT, T);
-    __syncthreads();  // the previous block's readers of Qs are done
-    for (int i = tid; i < kAtRows * (HD / 4); i += kPfThreads) {
-      const int r = i / (HD / 4), c = (i % (HD / 4)) * 4, t = t0 + r / G;
+    const int last = p0 + t1 - 1;  // the block's last query position
+    __syncthreads();  // the previous block's readers of Qs and of the buffers are done
+    fill(c, 0, last);
+    for (int i = tid; i < R * (HD / 4); i += NT) {
+      const int r = i / (HD / 4), cc = (i % (HD / 4)) * 4, t = t0 + r / G;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (t < t1) v = *reinterpret_cast<const float4*>(q + ((int64_t)t * H + g * G + r % G) * HD + c);
-      *reinterpret_cast<float4*>(Qs + r * A::kLd + c) = v;
+      if (t < t1) v = *reinterpret_cast<const float4*>(q + ((int64_t)t * H + g * G + r % G) * HD + cc);
+      *reinterpret_cast<float4*>(Qs + r * A::kLd + cc) = v;
     }
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
     float o[2][A::kDims];
@@ -238,20 +278,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_attn_tiled_kernel(const floa
       const int t = t0 + (2 * tr + rr) / G;
       tq[rr] = t < t1 ? p0 + t : -1;
     }
-    const int last = p0 + t1 - 1;  // the block's last query position
-    for (int pb = 0; pb <= last; pb += kAtPos) {
-      __syncthreads();  // previous tile's readers of Ks/Vs/Ps are done
-      for (int i = tid; i < kAtPos * (HD / 4); i += kPfThreads) {
-        const int r = i / (HD / 4), c = (i % (HD / 4)) * 4, p = pb + r;
-        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-        if (p <= last) {
-          kv = *reinterpret_cast<const float4*>(kb + (int64_t)p * HD + c);
-          vv = *reinterpret_cast<const float4*>(vb + (int64_t)p * HD + c);
-        }
-        *reinterpret_cast<float4*>(Ks + r * A::kLd + c) = kv;
-        *reinterpret_cast<float4*>(Vs + r * A::kLd + c) = vv;
-      }
-      __syncthreads();
+    for (int pb = 0; pb <= last; pb += kAtPos, ++c) {
+      const float* Ks = KV + (c & 1) * 2 * A::kKV;
+      const float* Vs = Ks + A::kKV;
+      // Tile c and its zeroed rows become visible, and tile c - 1's readers
+      // are done; a wait that gave up anywhere stops the whole CTA.
+      ok = __syncthreads_and(mbar_wait(&bars[c & 1], (uint32_t)((c >> 1) & 1), err));
+      if (!ok) break;
+      if (pb + kAtPos <= last) fill(c + 1, pb + kAtPos, last);
       float sc[2][8];
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr)
@@ -263,7 +297,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_attn_tiled_kernel(const floa
         const float4 qb = *reinterpret_cast<const float4*>(Qs + (2 * tr + 1) * A::kLd + d);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float4 k = *reinterpret_cast<const float4*>(Ks + (tc * 8 + i) * A::kLd + d);
+          const float4 k = *reinterpret_cast<const float4*>(Ks + (tc + 8 * i) * A::kLd + d);
           sc[0][i] = fmaf(qa.x, k.x, sc[0][i]);
           sc[0][i] = fmaf(qa.y, k.y, sc[0][i]);
           sc[0][i] = fmaf(qa.z, k.z, sc[0][i]);
@@ -279,7 +313,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_attn_tiled_kernel(const floa
         float mx = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int p = pb + tc * 8 + i;
+          const int p = pb + tc + 8 * i;
           sc[rr][i] = p <= tq[rr] ? sc[rr][i] * scale : -INFINITY;
           mx = fmaxf(mx, sc[rr][i]);
         }
@@ -302,9 +336,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_attn_tiled_kernel(const floa
         m[rr] = mnew;
 #pragma unroll
         for (int d = 0; d < A::kDims; ++d) o[rr][d] *= corr;
-        float* prow = Ps + (2 * tr + rr) * A::kPLd + tc * 8;
-        *reinterpret_cast<float4*>(prow) = make_float4(sc[rr][0], sc[rr][1], sc[rr][2], sc[rr][3]);
-        *reinterpret_cast<float4*>(prow + 4) = make_float4(sc[rr][4], sc[rr][5], sc[rr][6], sc[rr][7]);
+        float* prow = Ps + (2 * tr + rr) * A::kPLd + tc;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) prow[8 * i] = sc[rr][i];
       }
       __syncthreads();
 #pragma unroll 2
@@ -314,10 +348,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_attn_tiled_kernel(const floa
         const float wa[4] = {pa.x, pa.y, pa.z, pa.w}, wq[4] = {pq.x, pq.y, pq.z, pq.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float* vrow = Vs + (p + j) * A::kLd + tc * A::kDims;
+          const float* vrow = Vs + (p + j) * A::kLd + tc * 4;
 #pragma unroll
           for (int d = 0; d < A::kDims; d += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(vrow + d);
+            const float4 v = *reinterpret_cast<const float4*>(vrow + 8 * d);
             o[0][d] = fmaf(wa[j], v.x, o[0][d]);
             o[0][d + 1] = fmaf(wa[j], v.y, o[0][d + 1]);
             o[0][d + 2] = fmaf(wa[j], v.z, o[0][d + 2]);
@@ -330,28 +364,38 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_attn_tiled_kernel(const floa
         }
       }
     }
+    if (!ok) break;
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
       if (tq[rr] < 0) continue;
       const int r = 2 * tr + rr, t = t0 + r / G;
-      float* dst = out + ((int64_t)t * H + g * G + r % G) * HD + tc * A::kDims;
+      float* dst = out + ((int64_t)t * H + g * G + r % G) * HD + tc * 4;
 #pragma unroll
       for (int d = 0; d < A::kDims; d += 4)
-        *reinterpret_cast<float4*>(dst + d) =
+        *reinterpret_cast<float4*>(dst + 8 * d) =
             make_float4(o[rr][d] / l[rr], o[rr][d + 1] / l[rr], o[rr][d + 2] / l[rr], o[rr][d + 3] / l[rr]);
     }
   }
+  // After a wait gave up, tile c's copies (the only ones in flight) get one
+  // more bounded wait before the CTA exits.
+  if (!ok && tid == 0) mbar_wait(&bars[c & 1], (uint32_t)((c >> 1) & 1), err);
+}
+
+template <int HD, int R>
+int launch_attn_tiled(const PrefillArgs& a, const float* kc, const float* vc, int T, int p0, cudaStream_t st) {
+  using A = AttnTile<HD, R>;
+  const int G = a.H / a.kvH, BT = R / G, nb = (T + BT - 1) / BT;
+  XPU_TRY_CUDA(ensure_smem_attr((const void*)pf_attn_tiled_kernel<HD, R>, A::kSmem));
+  pf_attn_tiled_kernel<HD, R><<<dim3((nb + 1) / 2, a.kvH), A::kThreads, A::kSmem, st>>>(
+      a.q, kc, vc, T, a.H, a.kvH, a.S, p0, a.attn_scale, a.attn, device_error_word());
+  XPU_TRY_CUDA(cudaGetLastError());
+  return XPU_OK;
 }
 
 template <int HD>
 int launch_attn_tiled(const PrefillArgs& a, const float* kc, const float* vc, int T, int p0, cudaStream_t st) {
-  const int G = a.H / a.kvH, BT = kAtRows / G, nb = (T + BT - 1) / BT;
-  const size_t smem = AttnTile<HD>::kSmem;
-  XPU_TRY_CUDA(ensure_smem_attr((const void*)pf_attn_tiled_kernel<HD>, smem));
-  pf_attn_tiled_kernel<HD><<<dim3((nb + 1) / 2, a.kvH), kPfThreads, smem, st>>>(a.q, kc, vc, T, a.H, a.kvH, a.S, p0,
-                                                                                a.attn_scale, a.attn);
-  XPU_TRY_CUDA(cudaGetLastError());
-  return XPU_OK;
+  const int G = a.H / a.kvH;
+  return 32 % G == 0 ? launch_attn_tiled<HD, 32>(a, kc, vc, T, p0, st) : launch_attn_tiled<HD, 64>(a, kc, vc, T, p0, st);
 }
 
 // matvecQ8Ffn's epilogue (ops/matvec/reference.ts:196-207) elementwise:
@@ -380,8 +424,9 @@ int prefill_chunk(const PrefillArgs& a, const int32_t* d_tokens, int T, int p0, 
   XPU_TRY_CUDA(cudaGetLastError());
   const size_t attn_smem = sizeof(float) * ((size_t)G * a.hd + (size_t)G * kPfChunk + 3 * (size_t)G);
   // The tiled attention takes head_dim 32, 64 or 128 with the G query heads
-  // of a kv head dividing its 64-row block; other shapes keep pf_attn_kernel.
-  const bool tiled = (a.hd == 32 || a.hd == 64 || a.hd == 128) && G <= kAtRows && kAtRows % G == 0;
+  // of a kv head dividing its 32- or 64-row block; other shapes keep
+  // pf_attn_kernel.
+  const bool tiled = (a.hd == 32 || a.hd == 64 || a.hd == 128) && 64 % G == 0;
   int rc;
   for (int l = 0; l < a.layers; ++l) {
     const PrefillLayer& L = a.layer[l];
@@ -404,8 +449,7 @@ int prefill_chunk(const PrefillArgs& a, const int32_t* d_tokens, int T, int p0, 
     if ((rc = matmul_q8_dev(a.attn, L.wo, L.ldw_qd, L.so, T, h, qd, a.hid2, a.hid, st))) return rc;
     pf_rmsnorm_kernel<<<T, kPfThreads, 0, st>>>(a.hid2, L.ffn_norm, (int)h, a.eps, a.xn);
     XPU_TRY_CUDA(cudaGetLastError());
-    if ((rc = matmul_q8_dev(a.xn, L.wg, L.ldw_h, L.sg, T, F, h, a.gate, nullptr, st)) ||
-        (rc = matmul_q8_dev(a.xn, L.wu, L.ldw_h, L.su, T, F, h, a.up, nullptr, st)))
+    if ((rc = matmul_q8_pair_dev(a.xn, L.wg, L.sg, a.gate, L.wu, L.su, a.up, L.ldw_h, T, F, h, st)))
       return rc;
     const int64_t nf = (int64_t)T * F;
     pf_silu_mul_kernel<<<(unsigned)std::min<int64_t>((nf + kPfThreads - 1) / kPfThreads, 4096), kPfThreads, 0, st>>>(

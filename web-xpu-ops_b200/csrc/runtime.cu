@@ -130,6 +130,10 @@ cudaError_t ensure_smem_attr(const void* kernel, size_t bytes) {
   size_t want = (size_t)device_info().max_smem_optin - fa.sharedSizeBytes;
   if (want < bytes) return cudaErrorInvalidValue;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
+  // The whole unified L1/shared array as shared memory, so that the CTAs the
+  // kernel's size allows per SM all fit.
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess) have = want;
   return e;
 }
