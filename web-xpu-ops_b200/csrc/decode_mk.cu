@@ -460,18 +460,56 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
   const int group = warp / wpg, wi = warp - group * wpg, ti = wi * 32 + lane;
   const bool active = group < rg;
   const int cs = ti < U ? ti : U - 1;  // slice read (clamped; x is 0 past U)
-  f2 xr[8];
+  // The slice as four int8 limbs per element, with the thread's own
+  // exponent E (of its largest magnitude, floored at -96 so that 2^(E - 30)
+  // stays a normal float): X = round(x 2^(30 - E)), |X| <= 2^30, written as
+  // balanced base-256 digits (the bytes of X + 0x80808080, top bits
+  // flipped).  xl[i][j] holds digit j of elements 4i .. 4i + 3, the word
+  // layout of the packed codes, so a row's partial is 16 dp4a into four
+  // exact int32 limb sums.  A non-finite element makes the partials NaN.
+  int xl[4][4];
+  float xpow;
+  {
+    float xv[16];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float4 t = ti < U ? reinterpret_cast<const float4*>(xs)[e * UP + ti] : make_float4(0.f, 0.f, 0.f, 0.f);
-    xr[2 * e] = make_f2(t.x, t.y);
-    xr[2 * e + 1] = make_f2(t.z, t.w);
+    for (int e = 0; e < 4; ++e) {
+      const float4 t = ti < U ? reinterpret_cast<const float4*>(xs)[e * UP + ti] : make_float4(0.f, 0.f, 0.f, 0.f);
+      xv[4 * e] = t.x;
+      xv[4 * e + 1] = t.y;
+      xv[4 * e + 2] = t.z;
+      xv[4 * e + 3] = t.w;
+    }
+    float mx = 0.0f;
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      bad |= !isfinite(xv[i]);
+      mx = fmaxf(mx, fabsf(xv[i]));
+    }
+    int E = 0;
+    if (mx > 0.0f && !bad) frexpf(mx, &E);
+    E = max(E, -96);
+    const float sc = ldexpf(1.0f, 30 - E);
+    xpow = bad ? __int_as_float(0x7fffffff) : ldexpf(1.0f, E - 30);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t u[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int X = bad ? 0 : __float2int_rn(xv[4 * i + c] * sc);
+        u[c] = ((uint32_t)X + 0x80808080u) ^ 0x80808080u;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t sel = (uint32_t)j | ((uint32_t)(4 + j) << 4);
+        xl[i][j] = (int)__byte_perm(__byte_perm(u[0], u[1], sel), __byte_perm(u[2], u[3], sel), 0x5410u);
+      }
+    }
   }
 
   // 3. Pieces of the share, in the producer's order: piece q holds rows
   // [q P, q P + rows) of each stream; row r of the piece (stream 0 rows,
   // then stream 1 rows) belongs to row group r % rg.
-  const f2 zero2 = make_f2(0.0f, 0.0f);
   const int npieces = (n + P - 1) / P;
   unsigned long long waited = 0, first_ready = 0;
   for (int q = 0; q < npieces; ++q) {
@@ -499,17 +537,24 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
       wv[t] = (active && r < R) ? *reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * (size_t)cs)
                                 : make_uint4(0u, 0u, 0u, 0u);
     }
-    f2 acc[kMkRowsPerWarp][2];
+    float v[kMkRowsPerWarp];
 #pragma unroll
     for (int t = 0; t < kMkRowsPerWarp; ++t) {
-      acc[t][0] = acc[t][1] = zero2;
-      dot16(wv[t], xr, acc[t]);
+      const int w[4] = {(int)wv[t].x, (int)wv[t].y, (int)wv[t].z, (int)wv[t].w};
+      int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a0 = __dp4a(w[i], xl[i][0], a0);
+        a1 = __dp4a(w[i], xl[i][1], a1);
+        a2 = __dp4a(w[i], xl[i][2], a2);
+        a3 = __dp4a(w[i], xl[i][3], a3);
+      }
+      // sum_j 256^j a_j, exact in two int32 halves (|a_j| <= 2^18).
+      const int lo = a0 + a1 * 256, hi = a2 + a3 * 256;
+      v[t] = fmaf((float)hi, 65536.0f, (float)lo) * xpow;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
-    float v[kMkRowsPerWarp];
-#pragma unroll
-    for (int t = 0; t < kMkRowsPerWarp; ++t) v[t] = hsum2(acc[t]);
     const float tot = warp_reduce_rows<kMkRowsPerWarp>(v, lane);
     const int t = lane / (32 / kMkRowsPerWarp), r = group + rg * t;
     if (active && lane % (32 / kMkRowsPerWarp) == 0 && r < R) {
