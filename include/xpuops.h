@@ -152,6 +152,26 @@ XPU_API int xpu_matvec_q8_stack_dev(const uint32_t* weights, int64_t weight_stri
 #define XPU_MATVEC_TENSOR_CORES  2
 XPU_API int xpu_set_matvec_path(int32_t path);
 XPU_API int xpu_matvec_path(int32_t* path);
+
+/* Row-sharded matvecQ8 over the GPUs of one node from one host process
+ * (SURVEY's xpu_dist entry points; the multi-process form is
+ * torch.distributed + NCCL, xpuops/dist.py).  No counterpart in the
+ * reference, which runs one WebGPU device.  NCCL is loaded at run time
+ * (libnccl.so.2); failures report XPU_ENCCL.
+ * xpu_dist_create: one NCCL communicator and stream per listed device.
+ * xpu_dist_matvec_q8_rowshard: a stack of `count` matrices of N rows on one
+ * x; device g (the g-th listed) holds rows [g R, (g + 1) R) of every
+ * matrix, R = N / ngpus (N must divide): weights[g] (device g memory,
+ * matrix m at weights[g] + m * weight_stride, R rows of ceil(K/4) words),
+ * scales[g] ([count][R]) and vectors[g] (x, K floats).  On return every
+ * outputs[g] ([count][N] floats on device g) holds the whole result, equal
+ * to xpu_matvec_q8_stack_dev on one GPU.  Blocking. */
+typedef struct xpu_dist xpu_dist;
+XPU_API int xpu_dist_create(int32_t ngpus, const int32_t* devices, xpu_dist** dist);
+XPU_API int xpu_dist_matvec_q8_rowshard(xpu_dist* dist, const uint32_t* const* weights, int64_t weight_stride,
+                                        const float* const* scales, const float* const* vectors, int64_t count,
+                                        int64_t N, int64_t K, float* const* outputs);
+XPU_API int xpu_dist_destroy(xpu_dist* dist);
 /* ops/gqa/reference.ts:203-303 `groupedAttention` for one decode query
  * (B = 1, L = 1, causal, queryOffset = s_eff - 1, no mask), as the resident
  * engine runs it each step (llm/engine-q8-resident.ts:1852-1853):

@@ -81,3 +81,19 @@ def test_two_rank_sharded_stack_matches_single_process(tmp_path, world, N):
         codes, scales = orc.quantize(wf, N, K)
         want = orc.matvec_q8(orc.pack_q8(codes, N, K), scales, x, N, K)
         np.testing.assert_array_equal(got[m], want)
+
+
+def test_single_process_group_rejects_bad_arguments_before_device_work():
+    """xpu_dist_create / xpu_dist_matvec_q8_rowshard validate their
+    arguments on the host (no device needed for these paths)."""
+    import ctypes as C
+
+    from xpuops._lib import XPU_EINVAL, lib
+
+    L = lib()
+    h = C.c_void_p()
+    assert L.xpu_dist_create(0, None, C.byref(h)) == XPU_EINVAL
+    assert L.xpu_dist_create(1, None, C.byref(h)) == XPU_EINVAL
+    assert L.xpu_dist_create(1, (C.c_int32 * 1)(0), None) == XPU_EINVAL
+    assert L.xpu_dist_matvec_q8_rowshard(None, None, 0, None, None, 1, 8, 8, None) == XPU_EINVAL
+    assert L.xpu_dist_destroy(None) == 0

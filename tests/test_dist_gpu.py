@@ -26,7 +26,9 @@ def _port():
     return p
 
 
-def _stack(rank_rows, first_row):
+def _shard(rank_rows, first_row):
+    """Rows [first_row, first_row + rank_rows) of every matrix and x, on the
+    current device."""
     from xpuops import ops
     from xpuops.synth import tensor_seed
 
@@ -39,6 +41,15 @@ def _stack(rank_rows, first_row):
         ops.quantizePackQ8_dev(tmp, rank_rows, K, w.data_ptr() + 4 * m * rank_rows * W, s.data_ptr() + 4 * m * rank_rows)
     x = torch.empty(K, dtype=torch.float32, device="cuda")
     ops.fill_normal_dev(x, K, tensor_seed(8, 0))
+    torch.cuda.synchronize()
+    return w, s, x
+
+
+def _stack(rank_rows, first_row):
+    from xpuops import ops
+
+    W = K // 4
+    w, s, x = _shard(rank_rows, first_row)
     y = torch.empty(M * rank_rows, dtype=torch.float32, device="cuda")
     ops.matvecQ8Stack_dev(w, rank_rows * W, s, x, M, rank_rows, K, y)
     torch.cuda.synchronize()
@@ -85,3 +96,34 @@ def test_two_gpu_row_shard_equals_one_gpu(tmp_path, path):
     finally:
         ops.setMatvecPath(ops.MATVEC_AUTO)
     np.testing.assert_array_equal(np.load(out), single)
+
+
+@pytest.mark.parametrize("path", ["cuda_cores", "tensor_cores"])
+def test_single_process_group_equals_one_gpu(path):
+    """xpu_dist_matvec_q8_rowshard: one process, two GPUs, each with its row
+    shard; every device ends with the whole stack's output, bit-identical to
+    the unsharded stack on one GPU."""
+    from xpuops import ops
+    from xpuops.dist import RowShardGroup
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    code = {"cuda_cores": ops.MATVEC_CUDA_CORES, "tensor_cores": ops.MATVEC_TENSOR_CORES}[path]
+    G, W = 2, K // 4
+    R = N // G
+    shards, outs = [], []
+    for g in range(G):
+        torch.cuda.set_device(g)
+        shards.append(_shard(R, g * R))
+        outs.append(torch.full((M * N,), float("nan"), dtype=torch.float32, device="cuda"))
+    ops.setMatvecPath(code)
+    try:
+        with RowShardGroup(range(G)) as grp:
+            grp.matvecQ8StackRowShard([sh[0] for sh in shards], R * W, [sh[1] for sh in shards],
+                                      [sh[2] for sh in shards], M, N, K, outs)
+        torch.cuda.set_device(0)
+        single = _stack(N, 0).cpu().numpy()
+    finally:
+        ops.setMatvecPath(ops.MATVEC_AUTO)
+    for g in range(G):
+        np.testing.assert_array_equal(outs[g].cpu().numpy(), single)
