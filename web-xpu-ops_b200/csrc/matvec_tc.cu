@@ -406,11 +406,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const double sc1 = ldexp(1.0, 62 - E);
 
     // Finishes row `row` of tile `tile` from its 16 accumulators.
-    auto finish_row = [&](int64_t tile, int row, const int (&D)[16]) {
+    // The row's scale, loaded before its accumulator is ready (0 past N).
+    auto row_scale = [&](int64_t tile, int row) -> float {
+      const int64_t mi = tile / g.tiles_per_mat;
+      const int64_t grow = (tile % g.tiles_per_mat) * kTcBM + row;
+      return grow < g.N ? __ldg(g.s + mi * g.s_stride + grow) : 0.0f;
+    };
+    auto finish_row = [&](int64_t tile, int row, const int (&D)[16], float scale) {
       const int64_t mi = tile / g.tiles_per_mat;
       const int64_t grow = (tile % g.tiles_per_mat) * kTcBM + row;
       if (grow >= g.N) return;
-      const double sc = (double)g.s[mi * g.s_stride + grow];
+      const double sc = (double)scale;
       double v;
       if (!flags) {
         double v1 = 0.0, v2 = 0.0;
@@ -438,6 +444,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto finish_segment = [&](int64_t j) -> bool {
       const Seg sg = cur.get(j);
       const int b = (int)(j & 1);
+      const float scale = row_scale(sg.tile, q * 32 + lane);
       if (tid == 0) s_flag = !abort_flag && mbar_wait(&tfull[b], (uint32_t)((j / 2) & 1), g.err);
       named_bar_sync(kTcBarWriters, kTcWriters);
       const bool ready = s_flag;
@@ -451,7 +458,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[b]);
       const int row = q * 32 + lane;
       if (sg.whole) {
-        finish_row(sg.tile, row, D);
+        finish_row(sg.tile, row, D, scale);
         return true;
       }
       // Split tile: publish this CTA's partial, take a ticket.
@@ -504,7 +511,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               sum[4 * i + 3] += v[u][i].w;
             }
         }
-        finish_row(sg.tile, row, sum);
+        finish_row(sg.tile, row, sum, scale);
       }
       return true;
     };
