@@ -608,8 +608,8 @@ bool matvec_tc_applies(const uint32_t* w, int64_t mat_stride, int64_t count, int
   const int path = g_matvec_path.load(std::memory_order_relaxed);
   if (path == XPU_MATVEC_CUDA_CORES) return false;
   if (path == XPU_MATVEC_TENSOR_CORES) return true;
-  const int64_t bytes = count * N * W * 4;
-  return bytes >= kTcMinBytes || (K >= kTcLongRows && bytes >= kTcMinBytesLongRows);
+  const double bytes = (double)count * (double)N * (double)W * 4.0;  // up to ~2^63: no int64 product
+  return bytes >= (double)kTcMinBytes || (K >= kTcLongRows && bytes >= (double)kTcMinBytesLongRows);
 }
 
 // The weight tensor map of one (pointer, shape, stride), cached: encoding is
