@@ -81,3 +81,26 @@ def test_prefill_benchmark_geometry():
         (got,) = eng.forward(prompt)
         want = oracle.forward(prompt)
         assert logits_agree(got, want, 1e-3) is None
+
+
+@pytest.mark.parametrize("heads,kv_heads,head_dim,n_prompt", [(16, 4, 128, 130), (8, 8, 64, 37), (32, 2, 32, 70),
+                                                             (64, 1, 32, 45), (16, 4, 128, 600)])
+def test_prefill_attention_geometries(heads, kv_heads, head_dim, n_prompt):
+    """The tiled prefill attention's other blocks: head_dim 128 (config 3's
+    heads), one query head per kv head (G = 1), 16 and 64 query heads per kv
+    head (32- and 64-row blocks), and a 600-token prompt whose second chunk
+    starts at position 512.  Hidden 256 throughout (the projections map it to
+    and from heads x head_dim)."""
+    cfg = xpuops.LlamaConfig(numLayers=2, hiddenSize=256, numHeads=heads, numKvHeads=kv_heads, headDim=head_dim,
+                             ffnHidden=512, vocabSize=500, ropeTheta=10000.0, rmsNormEps=1e-5,
+                             maxSeqLen=n_prompt + 8)
+    weights = random_llama(cfg, seed=heads + head_dim + n_prompt)
+    prompt = np.random.default_rng(n_prompt).integers(0, cfg.vocabSize, n_prompt).tolist()
+    oracle = orc.LlamaOracle(cfg, weights)
+    with LlamaEngineQ8Resident.create(cfg, weights) as eng:
+        (got,) = eng.forward(prompt)
+        want = oracle.forward(prompt)
+        assert logits_agree(got, want, 1e-3) is None
+        tok = orc.argmax(want)
+        (got,) = eng.forward([tok])
+        assert logits_agree(got, oracle.forward([tok]), 1e-3) is None
