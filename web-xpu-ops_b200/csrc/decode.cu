@@ -701,8 +701,11 @@ int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, in
   if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess)
     return fail(cuda_status(cudaGetLastError(), "cudaStreamCreate"));
 
-  int64_t max_codes = (int64_t)c.vocab_size * h;
-  for (int i = 0; i < c.num_layers; ++i) max_codes = std::max<int64_t>(max_codes, (int64_t)c.ffn_hidden * h);
+  // The staging buffer holds the largest matrix uploaded: embeddings and
+  // lm_head [vocab, h], wq [H hd, h], wk/wv [kvH hd, h], wo [h, H hd],
+  // gate/up [ffn, h], down [h, ffn].
+  const int64_t qdim = (int64_t)c.num_heads * c.head_dim, kvdim = (int64_t)c.num_kv_heads * c.head_dim;
+  const int64_t max_codes = std::max<int64_t>({(int64_t)c.vocab_size * h, qdim * h, kvdim * h, (int64_t)c.ffn_hidden * h});
   int8_t* tmp = nullptr;
   if ((rc = dev_alloc(e, &tmp, (size_t)max_codes))) return fail(rc);
 
