@@ -291,6 +291,25 @@ typedef struct xpu_llama xpu_llama;
 XPU_API int xpu_llama_create(const xpu_llama_config* config,
                      const xpu_llama_weights_q8* weights, int device,
                      xpu_llama** engine);
+/* llm/weights-q8-io.ts:14-128 (llamaConfigFromManifest + buildLlamaWeightsQ8)
+ * then create: `manifest_json` is the converter's manifest (a "config"
+ * object and a "weights" array of {name, kind "quant", shape [N, K],
+ * codesOffset, scaleOffset} / {name, kind "norm", shape, offset} entries),
+ * `codes`/`scales`/`norms` the three buffers it indexes (lengths in
+ * elements), `max_seq_len` the loader's sequence-length policy.  Every entry
+ * is checked against the buffers before any device work; a missing name
+ * gives the reference's message.  Converted weights already have the RoPE
+ * row permutation applied (xpu_permute_rope_channels). */
+XPU_API int xpu_llama_create_from_manifest(const char* manifest_json, const int8_t* codes, int64_t codes_len,
+                                           const float* scales, int64_t scales_len, const float* norms,
+                                           int64_t norms_len, int32_t max_seq_len, int32_t device,
+                                           xpu_llama** engine);
+/* llm/weights.ts:95-115 permuteRopeChannels: an HF [heads * head_dim,
+ * in_features] projection with rotate_half channel order -> this engine's
+ * adjacent-pair order (rows i and i + head_dim/2 of each head become rows
+ * 2i and 2i + 1).  Host arrays; `out` must not alias `weight`. */
+XPU_API int xpu_permute_rope_channels(const float* weight, int64_t heads, int64_t head_dim, int64_t in_features,
+                                      float* out);
 
 /* llm/engine-q8-resident.ts:1276-1283 `forward(tokens)`: the first call after
  * create/reset prefills `tokens` (n >= 1) and writes the final position's

@@ -17,6 +17,6 @@ from .llama import (LLAMA_1B_DECODE_CONFIG, SARASHINA_2_2_1B_CONFIG, TINY_FIXTUR
 from .ops import (MATVEC_AUTO, MATVEC_CUDA_CORES, MATVEC_TENSOR_CORES, DeviceBuffer, matmulQ8, matmulQ8_dev, matvecPath,
                   matvecQ8, matvecQ8_dev, matvecQ8Ffn, matvecQ8Ffn_dev, matvecQ8Residual, matvecQ8Residual_dev,
                   packInt8Rows, packQ8, quantize, quantizePackQ8, setMatvecPath)
-from .weights_io import buildLlamaWeightsQ8, llamaConfigFromManifest
+from .weights_io import buildLlamaWeightsQ8, llamaConfigFromManifest, permuteRopeChannels
 
 __all__ = [n for n in dir() if not n.startswith("_")]

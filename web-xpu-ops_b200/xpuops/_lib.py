@@ -130,6 +130,8 @@ SIGNATURES = {
     "xpu_fill_normal_f32_dev": [P, I64, I64, C.c_uint64, C.c_double, C.c_double, C.c_double, C.c_double, P],
     "xpu_matvec_q8_stack_dev": [P, I64, P, P, I64, I64, I64, P, P],
     "xpu_set_matvec_path": [I32],
+    "xpu_llama_create_from_manifest": [C.c_char_p, P, I64, P, I64, P, I64, I32, I32, C.POINTER(P)],
+    "xpu_permute_rope_channels": [P, I64, I64, I64, P],
     "xpu_dist_create": [I32, C.POINTER(I32), C.POINTER(P)],
     "xpu_dist_matvec_q8_rowshard": [P, C.POINTER(P), I64, C.POINTER(P), C.POINTER(P), I64, I64, I64, C.POINTER(P)],
     "xpu_dist_destroy": [P],

@@ -171,6 +171,27 @@ class LlamaEngineQ8Resident:
         del keep
         return cls(config, h)
 
+    @classmethod
+    def fromManifest(cls, manifest, codes, scales, norms, maxSeqLen: int, device: int = 0) -> "LlamaEngineQ8Resident":
+        """A converted checkpoint (llm/weights-q8-io.ts): the manifest (dict or
+        JSON text) and its codes / scales / norms buffers, loaded through
+        xpu_llama_create_from_manifest."""
+        import json
+
+        text = manifest if isinstance(manifest, str) else json.dumps(manifest)
+        cfg = json.loads(text)["config"]
+        codes = np.ascontiguousarray(codes, dtype=np.int8)
+        scales = np.ascontiguousarray(scales, dtype=np.float32)
+        norms = np.ascontiguousarray(norms, dtype=np.float32)
+        require_device()
+        h = C.c_void_p()
+        check(lib().xpu_llama_create_from_manifest(text.encode(), codes.ctypes.data_as(C.c_void_p), codes.size,
+                                                   scales.ctypes.data_as(C.c_void_p), scales.size,
+                                                   norms.ctypes.data_as(C.c_void_p), norms.size, maxSeqLen, device,
+                                                   C.byref(h)))
+        from .weights_io import llamaConfigFromManifest
+        return cls(llamaConfigFromManifest(cfg, maxSeqLen), h)
+
     def _handle(self):
         if not self._h:
             raise RuntimeError("LlamaEngineQ8Resident: engine is closed")

@@ -52,3 +52,20 @@ def buildLlamaWeightsQ8(entries: Iterable[dict], codes: np.ndarray, scales: np.n
                                   wGate=q(f"layers.{i}.wGate"), wUp=q(f"layers.{i}.wUp"), wDown=q(f"layers.{i}.wDown"))
               for i in range(numLayers)]
     return LlamaWeightsQ8(embedTokens=q("embedTokens"), layers=layers, finalNorm=nm("finalNorm"), lmHead=q("lmHead"))
+
+
+def permuteRopeChannels(weight, heads: int, headDim: int, inFeatures: int) -> np.ndarray:
+    """llm/weights.ts:95-115 (xpu_permute_rope_channels): rows i and
+    i + headDim/2 of each head become rows 2i and 2i + 1."""
+    import ctypes as C
+
+    from ._lib import XpuInvalidArgument, check, lib
+
+    w = np.ascontiguousarray(weight, dtype=np.float32)
+    if w.size != heads * headDim * inFeatures:
+        raise XpuInvalidArgument(1, f"permuteRopeChannels: expected {heads * headDim * inFeatures} elements, "
+                                    f"got {w.size}")
+    out = np.empty_like(w)
+    check(lib().xpu_permute_rope_channels(w.ctypes.data_as(C.c_void_p), heads, headDim, inFeatures,
+                                          out.ctypes.data_as(C.c_void_p)))
+    return out
