@@ -560,6 +560,28 @@ def run_decode(args, torch, world, max_over_ranks, barrier):
             "e2e_host_forward": {"tokens_per_s": round(n_host / (host_ms / 1e3) * world, 1),
                                  "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * c.vocabSize},
         }
+        # The same decode with llm/sampler.ts top-p sampling on the device
+        # (temperature 1, topP 0.9) choosing every token; the rng is a seeded
+        # generator whose values are the steps' draws.
+        draws = iter(np.random.default_rng(44).random(warm + args.decode_steps).tolist())
+        opts = {"temperature": 1.0, "topP": 0.9, "rng": lambda: next(draws)}
+        eng.setKv(0, kv0[0], kv0[1], ctx)
+        eng.sampleSteps(first, warm, opts)
+        barrier()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(es)
+        stoks = eng.sampleSteps(first, args.decode_steps, opts)
+        d1.record(es)
+        d1.synchronize()
+        sms = max_over_ranks(d0.elapsed_time(d1))
+        out["sampled"] = {
+            "tokens_per_s_per_gpu": round(args.decode_steps / (sms / 1e3), 1),
+            "ms_per_token": round(sms / args.decode_steps, 4),
+            "sampler_us_per_token": round((sms - ms) / args.decode_steps * 1e3, 1),
+            "mode": "top-p on the device: temperature 1.0, topP 0.9, seeded draws",
+            "distinct_tokens": int(len(set(np.asarray(stoks).tolist()))),
+            "gpu_launches_per_token": (1 if persistent else 5 * c.numLayers + 3) + 3,
+        }
         # Prefill: a 512-token prompt through the batched prefill (tensor-core
         # matmulQ8 GEMMs), measured on the engine stream; forward() also
         # returns the final logits to the host.

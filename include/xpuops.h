@@ -220,6 +220,41 @@ XPU_API int xpu_fill_normal_f32_dev(float* out, int64_t n, int64_t start, uint64
                                     double mean, double std, double outlier_frac,
                                     double outlier_mul, void* stream);
 
+/* ---- the token sampler (llm/sampler.ts) ------------------------------- */
+/* llm/sampler.ts `sampleNext` (:149-166): the next token id from a logits
+ * vector, after a constraint's mask (:58-66).  XPU_SAMPLE_GREEDY is
+ * `argmax` (:68-79); XPU_SAMPLE_TOP_P is `sampleTopP` (:86-140): softmax of
+ * logit / temperature, the smallest probability-descending prefix whose mass
+ * reaches top_p, then one draw.  The reference's order of tokens
+ * (probability descending, ids ascending among equals) is kept; masses are
+ * summed exactly, so a token differs from the reference's f64 walk only
+ * where top_p or the draw lies within f64 rounding of a boundary. */
+#define XPU_SAMPLE_GREEDY 0
+#define XPU_SAMPLE_TOP_P  1
+/* The reference's `rng: () => number` (:55, default Math.random). */
+typedef double (*xpu_rng_fn)(void* ctx);
+/* Host arrays, blocking, on the current device.  `logits` are f64 (JS
+ * numbers; a Float32Array widens exactly).  `allowed` lists the legal ids,
+ * `allowed_count` < 0 meaning unconstrained (`null`) and 0 the reference's
+ * "sampleNext: constraint allows no token to follow this prefix" error.
+ * Top-p calls `rng(rng_ctx)` exactly once, after the option checks and the
+ * no-finite-logit check, as the reference does.  *token = -1 where the
+ * reference returns `undefined` (every probability 0 or NaN: an infinite
+ * logit).  Errors: XPU_EINVAL with the reference's message. */
+XPU_API int xpu_sample_next(const double* logits, int64_t n, const int32_t* allowed,
+                    int64_t allowed_count, int32_t mode, double temperature, double top_p,
+                    xpu_rng_fn rng, void* rng_ctx, int32_t* token);
+/* Device pointers, async on `stream`, graph-capturable: `logits` [n] f32,
+ * `allowed_bits` a bitset over ids ([ceil(n / 32)] u32, bit i of word i/32;
+ * NULL = unconstrained), `draw` one f64 (the rng's value; unused by greedy),
+ * `token` one int32 written with the id, -1 for "no finite logit to choose
+ * from" or -2 where the reference returns `undefined`.  Option errors are
+ * returned before anything is launched.  Its scratch (8 bytes per id) comes
+ * from the library's stream-ordered pool, as the tensor-core GEMV's does. */
+XPU_API int xpu_sample_next_dev(const float* logits, int64_t n, const uint32_t* allowed_bits,
+                        int32_t mode, double temperature, double top_p, const double* draw,
+                        int32_t* token, void* stream);
+
 /* ---- the resident Q8 Llama engine (llm/engine-q8-resident.ts) ---------- */
 
 /* ops/matmul/reference.ts:87-137 `matmulQ8({a, weight, scale, N, M, K})`:
@@ -377,6 +412,19 @@ XPU_API int xpu_llama_decode_dev(xpu_llama* engine, const int32_t* token_dev, in
  * next step's input with no host round trip.  `tokens_out` (host, nullable,
  * [steps]) receives each step's argmax.  Requires a prefilled engine. */
 XPU_API int xpu_llama_greedy_steps(xpu_llama* engine, int32_t first_token, int32_t steps,
+                           int32_t* tokens_out);
+/* `greedy_steps` with llm/sampler.ts `sampleNext` in "top-p" mode choosing
+ * every step's token on the device (xpu_sample_next_dev's kernels on the
+ * engine's stream): `draws` (host, [steps]) are the values the caller's rng
+ * returns, one per step in order; `allowed` / `allowed_count` a constraint
+ * applied to every step (allowed_count < 0: none; 0 is the reference's
+ * "constraint allows no token" error).  Option errors carry the reference's
+ * messages.  A step with no finite logit, or whose nucleus is empty (the
+ * reference returns `undefined`), makes the call return XPU_EINVAL after the
+ * loop; the engine has then taken every step. */
+XPU_API int xpu_llama_sample_steps(xpu_llama* engine, int32_t first_token, int32_t steps,
+                           double temperature, double top_p, const double* draws,
+                           const int32_t* allowed, int64_t allowed_count,
                            int32_t* tokens_out);
 XPU_API int xpu_llama_logits_dev(xpu_llama* engine, float** logits_dev);
 XPU_API int xpu_llama_stream(xpu_llama* engine, void** stream);

@@ -63,6 +63,8 @@ def _declare(L):
     L.or_gather_dequant_rows.argtypes = [P, P, I64, P, I64, I64, P]
     L.or_argmax.argtypes = [P, I64]
     L.or_argmax.restype = C.c_int32
+    L.or_sample_next.argtypes = [P, I64, P, C.c_int, C.c_double, C.c_double, C.c_double, P, P, C.c_char_p]
+    L.or_sample_next.restype = C.c_int
     L.or_llama_create.argtypes = [P, P, C.POINTER(P), C.c_char_p]
     L.or_llama_create.restype = C.c_int
     L.or_llama_forward.argtypes = [P, P, C.c_int32, P, C.c_char_p]
@@ -211,6 +213,29 @@ def gather_dequant_rows(codes, scale, indices, D: int) -> np.ndarray:
 def argmax(logits) -> int:
     a = _c(logits, np.float32)
     return int(lib().or_argmax(_p(a), a.size))
+
+
+def sample_next(logits, allowed=None, mode="greedy", temperature=1.0, top_p=1.0, draw=0.0):
+    """llm/sampler.ts `sampleNext` after the constraint check: `allowed` is an
+    iterable of legal ids (None = unconstrained), `draw` the rng's value.
+    Returns (token or None for the reference's `undefined`, diag) where diag
+    = (nucleus size, nucleus total, topP margin, draw margin); raises
+    OracleError with the reference's message."""
+    a = _c(logits, np.float64)
+    mask = None
+    if allowed is not None:
+        mask = np.zeros(max(a.size, 1), np.uint8)
+        ids = np.array([i for i in allowed if 0 <= i < a.size], np.int64)
+        mask[ids] = 1
+    tok = C.c_int32(0)
+    diag = np.zeros(4, np.float64)
+    err = C.create_string_buffer(256)
+    rc = lib().or_sample_next(_p(a), a.size, _p(mask) if mask is not None else None,
+                              0 if mode == "greedy" else 1, float(temperature), float(top_p),
+                              float(draw), C.byref(tok), _p(diag), err)
+    if rc:
+        raise OracleError(err.value.decode())
+    return (None if tok.value < 0 else int(tok.value)), tuple(float(d) for d in diag)
 
 
 # ---- engine ----------------------------------------------------------------

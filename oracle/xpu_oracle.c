@@ -581,3 +581,122 @@ void or_llama_destroy(or_llama* e) {
   free(e->q); free(e->q_roped); free(e->attn); free(e->k); free(e->v); free(e->k_roped); free(e->gated);
   free(e);
 }
+
+/* ------------------------------------------------------------------------ */
+/* The token sampler, llm/sampler.ts.                                        */
+
+typedef struct {
+  double p;
+  int64_t i;
+} or_prob;
+
+/* `.sort((a, b) => probs[b] - probs[a])` on ids filtered in ascending order:
+ * a stable sort, so equal probabilities keep ascending ids. */
+static int or_prob_desc(const void* a, const void* b) {
+  const or_prob* x = (const or_prob*)a;
+  const or_prob* y = (const or_prob*)b;
+  if (x->p != y->p) return x->p < y->p ? 1 : -1;
+  return x->i < y->i ? -1 : (x->i > y->i ? 1 : 0);
+}
+
+/* llm/sampler.ts:58-66 applyMask, :68-79 argmax, :86-140 sampleTopP,
+ * :149-166 sampleNext. */
+int or_sample_next(const double* logits, int64_t n, const uint8_t* allowed, int mode, double temperature,
+                   double top_p, double draw, int32_t* token, double* diag, char* err) {
+  double* masked = (double*)malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+  for (int64_t i = 0; i < n; ++i) masked[i] = (!allowed || allowed[i]) ? logits[i] : -INFINITY;
+  if (diag) diag[0] = diag[1] = diag[2] = diag[3] = 0.0;
+  if (mode == 0) {
+    int64_t best = -1;
+    double bv = -INFINITY;
+    for (int64_t i = 0; i < n; ++i)
+      if (masked[i] > bv) {
+        bv = masked[i];
+        best = i;
+      }
+    free(masked);
+    if (best < 0) {
+      snprintf(err, 256, "sampleNext: no finite logit to choose from");
+      return -1;
+    }
+    *token = (int32_t)best;
+    return 0;
+  }
+  if (!(temperature > 0)) {
+    free(masked);
+    snprintf(err, 256, "sampleTopP: temperature must be > 0");
+    return -1;
+  }
+  if (!(top_p > 0) || top_p > 1) {
+    free(masked);
+    snprintf(err, 256, "sampleTopP: topP must be in (0, 1]");
+    return -1;
+  }
+  double* probs = (double*)malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+  double max_scaled = -INFINITY;
+  for (int64_t i = 0; i < n; ++i) {
+    const double v = masked[i] / temperature;
+    probs[i] = v;
+    if (v > max_scaled) max_scaled = v;
+  }
+  free(masked);
+  if (max_scaled == -INFINITY) {
+    free(probs);
+    snprintf(err, 256, "sampleTopP: no finite logit to choose from");
+    return -1;
+  }
+  double total = 0.0;
+  for (int64_t i = 0; i < n; ++i) {
+    probs[i] = exp(probs[i] - max_scaled);
+    total += probs[i];
+  }
+  or_prob* order = (or_prob*)malloc((size_t)(n > 0 ? n : 1) * sizeof(or_prob));
+  int64_t len = 0;
+  for (int64_t i = 0; i < n; ++i)
+    if (probs[i] > 0) {
+      order[len].p = probs[i];
+      order[len].i = i;
+      ++len;
+    }
+  free(probs);
+  qsort(order, (size_t)len, sizeof(or_prob), or_prob_desc);
+  double cumulative = 0.0, prev_frac = 0.0;
+  int64_t cutoff = len;
+  double cut_margin = INFINITY;
+  for (int64_t k = 0; k < len; ++k) {
+    cumulative += order[k].p;
+    const double frac = cumulative / total;
+    if (frac >= top_p) {
+      cutoff = k + 1;
+      cut_margin = fmin(frac - top_p, top_p - prev_frac);
+      break;
+    }
+    prev_frac = frac;
+  }
+  double nucleus_total = 0.0;
+  for (int64_t k = 0; k < cutoff; ++k) nucleus_total += order[k].p;
+  const double d = draw * nucleus_total;
+  double acc = 0.0, draw_margin = 0.0;
+  int64_t pick = -1;
+  for (int64_t k = 0; k < cutoff; ++k) {
+    const double before = acc;
+    acc += order[k].p;
+    if (d < acc) {
+      pick = order[k].i;
+      draw_margin = fmin(acc - d, d - before) / nucleus_total;
+      break;
+    }
+  }
+  /* The floating-point edge: the last nucleus member (`undefined` when the
+   * nucleus is empty). */
+  if (pick < 0) pick = cutoff > 0 ? order[cutoff - 1].i : -1;
+  if (diag) {
+    diag[0] = (double)cutoff;
+    diag[1] = nucleus_total;
+    diag[2] = cut_margin;
+    diag[3] = draw_margin;
+  }
+  free(order);
+  *token = (int32_t)pick;
+  return 0;
+}

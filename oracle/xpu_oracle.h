@@ -82,6 +82,18 @@ void or_gather_dequant_rows(const int8_t* codes, const float* scale, int64_t row
 /* llm/engine.ts:226-232 */
 int32_t or_argmax(const float* logits, int64_t n);
 
+/* llm/sampler.ts:56-166 `sampleNext` after the constraint check: the mask
+ * (`allowed`, n bytes, 1 = legal; NULL = unconstrained) is applied to the raw
+ * logits, then greedy (mode 0, `argmax`) or temperature + top-p (mode 1,
+ * `sampleTopP`) with `draw` as the one value the injected rng returns.
+ * Returns 0 with *token (-1 where the reference returns `undefined`), or -1
+ * with the reference's error message in err.  diag (nullable, 4 doubles):
+ * the nucleus size, the nucleus total, and the distances of topP and of the
+ * draw from the nearest decision boundary (relative to total and nucleus
+ * total; 0 where the draw fell past the end). */
+int or_sample_next(const double* logits, int64_t n, const uint8_t* allowed, int mode, double temperature,
+                   double top_p, double draw, int32_t* token, double* diag, char* err);
+
 /* llm/engine-q8-resident.ts: create / forward / reset / position. */
 typedef struct or_llama or_llama;
 int or_llama_create(const xpu_llama_config* config, const xpu_llama_weights_q8* weights,

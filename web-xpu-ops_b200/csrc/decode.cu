@@ -26,6 +26,7 @@
 #include "decode_mk.cuh"
 #include "matvec_launch.cuh"
 #include "prefill.cuh"
+#include "sampler.cuh"
 
 namespace xpu {
 
@@ -957,6 +958,50 @@ int xpu_llama_greedy_steps(xpu_llama* e, int32_t first_token, int32_t steps, int
   if (rc) return rc;
   e->tokens_so_far = base + steps;
   return XPU_OK;
+}
+
+int xpu_llama_sample_steps(xpu_llama* e, int32_t first_token, int32_t steps, double temperature, double top_p,
+                           const double* draws, const int32_t* allowed, int64_t allowed_count, int32_t* tokens_out) {
+  XPU_REQUIRE(e && steps >= 0, XPU_EINVAL, "xpu_llama_sample_steps: bad arguments");
+  XPU_REQUIRE(steps == 0 || draws, XPU_EINVAL, "xpu_llama_sample_steps: null draws");
+  XPU_REQUIRE(allowed_count < 0 || allowed || allowed_count == 0, XPU_EINVAL,
+              "xpu_llama_sample_steps: null allowed list");
+  XPU_REQUIRE(allowed_count != 0, XPU_EINVAL, "sampleNext: constraint allows no token to follow this prefix");
+  int rc = sampler_check_options(temperature, top_p);
+  if (rc) return rc;
+  XPU_REQUIRE(e->tokens_so_far > 0, XPU_ESTATE, "xpu_llama_sample_steps: prefill first (forward or set_kv)");
+  XPU_REQUIRE((int64_t)e->tokens_so_far + steps <= e->c.max_seq_len, XPU_ERANGE,
+              "LlamaEngineQ8Resident.forward: position %lld exceeds maxSeqLen=%d",
+              (long long)e->tokens_so_far + steps, e->c.max_seq_len);
+  XPU_TRY_CUDA(cudaSetDevice(e->device));
+  EngineSampler es;
+  struct Close {
+    EngineSampler* es;
+    cudaStream_t st;
+    ~Close() {
+      if (es->mem) {
+        cudaStreamSynchronize(st);
+        scratch_free(es->mem, st);
+      }
+    }
+  } close{&es, e->stream};
+  if ((rc = engine_sampler_open(&es, e->c.vocab_size, allowed, allowed_count, draws, steps, e->stream))) return rc;
+  const int32_t base = e->tokens_so_far;
+  e->h_tokens[base] = first_token;
+  XPU_TRY_CUDA(cudaMemcpyAsync(e->d_token, e->h_tokens + base, 4, cudaMemcpyHostToDevice, e->stream));
+  for (int32_t s = 0; s < steps; ++s) {
+    if ((rc = launch_step(e))) return rc;
+    if ((rc = engine_sampler_step(&es, e->logits, temperature, top_p, s, e->d_pos, e->d_gen, e->d_next, e->d_token,
+                                  e->c.max_seq_len, e->stream)))
+      return rc;
+  }
+  if (tokens_out && steps > 0)
+    XPU_TRY_CUDA(cudaMemcpyAsync(tokens_out, e->d_gen + base, (size_t)steps * 4, cudaMemcpyDeviceToHost, e->stream));
+  XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  rc = finish_steps(e);
+  const int rc2 = engine_sampler_close(&es, e->stream);
+  e->tokens_so_far = base + steps;
+  return rc ? rc : rc2;
 }
 
 int xpu_llama_logits_dev(xpu_llama* e, float** logits_dev) {

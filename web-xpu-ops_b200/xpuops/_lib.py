@@ -99,6 +99,9 @@ class ForwardProfileC(C.Structure):
     ]
 
 
+# llm/sampler.ts `rng: () => number`, as the C ABI's xpu_rng_fn.
+RNG_FN = C.CFUNCTYPE(C.c_double, C.c_void_p)
+
 # name -> (argtypes); every function returns int (status) unless listed in _RESTYPE.
 SIGNATURES = {
     "xpu_last_error": [],
@@ -144,6 +147,9 @@ SIGNATURES = {
     "xpu_llama_profile_trace": [P, P, I64, C.POINTER(I64), C.POINTER(I32), C.POINTER(I32)],
     "xpu_llama_decode_dev": [P, P, P],
     "xpu_llama_greedy_steps": [P, I32, I32, P],
+    "xpu_llama_sample_steps": [P, I32, I32, C.c_double, C.c_double, P, P, I64, P],
+    "xpu_sample_next": [P, I64, P, I64, I32, C.c_double, C.c_double, RNG_FN, P, C.POINTER(I32)],
+    "xpu_sample_next_dev": [P, I64, P, I32, C.c_double, C.c_double, P, P, P],
     "xpu_llama_logits_dev": [P, C.POINTER(P)],
     "xpu_llama_stream": [P, C.POINTER(P)],
     "xpu_llama_reset": [P],

@@ -242,6 +242,23 @@ class LlamaEngineQ8Resident:
                                            out.ctypes.data_as(C.c_void_p)))
         return out[:steps]
 
+    def sampleSteps(self, first_token: int, steps: int, options, allowed=None) -> np.ndarray:
+        """`greedySteps` with llm/sampler.ts `sampleNext` in top-p mode picking
+        every step's token on the device.  `options` are top-p options
+        ({"temperature", "topP", "rng"}); the rng is called once per step, in
+        step order, before the loop starts, and its values are the steps'
+        draws.  `allowed` (optional ids) constrains every step."""
+        from .sampler import allowed_ids, topPOptions
+        temperature, top_p, rng = topPOptions(options)
+        draws = np.array([float(rng()) for _ in range(max(int(steps), 0))] or [0.0], np.float64)
+        ids = allowed_ids(allowed) if allowed is not None else None
+        out = np.zeros(max(steps, 1), np.int32)
+        check(lib().xpu_llama_sample_steps(
+            self._handle(), int(first_token), int(steps), temperature, top_p, draws.ctypes.data_as(C.c_void_p),
+            ids.ctypes.data_as(C.c_void_p) if ids is not None and ids.size else None,
+            -1 if ids is None else int(ids.size), out.ctypes.data_as(C.c_void_p)))
+        return out[:steps]
+
     def reset(self) -> None:
         """llm/engine-q8-resident.ts:993-996."""
         check(lib().xpu_llama_reset(self._handle()))
