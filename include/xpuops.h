@@ -249,8 +249,10 @@ XPU_API int xpu_sample_next(const double* logits, int64_t n, const int32_t* allo
  * NULL = unconstrained), `draw` one f64 (the rng's value; unused by greedy),
  * `token` one int32 written with the id, -1 for "no finite logit to choose
  * from" or -2 where the reference returns `undefined`.  Option errors are
- * returned before anything is launched.  Its scratch (8 bytes per id) comes
- * from the library's stream-ordered pool, as the tensor-core GEMV's does. */
+ * returned before anything is launched.  Its scratch (8 bytes per id plus a
+ * 5 MB probability histogram) is one per (device, stream), allocated and
+ * zeroed by the first call on the stream or one with a larger n (make that
+ * call outside any graph capture); later calls allocate nothing. */
 XPU_API int xpu_sample_next_dev(const float* logits, int64_t n, const uint32_t* allowed_bits,
                         int32_t mode, double temperature, double top_p, const double* draw,
                         int32_t* token, void* stream);

@@ -35,7 +35,10 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "matvec_launch.cuh"
@@ -218,8 +221,8 @@ __global__ void __launch_bounds__(kPrepThreads) sp_argmax_kernel(const T* __rest
 
 // ------------------------------------------------------ top-p: prepare --
 // llm/sampler.ts:95-105: maxScaled over logit / T (a NaN never wins), and
-// whether any scaled logit is NaN.  Also clears the band histogram that the
-// keys kernel fills.
+// whether any scaled logit is NaN.  Also resets the smallest-key word that
+// the keys kernel lowers.
 template <typename T>
 __global__ void __launch_bounds__(kPrepThreads) sp_max_kernel(const T* __restrict__ logits, int64_t n,
                                                               const uint32_t* __restrict__ allowed,
@@ -229,11 +232,6 @@ __global__ void __launch_bounds__(kPrepThreads) sp_max_kernel(const T* __restric
   __shared__ int sn[kPrepThreads / 32];
   griddep_wait();
   griddep_launch_dependents();
-  for (int b = blockIdx.x * kPrepThreads + threadIdx.x; b < kBands; b += gridDim.x * kPrepThreads) {
-    bands.lo[b] = 0;
-    bands.hi[b] = 0;
-    bands.cnt[b] = 0;
-  }
   if (blockIdx.x == 0 && threadIdx.x == 0) *bands.kmin = ~0ull;
   double m = -INFINITY;
   int nan = 0;
@@ -274,8 +272,7 @@ __global__ void __launch_bounds__(kPrepThreads) sp_keys_kernel(const T* __restri
                                                                const uint32_t* __restrict__ allowed,
                                                                double temperature, const double* __restrict__ pmax,
                                                                const int* __restrict__ pnan, int G,
-                                                               uint64_t* __restrict__ keys,
-                                                               uint64_t* __restrict__ pmass, SampleRes* res,
+                                                               uint64_t* __restrict__ keys, SampleRes* res,
                                                                SampleBands bands) {
   __shared__ double sm[kPrepThreads / 32];
   __shared__ int sn[kPrepThreads / 32];
@@ -322,11 +319,13 @@ __global__ void __launch_bounds__(kPrepThreads) sp_keys_kernel(const T* __restri
       }
       keys[i] = key;
     }
-    const unsigned int act = __ballot_sync(0xffffffffu, key != 0);
-    if (key) {
+    kmin = key && key < kmin ? key : kmin;
+    // keys below kMinBand (p < 2^-63) carry no mass and stay out of the bands
+    const bool banded = key >= ((uint64_t)kMinBand << kBandShift);
+    const unsigned int act = __ballot_sync(0xffffffffu, banded);
+    if (banded) {
       const uint64_t f = fixmass(key);
       mass = add(mass, u128(f));
-      kmin = key < kmin ? key : kmin;
       const unsigned int b = (unsigned int)(key >> kBandShift);
       const unsigned int peers = __match_any_sync(act, b);
       const unsigned int g0 = __reduce_add_sync(peers, (unsigned int)f & 0xffffu);
@@ -355,8 +354,9 @@ __global__ void __launch_bounds__(kPrepThreads) sp_keys_kernel(const T* __restri
       mass = add(mass, s_part[w]);
       kmin = s_kmin[w] < kmin ? s_kmin[w] : kmin;
     }
-    pmass[2 * blockIdx.x] = mass.lo;
-    pmass[2 * blockIdx.x + 1] = mass.hi;
+    const unsigned long long old = atomicAdd(bands.total, (unsigned long long)mass.lo);
+    const unsigned long long carry = old + mass.lo < old ? 1ull : 0ull;
+    if (mass.hi + carry) atomicAdd(bands.total + 1, (unsigned long long)mass.hi + carry);
     if (kmin != ~0ull) atomicMin(bands.kmin, kmin);
   }
 }
@@ -369,7 +369,7 @@ struct Pred {
   int kind;
   double a, b;  // kind 0: total, topP; kind 1: draw
 };
-__device__ __forceinline__ bool eval(const Pred& p, U128 c) {
+__device__ __noinline__ bool eval(const Pred& p, U128 c) {
   const double v = to_double(c);
   return p.kind == 0 ? v / p.a >= p.b : p.a < v;
 }
@@ -446,41 +446,117 @@ __device__ unsigned int block_excl_scan(unsigned int v, SelShared& S) {
   return before + incl - v;
 }
 
+// Bands per thread in a band walk: b_hi - kMinBand + 1 <= 16128 <= this *
+// kSelThreads, so one run per thread covers any range.
+constexpr int kWalkRun = 16;  // <= 32: the crossing run is walked one band per lane
+static_assert(kWalkRun * kSelThreads >= (1023 << (52 - kBandShift)) - kMinBand + 1, "band walk runs");
+
+// Block-wide inclusive scan of (mass, count) pairs in one pass.
+__device__ void block_incl_scan2(U128& v, unsigned int& c, SelShared& S) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int o = 1; o < 32; o <<= 1) {
+    const U128 t = shfl_up(v, o);
+    const unsigned int tc = __shfl_up_sync(0xffffffffu, c, o);
+    if (lane >= o) {
+      v = add(v, t);
+      c += tc;
+    }
+  }
+  if (lane == 31) {
+    S.scan[warp] = v;
+    S.scan_cnt[warp] = c;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    U128 w = lane < kSelWarps ? S.scan[lane] : u128(0);
+    unsigned int wc = lane < kSelWarps ? S.scan_cnt[lane] : 0u;
+    for (int o = 1; o < 32; o <<= 1) {
+      const U128 t = shfl_up(w, o);
+      const unsigned int tc = __shfl_up_sync(0xffffffffu, wc, o);
+      if (lane >= o) {
+        w = add(w, t);
+        wc += tc;
+      }
+    }
+    if (lane < kSelWarps) {
+      S.scan[lane] = w;
+      S.scan_cnt[lane] = wc;
+    }
+  }
+  __syncthreads();
+  if (warp > 0) {
+    v = add(v, S.scan[warp - 1]);
+    c += S.scan_cnt[warp - 1];
+  }
+  __syncthreads();
+}
+
 // The first band, walking from b_hi down to b_lo (probability descending),
-// at which `pr` holds for the mass through that band: S.band and the mass of
-// the bands ahead of it (S.band_before).  Each thread sums a run of bands, a
-// block scan orders the runs, and the thread whose run crosses walks it.
-__device__ bool band_walk(const SampleBands& bands, int b_lo, int b_hi, const Pred& pr, SelShared& S) {
+// at which `pr` holds for the mass through that band: S.band, the mass of
+// the bands ahead of it (S.band_before) and the keys in it and ahead of it
+// (S.region_n).  Each thread sums a run of up to kWalkRun bands (four loads
+// in flight), one block scan orders the runs, and warp 0 walks the run that
+// crosses, a band per lane.
+__device__ __noinline__ bool band_walk(const SampleBands& bands, int b_lo, int b_hi, const Pred& pr, SelShared& S) {
   const int t = threadIdx.x;
   const int chunk = (b_hi - b_lo + kSelThreads) / kSelThreads;
   const int top = b_hi - t * chunk;
-  const int bot = top - chunk + 1 > b_lo ? top - chunk + 1 : b_lo;
   U128 m = u128(0);
   unsigned int cnt = 0;
-  for (int b = top; b >= bot; --b) {
-    m = add(m, band_mass(bands, b));
-    cnt += __ldcg(bands.cnt + b);
+  for (int q0 = 0; q0 < chunk; q0 += 4) {  // four bands' loads in flight
+    unsigned long long lo[4], hi[4];
+    unsigned int c[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int b = top - q0 - u;
+      const bool ok = q0 + u < chunk && b >= b_lo;
+      lo[u] = ok ? __ldcg(bands.lo + b) : 0ull;
+      hi[u] = ok ? __ldcg(bands.hi + b) : 0ull;
+      c[u] = ok ? __ldcg(bands.cnt + b) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      m = add(m, add(shl(hi[u], 32), u128(lo[u])));
+      cnt += c[u];
+    }
   }
-  const U128 incl = block_incl_scan(m, S);
-  const unsigned int cnt_before = block_excl_scan(cnt, S);
+  U128 incl = m;
+  unsigned int cincl = cnt;
+  block_incl_scan2(incl, cincl, S);
   if (t == 0) S.first = kNone;
   __syncthreads();
   if (top >= b_lo && eval(pr, incl)) atomicMin(&S.first, t);
   __syncthreads();
   if (S.first == kNone) return false;  // uniform: read after the barrier
-  if (t == S.first) {
-    U128 c = sub(incl, m);
-    unsigned int k = cnt_before;
-    for (int b = top; b >= bot; --b) {
-      const U128 c2 = add(c, band_mass(bands, b));
-      k += __ldcg(bands.cnt + b);
-      if (eval(pr, c2)) {
-        S.band = b;
-        S.band_before = c;
-        S.region_n = k;
-        break;
+  // The crossing run, one band per lane of warp 0: a warp scan of the run's
+  // masses from its starting mass, then the first lane where `pr` holds.
+  const int tc = S.first;
+  if (t == tc) {
+    S.scan[0] = sub(incl, m);  // the mass ahead of the run
+    S.scan_cnt[0] = cincl - cnt;
+  }
+  __syncthreads();
+  if (t < 32) {
+    const int b = b_hi - tc * chunk - t;
+    const bool ok = t < chunk && b >= b_lo;
+    const U128 mine = ok ? band_mass(bands, b) : u128(0);
+    U128 c = mine;
+    unsigned int k = ok ? __ldcg(bands.cnt + b) : 0u;
+    for (int o = 1; o < 32; o <<= 1) {
+      const U128 x = shfl_up(c, o);
+      const unsigned int xk = __shfl_up_sync(0xffffffffu, k, o);
+      if (t >= o) {
+        c = add(c, x);
+        k += xk;
       }
-      c = c2;
+    }
+    c = add(S.scan[0], c);
+    k += S.scan_cnt[0];
+    const unsigned int hits = __ballot_sync(0xffffffffu, ok && eval(pr, c));
+    if (hits && t == __ffs(hits) - 1) {
+      S.band = b;
+      S.band_before = sub(c, mine);
+      S.region_n = k;
     }
   }
   __syncthreads();
@@ -490,23 +566,32 @@ __device__ bool band_walk(const SampleBands& bands, int b_lo, int b_hi, const Pr
 // The keys and ids of bands [band, top_band] into the shared list (id order
 // is not kept); S.list_n = their count, or -1 when they overflow it.
 // S.list_band records `band` for a single band, -2 for a range.
-__device__ void gather_band(const uint64_t* __restrict__ keys, int64_t n, int band, int top_band,
+__device__ __noinline__ void gather_band(const uint64_t* __restrict__ keys, int64_t n, int band, int top_band,
                             unsigned long long* lkeys, uint32_t* lids, SelShared& S) {
   const int lane = threadIdx.x % 32;
   if (threadIdx.x == 0) S.list_fill = 0;
   __syncthreads();
-  constexpr int kU = 16;  // loads in flight per thread
+  // The band is in the key's high word: 32 high words in flight per thread,
+  // the full key loaded only for a match.
+  constexpr int kU = 32;
+  const unsigned int* hiw = reinterpret_cast<const unsigned int*>(keys) + 1;
+  const unsigned int lo_w = (unsigned int)band << (kBandShift - 32);
+  const unsigned int hi_w = ((unsigned int)top_band + 1u) << (kBandShift - 32);
   for (int64_t base = 0; base < n; base += (int64_t)kSelThreads * kU) {
-    uint64_t k[kU];
+    unsigned int h[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int64_t i = base + (int64_t)u * kSelThreads + threadIdx.x;
-      k[u] = i < n ? __ldcg((const unsigned long long*)keys + i) : 0;
+      h[u] = i < n ? __ldcg(hiw + 2 * i) : 0u;
     }
+    unsigned int hit = 0;
 #pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (h[u] >= lo_w && h[u] < hi_w) hit |= 1u << u;
+    if (!__any_sync(0xffffffffu, hit != 0)) continue;
+#pragma unroll 1
     for (int u = 0; u < kU; ++u) {
-      const int kb = (int)(k[u] >> kBandShift);
-      const bool c = k[u] && kb >= band && kb <= top_band;
+      const bool c = (hit >> u) & 1u;
       const unsigned int act = __ballot_sync(0xffffffffu, c);
       if (c) {
         const int leader = __ffs(act) - 1;
@@ -514,8 +599,9 @@ __device__ void gather_band(const uint64_t* __restrict__ keys, int64_t n, int ba
         if (lane == leader) at = atomicAdd(&S.list_fill, (unsigned int)__popc(act));
         at = __shfl_sync(act, at, leader) + __popc(act & ((1u << lane) - 1u));
         if (at < (unsigned int)kListCap) {
-          lkeys[at] = k[u];
-          lids[at] = (uint32_t)(base + (int64_t)u * kSelThreads + threadIdx.x);
+          const int64_t i = base + (int64_t)u * kSelThreads + threadIdx.x;
+          lkeys[at] = __ldcg((const unsigned long long*)keys + i);
+          lids[at] = (uint32_t)i;
         }
       }
     }
@@ -530,7 +616,7 @@ __device__ void gather_band(const uint64_t* __restrict__ keys, int64_t n, int ba
 
 // The largest id among the tokens whose key is `key` (the last of them in
 // the reference's order).
-__device__ int64_t last_with_key(const uint64_t* __restrict__ keys, int64_t n, uint64_t key, SelShared& S) {
+__device__ __noinline__ int64_t last_with_key(const uint64_t* __restrict__ keys, int64_t n, uint64_t key, SelShared& S) {
   unsigned int v = 0;  // id + 1; 0 = none
   for (int64_t i = threadIdx.x; i < n; i += kSelThreads)
     if (__ldcg((const unsigned long long*)keys + i) == key) v = (unsigned int)i + 1;
@@ -547,7 +633,7 @@ __device__ int64_t last_with_key(const uint64_t* __restrict__ keys, int64_t n, u
 }
 
 // The j-th (1-based) smallest id among the tokens whose key is `key`.
-__device__ void jth_with_key(const uint64_t* __restrict__ keys, int64_t n, uint64_t key, unsigned int j,
+__device__ __noinline__ void jth_with_key(const uint64_t* __restrict__ keys, int64_t n, uint64_t key, unsigned int j,
                              SelShared& S) {
   const int64_t chunk = (n + kSelThreads - 1) / kSelThreads;
   int64_t b0 = (int64_t)threadIdx.x * chunk;
@@ -570,8 +656,37 @@ __device__ void jth_with_key(const uint64_t* __restrict__ keys, int64_t n, uint6
 // Sorts the gathered band (S.list_n <= kListCap entries) into the
 // reference's order — key descending, id ascending — with a bitonic sort over
 // the next power of two, padding with (key 0, id max), which sorts last.
-__device__ void sort_list(unsigned long long* lkeys, uint32_t* lids, SelShared& S) {
+__device__ __noinline__ void sort_list(unsigned long long* lkeys, uint32_t* lids, SelShared& S) {
   const int m = S.list_n;
+  if (m <= 32) {  // one warp, in registers
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      unsigned long long key = lane < m ? lkeys[lane] : 0ull;
+      uint32_t id = lane < m ? lids[lane] : 0xffffffffu;
+#pragma unroll 1
+      for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll 1
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          const unsigned long long ok = __shfl_xor_sync(0xffffffffu, key, j);
+          const uint32_t oi = __shfl_xor_sync(0xffffffffu, id, j);
+          const bool lower = (lane & j) == 0, up = (lane & k) == 0;
+          const unsigned long long ka = lower ? key : ok, kb = lower ? ok : key;
+          const uint32_t ia = lower ? id : oi, ib = lower ? oi : id;
+          const bool a_first = ka > kb || (ka == kb && ia < ib);
+          // the lower lane of an ascending run, or the upper of a
+          // descending one, takes the pair's first entry
+          const bool take_a = (lower == up) == a_first;
+          key = take_a ? ka : kb;
+          id = take_a ? ia : ib;
+        }
+      if (lane < m) {
+        lkeys[lane] = key;
+        lids[lane] = id;
+      }
+    }
+    __syncthreads();
+    return;
+  }
   int P = 1;
   while (P < m) P <<= 1;
   for (int i = m + threadIdx.x; i < P; i += kSelThreads) {
@@ -603,8 +718,26 @@ __device__ void sort_list(unsigned long long* lkeys, uint32_t* lids, SelShared& 
 // position at which `pr` holds for the running mass (S.idx its id, S.cum the
 // mass through it).  Each thread takes a run of positions; a block scan of
 // the runs' masses gives each run its starting mass.
-__device__ void search_list(const unsigned long long* lkeys, const uint32_t* lids, const Pred& pr, SelShared& S) {
+__device__ __noinline__ void search_list(const unsigned long long* lkeys, const uint32_t* lids, const Pred& pr, SelShared& S) {
   const int m = S.list_n, tid = threadIdx.x;
+  if (m <= 32) {  // one warp: a warp scan of the masses
+    if (tid < 32) {
+      U128 c = tid < m ? u128(fixmass(lkeys[tid])) : u128(0);
+      for (int o = 1; o < 32; o <<= 1) {
+        const U128 t = shfl_up(c, o);
+        if (tid >= o) c = add(c, t);
+      }
+      c = add(S.band_before, c);
+      const unsigned int hits = __ballot_sync(0xffffffffu, tid < m && eval(pr, c));
+      const int h = hits ? __ffs(hits) - 1 : -1;
+      if (tid == (h >= 0 ? h : 0)) {
+        S.idx = h >= 0 ? (int64_t)lids[h] : -1;
+        S.cum = h >= 0 ? c : S.band_before;
+      }
+    }
+    __syncthreads();
+    return;
+  }
   const int per = (m + kSelThreads - 1) / kSelThreads;
   const int p0 = tid * per < m ? tid * per : m, p1 = p0 + per < m ? p0 + per : m;
   U128 run = u128(0);
@@ -634,14 +767,15 @@ __device__ void search_list(const unsigned long long* lkeys, const uint32_t* lid
   __syncthreads();
 }
 
-__device__ void band_select(const uint64_t* __restrict__ keys, int64_t n, const unsigned long long* lkeys,
-                            const uint32_t* lids, const Pred& pr, SelShared& S);
+__device__ __noinline__ void band_select(const uint64_t* __restrict__ keys, int64_t n,
+                                         const unsigned long long* lkeys, const uint32_t* lids, const Pred& pr,
+                                         SelShared& S);
 
 // The first token of band S.band at which `pr` holds: the band's keys are
 // gathered into shared memory once (kept for a second select in the same
 // band) and searched after a sort when few, radix-selected when more, and
 // radix-selected from every key when they overflow the list.
-__device__ void select_in_band(const uint64_t* __restrict__ keys, int64_t n, unsigned long long* lkeys,
+__device__ __noinline__ void select_in_band(const uint64_t* __restrict__ keys, int64_t n, unsigned long long* lkeys,
                                uint32_t* lids, const Pred& pr, SelShared& S) {
   if (S.list_band != S.band) {
     gather_band(keys, n, S.band, S.band, lkeys, lids, S);
@@ -651,6 +785,7 @@ __device__ void select_in_band(const uint64_t* __restrict__ keys, int64_t n, uns
     search_list(lkeys, lids, pr, S);
   else
     band_select(keys, n, lkeys, lids, pr, S);
+
 }
 
 // Inside band S.band, with S.band_before the mass ahead of it, for a band
@@ -659,8 +794,9 @@ __device__ void select_in_band(const uint64_t* __restrict__ keys, int64_t n, uns
 // every key when the band overflowed the list.  Each level fixes the next 8
 // key bits, stopping as soon as one token is left; tokens with equal keys
 // are ordered by id.
-__device__ void band_select(const uint64_t* __restrict__ keys, int64_t n, const unsigned long long* lkeys,
-                            const uint32_t* lids, const Pred& pr, SelShared& S) {
+__device__ __noinline__ void band_select(const uint64_t* __restrict__ keys, int64_t n,
+                                         const unsigned long long* lkeys, const uint32_t* lids, const Pred& pr,
+                                         SelShared& S) {
   const int tid = threadIdx.x, lane = tid % 32;
   const bool from_list = S.list_n >= 0 && S.list_band == S.band;
   const int64_t items = from_list ? (int64_t)S.list_n : n;
@@ -668,7 +804,10 @@ __device__ void band_select(const uint64_t* __restrict__ keys, int64_t n, const 
   unsigned long long val = (unsigned long long)S.band << kBandShift;
   U128 before = S.band_before;
   int d = 0;
-  for (int shift = kBandShift - kDigitBits; shift >= 0; shift -= kDigitBits) {
+  for (int top = kBandShift - 1; top >= 0; top -= kDigitBits) {
+    // this level's digit: key bits [shift, top], at most kDigitBits wide
+    const int shift = top - (kDigitBits - 1) > 0 ? top - (kDigitBits - 1) : 0;
+    const int nb = 1 << (top - shift + 1);
     if (tid < kBuckets) {
       S.c16[0][tid] = S.c16[1][tid] = S.c16[2][tid] = S.c16[3][tid] = 0;
       S.cnt[tid] = 0;
@@ -695,7 +834,7 @@ __device__ void band_select(const uint64_t* __restrict__ keys, int64_t n, const 
         }
         const unsigned int act = __ballot_sync(0xffffffffu, cand);
         if (cand) {
-          const unsigned int dg = (unsigned int)(key >> shift) & (kBuckets - 1);
+          const unsigned int dg = (unsigned int)(key >> shift) & (unsigned int)(nb - 1);
           const unsigned int peers = __match_any_sync(act, dg);
           const uint64_t f = fixmass(key);
           unsigned int g[4];
@@ -722,13 +861,13 @@ __device__ void band_select(const uint64_t* __restrict__ keys, int64_t n, const 
       }
       __syncthreads();
     }
-    // Digits from 255 down (keys descending): thread t holds digit 255 - t.
-    const int dg = kBuckets - 1 - tid;
-    const U128 m = tid < kBuckets ? S.acc[dg] : u128(0);
+    // Digits from nb - 1 down (keys descending): thread t holds digit nb - 1 - t.
+    const int dg = nb - 1 - tid;
+    const U128 m = tid < nb ? S.acc[dg] : u128(0);
     const U128 incl = block_incl_scan(m, S);
     if (tid == 0) S.first = kNone;
     __syncthreads();
-    if (tid < kBuckets && S.cnt[dg] && eval(pr, add(before, incl))) atomicMin(&S.first, tid);
+    if (tid < nb && S.cnt[dg] && eval(pr, add(before, incl))) atomicMin(&S.first, tid);
     __syncthreads();
     const int f = S.first;
     if (f == kNone) {  // cannot happen: the band was chosen because the predicate turns inside it
@@ -740,14 +879,14 @@ __device__ void band_select(const uint64_t* __restrict__ keys, int64_t n, const 
       __syncthreads();
       return;
     }
-    d = kBuckets - 1 - f;
+    d = nb - 1 - f;
     if (tid == f) S.cum = add(before, sub(incl, m));  // the mass ahead of digit d
     __syncthreads();
     before = S.cum;
     const bool single = S.cnt[d] == 1;
     const unsigned int single_id = S.imin[d];
     const U128 dmass = S.acc[d];
-    mask |= (unsigned long long)(kBuckets - 1) << shift;
+    mask |= (unsigned long long)(nb - 1) << shift;
     val |= (unsigned long long)d << shift;
     __syncthreads();  // every thread has read this level's results
     if (single) {
@@ -782,7 +921,6 @@ __device__ void band_select(const uint64_t* __restrict__ keys, int64_t n, const 
 // llm/sampler.ts:114-140 after the prepare kernels: the nucleus cutoff, then
 // the draw (`rng() * nucleusTotal`, with *draw the rng's value).
 __global__ void __launch_bounds__(kSelThreads) sp_select_kernel(const uint64_t* __restrict__ keys, int64_t n,
-                                                                const uint64_t* __restrict__ pmass, int G,
                                                                 SampleRes* res, SampleBands bands, double top_p,
                                                                 const double* __restrict__ draw,
                                                                 int32_t* __restrict__ token, StepSlots ss) {
@@ -795,10 +933,8 @@ __global__ void __launch_bounds__(kSelThreads) sp_select_kernel(const uint64_t* 
   griddep_wait();
   const int tid = threadIdx.x;
   const double m = res->max_scaled;
-  U128 part = u128(0);
-  for (int g = tid; g < G; g += kSelThreads) part = add(part, U128{__ldcg((const unsigned long long*)pmass + 2 * g), __ldcg((const unsigned long long*)pmass + 2 * g + 1)});
-  const U128 total = block_incl_scan(part, S);  // thread kSelThreads - 1 holds the sum
-  if (tid == kSelThreads - 1) {
+  if (tid == 0) {
+    const U128 total{__ldcg(bands.total), __ldcg(bands.total + 1)};
     s_total = total;
     s_code = m == -INFINITY ? kTokNoFinite : (m == INFINITY || (total.lo == 0 && total.hi == 0) ? kTokNoMass : 0);
     S.list_n = -1;
@@ -809,7 +945,8 @@ __global__ void __launch_bounds__(kSelThreads) sp_select_kernel(const uint64_t* 
   if (!s_code) {
     const U128 tot = s_total;
     const unsigned long long kmin = __ldcg(bands.kmin);
-    const int b_lo = (int)(kmin >> kBandShift), b_hi = (int)(kOneBits >> kBandShift);
+    const int b_hi = (int)(kOneBits >> kBandShift);
+    const int b_lo = (int)(kmin >> kBandShift) > kMinBand ? (int)(kmin >> kBandShift) : kMinBand;
     // The cutoff: with a NaN in the total no prefix reaches topP and the
     // nucleus is every token (llm/sampler.ts:117-124).
     int64_t cut_idx = -1;
@@ -818,6 +955,7 @@ __global__ void __launch_bounds__(kSelThreads) sp_select_kernel(const uint64_t* 
     if (!res->has_nan) {
       const Pred p0{0, to_double(tot), top_p};
       if (band_walk(bands, b_lo, b_hi, p0, S)) {
+
         if (S.region_n <= (unsigned int)kSortMax) {
           // Every key from the cutoff's band up fits the list: gather and
           // sort them once; the pick lies among them too.
@@ -857,6 +995,19 @@ __global__ void __launch_bounds__(kSelThreads) sp_select_kernel(const uint64_t* 
     tok = (int32_t)pick;
   }
   if (tid == 0) publish(tok, token, res, ss);
+  // Leave the band histogram zero for the next sampling: the keys kernel
+  // touched only bands [kMinBand, the top key's band].
+  if (!s_code) {
+    __syncthreads();
+    const int b_lo = (int)(__ldcg(bands.kmin) >> kBandShift) > kMinBand ? (int)(__ldcg(bands.kmin) >> kBandShift)
+                                                                         : kMinBand;
+    for (int b = b_lo + tid; b <= (int)(kOneBits >> kBandShift); b += kSelThreads) {
+      bands.lo[b] = 0;
+      bands.hi[b] = 0;
+      bands.cnt[b] = 0;
+    }
+    if (tid == 0) bands.total[0] = bands.total[1] = 0;
+  }
 }
 
 // ------------------------------------------------------------------ host --
@@ -904,6 +1055,42 @@ int prep_grid(int64_t n) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(want, 4 * (int64_t)device_info().sm_count));
 }
 
+// The sampling scratch of the entry points, one per (device, stream): laid
+// out for the largest grid, zeroed when allocated or grown, and left zero by
+// every select kernel, so consecutive samplings on a stream reuse it without
+// clearing.  Kept until the process exits.
+// `n` sizes the grid, `cap` the keys kept (0 for greedy).
+int stream_scratch(cudaStream_t st, int64_t n, int64_t cap, SampleScratch* s, int* G) {
+  int dev = 0;
+  XPU_TRY_CUDA(cudaGetDevice(&dev));
+  const int gmax = 4 * device_info().sm_count;
+  *G = prep_grid(n);
+  n = cap;
+  struct Slot {
+    void* mem = nullptr;
+    int64_t n = -1;
+  };
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, Slot> slots;
+  std::lock_guard<std::mutex> lock(mu);
+  Slot& slot = slots[{dev, st}];
+  if (slot.n < n) {
+    if (slot.mem) {
+      XPU_TRY_CUDA(cudaStreamSynchronize(st));
+      cudaFree(slot.mem);
+      slot.mem = nullptr;
+      slot.n = -1;
+    }
+    XPU_TRY_CUDA(cudaMalloc(&slot.mem, SampleScratch::bytes(gmax, n)));
+    slot.n = n;
+    s->carve(slot.mem, gmax);
+    XPU_TRY_CUDA(s->clear(st));
+    return XPU_OK;
+  }
+  s->carve(slot.mem, gmax);
+  return XPU_OK;
+}
+
 // Launches the top-p kernels; `draw` is a device pointer.  `ss` (engine
 // loop) makes the token the step's.
 template <typename T>
@@ -914,14 +1101,14 @@ int launch_top_p(const T* logits, int64_t n, const uint32_t* allowed, double tem
     XPU_TRY_CUDA(launch_ex(sp_max_kernel<T>, dim3(G), dim3(kPrepThreads), 0, LaunchOpts{st, false}, logits, n,
                            allowed, temperature, s.pmax, s.pnan, s.bands));
     XPU_TRY_CUDA(launch_ex(sp_keys_kernel<T>, dim3(G), dim3(kPrepThreads), 0, LaunchOpts{st, true}, logits, n,
-                           allowed, temperature, (const double*)s.pmax, (const int*)s.pnan, G, s.keys, s.pmass,
+                           allowed, temperature, (const double*)s.pmax, (const int*)s.pnan, G, s.keys,
                            s.res, s.bands));
   }
   if (select) {
     constexpr size_t kListBytes = (size_t)kListCap * 12;
     XPU_TRY_CUDA(ensure_smem_attr((const void*)sp_select_kernel, kListBytes + sizeof(SelShared) + 64));
     XPU_TRY_CUDA(launch_ex(sp_select_kernel, dim3(1), dim3(kSelThreads), kListBytes, LaunchOpts{st, prep},
-                           (const uint64_t*)s.keys, n, (const uint64_t*)s.pmass, G, s.res, s.bands, top_p, draw,
+                           (const uint64_t*)s.keys, n, s.res, s.bands, top_p, draw,
                            token, ss));
   }
   return XPU_OK;
@@ -1021,18 +1208,18 @@ int xpu_sample_next(const double* logits, int64_t n, const int32_t* allowed, int
     XPU_REQUIRE(rng, XPU_EINVAL, "xpu_sample_next: top-p needs an rng");
   }
   const std::vector<uint32_t> bits = allowed_count > 0 ? mask_bits(allowed, allowed_count, n) : std::vector<uint32_t>();
-  const int G = prep_grid(n);
+  SampleScratch s;
+  int G = 1;
+  int rc = stream_scratch(nullptr, n, n, &s, &G);
+  if (rc) return rc;
   const size_t words = bits.size();
-  const size_t bytes = SampleScratch::bytes(G, n) + (size_t)n * 8 + words * 4 + 32;
   void* mem = nullptr;
-  XPU_TRY_CUDA(cudaMalloc(&mem, bytes));
+  XPU_TRY_CUDA(cudaMalloc(&mem, (size_t)n * 8 + 16 + words * 4 + 16));
   struct Free {
     void* p;
     ~Free() { cudaFree(p); }
   } guard{mem};
-  SampleScratch s;
-  s.carve(mem, G);
-  char* tail = reinterpret_cast<char*>(s.keys) + (size_t)n * 8;
+  char* tail = static_cast<char*>(mem);
   double* d_logits = reinterpret_cast<double*>(tail);
   tail += (size_t)n * 8;
   double* d_draw = reinterpret_cast<double*>(tail);
@@ -1041,11 +1228,9 @@ int xpu_sample_next(const double* logits, int64_t n, const int32_t* allowed, int
   uint32_t* d_allowed = words ? reinterpret_cast<uint32_t*>(tail) : nullptr;
   if (n) XPU_TRY_CUDA(cudaMemcpy(d_logits, logits, (size_t)n * 8, cudaMemcpyHostToDevice));
   if (words) XPU_TRY_CUDA(cudaMemcpy(d_allowed, bits.data(), words * 4, cudaMemcpyHostToDevice));
-  XPU_TRY_CUDA(s.clear(nullptr));
   int32_t tok = 0;
   if (mode == XPU_SAMPLE_GREEDY) {
-    int rc = launch_greedy((const double*)d_logits, n, d_allowed, d_token, s, G, nullptr);
-    if (rc) return rc;
+    if ((rc = launch_greedy((const double*)d_logits, n, d_allowed, d_token, s, G, nullptr))) return rc;
     XPU_TRY_CUDA(cudaMemcpy(&tok, d_token, 4, cudaMemcpyDeviceToHost));
     XPU_REQUIRE(tok >= 0, XPU_EINVAL, "sampleNext: no finite logit to choose from");
     *token = tok;
@@ -1053,9 +1238,9 @@ int xpu_sample_next(const double* logits, int64_t n, const int32_t* allowed, int
   }
   // llm/sampler.ts:95-105 first: the rng is called only once maxScaled is
   // known to be finite or +Infinity, as in the reference.
-  int rc = launch_top_p((const double*)d_logits, n, d_allowed, temperature, top_p, d_draw, d_token, s, G, nullptr,
-                        true, false);
-  if (rc) return rc;
+  if ((rc = launch_top_p((const double*)d_logits, n, d_allowed, temperature, top_p, d_draw, d_token, s, G, nullptr,
+                         true, false)))
+    return rc;
   SampleRes r{};
   XPU_TRY_CUDA(cudaMemcpy(&r, s.res, sizeof r, cudaMemcpyDeviceToHost));
   XPU_REQUIRE(r.max_scaled != -INFINITY, XPU_EINVAL, "sampleTopP: no finite logit to choose from");
@@ -1082,19 +1267,13 @@ int xpu_sample_next_dev(const float* logits, int64_t n, const uint32_t* allowed_
     if (rc) return rc;
     XPU_REQUIRE(draw, XPU_EINVAL, "xpu_sample_next_dev: top-p needs a draw");
   }
-  const int G = prep_grid(n);
-  void* mem = nullptr;
-  XPU_TRY_CUDA(scratch_alloc(&mem, SampleScratch::bytes(G, mode == XPU_SAMPLE_TOP_P ? n : 0), st));
   SampleScratch s;
-  s.carve(mem, G);
-  cudaError_t e = s.clear(st);
-  int rc = e != cudaSuccess ? cuda_status(e, "xpu_sample_next_dev: scratch")
-           : mode == XPU_SAMPLE_GREEDY
-               ? launch_greedy(logits, n, allowed_bits, token, s, G, st)
-               : launch_top_p(logits, n, allowed_bits, temperature, top_p, draw, token, s, G, st, true, true);
-  e = scratch_free(mem, st);
+  int G = 1;
+  int rc = stream_scratch(st, n, mode == XPU_SAMPLE_TOP_P ? n : 0, &s, &G);
   if (rc) return rc;
-  return e == cudaSuccess ? XPU_OK : cuda_status(e, "xpu_sample_next_dev: scratch");
+  return mode == XPU_SAMPLE_GREEDY
+             ? launch_greedy(logits, n, allowed_bits, token, s, G, st)
+             : launch_top_p(logits, n, allowed_bits, temperature, top_p, draw, token, s, G, st, true, true);
 }
 
 }  // extern "C"

@@ -14,14 +14,20 @@ struct SampleRes {
 
 
 // The band histogram of the top-p keys: keys (the bits of a probability in
-// (0, 1]) grouped by their top 16 bits, key >> kBandShift <= 0x3FF0.
-constexpr int kBandShift = 48;
-constexpr int kBands = 1 << 14;
+// (0, 1]) grouped by their top 20 bits (exponent and 8 mantissa bits: bands
+// 1/256 of an octave wide), key >> kBandShift <= 0x3FF00.  Bands below
+// kMinBand (p < 2^-63, no mass) are not kept.  The histogram is zero
+// between samplings: clear() zeroes it once, the select kernel re-zeroes the
+// bands it used.
+constexpr int kBandShift = 44;
+constexpr int kBands = 1 << 18;
+constexpr int kMinBand = (1023 - 63) << (52 - kBandShift);
 struct SampleBands {
   unsigned long long* lo;  // exact mass (p * 2^63 summed) per band, low word
   unsigned long long* hi;  // high word
   unsigned int* cnt;       // keys per band
   unsigned long long* kmin;  // the smallest positive key
+  unsigned long long* total;  // [2]: the exact total mass, low and high words
 };
 
 // Per-CTA results of the greedy argmax and the ticket that tells the last
@@ -37,22 +43,19 @@ struct ArgmaxParts {
 struct SampleScratch {
   double* pmax = nullptr;
   int* pnan = nullptr;
-  uint64_t* pmass = nullptr;
   SampleRes* res = nullptr;
   ArgmaxParts parts{};
   SampleBands bands{};
   uint64_t* keys = nullptr;
   void* base = nullptr;
   static size_t bytes(int G, int64_t n) {
-    return (size_t)G * (8 + 8 + 16 + 8 + 8) + 64 + 16 + (size_t)kBands * 20 + 16 + (size_t)n * 8;
+    return (size_t)G * (8 + 8 + 8 + 8) + 64 + 16 + (size_t)kBands * 20 + 32 + (size_t)n * 8;
   }
   void carve(void* p, int G) {
     base = p;
     char* c = static_cast<char*>(p);
     pmax = reinterpret_cast<double*>(c);
     c += (size_t)G * 8;
-    pmass = reinterpret_cast<uint64_t*>(c);
-    c += (size_t)G * 16;
     pnan = reinterpret_cast<int*>(c);
     c += (size_t)G * 8;
     parts.v = reinterpret_cast<double*>(c);
@@ -68,13 +71,17 @@ struct SampleScratch {
     bands.hi = reinterpret_cast<unsigned long long*>(c);
     c += (size_t)kBands * 8;
     bands.kmin = reinterpret_cast<unsigned long long*>(c);
-    c += 16;
+    bands.total = bands.kmin + 2;
+    c += 32;
     bands.cnt = reinterpret_cast<unsigned int*>(c);
     c += (size_t)kBands * 4;
     keys = reinterpret_cast<uint64_t*>(c);
   }
-  // Zeroes the result word and the argmax ticket (adjacent).
-  cudaError_t clear(cudaStream_t st) const { return cudaMemsetAsync(res, 0, 64 + 16, st); }
+  // Zeroes the result word, the argmax ticket and the band histogram
+  // (adjacent, res up to keys).
+  cudaError_t clear(cudaStream_t st) const {
+    return cudaMemsetAsync(res, 0, (size_t)(reinterpret_cast<char*>(keys) - reinterpret_cast<char*>(res)), st);
+  }
 };
 
 // The sampling loop of xpu_llama_sample_steps: scratch for one vocabulary,
