@@ -212,12 +212,17 @@ __device__ __forceinline__ void write_limb_columns(uint8_t* tile, const float* _
 // ----------------------------------------------------------- vector stats --
 // Block b of `gridDim.x`: the largest and smallest nonzero magnitudes and
 // the finiteness of its share of x, into stats[b]; block 0 also zeroes the
-// GEMV's tickets.  The GEMV (a programmatic dependent launch) starts
-// streaming weights meanwhile and reads these after griddepcontrol.wait.
+// GEMV's tickets.  Both launches are programmatic dependent launches.  This
+// kernel can be resident before the previous kernel of the stream (say the
+// GEMV that produced x) finishes, and waits for it before touching anything
+// (x, and scratch that may reuse that kernel's).  Only then does it let the
+// GEMV start, whose weight stream runs before the GEMV's own wait and so
+// must not begin while any earlier kernel (one packing those weights) runs.
 constexpr int kStatThreads = 256;
 __global__ void __launch_bounds__(kStatThreads) mv_xstat_kernel(const float* __restrict__ x, int K,
                                                                 float4* __restrict__ stats,
                                                                 unsigned int* __restrict__ ticket, int nticket) {
+  griddep_wait();
   griddep_launch_dependents();
   __shared__ float smx[kStatThreads / 32], smn[kStatThreads / 32];
   __shared__ int sbad[kStatThreads / 32];
@@ -270,6 +275,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ float red_max[4], red_min[4];
   __shared__ int red_bad[4];
   __shared__ volatile int s_flag;  // warps 2-5: one thread's result for all
+  // The next launch of the stream may become resident now; every dependent
+  // the library launches waits for this grid before reading its outputs.
+  griddep_launch_dependents();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
@@ -698,8 +706,8 @@ int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const f
   // kind::i8: int32 accumulator, signed A and B, K-major, M = 128, N = 16.
   g.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcLimbs >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
   g.err = device_error_word();
-  mv_xstat_kernel<<<nstats, kStatThreads, 0, st>>>(x, (int)K, const_cast<float4*>(g.stats), g.ticket, grid);
-  cudaError_t ce = cudaGetLastError();
+  cudaError_t ce = launch_ex(mv_xstat_kernel, dim3(nstats), dim3(kStatThreads), 0, LaunchOpts{st, true}, x, (int)K,
+                             const_cast<float4*>(g.stats), g.ticket, (int)grid);
   if (ce == cudaSuccess) {
     const size_t smem = (size_t)kTcStages * kTcStageBytes + 1024;
     ce = ensure_smem_attr((const void*)mv_tc_kernel, smem);
