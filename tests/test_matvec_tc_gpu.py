@@ -199,6 +199,28 @@ def test_special_vectors_and_scales(tc):
         tc_check(y, w, s, x, N, K)
 
 
+@pytest.mark.parametrize("N,K", [(16384, 6144), (20000, 8000)])
+def test_single_gemvs_with_dynamic_chunks(tc, N, K):
+    """Single GEMVs with at least 32 slices per CTA, 128 row tiles or more
+    and rows of at most 64 slices leave their last eighth of row tiles to
+    two-stage chunks that CTAs claim at run time and sum at the end: six
+    chunks per tile (K = 6144), and a partial last tile, a last chunk of
+    seven slices (two stages, the second of three) and a part slice
+    (N = 20000, K = 8000).  The oracle's results, bit-identical on repeats."""
+    w, s = _synth(N, K, 900 + K)
+    x = fill_normal(K, 901 + K)
+    dw, ds, dx = ops.DeviceBuffer.from_numpy(w), ops.DeviceBuffer.from_numpy(s), ops.DeviceBuffer.from_numpy(x)
+    outs = []
+    for _ in range(3):
+        dy = ops.DeviceBuffer(4 * N)
+        ops.matvecQ8_dev(dw, ds, dx, N, K, dy)
+        ops.stream_sync()
+        outs.append(dy.download(np.float32, N))
+    np.testing.assert_array_equal(outs[0], outs[1])
+    np.testing.assert_array_equal(outs[0], outs[2])
+    tc_check(outs[0], w, s, x, N, K)
+
+
 def test_deterministic(tc):
     w, s = _synth(2048, 4096, 12)
     x = fill_normal(4096, 13)
