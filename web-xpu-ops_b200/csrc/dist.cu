@@ -6,7 +6,7 @@
 // as xpu_matvec_q8_stack_dev, and one NCCL all-gather per matrix (NVLink /
 // NVSwitch) leaves the whole [count][N] result on every device.  NCCL is
 // loaded at run time (libnccl.so.2), so the library has no link-time
-// dependency on it; the collectives run on plain NCCL, no multicast loads.
+// dependency on it; the collectives are plain NCCL all-gathers.
 #include <dlfcn.h>
 #include <nccl.h>
 
