@@ -9,7 +9,7 @@
 //   sp_keys_kernel    (grid)   p = exp(s - maxScaled) as a sort key (the bits
 //                              of a positive double order like the double),
 //                              the exact total mass, and a histogram of the
-//                              keys' top 16 bits ("bands", 1/16 of an octave
+//                              keys' top 20 bits ("bands", 1/256 of an octave
 //                              of probability each): count and exact mass
 //   sp_select_kernel  (1 CTA)  two "mass selects", each finding the first
 //                              token, in the reference's order (probability
@@ -18,9 +18,12 @@
 //                              >= topP for the cutoff, draw < cumulative for
 //                              the pick: a scan over the bands finds the band
 //                              where the predicate turns, that band's keys are
-//                              gathered into shared memory, and 8-bit radix
-//                              levels over them narrow it to one token (equal
-//                              keys are ordered by id).
+//                              gathered into shared memory and sorted (key
+//                              descending, id ascending), or narrowed by 8-bit
+//                              radix levels when there are many; a scan of the
+//                              sorted masses then gives the token.  When every
+//                              key from the cutoff's band up fits, one gathered
+//                              list serves both selects.
 //
 // Masses are p * 2^63 truncated to integers and summed exactly (128 bits), so
 // no result depends on the order of the additions; the reference adds f64s
