@@ -164,6 +164,23 @@ def test_shapes_outside_the_persistent_step_keep_the_graph():
         assert logits_agree(logits, oracle.forward([5, 9, 2]), 1e-3) is None
 
 
+def test_ragged_rows_with_several_staging_passes():
+    """Hidden 1030 and FFN 2050 (rows of 258 and 513 words): every decode GEMV
+    takes the general kernel with its rmsnorm prologue, QKV/RoPE, FFN and
+    residual epilogues, and x spans more than one staging pass of the CTA."""
+    cfg = xpuops.LlamaConfig(numLayers=2, hiddenSize=1030, numHeads=2, numKvHeads=1, headDim=64, ffnHidden=2050,
+                             vocabSize=300, ropeTheta=10000.0, rmsNormEps=1e-5, maxSeqLen=16)
+    weights = random_llama(cfg, seed=4)
+    oracle = orc.LlamaOracle(cfg, weights)
+    with LlamaEngineQ8Resident.create(cfg, weights) as eng:
+        assert eng.decodePath == GRAPH
+        (logits,) = eng.forward([5, 9, 2])
+        assert logits_agree(logits, oracle.forward([5, 9, 2]), 1e-3) is None
+        for tok in (7, 11):
+            (logits,) = eng.forward([tok])
+            assert logits_agree(logits, oracle.forward([tok]), 1e-3) is None
+
+
 def test_forward_profile(fixture):
     """llm/engine-q8-resident.ts:33-152 ForwardProfile: the wall-clock fields
     on both paths; per-phase device entries ("L<l>:<kernel>", then lm_head)

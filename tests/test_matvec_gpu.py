@@ -229,6 +229,22 @@ def test_bulk_and_general_kernel_shapes(N, K):
     check_matvec(xpuops.matvecQ8(w, s, x, N, K), w, s, x, N, K)
 
 
+@pytest.mark.parametrize("N,K", [(1000, 4097), (33, 40001), (5, 6)])
+def test_general_kernel_fused_forms(N, K):
+    """Rows that are not whole 16-byte slots take the general kernel in every
+    form: plain, matvecQ8Ffn (gate and up rows in one unit) and
+    matvecQ8Residual, with x staged over several passes for the larger K."""
+    _, wg, sg = _synth_q8(N, K, 1200 + K)
+    _, wu, su = _synth_q8(N, K, 1201 + K)
+    x = fill_normal(K, 1202)
+    check_matvec(xpuops.matvecQ8(wu, su, x, N, K), wu, su, x, N, K)
+    g = xpuops.matvecQ8Ffn(wg, sg, wu, su, x, N, K)
+    assert agree(g, orc.matvec_q8_ffn(wg, sg, wu, su, x, N, K), rel=1e-4, abs_=1e-5) is None
+    r = fill_normal(N, 1203)
+    yr = xpuops.matvecQ8Residual(wg, sg, x, r, N, K)
+    assert agree(yr, orc.matvec_q8_residual(wg, sg, x, r, N, K), rel=1e-4, abs_=1e-5) is None
+
+
 def test_results_are_deterministic():
     _, w, s = _synth_q8(4096, 4096, 5)
     x = fill_normal(4096, 6)

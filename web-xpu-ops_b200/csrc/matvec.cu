@@ -118,7 +118,7 @@ int plan_matvec(MvParams& p, int epi, int pro, MvPlan& plan) {
     XPU_REQUIRE(reinterpret_cast<uintptr_t>(p.w2) % 16 == reinterpret_cast<uintptr_t>(p.w) % 16, XPU_EINVAL,
                 "matvecQ8Ffn: gate and up weights must share their offset within 16 bytes");
   }
-  plan.smem = (size_t)(48 + 4 * p.W) * sizeof(float);
+  plan.smem = (size_t)gen_xs_floats(p.W) * sizeof(float);
   XPU_REQUIRE(plan.smem + 4096 <= (size_t)di.max_smem_optin, XPU_EINVAL,
               "matvecQ8: K=%lld exceeds this build's limit for rows that are not 16-byte aligned",
               (long long)p.K);
@@ -126,8 +126,13 @@ int plan_matvec(MvParams& p, int epi, int pro, MvPlan& plan) {
   const int64_t units = ceil_div(p.N, rb);
   const int per_sm = std::max(1, std::min(8, (int)((size_t)di.max_smem_optin / (plan.smem + 2048))));
   plan.rt = 2;
-  plan.grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(units, (int64_t)di.sm_count * per_sm)));
-  plan.block = dim3(256);
+  // One unit per warp: enough CTAs for every unit, at most the CTAs that fit
+  // on the device at once; 16 warps a CTA where shared memory (x) allows only
+  // one or two CTAs an SM, else 8.
+  const int threads = plan.smem > 64 * 1024 ? 512 : 256;
+  plan.grid = dim3(
+      (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(units, threads / 32), (int64_t)di.sm_count * per_sm)));
+  plan.block = dim3((unsigned)threads);
   return XPU_OK;
 }
 

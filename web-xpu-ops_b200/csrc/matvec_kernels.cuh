@@ -17,10 +17,11 @@
 //    16-column slices of K and keeps x for them in registers for the whole
 //    launch, so x is read from memory once per CTA and shared memory
 //    carries weights only.
-//  * mv_gen_kernel — any alignment, any K.  Direct 128-bit loads on the
-//    16-byte grid of the buffer; a word of a neighbouring row (a load that
-//    straddles a row boundary) or a padding lane multiplies a zero of the
-//    zero-padded x staged in shared memory, so nothing outside a row counts.
+//  * mv_gen_kernel — any alignment, any K.  One warp per unit of rows,
+//    direct 128-bit loads on the 16-byte grid of the buffer, double-buffered;
+//    a word of a neighbouring row (a load that straddles a row boundary) or a
+//    padding lane multiplies a zero of the zero-padded x staged in shared
+//    memory, so nothing outside a row counts.
 #pragma once
 
 #include "common.cuh"
@@ -361,18 +362,53 @@ __global__ void __launch_bounds__(CPT >= 4 ? 512 : 576, 1) mv_bulk_kernel(MvPara
 }
 
 // --------------------------------------------------------- general kernel --
-// Units of RB rows (RB = 2: a QKV pair, or gate+up for FFN with RB = 1).
-// x staged in shared memory as xs[16 + k] = x[k] with at least 16 zeros on
-// both sides, so a 16-code slice whose first code sits at column kc (which
-// can be negative or past K for straddling loads) reads xs[16 + kc ...].
+// x is staged in shared memory as xs[16 + k] = x[k] with at least 16 zeros on
+// both sides, so a 16-code slot whose first code sits at column kc (negative
+// or past K for a load that straddles a row boundary) reads xs[16 + kc ...].
+// A lane reads its slot's four 16-byte chunks of x in the order (e + rl) & 3,
+// rl = (lane >> 1) & 3: the eight lanes of a quarter warp read chunks four
+// apart, and the rotation puts them in eight distinct bank groups for every
+// row phase, where the plain order would conflict 4-way.  The slot's weight
+// words are rotated the same way, so word i still meets x chunk i.
+__device__ __forceinline__ uint4 gen_rotate_words(const uint4& w, int rl) {
+  uint32_t a0 = w.x, a1 = w.y, a2 = w.z, a3 = w.w;
+  if (rl & 1) {
+    const uint32_t t = a0;
+    a0 = a1;
+    a1 = a2;
+    a2 = a3;
+    a3 = t;
+  }
+  if (rl & 2) {
+    uint32_t t = a0;
+    a0 = a2;
+    a2 = t;
+    t = a1;
+    a1 = a3;
+    a3 = t;
+  }
+  return make_uint4(a0, a1, a2, a3);
+}
+
+// Floats of the staged x: 16 zeros, 4W columns, >= 32 zeros, whole chunks.
+__host__ __device__ constexpr int64_t gen_xs_floats(int64_t W) { return (48 + 4 * W + 15) & ~int64_t(15); }
+
+// Units of RB rows (RB = 2: a QKV pair, or gate+up for FFN with RB = 1), one
+// unit per warp at a time: the lanes stride the unit's 16-byte slots and load
+// GU slots of every row of the unit before using any (no branch between the
+// loads, so all RT * GU are in flight), and a warp reduction ends the unit
+// with no block barrier.  Only the first and the last slot of the whole
+// buffer can be partial; lane 0 of the warp owning them reads those with
+// per-word bounds checks after the main loop.
 template <int RT, int EPI, int PRO>
-__global__ void __launch_bounds__(256) mv_gen_kernel(MvParams p, int64_t off_words) {
+__global__ void __launch_bounds__(512) mv_gen_kernel(MvParams p, int64_t off_words) {
   extern __shared__ __align__(16) float xs[];
-  __shared__ float red[8][RT];
-  __shared__ double red_d[8];
+  __shared__ double red_d[16];
   constexpr int NSTREAM = EPI == EPI_FFN ? 2 : 1;
   constexpr int RB = RT / NSTREAM;
+  constexpr int GU = 4;
   const int tid = threadIdx.x, nt = blockDim.x, warp = tid / 32, lane = tid % 32;
+  const int nwarps = nt / 32;
   const int64_t units = (p.N + RB - 1) / RB;
   const int64_t total_words = p.N * p.W;
   // Full uint4 slots of the 16-byte grid starting at the aligned base.
@@ -383,83 +419,175 @@ __global__ void __launch_bounds__(256) mv_gen_kernel(MvParams p, int64_t off_wor
 
   griddep_launch_dependents();
   griddep_wait();
-  // Stage x (normalised for PRO_RMSNORM) with zero padding.
-  const int64_t xs_len = 16 + 4 * p.W + 32;
+  // Stage x (normalised for PRO_RMSNORM) with zero padding, a 16-byte chunk
+  // per load (x on the 16-byte grid; else four scalar loads), four chunks in
+  // flight per thread.
+  const int nchunks = (int)(gen_xs_floats(p.W) / 4);
+  const int K = (int)p.K, kchunks = (K + 3) / 4;
+  const bool xvec = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+  float4* xs4 = reinterpret_cast<float4*>(xs);
   double ss = 0.0;
-  for (int64_t i = tid; i < xs_len; i += nt) {
-    int64_t k = i - 16;
-    float v = (k >= 0 && k < p.K) ? p.x[k] : 0.0f;
-    xs[i] = v;
-    if constexpr (PRO == PRO_RMSNORM) ss += (double)v * (double)v;
+  for (int q0 = tid; q0 < nchunks; q0 += 4 * nt) {
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int m = q0 + j * nt - 4;  // x chunk: x[4m .. 4m + 3]
+      v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (m >= 0 && m < kchunks) {
+        const int k = 4 * m;
+        if (xvec && k + 3 < K) {
+          v[j] = *reinterpret_cast<const float4*>(p.x + k);
+        } else {
+          v[j].x = p.x[k];
+          if (k + 1 < K) v[j].y = p.x[k + 1];
+          if (k + 2 < K) v[j].z = p.x[k + 2];
+          if (k + 3 < K) v[j].w = p.x[k + 3];
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int q = q0 + j * nt;
+      if (q < nchunks) {
+        xs4[q] = v[j];
+        if constexpr (PRO == PRO_RMSNORM)
+          ss += (double)v[j].x * v[j].x + (double)v[j].y * v[j].y + (double)v[j].z * v[j].z + (double)v[j].w * v[j].w;
+      }
+    }
   }
   if constexpr (PRO == PRO_RMSNORM) {
     double s = warp_sum_d(ss);
     if (lane == 0) red_d[warp] = s;
     __syncthreads();
     double tot = 0.0;
-    for (int w = 0; w < nt / 32; ++w) tot += red_d[w];
-    double scale = 1.0 / sqrt(tot / (double)p.K + p.eps);
-    for (int64_t k = tid; k < p.K; k += nt) xs[16 + k] = (float)((double)xs[16 + k] * scale * (double)p.gamma[k]);
+    for (int w = 0; w < nwarps; ++w) tot += red_d[w];
+    const double scale = 1.0 / sqrt(tot / (double)p.K + p.eps);
+    for (int m0 = tid; m0 < kchunks; m0 += 4 * nt) {
+      float g[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = 4 * (m0 + j * nt) + e;
+          g[j][e] = k < K ? p.gamma[k] : 0.0f;
+        }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = m0 + j * nt;
+        if (m < kchunks) {
+          float4& c = xs4[4 + m];
+          const int k = 4 * m;  // the padding past K stays exactly 0
+          c.x = (float)((double)c.x * scale * (double)g[j][0]);
+          if (k + 1 < K) c.y = (float)((double)c.y * scale * (double)g[j][1]);
+          if (k + 2 < K) c.z = (float)((double)c.z * scale * (double)g[j][2]);
+          if (k + 3 < K) c.w = (float)((double)c.w * scale * (double)g[j][3]);
+        }
+      }
+    }
   }
   __syncthreads();
 
-  int64_t it = 0;
-  for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+  const float4* x4 = reinterpret_cast<const float4*>(xs);
+  const int rl = (lane >> 1) & 3;
+  // Adds slot c of a row (phase o) with weights w to acc.
+  auto slot_dot = [&](const uint4& w, int c, int o, f2 (&acc)[2]) {
+    // The slot's first code is column 16c - 4o: chunk 4 + 4c - o.
+    const float4* xp = x4 + (4 + 4 * c - o);
+    f2 xv[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float4 t = xp[(e + rl) & 3];
+      xv[2 * e] = make_f2(t.x, t.y);
+      xv[2 * e + 1] = make_f2(t.z, t.w);
+    }
+    dot16(gen_rotate_words(w, rl), xv, acc);
+  };
+  for (int64_t u = (int64_t)blockIdx.x * nwarps + warp; u < units; u += (int64_t)gridDim.x * nwarps) {
     const int64_t row0 = u * RB;
     const f2 zero2 = make_f2(0.0f, 0.0f);
     f2 acc[RT][2];
-#pragma unroll
-    for (int r = 0; r < RT; ++r) acc[r][0] = acc[r][1] = zero2;
+    const uint4* rp[RT];
+    int ro[RT], clo[RT], chi[RT];
+    int cmax = 0;
 #pragma unroll
     for (int r = 0; r < RT; ++r) {
+      acc[r][0] = acc[r][1] = zero2;
       const int64_t row = row0 + (r % RB);
-      if (row >= p.N) continue;
       const uint32_t* b = (NSTREAM == 2 && r >= RB) ? base2 : base;
       const int64_t g0 = off_words + row * p.W;
       const int64_t q0 = g0 >> 2;
-      const int o = (int)(g0 & 3);
-      const int64_t nq = (o + p.W + 3) >> 2;
-#pragma unroll 4
-      for (int64_t c = tid; c < nq; c += nt) {
-        const int64_t q = q0 + c;
-        uint4 w;
-        if (q >= q_first_full && q <= q_last_full) {
-          w = ldg_stream_v4(b + 4 * q);
-        } else {  // partial slot at either end of the buffer
+      ro[r] = (int)(g0 & 3);
+      rp[r] = reinterpret_cast<const uint4*>(b) + q0;
+      // Full slots of this row: c in [clo, chi).
+      clo[r] = q0 < q_first_full ? 1 : 0;
+      const int64_t nq = (ro[r] + p.W + 3) >> 2, nfull = q_last_full - q0 + 1;
+      chi[r] = row < p.N ? (int)(nq < nfull ? nq : nfull) : 0;
+      cmax = max(cmax, chi[r]);
+    }
+    // Batches of GU slots per row and lane, double-buffered: the loads of
+    // the next batch are in flight while this one is multiplied.
+    auto load_batch = [&](int c0, uint4(&w)[RT][GU]) {
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+#pragma unroll
+        for (int j = 0; j < GU; ++j) {
+          const int c = c0 + 32 * j;
+          w[r][j] = (c >= clo[r] && c < chi[r]) ? ldg_stream_v4(rp[r] + c) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    auto dot_batch = [&](int c0, const uint4(&w)[RT][GU]) {
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+#pragma unroll
+        for (int j = 0; j < GU; ++j) {
+          const int c = c0 + 32 * j;
+          if (c >= clo[r] && c < chi[r]) slot_dot(w[r][j], c, ro[r], acc[r]);
+        }
+    };
+    uint4 wa[RT][GU], wb[RT][GU];
+    load_batch(lane, wa);
+    for (int b0 = 0; b0 < cmax;) {  // b0 is the same in every lane
+      load_batch(b0 + 32 * GU + lane, wb);
+      dot_batch(b0 + lane, wa);
+      b0 += 32 * GU;
+      if (b0 >= cmax) break;
+      load_batch(b0 + 32 * GU + lane, wa);
+      dot_batch(b0 + lane, wb);
+      b0 += 32 * GU;
+    }
+    if (lane == 0) {  // the partial slots at the two ends of the buffer
+#pragma unroll
+      for (int r = 0; r < RT; ++r) {
+        const int64_t row = row0 + (r % RB);
+        if (row >= p.N) continue;
+        const uint32_t* b = (NSTREAM == 2 && r >= RB) ? base2 : base;
+        const int64_t q0 = (off_words + row * p.W) >> 2;
+        const int nq = (ro[r] + (int)p.W + 3) >> 2;
+        for (int c = 0; c < nq; c += max(1, nq - 1)) {
+          const int64_t q = q0 + c;
+          if (q >= q_first_full && q <= q_last_full) continue;
           uint32_t v[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            int64_t gw = 4 * q + e;
+            const int64_t gw = 4 * q + e;
             v[e] = (gw >= off_words && gw < off_words + total_words) ? ldg_stream_u32(b + gw) : 0u;
           }
-          w = make_uint4(v[0], v[1], v[2], v[3]);
+          slot_dot(make_uint4(v[0], v[1], v[2], v[3]), c, ro[r], acc[r]);
         }
-        const float4* xp = reinterpret_cast<const float4*>(xs + 16 + 16 * c - 4 * o);
-        f2 xv[8];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float4 t = xp[e];
-          xv[2 * e] = make_f2(t.x, t.y);
-          xv[2 * e + 1] = make_f2(t.z, t.w);
-        }
-        dot16(w, xv, acc[r]);
       }
     }
-    float* rb = &red[0][0];
+    float tot[RT];
 #pragma unroll
-    for (int r = 0; r < RT; ++r) {
-      float v = warp_sum(hsum2(acc[r]));
-      if (lane == 0) red[warp][r] = v;
-    }
-    __syncthreads();
+    for (int r = 0; r < RT; ++r) tot[r] = warp_sum(hsum2(acc[r]));
     constexpr int OUTS = mv_outputs_per_unit<EPI>(RB);
     auto sum = [&](int r) {
-      float t = 0.0f;
-      for (int w = 0; w < nt / 32; ++w) t += rb[w * RT + r];
+      float t = tot[0];
+#pragma unroll
+      for (int i = 1; i < RT; ++i)
+        if (r == i) t = tot[i];
       return t;
     };
-    if (tid < OUTS) mv_epilogue<EPI>(p, row0, tid, RB, sum);
-    __syncthreads();
+    if (lane < OUTS) mv_epilogue<EPI>(p, row0, lane, RB, sum);
   }
 }
 

@@ -87,7 +87,15 @@ int launch_mv_impl(const MvParams& p, const MvPlan& plan, const LaunchOpts& o) {
   } else {
     void (*g)(MvParams, int64_t) = mv_gen_kernel<2, EPI, PRO>;
     XPU_TRY_CUDA(ensure_smem_attr((const void*)g, plan.smem));
-    XPU_TRY_CUDA(launch_ex(g, plan.grid, plan.block, plan.smem, o, p, plan.off_words));
+    // Every CTA resident at once (the warps loop over the units), so that no
+    // second wave repeats the staging of x.
+    int per_sm = 0, dev = 0, sms = 0;
+    XPU_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, g, (int)plan.block.x, plan.smem));
+    XPU_TRY_CUDA(cudaGetDevice(&dev));
+    XPU_TRY_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    dim3 grid = plan.grid;
+    grid.x = (unsigned)std::max(1, std::min((int)grid.x, std::max(1, per_sm) * sms));
+    XPU_TRY_CUDA(launch_ex(g, grid, plan.block, plan.smem, o, p, plan.off_words));
   }
   return XPU_OK;
 }
