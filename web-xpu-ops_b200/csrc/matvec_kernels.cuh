@@ -502,6 +502,21 @@ __global__ void __launch_bounds__(512) mv_gen_kernel(MvParams p, int64_t off_wor
     }
     dot16(gen_rotate_words(w, rl), xv, acc);
   };
+  // The gate and up rows of an FFN unit (one row index, weights at one
+  // offset from the 16-byte grid, so one phase and one slot range): slot c of
+  // both with one read of x.
+  auto slot_dot2 = [&](const uint4& w0, const uint4& w1, int c, int o, f2 (&acc0)[2], f2 (&acc1)[2]) {
+    const float4* xp = x4 + (4 + 4 * c - o);
+    f2 xv[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float4 t = xp[(e + rl) & 3];
+      xv[2 * e] = make_f2(t.x, t.y);
+      xv[2 * e + 1] = make_f2(t.z, t.w);
+    }
+    dot16(gen_rotate_words(w0, rl), xv, acc0);
+    dot16(gen_rotate_words(w1, rl), xv, acc1);
+  };
   for (int64_t u = (int64_t)blockIdx.x * nwarps + warp; u < units; u += (int64_t)gridDim.x * nwarps) {
     const int64_t row0 = u * RB;
     const f2 zero2 = make_f2(0.0f, 0.0f);
@@ -536,6 +551,14 @@ __global__ void __launch_bounds__(512) mv_gen_kernel(MvParams p, int64_t off_wor
         }
     };
     auto dot_batch = [&](int c0, const uint4(&w)[RT][GU]) {
+      if constexpr (NSTREAM == 2 && RT == 2) {
+#pragma unroll
+        for (int j = 0; j < GU; ++j) {
+          const int c = c0 + 32 * j;
+          if (c >= clo[0] && c < chi[0]) slot_dot2(w[0][j], w[1][j], c, ro[0], acc[0], acc[1]);
+        }
+        return;
+      }
 #pragma unroll
       for (int r = 0; r < RT; ++r)
 #pragma unroll
