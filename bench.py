@@ -71,7 +71,7 @@ def dist_env():
 
 
 def algorithmic_bytes(rows: int, K: int, matrices: int) -> int:
-    """codes + scales + y of `rows` rows per matrix, and x once (SURVEY 8(d) formula per launch, x shared)."""
+    """codes + scales + y of `rows` rows per matrix, and x once (the per-launch bytes of matvecQ8, x shared)."""
     W = (K + 3) // 4
     return matrices * (rows * W * 4 + rows * 4 + rows * 4) + K * 4
 

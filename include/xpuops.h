@@ -154,7 +154,7 @@ XPU_API int xpu_set_matvec_path(int32_t path);
 XPU_API int xpu_matvec_path(int32_t* path);
 
 /* Row-sharded matvecQ8 over the GPUs of one node from one host process
- * (SURVEY's xpu_dist entry points; the multi-process form is
+ * (the single-process multi-GPU entry points; the multi-process form is
  * torch.distributed + NCCL, xpuops/dist.py).  No counterpart in the
  * reference, which runs one WebGPU device.  NCCL is loaded at run time
  * (libnccl.so.2); failures report XPU_ENCCL.

@@ -98,7 +98,9 @@ def tiny_fixture(ref: Path) -> dict:
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the web-xpu-ops reference tree>")
+    ref = Path(sys.argv[1]).resolve()
     qc = load_quant_common(ref)
     (HERE / "quant_selftest.json").write_text(json.dumps(selftest_json(qc), indent=1) + "\n")
     np.savez_compressed(HERE / "quant_random.npz", **random_rows(qc))
