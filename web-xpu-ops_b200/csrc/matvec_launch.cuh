@@ -63,6 +63,9 @@ cudaError_t launch_ex(void (*kernel)(Args...), dim3 grid, dim3 block, size_t sme
 // once per (kernel, device).
 cudaError_t ensure_smem_attr(const void* kernel, size_t bytes);
 
+// CTAs of `kernel` resident on the current device at once (cached).
+cudaError_t resident_ctas(const void* kernel, int threads, size_t smem, int* total);
+
 template <int EPI, int PRO>
 int launch_mv_impl(const MvParams& p, const MvPlan& plan, const LaunchOpts& o) {
   void (*k)(MvParams) = nullptr;
@@ -89,12 +92,10 @@ int launch_mv_impl(const MvParams& p, const MvPlan& plan, const LaunchOpts& o) {
     XPU_TRY_CUDA(ensure_smem_attr((const void*)g, plan.smem));
     // Every CTA resident at once (the warps loop over the units), so that no
     // second wave repeats the staging of x.
-    int per_sm = 0, dev = 0, sms = 0;
-    XPU_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, g, (int)plan.block.x, plan.smem));
-    XPU_TRY_CUDA(cudaGetDevice(&dev));
-    XPU_TRY_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    int resident = 0;
+    XPU_TRY_CUDA(resident_ctas((const void*)g, (int)plan.block.x, plan.smem, &resident));
     dim3 grid = plan.grid;
-    grid.x = (unsigned)std::max(1, std::min((int)grid.x, std::max(1, per_sm) * sms));
+    grid.x = (unsigned)std::max(1, std::min((int)grid.x, resident));
     XPU_TRY_CUDA(launch_ex(g, grid, plan.block, plan.smem, o, p, plan.off_words));
   }
   return XPU_OK;

@@ -2,6 +2,7 @@
 // points of the C ABI.
 #include <stdarg.h>
 
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 
@@ -136,6 +137,48 @@ cudaError_t ensure_smem_attr(const void* kernel, size_t bytes) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess) have = want;
   return e;
+}
+
+// CTAs of `kernel` (at `threads` threads and `smem` bytes of dynamic shared
+// memory) resident on the current device at once, cached per (kernel, device,
+// threads, smem): the occupancy calculation is pure in these.
+cudaError_t resident_ctas(const void* kernel, int threads, size_t smem, int* total) {
+  struct Key {
+    const void* kernel;
+    int dev, threads;
+    size_t smem;
+    bool operator==(const Key& o) const {
+      return kernel == o.kernel && dev == o.dev && threads == o.threads && smem == o.smem;
+    }
+  };
+  struct KeyHash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.kernel) ^ (std::hash<size_t>()(k.smem) * 31u) ^ ((size_t)k.dev << 20) ^
+             ((size_t)k.threads << 4);
+    }
+  };
+  static std::mutex mu;
+  static std::unordered_map<Key, int, KeyHash> cache;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const Key key{kernel, dev, threads, smem};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *total = it->second;
+      return cudaSuccess;
+    }
+  }
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+  if (e != cudaSuccess) return e;
+  const int n = std::max(1, per_sm) * device_info().sm_count;
+  std::lock_guard<std::mutex> lock(mu);
+  cache.emplace(key, n);
+  *total = n;
+  return cudaSuccess;
 }
 
 }  // namespace xpu
