@@ -1,6 +1,6 @@
 """The C ABI without a GPU: the library loads, exports every entry point that
-include/xpuops.h declares, and refuses work when no device is present
-(there is no CPU fallback)."""
+include/xpuops.h declares, checks argument contracts before any device work,
+and refuses work when no device is present (there is no CPU fallback)."""
 import ctypes as C
 import re
 import subprocess
@@ -72,3 +72,21 @@ def test_no_cpu_fallback_without_a_device():
         pytest.skip("a CUDA device is present")
     with pytest.raises(xpuops.XpuError, match="no CUDA device"):
         xpuops.matvecQ8(np.zeros(1, np.uint32), [1.0], [1.0, 1.0, 1.0], 1, 3)
+
+
+@pytest.mark.parametrize("H,kvH,S,s_eff,msg", [
+    (6, 4, 5, 4, "kvHeads=4 must divide H=6"),  # ops/gqa/wgsl.test.ts:357
+    (6, 0, 5, 4, "positive integer"),  # :360
+    (4, 2, 5, 0, r"sEff must be an integer in \[1, S=5\]"),  # ops/gqa/wgsl-seff.test.ts:182
+    (4, 2, 5, 6, r"sEff must be an integer in \[1, S=5\]"),  # :183
+])
+def test_attention_contract_errors_before_any_device_work(H, kvH, S, s_eff, msg):
+    """groupedAttention's argument contract, with the reference's messages:
+    the C ABI checks it before it touches a device (the host pointers passed
+    here are never read), so the same errors come back on a CPU-only host."""
+    import xpuops
+    from xpuops import ops
+    buf = np.zeros(16, np.float32)
+    p = buf.ctypes.data
+    with pytest.raises(xpuops.XpuInvalidArgument, match=msg):
+        ops.groupedAttentionDecode_dev(p, p, p, H, kvH, 4, S, s_eff, p)
