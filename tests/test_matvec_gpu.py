@@ -245,6 +245,16 @@ def test_general_kernel_fused_forms(N, K):
     assert agree(yr, orc.matvec_q8_residual(wg, sg, x, r, N, K), rel=1e-4, abs_=1e-5) is None
 
 
+def test_general_kernel_rejects_k_past_its_shared_memory():
+    """Rows off the 16-byte grid stage x in shared memory, so their K is
+    bounded (about 57,000 on B200): past it the call fails loudly with
+    XPU_EINVAL and computes nothing."""
+    N, K = 2, 60001
+    w = np.zeros(N * ((K + 3) // 4), np.uint32)
+    with pytest.raises(xpuops.XpuInvalidArgument, match="exceeds this build's limit"):
+        xpuops.matvecQ8(w, np.ones(N, np.float32), np.ones(K, np.float32), N, K)
+
+
 def test_results_are_deterministic():
     _, w, s = _synth_q8(4096, 4096, 5)
     x = fill_normal(4096, 6)
