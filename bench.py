@@ -45,6 +45,7 @@ sys.path.insert(0, str(ROOT / "web-xpu-ops_b200"))
 sys.path.insert(0, str(ROOT))
 
 MATRICES, ROWS, COLS = 80, 28672, 8192
+SPEC_GBS = 8000.0  # B200 HBM3e data-sheet bandwidth
 METRIC = "matvecQ8 achieved HBM GB/s vs B200 peak; Q8 decode tokens/s, 1-8 GPUs"
 
 
@@ -59,6 +60,7 @@ def parse():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--oracle-tokens", type=int, default=4)
     ap.add_argument("--rows", type=int, default=ROWS, help=argparse.SUPPRESS)
     ap.add_argument("--cols", type=int, default=COLS, help=argparse.SUPPRESS)
     args = ap.parse_args()
@@ -203,6 +205,9 @@ def run_ours(args, rank, world, local):
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
     M, K = args.matrices, COLS
+    # This GPU's own read ceiling, measured now (harness/roofline.ts
+    # measureRoofline): one pass over a hash-filled 2 GiB buffer, fastest of 5.
+    probe = ops.measureRoofline()
     weights, scales, x, R = build_stack(torch, ops, rank, world, M, sp)
     W = K // 4
     y_local = torch.empty(M * R, dtype=torch.float32, device="cuda")
@@ -305,7 +310,9 @@ def run_ours(args, rank, world, local):
 
     target = None
     if world == 1 and M >= 8:
-        target = run_target_gemv(torch, ops, weights, scales, x, R, K, sp)
+        target = run_target_gemv(torch, ops, weights, scales, x, R, K, sp, probe["bandwidth"] / 1e9)
+
+    quant = run_quantize(torch, ops, sp) if world == 1 and rank == 0 else None
 
     decode = None
     if not args.no_decode:
@@ -338,6 +345,14 @@ def run_ours(args, rank, world, local):
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "stream_probe": {"gbs": round(probe["bandwidth"] / 1e9, 1),
+                                          "frac": round(achieved / (probe["bandwidth"] / 1e9), 4),
+                                          "load_gbs": round(probe["loadBandwidth"] / 1e9, 1),
+                                          "bulk_gbs": round(probe["bulkBandwidth"] / 1e9, 1),
+                                          "how": "xpu_measure_roofline in this run: one read pass over a "
+                                                 "hash-filled 2 GiB buffer, fastest of 5 after a warm-up; the "
+                                                 "faster of 16-byte loads and bulk copies"},
+                         "spec": {"gbs": SPEC_GBS, "frac": round(achieved / SPEC_GBS, 4)},
                          "traffic": traffic, "traffic_source": traffic_cmd,
                          "kernel": ("mv_tc_kernel (matvecQ8 on tcgen05 tensor cores, x as exact int8 limbs): one "
                                     "persistent stream-K launch per step over the stack" if on_tc else
@@ -352,6 +367,7 @@ def run_ours(args, rank, world, local):
             "clocks": clocks,
             "cpu_baseline": cpu,
             "decode": decode,
+            "quantize": quant,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -359,11 +375,13 @@ def run_ours(args, rank, world, local):
         dist.destroy_process_group()
 
 
-def run_target_gemv(torch, ops, weights, scales, x, R, K, sp):
+def run_target_gemv(torch, ops, weights, scales, x, R, K, sp, stream_gbs):
     """The BASELINE target: single matvecQ8 GEMVs, each its own launch (no
     fusion), 28672 x 8192 (matrices of the stack) and 8192 x 28672 (eight
     fresh matrices), rotating over the matrices so that L2 never holds the
-    weights being read.  CUDA events on the launching stream."""
+    weights being read.  CUDA events on the launching stream.  Each shape is
+    timed under the library's default choice (XPU_MATVEC_AUTO) and on each
+    path pinned, and the entry names the kernel AUTO ran."""
     from xpuops.synth import tensor_seed
 
     peak, _ = measured_peaks()
@@ -384,11 +402,26 @@ def run_target_gemv(torch, ops, weights, scales, x, R, K, sp):
         torch.cuda.synchronize()
         return ev[0].elapsed_time(ev[1]) / 1e3 / (reps * n)
 
+    def entry(N, Kx, launch, n):
+        b = algorithmic_bytes(N, Kx, 1)
+        res = {}
+        for name, path in (("auto", ops.MATVEC_AUTO), ("cuda_cores", ops.MATVEC_CUDA_CORES),
+                           ("tensor_cores", ops.MATVEC_TENSOR_CORES)):
+            ops.setMatvecPath(path)
+            try:
+                t = time_launches(launch, n)
+            finally:
+                ops.setMatvecPath(ops.MATVEC_AUTO)
+            res[name] = {"us": round(t * 1e6, 2), "GBs": round(b / t / 1e9, 1), "frac": round(b / t / 1e9 / peak, 4),
+                         "frac_stream_probe": round(b / t / 1e9 / stream_gbs, 4),
+                         "frac_spec": round(b / t / 1e9 / SPEC_GBS, 4)}
+        on_tc = tensor_cores_serve(1, N, Kx)
+        res["auto"]["kernel"] = "mv_tc_kernel" if on_tc else "mv_bulk_kernel"
+        return res
+
     n = min(16, weights.numel() // (R * W))
-    t = time_launches(lambda i: ops.matvecQ8_dev(weights.data_ptr() + 4 * i * R * W, scales.data_ptr() + 4 * i * R,
-                                                 x, R, K, y, sp), n)
-    b = algorithmic_bytes(R, K, 1)
-    out[f"{R}x{K}"] = {"us": round(t * 1e6, 2), "GBs": round(b / t / 1e9, 1), "frac": round(b / t / 1e9 / peak, 4)}
+    out[f"{R}x{K}"] = entry(R, K, lambda i: ops.matvecQ8_dev(weights.data_ptr() + 4 * i * R * W,
+                                                             scales.data_ptr() + 4 * i * R, x, R, K, y, sp), n)
     N2, K2 = K, R  # the other orientation
     W2 = K2 // 4
     w2 = torch.empty(8 * N2 * W2, dtype=torch.int32, device="cuda")
@@ -401,12 +434,54 @@ def run_target_gemv(torch, ops, weights, scales, x, R, K, sp):
     x2 = torch.empty(K2, dtype=torch.float32, device="cuda")
     ops.fill_normal_dev(x2, K2, tensor_seed(3, 0), stream=sp)
     y2 = torch.empty(N2, dtype=torch.float32, device="cuda")
-    t = time_launches(lambda i: ops.matvecQ8_dev(w2.data_ptr() + 4 * i * N2 * W2, s2.data_ptr() + 4 * i * N2, x2,
-                                                 N2, K2, y2, sp), 8)
-    b = algorithmic_bytes(N2, K2, 1)
-    out[f"{N2}x{K2}"] = {"us": round(t * 1e6, 2), "GBs": round(b / t / 1e9, 1), "frac": round(b / t / 1e9 / peak, 4)}
-    out["note"] = "each GEMV its own launch (xpu_matvec_q8_dev), rotating over 8-16 matrices; frac of measured HBM peak"
+    out[f"{N2}x{K2}"] = entry(N2, K2, lambda i: ops.matvecQ8_dev(w2.data_ptr() + 4 * i * N2 * W2,
+                                                                s2.data_ptr() + 4 * i * N2, x2, N2, K2, y2, sp), 8)
+    out["note"] = ("each GEMV its own launch (xpu_matvec_q8_dev), rotating over 8-16 matrices; auto = the "
+                   "library's default path choice, whose kernel is named; frac of measured HBM peak")
     return out
+
+
+def run_quantize(torch, ops, sp):
+    """ops/quantize/reference.ts `quantize` + ops/matvec/reference.ts `packQ8`
+    fused on the device (xpu_quantize_pack_q8_dev), config 1's 4096 x 4096 f32
+    weights, rotating over 8 matrices (512 MB, past L2); bytes = f32 read +
+    packed words and scales written.  Beside it the oracle's quantize + pack
+    of the same matrix on one thread."""
+    import oracle.oracle as orc
+    from xpuops.synth import tensor_seed
+
+    N = K = 4096
+    W = K // 4
+    f = torch.empty(8, N * K, dtype=torch.float32, device="cuda")
+    for i in range(8):
+        ops.fill_normal_dev(f[i], N * K, tensor_seed(0, i), 0.0, 0.02, stream=sp)
+    w = torch.empty(N * W, dtype=torch.int32, device="cuda")
+    s = torch.empty(N, dtype=torch.float32, device="cuda")
+    for i in range(8):
+        ops.quantizePackQ8_dev(f[i], N, K, w, s, stream=sp)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record()
+    for _ in range(reps):
+        for i in range(8):
+            ops.quantizePackQ8_dev(f[i], N, K, w, s, stream=sp)
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / (8 * reps)
+    b = 4 * N * K + 4 * N * W + 4 * N
+    peak, _ = measured_peaks()
+    host = f[7].cpu().numpy()
+    c0 = time.perf_counter()
+    codes, sc = orc.quantize(host, N, K)
+    packed = orc.pack_q8(codes, N, K)
+    ct = time.perf_counter() - c0
+    exact = bool(np.array_equal(packed, w.cpu().numpy().view(np.uint32)) and np.array_equal(sc, s.cpu().numpy()))
+    return {"workload": "quantize + packQ8 of config 1 (4096 x 4096 f32, N(0, 0.02^2))",
+            "us": round(t * 1e6, 2), "GBs": round(b / t / 1e9, 1), "frac": round(b / t / 1e9 / peak, 4),
+            "bit_exact_vs_oracle": exact,
+            "cpu_baseline": {"us": round(ct * 1e6, 1), "GBs": round(b / ct / 1e9, 4), "cores": 1, "kind": "port",
+                             "sample": "the oracle's quantize + pack of the same matrix, one pass, one thread"}}
 
 
 def cpu_baseline(weights, scales, x, R, K, seconds):
@@ -494,13 +569,13 @@ def run_decode(args, torch, world, max_over_ranks, barrier):
     rng = np.random.default_rng(41)
     eng = LlamaEngineQ8Resident.create(cfg, weights, torch.cuda.current_device())
     try:
-        kv0 = None
+        kvs = []
         for l in range(c.numLayers):
             k = rng.standard_normal(c.numKvHeads * ctx * c.headDim, dtype=np.float32)
             v = rng.standard_normal(c.numKvHeads * ctx * c.headDim, dtype=np.float32)
             eng.setKv(l, k, v, ctx)
-            if l == 0:
-                kv0 = (k, v)
+            kvs.append((k, v))
+        kv0 = kvs[0]
         first = int(rng.integers(0, c.vocabSize))
         warm = 3
         es = torch.cuda.ExternalStream(eng.stream())
@@ -610,6 +685,8 @@ def run_decode(args, torch, world, max_over_ranks, barrier):
             "e2e_ms": round(pwall, 3),
             "path": "batched prefill: tcgen05 matmulQ8 GEMMs (int8 weights x int8 activation limbs)",
         }
+        if world == 1 and args.oracle_tokens > 0:
+            out["oracle"] = decode_oracle_check(cfg, weights, kvs, ctx, first, warm, toks, args.oracle_tokens)
         for pth in paths[1:]:
             oms, otoks = res[pth]
             out["persistent_path" if pth == PERSISTENT else "graph_path"] = {
@@ -621,19 +698,62 @@ def run_decode(args, torch, world, max_over_ranks, barrier):
         eng.close()
 
 
+def decode_oracle_check(cfg, weights, kvs, ctx, first, warm, toks, n):
+    """The decode benchmark's first `n` greedy tokens against the oracle (a C
+    restatement of llm/engine-q8-resident.ts:1774-1892, f64, one thread like
+    JavaScript), replaying the benchmark's sequence: the cache prefilled to
+    `ctx`, `warm` greedy steps from `first`, then the timed steps from `first`
+    again.  Also the oracle's decode rate: the CPU baseline of decode
+    tokens/s."""
+    import oracle.oracle as orc
+
+    t0 = time.perf_counter()
+    o = orc.LlamaOracle(cfg, weights)
+    for l, (k, v) in enumerate(kvs):
+        o.set_kv(l, k, v, ctx)
+    build_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    tok = first
+    for _ in range(warm):
+        tok = orc.argmax(o.forward([tok]))
+    want, margins, tok = [], [], first
+    for _ in range(n):
+        logits = o.forward([tok])
+        srt = np.sort(logits.astype(np.float64))
+        margins.append(float(srt[-1] - srt[-2]) / float(np.max(np.abs(logits))))
+        tok = orc.argmax(logits)
+        want.append(int(tok))
+    el = time.perf_counter() - t0
+    o.close()
+    got = [int(t) for t in toks[:n]]
+    decided = [i for i in range(n) if margins[i] > 1e-3]
+    return {"tokens": n, "oracle": want, "ours": got, "equal": int(sum(a == b for a, b in zip(got, want))),
+            "equal_where_margin_exceeds_1e-3": all(got[i] == want[i] for i in decided),
+            "top2_margins_rel": [round(m, 6) for m in margins],
+            "cpu_baseline": {"tokens_per_s": round((warm + n) / el, 4), "cores": 1, "kind": "port",
+                             "sample": f"{warm + n} decode steps of the benchmark model at context {ctx}.."
+                                       f"{ctx + warm + n} on the oracle, one thread ({el:.1f} s; model build "
+                                       f"{build_s:.1f} s untimed)"}}
+
+
 # ------------------------------------------------------- reference arm ---
 
 def run_reference(args, rank, world):
     """The reference's CPU path for this workload: ops/matvec/reference.ts
     `matvecQ8`, restated in C (oracle/), the TypeScript itself having no
-    runtime on this image; every host thread, on a bounded sample."""
+    runtime on this image.  Inputs are built on the host by the oracle (the
+    same seeded recipe as the GPU arm), so this arm loads no GPU code.  Timed
+    with every host thread on one whole matrix of the stack per step, and
+    once single-threaded as JavaScript runs it."""
     if rank != 0:
         return
     import oracle.oracle as orc
 
     K, R = COLS, ROWS  # one whole matrix of the stack per step
     threads = os.cpu_count() or 1
-    w, s, x, how = reference_sample(R, K)
+    g0 = time.perf_counter()
+    w, s, x = reference_sample(R, K, threads)
+    gen_s = time.perf_counter() - g0
     for _ in range(max(1, min(args.warmup, 3))):
         orc.matvec_q8(w, s, x, R, K, threads=threads)
     t0 = time.perf_counter()
@@ -641,6 +761,10 @@ def run_reference(args, rank, world):
         orc.matvec_q8(w, s, x, R, K, threads=threads)
     el = time.perf_counter() - t0
     value = algorithmic_bytes(R, K, 1) * args.steps / el / 1e9
+    t1 = time.perf_counter()
+    orc.matvec_q8(w, s, x, R, K)
+    one = time.perf_counter() - t1
+    single = algorithmic_bytes(R, K, 1) / one / 1e9
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -659,37 +783,33 @@ def run_reference(args, rank, world):
                                f"each step one [{R} x {K}] matrix of it on the CPU",
                    "matrices": args.matrices, "N": ROWS, "K": COLS, "parallelism": f"{threads} host threads"},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"one [{R} x {K}] matrix per step ({how}), {args.steps} steps",
+                         "sample": f"one [{R} x {K}] matrix per step, {args.steps} steps, {threads} threads "
+                                   f"(rows split over POSIX threads)",
+                         "single_thread": {"value": round(single, 4), "unit": "GB/s", "cores": 1,
+                                           "sample": f"one pass over the same matrix, {one:.2f} s"},
+                         "inputs": f"built on the host by the oracle in {gen_s:.1f} s, untimed",
                          "cpu": _cpu_model()},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference.ts cannot run here (no JavaScript runtime on the image); the C restatement of "
-                "ops/matvec/reference.ts:117-131 stands in",
+                "ops/matvec/reference.ts:117-131 stands in.  JavaScript runs it on one thread: that figure is "
+                "cpu_baseline.single_thread.",
     }
     print(json.dumps(line), flush=True)
 
 
-def reference_sample(R, K):
-    """Matrix 0 of the stack: generated by the GPU when one is visible (as
-    our arm does), else by the host recipe (slower, identical values up to
-    one f32 ulp)."""
+def reference_sample(R, K, threads):
+    """Matrix 0 of the stack and x, built on the host by the oracle's C
+    restatement of the seeded recipe (xpuops/synth.py; the GPU arm's device
+    fill follows the same recipe), quantized and packed by the oracle."""
     import oracle.oracle as orc
-    from xpuops.synth import fill_normal, tensor_seed
+    from xpuops.synth import tensor_seed
 
-    try:
-        import torch
-
-        if torch.cuda.is_available():
-            from xpuops import ops
-
-            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-            weights, scales, x, _ = build_stack(torch, ops, 0, 1, 1, torch.cuda.current_stream().cuda_stream)
-            return (weights.cpu().numpy().view(np.uint32), scales.cpu().numpy(), x.cpu().numpy(),
-                    "generated on the GPU, untimed")
-    except Exception:
-        pass
-    wf = fill_normal(R * K, tensor_seed(0, 0), 0.0, 0.02)
-    codes, sc = orc.quantize(wf, R, K)
-    return orc.pack_q8(codes, R, K), sc, fill_normal(K, tensor_seed(1, 0)), "generated on the host, untimed"
+    wf = orc.fill_normal(R * K, tensor_seed(0, 0), 0.0, 0.02, threads=threads)
+    codes, sc = orc.quantize_mt(wf, R, K, threads)
+    del wf
+    packed = orc.pack_q8(codes, R, K)
+    del codes
+    return packed, sc, orc.fill_normal(K, tensor_seed(1, 0))
 
 
 def main():

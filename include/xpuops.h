@@ -65,6 +65,11 @@ XPU_API int xpu_memcpy_d2d(void* dst, const void* src, size_t bytes, void* strea
 XPU_API int xpu_memset(void* dst, int value, size_t bytes, void* stream);
 XPU_API int xpu_stream_sync(void* stream);
 XPU_API int xpu_set_device(int device);
+/* No counterpart in the reference (a diagnostic).  The number of allocations
+ * the library has made in this process, on any device: device memory, blocks
+ * of its stream-ordered scratch pool and pinned host memory.  A caller that
+ * must not allocate can read it before and after its calls. */
+XPU_API int xpu_alloc_count(int64_t* count);
 
 /* ---- host-array ops: synchronous, caller-owned arrays, mirror the TS API --
  * Each copies its inputs to the current device, runs the sm_100a kernel and
@@ -177,7 +182,9 @@ XPU_API int xpu_dist_destroy(xpu_dist* dist);
  * engine runs it each step (llm/engine-q8-resident.ts:1852-1853):
  * out[h] = softmax(q[h] . K[g]^T * scale) . V[g] over positions [0, s_eff),
  * g = h / (H / kv_heads).  q, out: [H, D]; k_cache, v_cache: [kv_heads, S, D]
- * with S the position stride (maxSeqLen).  scale <= 0 means 1/sqrt(D).
+ * with S the position stride (maxSeqLen).  scale NaN means the reference's
+ * default 1/sqrt(D) (`args.scale ?? defaultScale(D)`, ops/gqa/reference.ts:207);
+ * any other value, 0 or negative included, is used as given.
  * Positions are split over CTAs; the splits' softmax partials live in a
  * workspace this call allocates and frees in stream order
  * (cudaMallocAsync / cudaFreeAsync). */
@@ -200,6 +207,23 @@ XPU_API int xpu_gqa_decode_dev(const float* q, const float* k_cache, const float
 XPU_API int xpu_gqa_decode_noalloc(const float* q, const float* k_cache, const float* v_cache,
                                    int32_t H, int32_t kv_heads, int32_t D, int32_t S,
                                    int32_t s_eff, float scale, float* out, void* stream);
+/* harness/roofline.ts:17-22,162-198 `measureRoofline`: what this GPU gives
+ * right now, measured.  A buffer of stream_bytes (0 = 2 GiB; a multiple of
+ * 32 KB, at least 32 MiB, far above L2) is filled with a 32-bit hash per word
+ * and read exactly once per launch, the fastest of `runs` (0 = 5) timed
+ * launches after one warm-up.  Two read probes run on the current device:
+ * 16-byte vector loads (the reference's kernel) and 1-D bulk copies (TMA)
+ * into shared memory, the route of the library's GEMV kernels; `bandwidth`
+ * is the faster.  `compute` counts an FMA as 2 FLOP over independent f32
+ * chains.  Allocates and frees its buffer; blocking. */
+typedef struct xpu_roofline {
+  double bandwidth;      /* best bytes/s read from device memory */
+  double compute;        /* best f32 FLOP/s */
+  double load_bandwidth; /* the vector-load probe, bytes/s */
+  double bulk_bandwidth; /* the bulk-copy probe, bytes/s */
+  int64_t stream_bytes;
+} xpu_roofline;
+XPU_API int xpu_measure_roofline(int64_t stream_bytes, int32_t runs, xpu_roofline* out);
 /* ops/quantize/wgsl/kernel.wgsl bindings (input, codes, scales), but with
  * reference.ts's rounding, so the codes are bit-exact. */
 XPU_API int xpu_quantize_dev(const float* input, int64_t N, int64_t D,

@@ -75,6 +75,9 @@ def _declare(L):
     L.or_llama_set_kv.argtypes = [P, C.c_int32, P, P, C.c_int32, C.c_char_p]
     L.or_llama_set_kv.restype = C.c_int
     L.or_llama_destroy.argtypes = [P]
+    L.or_fill_normal_f32.argtypes = [P, I64, I64, C.c_uint64, C.c_double, C.c_double, C.c_double, C.c_double,
+                                     C.c_int]
+    L.or_quantize_mt.argtypes = [P, I64, I64, P, P, C.c_int]
 
 
 def _p(a: np.ndarray):
@@ -98,6 +101,24 @@ def quantize(input, N: int, D: int):
     sc = np.zeros(N, np.float32)
     lib().or_quantize(_p(x), N, D, _p(out), _p(sc))
     return out, sc
+
+
+def quantize_mt(input, N: int, D: int, threads: int):
+    """quantize() with rows split over `threads` threads (same result)."""
+    x = _c(input, np.float32)
+    out = np.zeros(N * D, np.int32)
+    sc = np.zeros(N, np.float32)
+    lib().or_quantize_mt(_p(x), N, D, _p(out), _p(sc), threads)
+    return out, sc
+
+
+def fill_normal(n: int, seed: int, mean: float = 0.0, std: float = 1.0, outlier_frac: float = 0.0,
+                outlier_mul: float = 1.0, start: int = 0, threads: int = 1) -> np.ndarray:
+    """xpuops.synth.fill_normal's seeded recipe in C, on `threads` threads."""
+    out = np.empty(n, np.float32)
+    lib().or_fill_normal_f32(_p(out), n, start, seed & 0xFFFFFFFFFFFFFFFF, mean, std, outlier_frac, outlier_mul,
+                             threads)
+    return out
 
 
 def js_round(x: float) -> float:

@@ -700,3 +700,94 @@ int or_sample_next(const double* logits, int64_t n, const uint8_t* allowed, int 
   *token = (int32_t)pick;
   return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Seeded synthetic inputs (not a reference function): the recipe of
+ * xpuops/synth.py `fill_normal`, which the device fill of the library also
+ * follows, so that the benchmark's CPU legs can build the same matrices on
+ * the host without the GPU library.  Element i of the stream:
+ *   h(lane) = mix64(seed * 0x9E3779B97F4A7C15 + (3 i + lane + 1) * 0xD1B54A32D192ED03)
+ *   u1 = ((h(0) >> 11) + 1) 2^-53, u2 = (h(1) >> 11) 2^-53
+ *   v = mean + std * sqrt(-2 ln u1) cos(2 pi u2), times outlier_mul when
+ *   (h(2) >> 11) 2^-53 < outlier_frac; stored as f32.
+ * mix64 is splitmix64's output function. */
+static inline uint64_t or_mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+static inline uint64_t or_hash3(uint64_t seed, uint64_t i, uint64_t lane) {
+  return or_mix64(seed * 0x9E3779B97F4A7C15ull + (3 * i + lane + 1) * 0xD1B54A32D192ED03ull);
+}
+
+typedef struct {
+  float* out;
+  int64_t begin, end, start;
+  uint64_t seed;
+  double mean, stdv, frac, mul;
+} fill_job;
+
+static void* fill_worker(void* arg) {
+  const fill_job* j = (const fill_job*)arg;
+  const double inv53 = 1.0 / 9007199254740992.0;
+  for (int64_t k = j->begin; k < j->end; ++k) {
+    const uint64_t i = (uint64_t)(j->start + k);
+    double u1 = (double)((or_hash3(j->seed, i, 0) >> 11) + 1) * inv53;
+    double u2 = (double)(or_hash3(j->seed, i, 1) >> 11) * inv53;
+    double v = j->mean + j->stdv * (sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2));
+    if (j->frac > 0.0 && (double)(or_hash3(j->seed, i, 2) >> 11) * inv53 < j->frac) v *= j->mul;
+    j->out[k] = (float)v;
+  }
+  return NULL;
+}
+
+void or_fill_normal_f32(float* out, int64_t n, int64_t start, uint64_t seed, double mean, double stdv,
+                        double outlier_frac, double outlier_mul, int threads) {
+  if (threads < 1) threads = 1;
+  if (threads > 256) threads = 256;
+  if (n < 65536) threads = 1;
+  fill_job jobs[256];
+  pthread_t tid[256];
+  int running[256];
+  for (int t = 0; t < threads; ++t) {
+    jobs[t] = (fill_job){out, n * t / threads, n * (t + 1) / threads, start, seed, mean, stdv, outlier_frac,
+                         outlier_mul};
+    running[t] = t > 0 && pthread_create(&tid[t], NULL, fill_worker, &jobs[t]) == 0;
+    if (t > 0 && !running[t]) fill_worker(&jobs[t]);
+  }
+  fill_worker(&jobs[0]);
+  for (int t = 1; t < threads; ++t)
+    if (running[t]) pthread_join(tid[t], NULL);
+}
+
+/* or_quantize over row blocks on `threads` POSIX threads (rows are
+ * independent, so the result is or_quantize's). */
+typedef struct {
+  const float* in;
+  int64_t r0, r1, D;
+  int32_t* codes;
+  float* scales;
+} quant_job;
+
+static void* quant_worker(void* arg) {
+  const quant_job* j = (const quant_job*)arg;
+  or_quantize(j->in + j->r0 * j->D, j->r1 - j->r0, j->D, j->codes + j->r0 * j->D, j->scales + j->r0);
+  return NULL;
+}
+
+void or_quantize_mt(const float* input, int64_t N, int64_t D, int32_t* output, float* scales, int threads) {
+  if (threads < 1) threads = 1;
+  if (threads > 256) threads = 256;
+  if (threads > N) threads = N > 0 ? (int)N : 1;
+  quant_job jobs[256];
+  pthread_t tid[256];
+  int running[256];
+  for (int t = 0; t < threads; ++t) {
+    jobs[t] = (quant_job){input, N * t / threads, N * (t + 1) / threads, D, output, scales};
+    running[t] = t > 0 && pthread_create(&tid[t], NULL, quant_worker, &jobs[t]) == 0;
+    if (t > 0 && !running[t]) quant_worker(&jobs[t]);
+  }
+  quant_worker(&jobs[0]);
+  for (int t = 1; t < threads; ++t)
+    if (running[t]) pthread_join(tid[t], NULL);
+}

@@ -105,6 +105,13 @@ int or_llama_set_kv(or_llama* e, int32_t layer, const float* k, const float* v, 
                     char* err);
 void or_llama_destroy(or_llama* e);
 
+/* Seeded synthetic inputs, the recipe of xpuops/synth.py `fill_normal`
+ * (elements [start, start + n) of the seed's stream), on `threads` threads. */
+void or_fill_normal_f32(float* out, int64_t n, int64_t start, uint64_t seed, double mean, double stdv,
+                        double outlier_frac, double outlier_mul, int threads);
+/* or_quantize with rows split over `threads` POSIX threads. */
+void or_quantize_mt(const float* input, int64_t N, int64_t D, int32_t* output, float* scales, int threads);
+
 #ifdef __cplusplus
 }
 #endif

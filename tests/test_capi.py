@@ -90,3 +90,26 @@ def test_attention_contract_errors_before_any_device_work(H, kvH, S, s_eff, msg)
     p = buf.ctypes.data
     with pytest.raises(xpuops.XpuInvalidArgument, match=msg):
         ops.groupedAttentionDecode_dev(p, p, p, H, kvH, 4, S, s_eff, p)
+
+
+def test_roofline_probe_contract_before_any_device_work(lib):
+    """xpu_measure_roofline checks its arguments before it touches a device:
+    a null result, a buffer below 32 MiB or off the 32 KB grid, runs outside
+    [1, 1000] (0 picks the defaults) come back as XPU_EINVAL."""
+    from xpuops._lib import RooflineC
+    fn = lib.xpu_measure_roofline
+    fn.argtypes = [C.c_int64, C.c_int32, C.c_void_p]
+    fn.restype = C.c_int
+    r = RooflineC()
+    assert fn(0, 0, None) == 1
+    assert fn(16 << 20, 0, C.byref(r)) == 1
+    assert fn((64 << 20) + 4096, 0, C.byref(r)) == 1
+    assert fn(64 << 20, -1, C.byref(r)) == 1
+    assert fn(64 << 20, 1001, C.byref(r)) == 1
+
+
+def test_alloc_count_is_readable_without_a_device(lib):
+    lib.xpu_alloc_count.argtypes = [C.c_void_p]
+    n = C.c_int64(-1)
+    assert lib.xpu_alloc_count(C.byref(n)) == 0 and n.value >= 0
+    assert lib.xpu_alloc_count(None) == 1

@@ -14,7 +14,7 @@ from xpuops import ops
 pytestmark = pytest.mark.gpu
 
 
-def run_case(H, kvH, D, S, s_eff, seed=0, poison_tail=False, scale=0.0):
+def run_case(H, kvH, D, S, s_eff, seed=0, poison_tail=False, scale=None):
     rng = np.random.default_rng(seed)
     q = rng.standard_normal(H * D).astype(np.float32)
     k = rng.standard_normal(kvH * S * D).astype(np.float32)
@@ -24,7 +24,7 @@ def run_case(H, kvH, D, S, s_eff, seed=0, poison_tail=False, scale=0.0):
         v.reshape(kvH, S, D)[:, s_eff:] = np.inf
     got = ops.groupedAttentionDecode(q, k, v, H, kvH, D, S, s_eff, scale)
     want = orc.grouped_attention(q, k, v, 1, H, kvH, 1, S, D, D, causal=True, query_offset=s_eff - 1,
-                                 s_eff=s_eff, scale=None if scale <= 0 else scale)
+                                 s_eff=s_eff, scale=scale)
     return got, want
 
 
@@ -48,8 +48,11 @@ def test_positions_past_seff_are_never_read():
     assert agree(got, want, rel=1e-4, abs_=1e-5 * float(np.max(np.abs(want)))) is None
 
 
-def test_explicit_scale():
-    got, want = run_case(8, 2, 32, 64, 40, seed=4, scale=0.3)
+@pytest.mark.parametrize("scale", [0.3, 0.0, -0.5])
+def test_explicit_scale(scale):
+    """ops/gqa/reference.ts:207 `args.scale ?? defaultScale(D)`: an explicit
+    scale is used as given, 0 (uniform weights) and negative ones included."""
+    got, want = run_case(8, 2, 32, 64, 40, seed=4, scale=scale)
     assert agree(got, want, rel=1e-4, abs_=1e-5 * float(np.max(np.abs(want)))) is None
 
 

@@ -273,7 +273,10 @@ AttnParams gqa_params(const float* q, const float* k, const float* v, int H, int
   a.S = S;
   a.nsplit = nsplit;
   a.chunk_max = (s_eff + nsplit - 1) / nsplit;
-  a.scale = scale > 0.0f ? scale : (float)(1.0 / sqrt((double)D));
+  // ops/gqa/reference.ts:207 `args.scale ?? defaultScale(D)`: NaN stands for
+  // the absent argument; every other value, 0 and negatives included, is used
+  // as given.
+  a.scale = isnan(scale) ? (float)(1.0 / sqrt((double)D)) : scale;
   return a;
 }
 

@@ -27,7 +27,7 @@ struct Scratch {
   template <typename T>
   int alloc(T** out, size_t count) {
     void* v = nullptr;
-    cudaError_t e = cudaMalloc(&v, count ? count * sizeof(T) : 16);
+    cudaError_t e = device_malloc(&v, count ? count * sizeof(T) : 16);
     if (e != cudaSuccess) return cuda_status(e, "cudaMalloc (op scratch)");
     p[n++] = v;
     *out = static_cast<T*>(v);

@@ -52,6 +52,21 @@ const DeviceInfo& device_info();  // of the current device (cached per device)
 cudaError_t scratch_alloc(void** ptr, size_t bytes, cudaStream_t st);
 cudaError_t scratch_free(void* ptr, cudaStream_t st);
 
+// Every allocation the library makes (device memory, pool blocks, pinned
+// host memory) goes through these helpers, which count it; the count is
+// exported as xpu_alloc_count.
+void count_alloc();
+template <class T>
+cudaError_t device_malloc(T** ptr, size_t bytes) {
+  count_alloc();
+  return cudaMalloc(reinterpret_cast<void**>(ptr), bytes);
+}
+template <class T>
+cudaError_t host_malloc_pinned(T** ptr, size_t bytes) {
+  count_alloc();
+  return cudaMallocHost(reinterpret_cast<void**>(ptr), bytes);
+}
+
 // Launch knob shared by every kernel: whether to attach the programmatic
 // stream serialization attribute (PDL) so the kernel may start before its
 // predecessor finishes; kernels call griddep_wait() before reading any

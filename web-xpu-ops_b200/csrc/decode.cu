@@ -166,7 +166,7 @@ int dev_alloc(xpu_llama* e, T** p, size_t count) {
   void* v = nullptr;
   size_t bytes = count * sizeof(T);
   if (bytes == 0) bytes = 16;
-  cudaError_t err = cudaMalloc(&v, bytes);
+  cudaError_t err = device_malloc(&v, bytes);
   if (err != cudaSuccess) return cuda_status(err, "cudaMalloc (engine)");
   e->allocs.push_back(v);
   *p = static_cast<T*>(v);
@@ -792,9 +792,9 @@ int create_engine(const xpu_llama_config* cfg, const xpu_llama_weights_q8* w, in
       cudaMemset(e->d_next, 0, 16) != cudaSuccess || cudaMemset(e->d_pos, 0, 16) != cudaSuccess ||
       cudaMemset(e->logits, 0, (size_t)c.vocab_size * 4) != cudaSuccess)
     return fail(cuda_status(cudaGetLastError(), "cudaMemset state"));
-  if (cudaMallocHost(&e->h_tokens, (size_t)c.max_seq_len * 4) != cudaSuccess ||
-      cudaMallocHost(&e->h_misc, 16) != cudaSuccess ||
-      cudaMallocHost(&e->h_logits, (size_t)c.vocab_size * 4) != cudaSuccess)
+  if (host_malloc_pinned(&e->h_tokens, (size_t)c.max_seq_len * 4) != cudaSuccess ||
+      host_malloc_pinned(&e->h_misc, 16) != cudaSuccess ||
+      host_malloc_pinned(&e->h_logits, (size_t)c.vocab_size * 4) != cudaSuccess)
     return fail(cuda_status(cudaGetLastError(), "cudaMallocHost"));
   if (cudaDeviceSynchronize() != cudaSuccess) return fail(cuda_status(cudaGetLastError(), "create sync"));
   // One eager step first, so every kernel is loaded and configured before
@@ -855,7 +855,7 @@ int xpu_llama_forward_profiled(xpu_llama* e, const int32_t* tokens, int32_t n, f
   if (breakdown && !e->mk_trace) {
     int rc = dev_alloc(e, &e->mk_trace, trace_n);
     if (rc) return rc;
-    XPU_TRY_CUDA(cudaMallocHost(&e->h_trace, trace_n * 8));
+    XPU_TRY_CUDA(host_malloc_pinned(&e->h_trace, trace_n * 8));
   }
   const int32_t base = e->tokens_so_far;
   memcpy(e->h_tokens + base, tokens, (size_t)n * 4);

@@ -3,13 +3,15 @@
 // hosts that have no torch.distributed (a TypeScript host over N-API, a C
 // program).  Device g holds rows [g R, (g + 1) R) of every matrix (R = N /
 // ngpus) and a copy of x; each device runs its shard with the same kernels
-// as xpu_matvec_q8_stack_dev, and one NCCL all-gather per matrix (NVLink /
-// NVSwitch) leaves the whole [count][N] result on every device.  NCCL is
+// as xpu_matvec_q8_stack_dev, one NCCL all-gather per call (NVLink /
+// NVSwitch) brings every device's shards of all matrices to every device,
+// and a reorder kernel leaves the whole [count][N] result.  NCCL is
 // loaded at run time (libnccl.so.2), so the library has no link-time
 // dependency on it; the collectives are plain NCCL all-gathers.
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -19,8 +21,9 @@ struct xpu_dist {
   std::vector<int> dev;
   std::vector<ncclComm_t> comm;
   std::vector<cudaStream_t> stream;
-  std::vector<float*> local;
-  std::vector<size_t> cap;  // floats allocated in local[g]
+  std::vector<float*> local;     // [count][R]: this device's shard of every matrix
+  std::vector<float*> gathered;  // [G][count][R]: every device's shards, rank-major
+  std::vector<size_t> cap;       // floats allocated in local[g] (gathered[g] holds G times that)
 };
 
 namespace xpu {
@@ -68,8 +71,24 @@ struct DeviceGuard {
   }
 };
 
-// Collectives per NCCL group (one all-gather per matrix per device).
-constexpr int64_t kGroupOps = 512;
+// gathered [G][count][R] (an all-gather's rank-major order) -> out
+// [count][G R]: matrix m's rows of device g land at out + m N + g R.
+__global__ void dist_reorder_kernel(const float4* __restrict__ gathered, float4* __restrict__ out, int64_t count,
+                                    int64_t R4, int G) {
+  const int64_t per_dev = count * R4, total = per_dev * G;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t g = i / per_dev, rest = i - g * per_dev, m = rest / R4, r = rest - m * R4;
+    out[(m * G + g) * R4 + r] = gathered[i];
+  }
+}
+__global__ void dist_reorder_scalar_kernel(const float* __restrict__ gathered, float* __restrict__ out, int64_t count,
+                                           int64_t R, int G) {
+  const int64_t per_dev = count * R, total = per_dev * G;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t g = i / per_dev, rest = i - g * per_dev, m = rest / R, r = rest - m * R;
+    out[(m * G + g) * R + r] = gathered[i];
+  }
+}
 
 }  // namespace
 }  // namespace xpu
@@ -86,6 +105,7 @@ int xpu_dist_destroy(xpu_dist* d) {
     cudaSetDevice(d->dev[g]);
     if (g < d->comm.size() && d->comm[g] && n) n->comm_destroy(d->comm[g]);
     if (g < d->local.size() && d->local[g]) cudaFree(d->local[g]);
+    if (g < d->gathered.size() && d->gathered[g]) cudaFree(d->gathered[g]);
     if (g < d->stream.size() && d->stream[g]) cudaStreamDestroy(d->stream[g]);
   }
   delete d;
@@ -117,6 +137,7 @@ int xpu_dist_create(int32_t ngpus, const int32_t* devices, xpu_dist** out) {
   d->comm.assign(ngpus, nullptr);
   d->stream.assign(ngpus, nullptr);
   d->local.assign(ngpus, nullptr);
+  d->gathered.assign(ngpus, nullptr);
   d->cap.assign(ngpus, 0);
   for (int g = 0; g < ngpus; ++g) {
     cudaSetDevice(d->dev[g]);
@@ -156,30 +177,47 @@ int xpu_dist_matvec_q8_rowshard(xpu_dist* d, const uint32_t* const* weights, int
     const size_t need = (size_t)(count * R);
     if (d->cap[g] < need) {
       if (d->local[g]) cudaFree(d->local[g]);
-      d->local[g] = nullptr;
+      if (d->gathered[g]) cudaFree(d->gathered[g]);
+      d->local[g] = d->gathered[g] = nullptr;
       d->cap[g] = 0;
-      cudaError_t e = cudaMalloc(&d->local[g], need * sizeof(float));
-      if (e != cudaSuccess) return cuda_status(e, "xpu_dist_matvec_q8_rowshard: shard buffer");
+      cudaError_t e = device_malloc(&d->local[g], need * sizeof(float));
+      if (e == cudaSuccess) e = device_malloc(&d->gathered[g], need * G * sizeof(float));
+      if (e != cudaSuccess) return cuda_status(e, "xpu_dist_matvec_q8_rowshard: shard buffers");
       d->cap[g] = need;
     }
     rc = xpu_matvec_q8_stack_dev(weights[g], weight_stride, scales[g], vectors[g], count, R, K, d->local[g],
                                  d->stream[g]);
   }
   if (rc) return rc;
-  // Matrix m of device g's shard lands at rows [g R, (g + 1) R) of
-  // outputs[*] + m N: one all-gather of R floats per matrix and device.
-  const int64_t step = std::max<int64_t>(1, kGroupOps / G);  // matrices per group
-  for (int64_t m0 = 0; m0 < count && !rc; m0 += step) {
-    const int64_t m1 = std::min<int64_t>(count, m0 + step);
+  // One all-gather of every device's whole shard ([count][R] floats), then
+  // matrix m of device g's shard moves to rows [g R, (g + 1) R) of
+  // outputs[*] + m N.
+  if (G == 1) {
+    cudaSetDevice(d->dev[0]);
+    cudaError_t e = cudaMemcpyAsync(outputs[0], d->local[0], (size_t)(count * R) * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, d->stream[0]);
+    if (e != cudaSuccess) rc = cuda_status(e, "xpu_dist_matvec_q8_rowshard: copy");
+  } else {
     rc = nccl_status(n, n->group_start(), "ncclGroupStart");
-    for (int64_t m = m0; m < m1 && !rc; ++m)
-      for (int g = 0; g < G && !rc; ++g)
-        rc = nccl_status(n,
-                         n->all_gather(d->local[g] + m * R, outputs[g] + m * N, (size_t)R, ncclFloat, d->comm[g],
-                                       d->stream[g]),
-                         "ncclAllGather");
+    for (int g = 0; g < G && !rc; ++g)
+      rc = nccl_status(n,
+                       n->all_gather(d->local[g], d->gathered[g], (size_t)(count * R), ncclFloat, d->comm[g],
+                                     d->stream[g]),
+                       "ncclAllGather");
     const int rc2 = nccl_status(n, n->group_end(), "ncclGroupEnd");
     if (!rc) rc = rc2;
+    for (int g = 0; g < G && !rc; ++g) {
+      cudaSetDevice(d->dev[g]);
+      const int grid = std::max(1, std::min(device_info().sm_count * 4, (int)((count * N + 1023) / 1024)));
+      const bool vec = R % 4 == 0 && reinterpret_cast<uintptr_t>(outputs[g]) % 16 == 0;
+      if (vec)
+        dist_reorder_kernel<<<grid, 256, 0, d->stream[g]>>>(reinterpret_cast<const float4*>(d->gathered[g]),
+                                                            reinterpret_cast<float4*>(outputs[g]), count, R / 4, G);
+      else
+        dist_reorder_scalar_kernel<<<grid, 256, 0, d->stream[g]>>>(d->gathered[g], outputs[g], count, R, G);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) rc = cuda_status(e, "xpu_dist_matvec_q8_rowshard: reorder");
+    }
   }
   // Blocking, like the host-array ops: every device holds the result.
   for (int g = 0; g < G; ++g) {

@@ -3,6 +3,7 @@
 #include <stdarg.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 
@@ -105,7 +106,14 @@ static cudaError_t scratch_pool(cudaMemPool_t* pool) {
   return cudaSuccess;
 }
 
+namespace {
+std::atomic<long long> g_alloc_count{0};
+}
+
+void count_alloc() { g_alloc_count.fetch_add(1, std::memory_order_relaxed); }
+
 cudaError_t scratch_alloc(void** ptr, size_t bytes, cudaStream_t st) {
+  count_alloc();
   cudaMemPool_t pool;
   cudaError_t e = scratch_pool(&pool);
   if (e != cudaSuccess) return e;
@@ -205,6 +213,12 @@ int xpu_device_count(int* count) {
   return XPU_OK;
 }
 
+int xpu_alloc_count(int64_t* count) {
+  XPU_REQUIRE(count, XPU_EINVAL, "xpu_alloc_count: null pointer");
+  *count = g_alloc_count.load(std::memory_order_relaxed);
+  return XPU_OK;
+}
+
 int xpu_set_device(int device) {
   XPU_TRY_CUDA(cudaSetDevice(device));
   return XPU_OK;
@@ -214,7 +228,7 @@ int xpu_malloc(void** ptr, size_t bytes) {
   XPU_REQUIRE(ptr, XPU_EINVAL, "xpu_malloc: null pointer");
   *ptr = nullptr;
   if (bytes == 0) return XPU_OK;
-  XPU_TRY_CUDA(cudaMalloc(ptr, bytes));
+  XPU_TRY_CUDA(device_malloc(ptr, bytes));
   return XPU_OK;
 }
 

@@ -1084,7 +1084,7 @@ int stream_scratch(cudaStream_t st, int64_t n, int64_t cap, SampleScratch* s, in
       slot.mem = nullptr;
       slot.n = -1;
     }
-    XPU_TRY_CUDA(cudaMalloc(&slot.mem, SampleScratch::bytes(gmax, n)));
+    XPU_TRY_CUDA(device_malloc(&slot.mem, SampleScratch::bytes(gmax, n)));
     slot.n = n;
     s->carve(slot.mem, gmax);
     XPU_TRY_CUDA(s->clear(st));
@@ -1217,7 +1217,7 @@ int xpu_sample_next(const double* logits, int64_t n, const int32_t* allowed, int
   if (rc) return rc;
   const size_t words = bits.size();
   void* mem = nullptr;
-  XPU_TRY_CUDA(cudaMalloc(&mem, (size_t)n * 8 + 16 + words * 4 + 16));
+  XPU_TRY_CUDA(device_malloc(&mem, (size_t)n * 8 + 16 + words * 4 + 16));
   struct Free {
     void* p;
     ~Free() { cudaFree(p); }

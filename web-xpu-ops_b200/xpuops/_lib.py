@@ -99,6 +99,13 @@ class ForwardProfileC(C.Structure):
     ]
 
 
+class RooflineC(C.Structure):
+    """include/xpuops.h `xpu_roofline`."""
+
+    _fields_ = [("bandwidth", C.c_double), ("compute", C.c_double), ("load_bandwidth", C.c_double),
+                ("bulk_bandwidth", C.c_double), ("stream_bytes", I64)]
+
+
 # llm/sampler.ts `rng: () => number`, as the C ABI's xpu_rng_fn.
 RNG_FN = C.CFUNCTYPE(C.c_double, C.c_void_p)
 
@@ -115,6 +122,7 @@ SIGNATURES = {
     "xpu_memset": [P, C.c_int, C.c_size_t, P],
     "xpu_stream_sync": [P],
     "xpu_set_device": [C.c_int],
+    "xpu_alloc_count": [C.POINTER(I64)],
     "xpu_quantize": [P, I64, I64, P, P],
     "xpu_pack_q8": [P, I64, I64, P],
     "xpu_pack_int8_rows": [P, I64, I64, P],
@@ -141,6 +149,7 @@ SIGNATURES = {
     "xpu_matvec_path": [C.POINTER(I32)],
     "xpu_gqa_decode_dev": [P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P],
     "xpu_gqa_decode_noalloc": [P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P],
+    "xpu_measure_roofline": [I64, I32, C.POINTER(RooflineC)],
     "xpu_llama_create": [C.POINTER(LlamaConfigC), C.POINTER(LlamaWeightsC), C.c_int, C.POINTER(P)],
     "xpu_llama_forward": [P, P, I32, P, P],
     "xpu_llama_forward_profiled": [P, P, I32, P, P, C.POINTER(ForwardProfileC)],

@@ -261,14 +261,16 @@ def stream_sync(stream=None) -> None:
 
 
 def groupedAttentionDecode_dev(q, k_cache, v_cache, H: int, kvHeads: int, D: int, S: int, sEff: int, output,
-                               scale: float = 0.0, stream=None) -> None:
+                               scale=None, stream=None) -> None:
     """ops/gqa/reference.ts:203-303 for one decode query (causal,
-    queryOffset = sEff - 1): device pointers, async on `stream`."""
-    check(lib().xpu_gqa_decode_dev(_ptr(q), _ptr(k_cache), _ptr(v_cache), H, kvHeads, D, S, sEff, scale,
-                                   _ptr(output), _ptr(stream) or None))
+    queryOffset = sEff - 1): device pointers, async on `stream`.  `scale`
+    None is the reference's default 1/sqrt(D); any number is used as given."""
+    check(lib().xpu_gqa_decode_dev(_ptr(q), _ptr(k_cache), _ptr(v_cache), H, kvHeads, D, S, sEff,
+                                   float("nan") if scale is None else float(scale), _ptr(output),
+                                   _ptr(stream) or None))
 
 
-def groupedAttentionDecode(q, k, v, H: int, kvHeads: int, D: int, S: int, sEff: int, scale: float = 0.0):
+def groupedAttentionDecode(q, k, v, H: int, kvHeads: int, D: int, S: int, sEff: int, scale=None):
     """Host-array form of groupedAttentionDecode_dev: returns out [H * D]."""
     require_device()
     qa, ka, va = _c(q, np.float32), _c(k, np.float32), _c(v, np.float32)
@@ -280,3 +282,16 @@ def groupedAttentionDecode(q, k, v, H: int, kvHeads: int, D: int, S: int, sEff: 
     groupedAttentionDecode_dev(dq, dk, dv, H, kvHeads, D, S, sEff, do, scale)
     stream_sync()
     return do.download(np.float32, H * D)
+
+
+def measureRoofline(stream_bytes: int = 0, runs: int = 0) -> dict:
+    """harness/roofline.ts:162-198 `measureRoofline` on the current device:
+    {bandwidth (bytes/s read from HBM), compute (f32 FLOP/s)}, plus the two
+    read probes it took the best of and the buffer size.  0 takes the
+    library's defaults (2 GiB, 5 timed runs)."""
+    from ._lib import RooflineC
+    require_device()
+    r = RooflineC()
+    check(lib().xpu_measure_roofline(stream_bytes, runs, C.byref(r)))
+    return {"bandwidth": r.bandwidth, "compute": r.compute, "loadBandwidth": r.load_bandwidth,
+            "bulkBandwidth": r.bulk_bandwidth, "streamBytes": r.stream_bytes}
