@@ -145,8 +145,12 @@ struct xpu_llama {
   xpu::MkParams mk{};
   size_t mk_smem = 0;
   int mk_grid = 0;
-  unsigned long long* mk_bar = nullptr;
   unsigned int* mk_ticket = nullptr;
+  unsigned int* mk_step = nullptr;  // the persistent step's epoch counter
+  // the persistent step's vectors, as tagged words (decode_mk.cuh)
+  unsigned long long *t_hidden_a = nullptr, *t_hidden_b = nullptr, *t_q = nullptr, *t_knew = nullptr,
+                     *t_vnew = nullptr, *t_attn = nullptr, *t_gated = nullptr;
+  unsigned long long *t_part_m = nullptr, *t_part_l = nullptr, *t_part_acc = nullptr;
   unsigned long long* mk_trace = nullptr;  // profile timestamps, allocated on first use
   unsigned long long* h_trace = nullptr;
   bool trace_valid = false;
@@ -359,10 +363,17 @@ int set_device_pos(xpu_llama* e, int32_t pos) {
 // Zeroes the grid-barrier, ticket and attention counters (after a failed
 // step they may hold a partial count).
 int rearm_counters(xpu_llama* e) {
-  if (e->mk_bar) XPU_TRY_CUDA(cudaMemsetAsync(e->mk_bar, 0, 8, e->stream));
   if (e->mk_ticket) XPU_TRY_CUDA(cudaMemsetAsync(e->mk_ticket, 0, 4, e->stream));
   XPU_TRY_CUDA(cudaMemsetAsync(e->counter, 0, (size_t)e->c.num_kv_heads * 4, e->stream));
   XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
+  if (e->mk_step) {
+    // A step that did not finish may have left words of its epochs: move on
+    // to fresh ones.
+    unsigned int s = 0;
+    XPU_TRY_CUDA(cudaMemcpy(&s, e->mk_step, 4, cudaMemcpyDeviceToHost));
+    s += 1;
+    XPU_TRY_CUDA(cudaMemcpy(e->mk_step, &s, 4, cudaMemcpyHostToDevice));
+  }
   return XPU_OK;
 }
 
@@ -392,6 +403,24 @@ int setup_persistent(xpu_llama* e) {
   const int L = c.num_layers;
   MkParams& p = e->mk;
   p = MkParams{};
+  // The vectors the step hands between CTAs, as tagged words, zeroed (epoch
+  // 0 is never a step's).  Vectors that every CTA reads have kMkReps
+  // replicas, rep(n) words apart (an odd number of 128-byte lines, so the
+  // replicas spread over the L2 slices).
+  auto rep = [](int64_t n) { return (n + 15) / 16 * 16 + 16; };
+  auto tagged = [&](unsigned long long** t, int64_t n, int reps) -> int {
+    const int64_t words = reps * rep(n);
+    int rc = dev_alloc(e, t, (size_t)words);
+    if (!rc) XPU_TRY_CUDA(cudaMemsetAsync(*t, 0, (size_t)words * 8, e->stream));
+    return rc;
+  };
+  {
+    int rc;
+    if ((rc = tagged(&e->t_hidden_a, h, kMkReps)) || (rc = tagged(&e->t_hidden_b, h, kMkReps)) ||
+        (rc = tagged(&e->t_q, qd, kMkReps)) || (rc = tagged(&e->t_knew, kvd, 1)) || (rc = tagged(&e->t_vnew, kvd, 1)) ||
+        (rc = tagged(&e->t_attn, qd, kMkReps)) || (rc = tagged(&e->t_gated, c.ffn_hidden, kMkReps)))
+      return rc;
+  }
   // Per-kind descriptors: layer 0's buffers and the stride to the next
   // layer's (the stacked allocations of create_engine).
   auto stride_w = [&](Linear Layer::*m) { return L > 1 ? (int64_t)((e->layers[1].*m).w - (e->layers[0].*m).w) : 0; };
@@ -433,38 +462,51 @@ int setup_persistent(xpu_llama* e) {
     d.w_stride = stride_w(&Layer::down);
     d.s_stride = stride_s(&Layer::down);
   }
-  q.x = e->hidden_a;
-  q.y = e->q;
+  q.xt = e->t_hidden_a;
+  q.xt_rep = rep(h);
+  q.yt = e->t_q;
+  q.yt_rep = rep(qd);
   q.N = (int)(qd + 2 * kvd);
   q.K = (int)h;
   q.epi = EPI_QKV;
-  o.x = e->attn;
-  o.residual = e->hidden_a;
-  o.y = e->hidden_b;
+  o.xt = e->t_attn;
+  o.xt_rep = rep(qd);
+  o.rt = e->t_hidden_a;
+  o.yt = e->t_hidden_b;
+  o.yt_rep = rep(h);
   o.N = (int)h;
   o.K = (int)qd;
   o.epi = EPI_RESID;
-  f.x = e->hidden_b;
-  f.y = e->gated;
+  f.xt = e->t_hidden_b;
+  f.xt_rep = rep(h);
+  f.yt = e->t_gated;
+  f.yt_rep = rep(c.ffn_hidden);
   f.N = c.ffn_hidden;
   f.K = (int)h;
   f.epi = EPI_FFN;
-  d.x = e->gated;
-  d.residual = e->hidden_b;
-  d.y = e->hidden_a;
+  d.xt = e->t_gated;
+  d.xt_rep = rep(c.ffn_hidden);
+  d.rt = e->t_hidden_b;
+  d.yt = e->t_hidden_a;
+  d.yt_rep = rep(h);
   d.N = (int)h;
   d.K = c.ffn_hidden;
   d.epi = EPI_RESID;
   hg.w = e->lm_head.w;
   hg.s = e->lm_head.s;
-  hg.x = e->hidden_a;
+  hg.xt = e->t_hidden_a;
+  hg.xt_rep = rep(h);
   hg.gamma = e->final_norm;
   hg.y = e->logits;
   hg.N = c.vocab_size;
   hg.K = (int)h;
   hg.epi = EPI_PLAIN;
-  p.attn_q = e->q;
-  p.attn_out = e->attn;
+  p.attn_q = e->t_q;
+  p.q_rep = rep(qd);
+  p.attn_out = e->t_attn;
+  p.attn_rep = rep(qd);
+  p.knew = e->t_knew;
+  p.vnew = e->t_vnew;
 
 
   p.layers = L;
@@ -472,7 +514,7 @@ int setup_persistent(xpu_llama* e) {
   p.embed_scale = e->embed_scale;
   p.vocab = c.vocab_size;
   p.hidden = (int)h;
-  p.hidden0 = e->hidden_a;
+  p.hidden0 = e->t_hidden_a;
   p.eps = c.rms_norm_eps;
   p.inv_freq = e->inv_freq;
   p.q_rows = (int)qd;
@@ -482,10 +524,6 @@ int setup_persistent(xpu_llama* e) {
   p.H = c.num_heads;
   p.kvH = c.num_kv_heads;
   p.attn_scale = (float)(1.0 / sqrt((double)hd));
-  p.part_m = e->part_m;
-  p.part_l = e->part_l;
-  p.part_acc = e->part_acc;
-  p.attn_counter = e->counter;
   p.token = e->d_token;
   p.pos = e->d_pos;
   p.next = e->d_next;
@@ -499,11 +537,18 @@ int setup_persistent(xpu_llama* e) {
     return XPU_OK;
   }
   if (rc) return rc;
-  if ((rc = dev_alloc(e, &e->mk_bar, 1)) || (rc = dev_alloc(e, &e->mk_ticket, 1)) ||
-      (rc = dev_alloc(e, &p.cand_v, (size_t)e->mk_grid)) || (rc = dev_alloc(e, &p.cand_i, (size_t)e->mk_grid)))
+  if ((rc = dev_alloc(e, &e->mk_ticket, 1)) || (rc = dev_alloc(e, &e->mk_step, 1)) ||
+      (rc = dev_alloc(e, &p.cand_v, (size_t)e->mk_grid)) || (rc = dev_alloc(e, &p.cand_i, (size_t)e->mk_grid)) ||
+      (rc = tagged(&e->t_part_m, (int64_t)c.num_heads * p.nsplit, 1)) ||
+      (rc = tagged(&e->t_part_l, (int64_t)c.num_heads * p.nsplit, 1)) ||
+      (rc = tagged(&e->t_part_acc, (int64_t)c.num_heads * p.nsplit * hd, 1)))
     return rc;
-  p.bar = e->mk_bar;
+  XPU_TRY_CUDA(cudaMemsetAsync(e->mk_step, 0, 4, e->stream));
+  p.part_m = e->t_part_m;
+  p.part_l = e->t_part_l;
+  p.part_acc = e->t_part_acc;
   p.ticket = e->mk_ticket;
+  p.step_epoch = e->mk_step;
   if ((rc = rearm_counters(e))) return rc;
   // A first step, so the kernel is loaded before use; its effects (cache
   // slot 0, logits, token and position words) are reset or overwritten.

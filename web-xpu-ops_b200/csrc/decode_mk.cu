@@ -7,22 +7,24 @@
 // weight for FFN).
 //
 // Consumers, per GEMV phase:
-//  1. stage the input vector in shared memory (the embedding row for layer
-//     0), normalised by rmsnorm when the phase has a gain;
+//  1. row group 0 polls the input vector's words (or gathers the embedding
+//     row for layer 0), multiplies by the rmsnorm gain when the phase has
+//     one, and stages it in shared memory;
 //  2. load their 16-column slices of it into registers: warps form rg row
 //     groups of wpg warps, a group's threads own the columns of a row (cpt
 //     slices each), and group g takes rows g, g + rg, ... of every piece;
 //  3. for each piece: dot products over the stage, release it to the
 //     producer, reduce across the warp and park one partial per (warp of
 //     the group, share row) in shared memory;
-//  4. finish every share row (sum of the group's partials) with the phase's
-//     epilogue — the same arithmetic as the per-kernel path.
+//  4. finish every share row (sum of the group's partials, times the
+//     rmsnorm scale) with the phase's epilogue and store it as words of the
+//     phase's epoch.
 // Attention: item (kv head, split) per CTA; splits write un-normalised
-// partials, meet at a per-kv-head barrier, and each merges a share of the
-// kv head's outputs.
-// Grid barriers: a monotonically increasing arrival counter, zeroed by the
-// last CTA at the end of the step; every wait is bounded (a timeout sets
-// the device error word and the CTA finishes the step without waiting).
+// partials as words of the phase's epoch, and each merges a share of the kv
+// head's outputs from all splits' words.
+// Hand-over between phases: tagged words (decode_mk.cuh); every poll is
+// bounded (a timeout sets the device error word and the CTA finishes the
+// step without waiting).
 #include <math.h>
 
 #include <algorithm>
@@ -34,6 +36,7 @@
 namespace xpu {
 namespace {
 
+static_assert(kMkReps >= 1 && kMkReps <= 32, "one lane writes each replica of a merged output");
 constexpr int kMkSlots = 32;                 // pieces in flight at most
 constexpr uint32_t kMkPieceBytes = 65536;    // largest piece (one or two bulk copies)
 constexpr int64_t kMkPrefetchAhead = 384 * 1024;  // L2 prefetch distance of a CTA's stream
@@ -42,12 +45,6 @@ constexpr int kNct = 32 * kMkConsumerWarps;  // consumer threads
 constexpr int kMkRedMinFloats = kNct * 8;
 // float4 slots of the input vector each consumer thread stages per phase.
 constexpr int kMkVec = 4;
-
-__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // Share of CTA b: units [u0, u1) of n over G CTAs.
 __host__ __device__ __forceinline__ void mk_share(int64_t n, int b, int G, int64_t& u0, int64_t& u1) {
@@ -109,32 +106,6 @@ __device__ __forceinline__ void mk_mark(const MkParams& p, int phase, int e) {
 __device__ __forceinline__ void mk_wait(uint64_t* bar, uint32_t parity, unsigned int* err, volatile int* abort_flag) {
   if (*abort_flag) return;
   if (!mbar_wait(bar, parity, err)) *abort_flag = 1;
-}
-
-// Grid barrier among the consumers of all CTAs: arrival `target / G`.
-__device__ __forceinline__ void mk_grid_sync(const MkParams& p, int prev_phase, unsigned long long target,
-                                             volatile int* abort_flag) {
-  unsigned long long* bar = p.bar;
-  unsigned int* err = p.err;
-  named_bar_sync(1, kNct);
-  mk_mark(p, prev_phase, 3);
-  if (threadIdx.x == 0) {
-    // Release: the CTA's writes (ordered before this thread by the named
-    // barrier) become visible to every CTA that acquires the count.
-    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(bar), "l"(1ull) : "memory");
-    if (!*abort_flag) {
-      const uint64_t t0 = global_timer_ns();
-      unsigned int n = 0;
-      while (ld_acquire_u64(bar) < target) {
-        if ((++n & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
-          atomicOr(err, 1u);
-          *abort_flag = 1;
-          break;
-        }
-      }
-    }
-  }
-  named_bar_sync(1, kNct);
 }
 
 // ------------------------------------------------------------- producer --
@@ -318,12 +289,91 @@ __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, ui
     mbar_wait(&full[k % kMkSlots], (uint32_t)((k / kMkSlots) & 1), p.err);
 }
 
+// ------------------------------------------------------- tagged vectors --
+// A vector word: the f32 value in the low half, the epoch of the phase that
+// wrote it in the high half.  8-byte stores and loads are single-copy
+// atomic, so a poll sees a whole old word or a whole new one.
+__device__ __forceinline__ unsigned long long mk_tag(float v, uint32_t ep) {
+  return ((unsigned long long)ep << 32) | (unsigned long long)__float_as_uint(v);
+}
+__device__ __forceinline__ void st_tag1(unsigned long long* p, float a, uint32_t ep) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(mk_tag(a, ep)) : "memory");
+}
+__device__ __forceinline__ void st_tag2(unsigned long long* p, float a, float b, uint32_t ep) {
+  asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(mk_tag(a, ep)), "l"(mk_tag(b, ep))
+               : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tag1(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ ulonglong2 ld_tag2(const unsigned long long* p) {
+  ulonglong2 v;
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool tag_is(unsigned long long w, uint32_t ep) { return (uint32_t)(w >> 32) == ep; }
+__device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+
+// Bounded wait bookkeeping of a poll loop: false once the step was aborted
+// or the wait passed kWaitLimitNs (which aborts the step).
+struct MkPollClock {
+  uint64_t t0 = 0;
+  __device__ __forceinline__ bool keep_going(const MkParams& p, volatile int* abort_flag) {
+    if (*abort_flag) return false;
+    const uint64_t now = global_timer_ns();
+    if (t0 == 0) t0 = now;
+    if (now - t0 > kWaitLimitNs) {
+      atomicOr(p.err, 1u);
+      *abort_flag = 1;
+      return false;
+    }
+    return true;
+  }
+};
+
+// The first n <= 16 words of `src` (16-byte aligned, readable up to an even
+// count) once they all carry epoch ep; zeros past n, and zeros if the step
+// is aborted.
+__device__ __forceinline__ void mk_poll_words(const MkParams& p, const unsigned long long* src, int n, uint32_t ep,
+                                              float (&out)[16], volatile int* abort_flag) {
+  MkPollClock clk;
+  for (;;) {
+    ulonglong2 w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = 2 * j < n ? ld_tag2(src + 2 * j) : make_ulonglong2(0ull, 0ull);
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (2 * j < n) ok &= tag_is(w[j].x, ep);
+      if (2 * j + 1 < n) ok &= tag_is(w[j].y, ep);
+    }
+    if (ok) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        out[2 * j] = 2 * j < n ? tag_val(w[j].x) : 0.0f;
+        out[2 * j + 1] = 2 * j + 1 < n ? tag_val(w[j].y) : 0.0f;
+      }
+      return;
+    }
+    if (!clk.keep_going(p, abort_flag)) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j] = 0.0f;
+      return;
+    }
+  }
+}
+
 // --------------------------------------------------------- GEMV phase --
-// Returns, for the HEAD phase, the thread's first maximal logit of its rows.
-__device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, const MkView& v, uint8_t* smem,
-                                              uint64_t* full, uint64_t* empty, const uint32_t* slot_off,
-                                              int64_t& pbase, volatile int* abort_flag, int tok, int pos,
-                                              double* red_d, const double* rope, float& best, int& best_i) {
+// `ep` is this phase's epoch; its input words were written by the previous
+// phase (epoch ep - 1).  For the HEAD phase, tracks the thread's first
+// maximal logit of its rows.
+__device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint32_t ep, const MkView& v,
+                                              uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                              const uint32_t* slot_off, int64_t& pbase, volatile int* abort_flag,
+                                              int tok, int pos, double* red_d, const double* rope, float& best,
+                                              int& best_i) {
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int G = gridDim.x, b = blockIdx.x;
   const MkGemv* g = v.g;
@@ -333,110 +383,20 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
   const uint32_t row_bytes = (uint32_t)(4 * W);
   float* red = reinterpret_cast<float*>(smem + p.off_red);
   float* xs = reinterpret_cast<float*>(smem + p.off_xs);
+  double* ssd = red_d + (phase & 1) * kMkConsumerWarps;  // this phase's sum(x^2) per staging warp
   const int gr = mk_granule(epi);
   int64_t u0, u1;
   mk_share(g->N / gr, b, G, u0, u1);
   const int64_t r0 = u0 * gr;
   const int n = (int)((u1 - u0) * gr);
-
-  // 1. Input vector -> xs[0, 16U) (zero past K).  A thread issues all its
-  // loads (x and the rmsnorm gain, kMkVec float4 slots each) before using
-  // any, so staging costs one memory round trip.
-  const bool embed = v.embed;
-  const float* gam = v.gamma;
-  const int nv = 4 * U;  // float4 slots of xs
-  float4 xv[kMkVec], gv[kMkVec];
-  if (embed) {
-    // gatherDequantRows (llm/weights-q8.ts:207-222): out-of-range ids give zeros.
-    const bool tok_ok = tok >= 0 && tok < p.vocab;
-    const double escale = tok_ok ? (double)p.embed_scale[tok] : 0.0;
-    int64_t e0, e1;
-    mk_share(K, b, G, e0, e1);
-#pragma unroll
-    for (int i = 0; i < kMkVec; ++i) {
-      float t[4] = {0.f, 0.f, 0.f, 0.f};
-      const int v = tid + i * kNct;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int k = 4 * v + e;
-        if (v < nv && k < K) {
-          t[e] = tok_ok ? (float)((double)p.embed_codes[(int64_t)tok * K + k] * escale) : 0.0f;
-          if (k >= e0 && k < e1) p.hidden0[k] = t[e];
-        }
-      }
-      xv[i] = make_float4(t[0], t[1], t[2], t[3]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < kMkVec; ++i) {
-      const int v = tid + i * kNct, k = 4 * v;
-      xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (v < nv) {
-        if (k + 4 <= K) {
-          xv[i] = __ldcg(reinterpret_cast<const float4*>(g->x + k));
-        } else {
-          float t[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) t[e] = k + e < K ? __ldcg(g->x + k + e) : 0.0f;
-          xv[i] = make_float4(t[0], t[1], t[2], t[3]);
-        }
-      }
-    }
-  }
-  int gslot = -1;
-  if (gam) {
-    // The gain arrived in the ring as the phase's first piece (K floats).
-    const int64_t gidx = pbase++;
-    gslot = (int)(gidx % kMkSlots);
-    mk_wait(&full[gslot], (uint32_t)((gidx / kMkSlots) & 1), p.err, abort_flag);
-    const float* gs = reinterpret_cast<const float*>(smem + p.off_ring + slot_off[gslot]);
-#pragma unroll
-    for (int i = 0; i < kMkVec; ++i) {
-      const int v = tid + i * kNct;
-      gv[i] = (4 * v < K) ? reinterpret_cast<const float4*>(gs)[v] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    // ops/rmsnorm/reference.ts:80-96: scale = 1/sqrt(mean(x^2) + eps) in f64,
-    // out = f32(x * scale * gain).
-    double ss = 0.0;
-#pragma unroll
-    for (int i = 0; i < kMkVec; ++i)
-      ss += (double)xv[i].x * xv[i].x + (double)xv[i].y * xv[i].y + (double)xv[i].z * xv[i].z +
-            (double)xv[i].w * xv[i].w;
-    const double sw = warp_sum_d(ss);
-    if (lane == 0) red_d[warp] = sw;
-    named_bar_sync(1, kNct);
-    double tot = 0.0;
-    for (int w = 0; w < kMkConsumerWarps; ++w) tot += red_d[w];
-    const double scale = 1.0 / sqrt(tot / (double)K + p.eps);
-#pragma unroll
-    for (int i = 0; i < kMkVec; ++i) {
-      xv[i].x = (float)((double)xv[i].x * scale * (double)gv[i].x);
-      xv[i].y = (float)((double)xv[i].y * scale * (double)gv[i].y);
-      xv[i].z = (float)((double)xv[i].z * scale * (double)gv[i].z);
-      xv[i].w = (float)((double)xv[i].w * scale * (double)gv[i].w);
-    }
-  }
-  // xs holds float4 (slot c, quarter e) = x[16c + 4e .. 16c + 4e + 3] at
-  // index e * UP + c (UP = mk_xs_pitch(U)): the register loads below read
-  // consecutive float4s across a warp and these stores spread over all
-  // bank groups, so neither side has bank conflicts.
-  const int UP = mk_xs_pitch(U);
-#pragma unroll
-  for (int i = 0; i < kMkVec; ++i) {
-    const int v = tid + i * kNct;
-    if (v < nv) reinterpret_cast<float4*>(xs)[(v & 3) * UP + (v >> 2)] = xv[i];
-  }
-  if (gslot >= 0) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[gslot]);  // gain consumed
-  }
-  named_bar_sync(1, kNct);
-  mk_mark(p, phase, 1);
-
-  // Epilogue operands that do not depend on this phase's sums, loaded now so
-  // their latency hides behind the dot products: a thread finishes outputs
-  // tid, tid + kNct, ... and prefetches those of its first two.
   const int outs = epi == EPI_QKV ? n / 2 : n;
+  const bool norm = v.gamma != nullptr;
+
+  // Epilogue operands that do not depend on this phase's input, loaded
+  // first so that their latency hides behind the input's: a thread finishes
+  // outputs tid, tid + kNct, ... and prefetches those of its first two.  A
+  // residual row is this CTA's own output of an earlier phase (the shares
+  // of O and DOWN are the same rows).
   float pa[2], pb[2];
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
@@ -449,27 +409,100 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
       } else {
         pa[q] = v.s[r0 + t];
         if (epi == EPI_FFN) pb[q] = v.s2[r0 + t];
-        if (epi == EPI_RESID) pb[q] = __ldcg(g->residual + r0 + t);
+        if (epi == EPI_RESID) pb[q] = tag_val(__ldcg(g->rt + r0 + t));
       }
     }
   }
 
+  // 1. Input.  Row group 0 (warps 0 .. wpg - 1; thread ti owns the 16
+  // elements of slice ti) fetches the input vector: the embedding row
+  // (gatherDequantRows, llm/weights-q8.ts:207-222) or the previous phase's
+  // words, polled until they carry its epoch.  With rmsnorm
+  // (ops/rmsnorm/reference.ts:80-96) it multiplies by the gain and reduces
+  // sum(x^2) in f64; the scale 1/sqrt(mean(x^2) + eps) multiplies every
+  // element alike, so it is applied per output row in the epilogue.  The
+  // slice goes to shared memory for the other row groups.
+  int gslot = -1;
+  const float* gs = nullptr;
+  if (norm) {
+    // The gain arrived in the ring as the phase's first piece (K floats).
+    const int64_t gidx = pbase++;
+    gslot = (int)(gidx % kMkSlots);
+    if (warp < wpg) {
+      mk_wait(&full[gslot], (uint32_t)((gidx / kMkSlots) & 1), p.err, abort_flag);
+      gs = reinterpret_cast<const float*>(smem + p.off_ring + slot_off[gslot]);
+    }
+  }
+  const int UP = mk_xs_pitch(U);
+  if (warp < wpg) {
+    const int ti = tid;
+    float xv[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) xv[e] = 0.0f;
+    const int k0 = 16 * ti, nk = min(16, K - k0);
+    if (ti < U) {
+      if (v.embed) {
+        const bool tok_ok = tok >= 0 && tok < p.vocab;
+        const double escale = tok_ok ? (double)p.embed_scale[tok] : 0.0;
+        int64_t e0, e1;
+        mk_share(K, b, G, e0, e1);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int k = k0 + e;
+          if (e < nk) {
+            xv[e] = tok_ok ? (float)((double)p.embed_codes[(int64_t)tok * K + k] * escale) : 0.0f;
+            if (k >= e0 && k < e1) st_tag1(p.hidden0 + k, xv[e], ep);  // this CTA's residual rows
+          }
+        }
+      } else {
+        mk_poll_words(p, g->xt + (b % kMkReps) * g->xt_rep + k0, nk, ep - 1u, xv, abort_flag);
+      }
+      if (tid == 0) mk_mark_any(p, phase, 6);
+    }
+    double ss = 0.0;
+    if (norm) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        ss += (double)xv[e] * (double)xv[e];
+        xv[e] = e < nk ? __fmul_rn(xv[e], gs[min(k0 + e, K - 1)]) : 0.0f;
+      }
+    }
+    // xs holds float4 (slot c, quarter e) = x[16c + 4e .. 16c + 4e + 3] at
+    // index e * UP + c (UP = mk_xs_pitch(U)): the register loads below read
+    // consecutive float4s across a warp and these stores spread over all
+    // bank groups, so neither side has bank conflicts.
+    if (ti < U) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        reinterpret_cast<float4*>(xs)[e * UP + ti] = make_float4(xv[4 * e], xv[4 * e + 1], xv[4 * e + 2], xv[4 * e + 3]);
+    }
+    if (norm) {
+      const double sw = warp_sum_d(ss);
+      if (lane == 0) ssd[warp] = sw;
+    }
+  }
+  named_bar_sync(1, kNct);
+  if (gslot >= 0 && tid == 0) mbar_arrive_cnt(&empty[gslot], kMkConsumerWarps);  // gain consumed
+  mk_mark(p, phase, 1);
+
   // 2. The thread's 16-column slice in registers: a row group of wpg warps
   // covers a row (thread ti of the group owns slice ti), and group g takes
-  // rows g, g + rg, ... of every piece.
+  // rows g, g + rg, ... of every piece.  Warps past the last whole row
+  // group take no rows.
   const int group = warp / wpg, wi = warp - group * wpg, ti = wi * 32 + lane;
-  const bool active = group < rg;
+  const int n_act = rg * wpg;
+  const bool active = warp < n_act;
   const int cs = ti < U ? ti : U - 1;  // slice read (clamped; x is 0 past U)
   // The slice as four int8 limbs per element, with the thread's own
   // exponent E (of its largest magnitude, floored at -96 so that 2^(E - 30)
-  // stays a normal float): X = round(x 2^(30 - E)), |X| <= 2^30, written as
+  // stays a normal float): X = round(x 2^(30 - E)), |X| < 2^30, written as
   // balanced base-256 digits (the bytes of X + 0x80808080, top bits
   // flipped).  xl[i][j] holds digit j of elements 4i .. 4i + 3, the word
   // layout of the packed codes, so a row's partial is 16 dp4a into four
   // exact int32 limb sums.  A non-finite element makes the partials NaN.
   int xl[4][4];
-  float xpow;
-  {
+  float xpow = 0.0f;
+  if (active) {
     float xv[16];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -486,11 +519,10 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
       bad |= !isfinite(xv[i]);
       mx = fmaxf(mx, fabsf(xv[i]));
     }
-    int E = 0;
-    if (mx > 0.0f && !bad) frexpf(mx, &E);
-    E = max(E, -96);
-    const float sc = ldexpf(1.0f, 30 - E);
-    xpow = bad ? __int_as_float(0x7fffffff) : ldexpf(1.0f, E - 30);
+    // frexp's exponent from the bits: mx in [2^(E-1), 2^E) for a normal mx.
+    const int E = max((int)((__float_as_uint(mx) >> 23) & 0xffu) - 126, -96);
+    const float sc = __uint_as_float((uint32_t)(157 - E) << 23);  // 2^(30 - E)
+    xpow = bad ? __int_as_float(0x7fffffff) : __uint_as_float((uint32_t)(97 + E) << 23);  // 2^(E - 30)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t u[4];
@@ -509,57 +541,61 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
 
   // 3. Pieces of the share, in the producer's order: piece q holds rows
   // [q P, q P + rows) of each stream; row r of the piece (stream 0 rows,
-  // then stream 1 rows) belongs to row group r % rg.
+  // then stream 1 rows) belongs to row group r % rg.  Each active warp
+  // releases a piece once; warp 0 also releases it for the idle warps.
   const int npieces = (n + P - 1) / P;
   unsigned long long waited = 0, first_ready = 0;
-  for (int q = 0; q < npieces; ++q) {
-    const int64_t gidx = pbase + q;
-    const int slot = (int)(gidx % kMkSlots);
-    const uint32_t par = (uint32_t)((gidx / kMkSlots) & 1);
-    if (p.trace && tid == 0) {
-      const unsigned long long w0 = global_timer_ns();
-      mk_wait(&full[slot], par, p.err, abort_flag);
-      const unsigned long long w1 = global_timer_ns();
-      if (q == 0) first_ready = w1;
-      waited += w1 - w0;
-    } else {
-      mk_wait(&full[slot], par, p.err, abort_flag);
-    }
-    const int rows = n - q * P < P ? n - q * P : P;
-    const int R = ns * rows;
-    const uint8_t* st = smem + p.off_ring + slot_off[slot];
-    // All of the warp's slice loads first, then the math: kMkRowsPerWarp
-    // independent rows.
-    uint4 wv[kMkRowsPerWarp];
-#pragma unroll
-    for (int t = 0; t < kMkRowsPerWarp; ++t) {
-      const int r = group + rg * t;
-      wv[t] = (active && r < R) ? *reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * (size_t)cs)
-                                : make_uint4(0u, 0u, 0u, 0u);
-    }
-    float v[kMkRowsPerWarp];
-#pragma unroll
-    for (int t = 0; t < kMkRowsPerWarp; ++t) {
-      const int w[4] = {(int)wv[t].x, (int)wv[t].y, (int)wv[t].z, (int)wv[t].w};
-      int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a0 = __dp4a(w[i], xl[i][0], a0);
-        a1 = __dp4a(w[i], xl[i][1], a1);
-        a2 = __dp4a(w[i], xl[i][2], a2);
-        a3 = __dp4a(w[i], xl[i][3], a3);
+  if (active) {
+    const uint32_t rel = warp == 0 ? 1u + (uint32_t)(kMkConsumerWarps - n_act) : 1u;
+    for (int q = 0; q < npieces; ++q) {
+      const int64_t gidx = pbase + q;
+      const int slot = (int)(gidx % kMkSlots);
+      const uint32_t par = (uint32_t)((gidx / kMkSlots) & 1);
+      if (p.trace && tid == 0) {
+        const unsigned long long w0 = global_timer_ns();
+        mk_wait(&full[slot], par, p.err, abort_flag);
+        const unsigned long long w1 = global_timer_ns();
+        if (q == 0) first_ready = w1;
+        waited += w1 - w0;
+      } else {
+        mk_wait(&full[slot], par, p.err, abort_flag);
       }
-      // sum_j 256^j a_j, exact in two int32 halves (|a_j| <= 2^18).
-      const int lo = a0 + a1 * 256, hi = a2 + a3 * 256;
-      v[t] = fmaf((float)hi, 65536.0f, (float)lo) * xpow;
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-    const float tot = warp_reduce_rows<kMkRowsPerWarp>(v, lane);
-    const int t = lane / (32 / kMkRowsPerWarp), r = group + rg * t;
-    if (active && lane % (32 / kMkRowsPerWarp) == 0 && r < R) {
-      const int stream = r / rows, local = r - stream * rows;
-      red[wi * RS + stream * n + q * P + local] = tot;
+      const int rows = n - q * P < P ? n - q * P : P;
+      const int R = ns * rows;
+      const uint8_t* st = smem + p.off_ring + slot_off[slot];
+      // All of the warp's slice loads first, then the math: kMkRowsPerWarp
+      // independent rows.
+      uint4 wv[kMkRowsPerWarp];
+#pragma unroll
+      for (int t = 0; t < kMkRowsPerWarp; ++t) {
+        const int r = group + rg * t;
+        wv[t] = r < R ? *reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * (size_t)cs)
+                      : make_uint4(0u, 0u, 0u, 0u);
+      }
+      float vv[kMkRowsPerWarp];
+#pragma unroll
+      for (int t = 0; t < kMkRowsPerWarp; ++t) {
+        const int w[4] = {(int)wv[t].x, (int)wv[t].y, (int)wv[t].z, (int)wv[t].w};
+        int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          a0 = __dp4a(w[i], xl[i][0], a0);
+          a1 = __dp4a(w[i], xl[i][1], a1);
+          a2 = __dp4a(w[i], xl[i][2], a2);
+          a3 = __dp4a(w[i], xl[i][3], a3);
+        }
+        // sum_j 256^j a_j, exact in two int32 halves (|a_j| <= 2^18).
+        const int lo = a0 + a1 * 256, hi = a2 + a3 * 256;
+        vv[t] = fmaf((float)hi, 65536.0f, (float)lo) * xpow;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cnt(&empty[slot], rel);
+      const float tot = warp_reduce_rows<kMkRowsPerWarp>(vv, lane);
+      const int t = lane / (32 / kMkRowsPerWarp), r = group + rg * t;
+      if (lane % (32 / kMkRowsPerWarp) == 0 && r < R) {
+        const int stream = r / rows, local = r - stream * rows;
+        red[wi * RS + stream * n + q * P + local] = tot;
+      }
     }
   }
   pbase += npieces;
@@ -571,20 +607,31 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
   mk_mark(p, phase, 2);
 
   // 4. Epilogue over the share rows (ops/matvec/reference.ts:117-131,
-  // :196-207, :235-242; RoPE and the KV write as the per-kernel path).
+  // :196-207, :235-242; RoPE and the KV write as the per-kernel path), with
+  // the rmsnorm scale of the input where the phase has one.  Outputs go to
+  // every replica.
+  double rs = 1.0;
+  if (norm) {
+    double tot = 0.0;
+    for (int w = 0; w < wpg; ++w) tot += ssd[w];
+    rs = 1.0 / sqrt(tot / (double)K + p.eps);
+  }
   auto sum = [&](int r) {
-    float v = 0.0f;
-    for (int w = 0; w < wpg; ++w) v += red[w * RS + r];
-    return v;
+    float s = 0.0f;
+    for (int w = 0; w < wpg; ++w) s += red[w * RS + r];
+    return s;
   };
+  // Row value: sum * scale, rounded to f32 once (with the rmsnorm factor in
+  // f64 where the phase normalises its input).
+  auto rowval = [&](float s, float sc) { return norm ? (float)((double)s * rs * (double)sc) : __fmul_rn(s, sc); };
   if (epi == EPI_QKV) {
     const int64_t qk_end = (int64_t)p.q_rows + p.kv_rows;
     for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
       const int64_t row = r0 + 2 * t;
       const float sa = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
       const float sb = q < 2 ? (q == 0 ? pb[0] : pb[1]) : v.s[row + 1];
-      float a = __fmul_rn(sum(2 * t), sa);
-      float c = __fmul_rn(sum(2 * t + 1), sb);
+      float a = rowval(sum(2 * t), sa);
+      float c = rowval(sum(2 * t + 1), sb);
       if (row < qk_end) {
         // RoPE on the adjacent pair (ops/rope/reference.ts:379-401), f64,
         // with the step's cos/sin table.
@@ -596,16 +643,17 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
         c = (float)(x0 * sn + x1 * cs);
       }
       if (row < p.q_rows) {
-        g->y[row] = a;
-        g->y[row + 1] = c;
+        for (int r = 0; r < kMkReps; ++r) st_tag2(g->yt + r * g->yt_rep + row, a, c, ep);
       } else {
-        // KV cache slot `pos` (llm/engine-q8-resident.ts:1848-1851).
+        // KV cache slot `pos` (llm/engine-q8-resident.ts:1848-1851), and the
+        // same row as words for this step's attention.
         const bool is_k = row < qk_end;
         const int64_t local = is_k ? row - p.q_rows : row - qk_end;
         const int64_t h = local / p.head_dim, d = local % p.head_dim;
         float* dst = (is_k ? v.kcache : v.vcache) + ((h * p.max_seq + pos) * p.head_dim + d);
         dst[0] = a;
         dst[1] = c;
+        st_tag2((is_k ? p.knew : p.vnew) + local, a, c, ep);
       }
     }
   } else if (epi == EPI_FFN) {
@@ -613,30 +661,33 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, cons
       const int64_t row = r0 + t;
       const float sg = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
       const float su = q < 2 ? (q == 0 ? pb[0] : pb[1]) : v.s2[row];
-      const float gt_ = __fmul_rn(sum(t), sg);
-      const float up = __fmul_rn(sum(n + t), su);
-      g->y[row] = __fmul_rn(silu_f32(gt_), up);
+      const float gt_ = rowval(sum(t), sg);
+      const float up = rowval(sum(n + t), su);
+      const float y = __fmul_rn(silu_f32(gt_), up);
+      for (int r = 0; r < kMkReps; ++r) st_tag1(g->yt + r * g->yt_rep + row, y, ep);
     }
   } else if (epi == EPI_RESID) {
     for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
       const int64_t row = r0 + t;
       const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
-      const float res = q < 2 ? (q == 0 ? pb[0] : pb[1]) : __ldcg(g->residual + row);
-      g->y[row] = __fadd_rn(res, __fmul_rn(sum(t), sc));
+      const float res = q < 2 ? (q == 0 ? pb[0] : pb[1]) : tag_val(__ldcg(g->rt + row));
+      const float y = __fadd_rn(res, rowval(sum(t), sc));
+      for (int r = 0; r < kMkReps; ++r) st_tag1(g->yt + r * g->yt_rep + row, y, ep);
     }
   } else {
     constexpr int kNone = 0x7fffffff;
     for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
       const int64_t row = r0 + t;
       const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
-      const float v = __fmul_rn(sum(t), sc);
-      g->y[row] = v;
-      if (v == v && (best_i == kNone || v > best)) {  // ascending rows: ties keep the first
-        best = v;
+      const float val = rowval(sum(t), sc);
+      g->y[row] = val;
+      if (val == val && (best_i == kNone || val > best)) {  // ascending rows: ties keep the first
+        best = val;
         best_i = (int)row;
       }
     }
   }
+  mk_mark(p, phase, 3);
 }
 
 // ---------------------------------------------------- attention phase --
@@ -690,8 +741,10 @@ __device__ __forceinline__ void mk_scores_any(const float* q_s, const float* k_s
 
 // ops/gqa/reference.ts:203-303 for one decode query (sEff = pos + 1): item
 // (kv head g, split sp) scans positions [j0, j1) for the Gq heads of g, with
-// K and V rows streamed into the ring by the producer.
-__device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, int layer, uint8_t* smem,
+// K and V rows streamed into the ring by the producer.  The splits' softmax
+// partials are words of this phase's epoch; each split then merges a share
+// of the kv head's outputs from all splits' words.
+__device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, uint32_t ep, int layer, uint8_t* smem,
                                               uint64_t* full, uint64_t* empty, const uint32_t* slot_off,
                                               int64_t& pbase, volatile int* abort_flag, int pos) {
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -703,14 +756,28 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, int 
   float* stat = p_s + Gq * cm;                              // [Gq][2]
   const int L = pos + 1;
   const int items = p.kvH * nsp;
-  const float* kcache = p.kind[MK_QKV].kcache + layer * p.kind[MK_QKV].kv_stride;
-  const float* vcache = p.kind[MK_QKV].vcache + layer * p.kind[MK_QKV].kv_stride;
   mk_mark(p, phase, 1);  // CTAs without an item keep these
   mk_mark(p, phase, 2);
   for (int it = b; it < items; it += G) {
     const MkItem m = mk_item(p, it, L);
     const int g = m.g, sp = m.sp, j0 = m.j0, nn = m.j1 - m.j0;
-    for (int i = tid; i < Gq * hd; i += kNct) q_s[i] = __ldcg(p.attn_q + (int64_t)g * Gq * hd + i);
+    // The kv head's Gq query rows, words of the QKV phase (epoch ep - 1).
+    for (int i = 2 * tid; i < Gq * hd; i += 2 * kNct) {
+      const unsigned long long* src = p.attn_q + (b % kMkReps) * p.q_rep + (int64_t)g * Gq * hd + i;
+      MkPollClock clk;
+      for (;;) {
+        const ulonglong2 w = ld_tag2(src);
+        if (tag_is(w.x, ep - 1u) && tag_is(w.y, ep - 1u)) {
+          q_s[i] = tag_val(w.x);
+          q_s[i + 1] = tag_val(w.y);
+          break;
+        }
+        if (!clk.keep_going(p, abort_flag)) {
+          q_s[i] = q_s[i + 1] = 0.0f;
+          break;
+        }
+      }
+    }
     const float* k_s = nullptr;
     const float* v_s = nullptr;
     int slot = -1;
@@ -721,11 +788,25 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, int 
       float* kv = reinterpret_cast<float*>(smem + p.off_ring + slot_off[slot]);
       k_s = kv;
       v_s = kv + nn * hd;
-      if (pos >= j0 && pos < m.j1) {  // this step's row, written by the QKV phase
-        const int64_t row = ((int64_t)g * p.max_seq + pos) * hd;
-        for (int i = tid; i < hd; i += kNct) {
-          kv[(pos - j0) * hd + i] = __ldcg(kcache + row + i);
-          kv[(nn + pos - j0) * hd + i] = __ldcg(vcache + row + i);
+      if (pos >= j0 && pos < m.j1) {  // this step's row: the QKV phase's words
+        for (int i = 2 * tid; i < 2 * hd; i += 2 * kNct) {
+          const bool is_v = i >= hd;
+          const int d = is_v ? i - hd : i;
+          const unsigned long long* src = (is_v ? p.vnew : p.knew) + (int64_t)g * hd + d;
+          float* dst = kv + ((is_v ? nn : 0) + pos - j0) * hd + d;
+          MkPollClock clk;
+          for (;;) {
+            const ulonglong2 w = ld_tag2(src);
+            if (tag_is(w.x, ep - 1u) && tag_is(w.y, ep - 1u)) {
+              dst[0] = tag_val(w.x);
+              dst[1] = tag_val(w.y);
+              break;
+            }
+            if (!clk.keep_going(p, abort_flag)) {
+              dst[0] = dst[1] = 0.0f;
+              break;
+            }
+          }
         }
       }
     }
@@ -768,10 +849,10 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, int 
 #pragma unroll
         for (int h = 0; h < 8; ++h) acc[h] = 0.0f;
         for (int j = jg; j < nn; j += jgN) {
-          const float v = v_s[j * hd + c];
+          const float vj = v_s[j * hd + c];
 #pragma unroll
           for (int h = 0; h < 8; ++h)
-            if (h < hn) acc[h] = fmaf(p_s[(hb + h) * cm + j], v, acc[h]);
+            if (h < hn) acc[h] = fmaf(p_s[(hb + h) * cm + j], vj, acc[h]);
         }
 #pragma unroll
         for (int h = 0; h < 8; ++h)
@@ -782,38 +863,21 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, int 
         const int h = o / hd, cc = o - h * hd;
         float sacc = 0.0f;
         for (int jj = 0; jj < jgN; ++jj) sacc += red[(jj * 8 + h) * hd + cc];
-        p.part_acc[((int64_t)(g * Gq + hb + h) * nsp + sp) * hd + cc] = sacc;
+        st_tag1(p.part_acc + ((int64_t)(g * Gq + hb + h) * nsp + sp) * hd + cc, sacc, ep);
       }
       named_bar_sync(1, kNct);
     }
     if (slot >= 0 && lane == 0) mbar_arrive(&empty[slot]);  // K and V rows consumed
     if (tid < Gq) {
       const int hh = g * Gq + tid;
-      p.part_m[hh * nsp + sp] = nn > 0 ? stat[2 * tid] : -INFINITY;
-      p.part_l[hh * nsp + sp] = nn > 0 ? stat[2 * tid + 1] : 0.0f;
+      st_tag1(p.part_m + hh * nsp + sp, nn > 0 ? stat[2 * tid] : -INFINITY, ep);
+      st_tag1(p.part_l + hh * nsp + sp, nn > 0 ? stat[2 * tid + 1] : 0.0f, ep);
     }
     named_bar_sync(1, kNct);
     mk_mark(p, phase, 2);
-    // Group barrier of kv head g's splits (the count grows by nsplit per
-    // layer; the step's last CTA zeroes it), then each split merges its
-    // share of the group's outputs.
-    if (tid == 0) {
-      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.attn_counter + g) : "memory");
-      const unsigned int target = (unsigned)((layer + 1) * nsp);
-      const uint64_t t0 = global_timer_ns();
-      unsigned int n = 0, c = 0;
-      while (!*abort_flag) {
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(c) : "l"(p.attn_counter + g) : "memory");
-        if (c >= target) break;
-        if ((++n & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
-          atomicOr(p.err, 1u);
-          *abort_flag = 1;
-        }
-      }
-    }
-    named_bar_sync(1, kNct);
     // Merge (one warp per output, lanes over splits): with M = max_s m_s and
-    // w_s = exp(m_s - M), out = (sum_s w_s acc_s) / (sum_s w_s l_s).
+    // w_s = exp(m_s - M), out = (sum_s w_s acc_s) / (sum_s w_s l_s), from
+    // the splits' words of this phase; lane r writes replica r.
     const int nout = Gq * hd, o0 = (int)((int64_t)nout * sp / nsp), o1 = (int)((int64_t)nout * (sp + 1) / nsp);
     for (int o = o0 + warp; o < o1; o += kMkConsumerWarps) {
       const int h = o / hd, cc = o - h * hd, hh = g * Gq + h;
@@ -821,10 +885,23 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, int 
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int si = lane + 32 * u;
-        const bool ok = si < nsp;
-        mv[u] = ok ? __ldcg(&p.part_m[hh * nsp + si]) : -INFINITY;
-        lv[u] = ok ? __ldcg(&p.part_l[hh * nsp + si]) : 0.0f;
-        av[u] = ok ? __ldcg(&p.part_acc[((int64_t)hh * nsp + si) * hd + cc]) : 0.0f;
+        mv[u] = -INFINITY;
+        lv[u] = av[u] = 0.0f;
+        if (si < nsp) {
+          MkPollClock clk;
+          for (;;) {
+            const unsigned long long wm = ld_tag1(p.part_m + hh * nsp + si);
+            const unsigned long long wl = ld_tag1(p.part_l + hh * nsp + si);
+            const unsigned long long wa = ld_tag1(p.part_acc + ((int64_t)hh * nsp + si) * hd + cc);
+            if (tag_is(wm, ep) && tag_is(wl, ep) && tag_is(wa, ep)) {
+              mv[u] = tag_val(wm);
+              lv[u] = tag_val(wl);
+              av[u] = tag_val(wa);
+              break;
+            }
+            if (!clk.keep_going(p, abort_flag)) break;
+          }
+        }
       }
       float M = -INFINITY;
 #pragma unroll
@@ -839,9 +916,10 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, int 
       }
       l = warp_sum(l);
       acc = warp_sum(acc);
-      if (lane == 0) p.attn_out[(int64_t)hh * hd + cc] = acc / l;
+      if (lane < kMkReps) st_tag1(p.attn_out + lane * p.attn_rep + (int64_t)hh * hd + cc, acc / l, ep);
     }
   }
+  mk_mark(p, phase, 3);
 }
 
 // ------------------------------------------------------------- kernel --
@@ -851,7 +929,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   __shared__ __align__(8) uint64_t empty[kMkSlots];
   __shared__ uint32_t slot_off[kMkSlots];
   __shared__ uint32_t slot_len[kMkSlots];
-  __shared__ double red_d[kMkConsumerWarps];
+  __shared__ double red_d[2 * kMkConsumerWarps];
   __shared__ double rope[128];  // (sin, cos) per RoPE pair, head_dim <= 128
   __shared__ float bv[kMkConsumerWarps];
   __shared__ int bi[kMkConsumerWarps];
@@ -878,6 +956,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   // ---------------- consumers ----------------
   const int tok = __ldcg(p.token);
   const int pos = __ldcg(p.pos);
+  const int n_phase = 5 * p.layers + 1;
+  // Epochs of this step: phase i writes epoch base + i + 1.
+  const uint32_t step = __ldcg(p.step_epoch);
+  const uint32_t ebase = step * (uint32_t)(n_phase + 1);
   // RoPE angles of this step's position (ops/rope/reference.ts:226-244,
   // :379-401): sin and cos of pos * invFreq[i] in f64, once per CTA.
   for (int i = tid; i < p.head_dim / 2; i += kNct) {
@@ -886,24 +968,20 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     rope[2 * i] = sn;
     rope[2 * i + 1] = cs;
   }
-  const int n_phase = 5 * p.layers + 1;
+  named_bar_sync(1, kNct);
   int64_t pbase = 0;  // pieces issued before the current phase
-  unsigned long long target = 0;
   constexpr int kNone = 0x7fffffff;
   float best = -INFINITY;
   int best_i = kNone;
   for (int i = 0; i < n_phase; ++i) {
-    if (i > 0) {
-      target += (unsigned long long)G;
-      mk_grid_sync(p, i - 1, target, &abort_flag);
-    }
     mk_mark(p, i, 0);
+    const uint32_t ep = ebase + (uint32_t)i + 1u;
     const int kind = mk_kind(i, p.layers);
     if (kind < 0)
-      mk_attn_phase(p, i, i / 5, smem, full, empty, slot_off, pbase, &abort_flag, pos);
+      mk_attn_phase(p, i, ep, i / 5, smem, full, empty, slot_off, pbase, &abort_flag, pos);
     else
-      mk_gemv_phase(p, i, mk_view(p, kind, kind == MK_HEAD ? 0 : i / 5), smem, full, empty, slot_off, pbase, &abort_flag, tok, pos, red_d, rope,
-                    best, best_i);
+      mk_gemv_phase(p, i, ep, mk_view(p, kind, kind == MK_HEAD ? 0 : i / 5), smem, full, empty, slot_off, pbase,
+                    &abort_flag, tok, pos, red_d, rope, best, best_i);
   }
 
   // Greedy argmax (llm/engine.ts:226-232): per-CTA candidate of its
@@ -921,7 +999,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     bi[warp] = best_i;
   }
   named_bar_sync(1, kNct);
-  mk_mark(p, n_phase - 1, 3);
   if (tid == 0) {
     for (int w = 1; w < kMkConsumerWarps; ++w)
       if (bv[w] > best || (bv[w] == best && bi[w] < best_i)) {
@@ -963,10 +1040,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     *p.next = idx;
     *p.token = idx;
     *p.pos = pos + 1;
-    // Every CTA has passed its last barrier: re-arm the counters.
-    *p.bar = 0ull;
+    // Every CTA has taken its ticket: re-arm it, and move to the next
+    // step's epochs.
     *p.ticket = 0u;
-    for (int gg = 0; gg < p.kvH; ++gg) p.attn_counter[gg] = 0u;
+    *p.step_epoch = step + 1u;
   }
 }
 

@@ -6,16 +6,21 @@
 // step.  One producer thread per CTA streams its shares of all the step's
 // weights, phase after phase, through a ring of shared-memory stages with
 // cp.async.bulk; it never waits for the activations, so while the consumer
-// warps sit at a grid barrier the next phases' weights are already arriving.
+// warps wait for a phase's input the next phases' weights are already arriving.
 // Consumer warps run the phases in order:
-//   per layer  QKV  (rmsnorm prologue, RoPE + KV-cache write epilogue)
-//              ATTN (position splits over the CTAs, last-arriving CTA merges)
+//   per layer  QKV  (rmsnorm, RoPE + KV-cache write epilogue)
+//              ATTN (position splits over the CTAs, split merge)
 //              O    (residual epilogue)
-//              FFN  (rmsnorm prologue, SiLU-gated epilogue)
+//              FFN  (rmsnorm, SiLU-gated epilogue)
 //              DOWN (residual epilogue)
-//   HEAD       lm_head (rmsnorm prologue) and the greedy argmax
-// with one grid barrier between consecutive phases (each reads a vector the
-// previous one wrote in full).
+//   HEAD       lm_head (rmsnorm) and the greedy argmax
+// Phases hand their vectors over without grid barriers: every vector that
+// crosses CTAs is stored as 8-byte words, an f32 value in the low half and
+// the epoch of the phase that wrote it in the high half, and a consumer
+// polls the words it needs until they carry the epoch it expects.  A word
+// is written with one 8-byte store, so a load sees either the old word or
+// the new one, and the epoch tells which: no fence, no counter, and the poll
+// itself delivers the data.
 #pragma once
 
 #include "common.cuh"
@@ -33,14 +38,17 @@ struct MkGemv {
   const float* s;
   const float* s2;
   int64_t s_stride;  // floats
-  const float* x;         // input vector (the embedding row for QKV of layer 0)
-  const float* gamma;     // rmsnorm gain, or null
-  int64_t gamma_stride;   // floats
-  const float* residual;  // residual epilogue
-  float* y;
+  const unsigned long long* xt;  // input vector, tagged (the embedding row for QKV of layer 0); CTA b
+                                 // reads replica b % kMkReps, xt + (b % kMkReps) * xt_rep
+  const float* gamma;            // rmsnorm gain, or null
+  int64_t gamma_stride;          // floats
+  const unsigned long long* rt;  // residual epilogue: this CTA's own rows of an earlier output (replica 0)
+  unsigned long long* yt;        // output, tagged (QKV: the q rows), written to every replica
+  float* y;                      // HEAD: the logits (plain f32)
   float* kcache;  // QKV: the caches
   float* vcache;
   int64_t kv_stride;  // floats
+  int64_t xt_rep, yt_rep;  // words between replicas of xt / yt
   int N, K, W, U;  // rows, columns, words per row, 16-byte slots per row
   int epi;         // Epi (matvec_kernels.cuh)
   int ns;          // weight streams (2 for FFN)
@@ -52,41 +60,45 @@ enum MkKind : int { MK_QKV = 0, MK_O = 1, MK_FFN = 2, MK_DOWN = 3, MK_HEAD = 4, 
 
 struct MkParams {
   MkGemv kind[MK_KINDS];
-  const float* attn_q;  // attention input (QKV output) and output
-  float* attn_out;
+  const unsigned long long* attn_q;  // attention input (QKV output), tagged, replicated
+  unsigned long long* attn_out;      // attention output, tagged, replicated
+  int64_t q_rep, attn_rep;           // words between their replicas
+  unsigned long long* knew;          // this step's K and V rows at `pos`, tagged [kv_rows]
+  unsigned long long* vnew;
   int layers;
   // embedding (layer 0 input) and its copy into the residual stream
   const int8_t* embed_codes;
   const float* embed_scale;
   int vocab, hidden;
-  float* hidden0;  // the residual stream the embedding row is written to
+  unsigned long long* hidden0;  // the residual rows the embedding row is written to (tagged, replica 0)
   double eps;
   // RoPE / attention
   const double* inv_freq;
   int q_rows, kv_rows, head_dim, max_seq, H, kvH, nsplit, cmax;
   float attn_scale;
-  float* part_m;
-  float* part_l;
-  float* part_acc;
-  unsigned int* attn_counter;  // [kvH], zero between steps
+  unsigned long long* part_m;  // split partials, tagged: [H][nsplit]
+  unsigned long long* part_l;
+  unsigned long long* part_acc;  // [H][nsplit][head_dim]
   // step state
   int32_t* token;
   int32_t* pos;
   int32_t* next;
   int32_t* gen;
   const float* logits;
-  // grid synchronisation, zero between steps
-  unsigned long long* bar;
+  // step counter (epochs of step s are s * (phases + 1) + phase + 1) and
+  // the argmax ticket, zero between steps
+  unsigned int* step_epoch;
   unsigned int* ticket;
   float* cand_v;  // [grid] per-CTA argmax candidates
   int* cand_i;
   unsigned int* err;
   // Optional profile: when non-null, CTA b writes %globaltimer at
   // trace[(phase * grid + b) * kMkTraceEvents + e]: thread 0 at e = 0 phase
-  // start (after the grid barrier), 1 input staged, 2 dot products done
+  // start, 1 input staged (its producers' words arrived), 2 dot products done
   // (all warps), 3 epilogue done, 4 its first weight stage ready, 5 the
-  // total ns it waited for weight stages in the phase; the producer at 7
-  // when it issued the phase's last weight piece (6 unused).  The buffer is zeroed
+  // total ns it waited for weight stages in the phase, 6 its own input words
+  // arrived (GEMV phases); the producer at 7 when it issued the phase's last
+  // weight piece.  The buffer is zeroed
   // before a profiled step; events that did not happen stay 0.
   unsigned long long* trace;
   // shared-memory geometry
@@ -95,6 +107,10 @@ struct MkParams {
   int red_stride;  // floats per warp slot of the partial-sum area
 };
 
+// Replicas of every vector that all CTAs read: CTA b polls replica
+// b % kMkReps, so a line of a vector is polled by ~G / kMkReps CTAs instead
+// of all of them (the polls of one line queue at one L2 slice).
+constexpr int kMkReps = 16;
 constexpr int kMkConsumerWarps = 15;  // + 1 producer warp = 512 threads: 128 registers each
 constexpr int kMkThreads = 32 * (kMkConsumerWarps + 1);
 constexpr int kMkRowsPerWarp = 8;  // rows a row group takes from one piece
