@@ -41,8 +41,6 @@ constexpr int kMkSlots = 32;                 // pieces in flight at most
 constexpr uint32_t kMkPieceBytes = 65536;    // largest piece (one or two bulk copies)
 constexpr int64_t kMkPrefetchAhead = 384 * 1024;  // L2 prefetch distance of a CTA's stream
 constexpr int kNct = 32 * kMkConsumerWarps;  // consumer threads
-// Attention's P.V reduction parks up to kNct * 8 floats in the partial area.
-constexpr int kMkRedMinFloats = kNct * 8;
 // float4 slots of the input vector each consumer thread stages per phase.
 constexpr int kMkVec = 4;
 
@@ -313,6 +311,11 @@ __device__ __forceinline__ ulonglong2 ld_tag2(const unsigned long long* p) {
   asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ float ld_volatile_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ bool tag_is(unsigned long long w, uint32_t ep) { return (uint32_t)(w >> 32) == ep; }
 __device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
 
@@ -365,6 +368,41 @@ __device__ __forceinline__ void mk_poll_words(const MkParams& p, const unsigned 
   }
 }
 
+// A 16-element input slice as four int8 limbs per element, with the slice's
+// own exponent E (of its largest magnitude, floored at -96 so that
+// 2^(E - 30) stays a normal float): X = round(x 2^(30 - E)), |X| < 2^30,
+// written as balanced base-256 digits (the bytes of X + 0x80808080, top bits
+// flipped).  xl[i][j] holds digit j of elements 4i .. 4i + 3, the word layout
+// of the packed codes, so a row's partial is 16 dp4a into four exact int32
+// limb sums, times xpow = 2^(E - 30).  A non-finite element makes xpow NaN.
+__device__ __forceinline__ void mk_limbs(const float (&xv)[16], int (&xl)[4][4], float& xpow) {
+  float mx = 0.0f;
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    bad |= !isfinite(xv[i]);
+    mx = fmaxf(mx, fabsf(xv[i]));
+  }
+  // frexp's exponent from the bits: mx in [2^(E-1), 2^E) for a normal mx.
+  const int E = max((int)((__float_as_uint(mx) >> 23) & 0xffu) - 126, -96);
+  const float sc = __uint_as_float((uint32_t)(157 - E) << 23);  // 2^(30 - E)
+  xpow = bad ? __int_as_float(0x7fffffff) : __uint_as_float((uint32_t)(97 + E) << 23);  // 2^(E - 30)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t u[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int X = bad ? 0 : __float2int_rn(xv[4 * i + c] * sc);
+      u[c] = ((uint32_t)X + 0x80808080u) ^ 0x80808080u;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t sel = (uint32_t)j | ((uint32_t)(4 + j) << 4);
+      xl[i][j] = (int)__byte_perm(__byte_perm(u[0], u[1], sel), __byte_perm(u[2], u[3], sel), 0x5410u);
+    }
+  }
+}
+
 // --------------------------------------------------------- GEMV phase --
 // `ep` is this phase's epoch; its input words were written by the previous
 // phase (epoch ep - 1).  For the HEAD phase, tracks the thread's first
@@ -383,6 +421,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   const uint32_t row_bytes = (uint32_t)(4 * W);
   float* red = reinterpret_cast<float*>(smem + p.off_red);
   float* xs = reinterpret_cast<float*>(smem + p.off_xs);
+  float* xp = reinterpret_cast<float*>(smem + p.off_xpow);
   double* ssd = red_d + (phase & 1) * kMkConsumerWarps;  // this phase's sum(x^2) per staging warp
   const int gr = mk_granule(epi);
   int64_t u0, u1;
@@ -392,27 +431,23 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   const int outs = epi == EPI_QKV ? n / 2 : n;
   const bool norm = v.gamma != nullptr;
 
-  // Epilogue operands that do not depend on this phase's input, loaded
-  // first so that their latency hides behind the input's: a thread finishes
-  // outputs tid, tid + kNct, ... and prefetches those of its first two.  A
-  // residual row is this CTA's own output of an earlier phase (the shares
-  // of O and DOWN are the same rows).
-  float pa[2], pb[2];
+  // Epilogue operands, which do not depend on this phase's input: the
+  // scale of every share row, and the up scale (FFN) or the residual (O,
+  // DOWN: this CTA's own rows of an earlier output, the shares of O and
+  // DOWN being the same rows).  Operand j is loaded at the phase start by
+  // thread j % kNct (volatile loads, so their latency hides behind the
+  // input's instead of being moved next to their use) and parked in
+  // shared memory before the dot-product barrier.
+  float* eo = reinterpret_cast<float*>(smem + p.off_epi) + (phase & 1) * p.epi_floats;
+  const int ne = (epi == EPI_FFN || epi == EPI_RESID) ? 2 * n : n;
+  auto eop_load = [&](int j) -> float {
+    if (j < n) return ld_volatile_f32(v.s + r0 + j);
+    if (epi == EPI_FFN) return ld_volatile_f32(v.s2 + r0 + j - n);
+    return tag_val(ld_tag1(g->rt + r0 + j - n));
+  };
+  float eop[2];
 #pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int t = tid + q * kNct;
-    pa[q] = pb[q] = 0.0f;
-    if (t < outs) {
-      if (epi == EPI_QKV) {
-        pa[q] = v.s[r0 + 2 * t];
-        pb[q] = v.s[r0 + 2 * t + 1];
-      } else {
-        pa[q] = v.s[r0 + t];
-        if (epi == EPI_FFN) pb[q] = v.s2[r0 + t];
-        if (epi == EPI_RESID) pb[q] = tag_val(__ldcg(g->rt + r0 + t));
-      }
-    }
-  }
+  for (int q = 0; q < 2; ++q) eop[q] = tid + q * kNct < ne ? eop_load(tid + q * kNct) : 0.0f;
 
   // 1. Input.  Row group 0 (warps 0 .. wpg - 1; thread ti owns the 16
   // elements of slice ti) fetches the input vector: the embedding row
@@ -421,7 +456,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   // (ops/rmsnorm/reference.ts:80-96) it multiplies by the gain and reduces
   // sum(x^2) in f64; the scale 1/sqrt(mean(x^2) + eps) multiplies every
   // element alike, so it is applied per output row in the epilogue.  The
-  // slice goes to shared memory for the other row groups.
+  // slice's limbs (mk_limbs) go to shared memory for every row group.
   int gslot = -1;
   const float* gs = nullptr;
   if (norm) {
@@ -434,6 +469,14 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
     }
   }
   const int UP = mk_xs_pitch(U);
+  // The thread's slice as limbs (mk_limbs); with one row group the staging
+  // threads are the only ones and keep them in registers.
+  int xl[4][4];
+  float xpow = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xl[i][j] = 0;
   if (warp < wpg) {
     const int ti = tid;
     float xv[16];
@@ -467,14 +510,18 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
         xv[e] = e < nk ? __fmul_rn(xv[e], gs[min(k0 + e, K - 1)]) : 0.0f;
       }
     }
-    // xs holds float4 (slot c, quarter e) = x[16c + 4e .. 16c + 4e + 3] at
-    // index e * UP + c (UP = mk_xs_pitch(U)): the register loads below read
-    // consecutive float4s across a warp and these stores spread over all
-    // bank groups, so neither side has bank conflicts.
+    // xs holds the limb words of slice c, elements 4i .. 4i + 3, as a uint4
+    // at index i * UP + c (UP = mk_xs_pitch(U)), and xp[c] its power of two:
+    // consecutive threads store and load consecutive uint4s, so neither side
+    // has bank conflicts.
     if (ti < U) {
+      mk_limbs(xv, xl, xpow);
+      if (rg > 1) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        reinterpret_cast<float4*>(xs)[e * UP + ti] = make_float4(xv[4 * e], xv[4 * e + 1], xv[4 * e + 2], xv[4 * e + 3]);
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<uint4*>(xs)[i * UP + ti] = make_uint4(xl[i][0], xl[i][1], xl[i][2], xl[i][3]);
+        xp[ti] = xpow;
+      }
     }
     if (norm) {
       const double sw = warp_sum_d(ss);
@@ -493,50 +540,16 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   const int n_act = rg * wpg;
   const bool active = warp < n_act;
   const int cs = ti < U ? ti : U - 1;  // slice read (clamped; x is 0 past U)
-  // The slice as four int8 limbs per element, with the thread's own
-  // exponent E (of its largest magnitude, floored at -96 so that 2^(E - 30)
-  // stays a normal float): X = round(x 2^(30 - E)), |X| < 2^30, written as
-  // balanced base-256 digits (the bytes of X + 0x80808080, top bits
-  // flipped).  xl[i][j] holds digit j of elements 4i .. 4i + 3, the word
-  // layout of the packed codes, so a row's partial is 16 dp4a into four
-  // exact int32 limb sums.  A non-finite element makes the partials NaN.
-  int xl[4][4];
-  float xpow = 0.0f;
-  if (active) {
-    float xv[16];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float4 t = ti < U ? reinterpret_cast<const float4*>(xs)[e * UP + ti] : make_float4(0.f, 0.f, 0.f, 0.f);
-      xv[4 * e] = t.x;
-      xv[4 * e + 1] = t.y;
-      xv[4 * e + 2] = t.z;
-      xv[4 * e + 3] = t.w;
-    }
-    float mx = 0.0f;
-    bool bad = false;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      bad |= !isfinite(xv[i]);
-      mx = fmaxf(mx, fabsf(xv[i]));
-    }
-    // frexp's exponent from the bits: mx in [2^(E-1), 2^E) for a normal mx.
-    const int E = max((int)((__float_as_uint(mx) >> 23) & 0xffu) - 126, -96);
-    const float sc = __uint_as_float((uint32_t)(157 - E) << 23);  // 2^(30 - E)
-    xpow = bad ? __int_as_float(0x7fffffff) : __uint_as_float((uint32_t)(97 + E) << 23);  // 2^(E - 30)
+  if (active && rg > 1) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      uint32_t u[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int X = bad ? 0 : __float2int_rn(xv[4 * i + c] * sc);
-        u[c] = ((uint32_t)X + 0x80808080u) ^ 0x80808080u;
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t sel = (uint32_t)j | ((uint32_t)(4 + j) << 4);
-        xl[i][j] = (int)__byte_perm(__byte_perm(u[0], u[1], sel), __byte_perm(u[2], u[3], sel), 0x5410u);
-      }
+      const uint4 t = ti < U ? reinterpret_cast<const uint4*>(xs)[i * UP + ti] : make_uint4(0u, 0u, 0u, 0u);
+      xl[i][0] = (int)t.x;
+      xl[i][1] = (int)t.y;
+      xl[i][2] = (int)t.z;
+      xl[i][3] = (int)t.w;
     }
+    xpow = ti < U ? xp[ti] : 0.0f;
   }
 
   // 3. Pieces of the share, in the producer's order: piece q holds rows
@@ -603,6 +616,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
     if (npieces > 0) p.trace[((size_t)phase * G + b) * kMkTraceEvents + 4] = first_ready;
     p.trace[((size_t)phase * G + b) * kMkTraceEvents + 5] = waited;
   }
+  for (int j = tid, q = 0; j < ne; j += kNct, ++q) eo[j] = q < 2 ? (q == 0 ? eop[0] : eop[1]) : eop_load(j);
   named_bar_sync(1, kNct);
   mk_mark(p, phase, 2);
 
@@ -626,10 +640,9 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   auto rowval = [&](float s, float sc) { return norm ? (float)((double)s * rs * (double)sc) : __fmul_rn(s, sc); };
   if (epi == EPI_QKV) {
     const int64_t qk_end = (int64_t)p.q_rows + p.kv_rows;
-    for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
+    for (int t = tid; t < outs; t += kNct) {
       const int64_t row = r0 + 2 * t;
-      const float sa = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
-      const float sb = q < 2 ? (q == 0 ? pb[0] : pb[1]) : v.s[row + 1];
+      const float sa = eo[2 * t], sb = eo[2 * t + 1];
       float a = rowval(sum(2 * t), sa);
       float c = rowval(sum(2 * t + 1), sb);
       if (row < qk_end) {
@@ -657,28 +670,26 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
       }
     }
   } else if (epi == EPI_FFN) {
-    for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
+    for (int t = tid; t < outs; t += kNct) {
       const int64_t row = r0 + t;
-      const float sg = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
-      const float su = q < 2 ? (q == 0 ? pb[0] : pb[1]) : v.s2[row];
+      const float sg = eo[t], su = eo[n + t];
       const float gt_ = rowval(sum(t), sg);
       const float up = rowval(sum(n + t), su);
       const float y = __fmul_rn(silu_f32(gt_), up);
       for (int r = 0; r < kMkReps; ++r) st_tag1(g->yt + r * g->yt_rep + row, y, ep);
     }
   } else if (epi == EPI_RESID) {
-    for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
+    for (int t = tid; t < outs; t += kNct) {
       const int64_t row = r0 + t;
-      const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
-      const float res = q < 2 ? (q == 0 ? pb[0] : pb[1]) : tag_val(__ldcg(g->rt + row));
+      const float sc = eo[t], res = eo[n + t];
       const float y = __fadd_rn(res, rowval(sum(t), sc));
       for (int r = 0; r < kMkReps; ++r) st_tag1(g->yt + r * g->yt_rep + row, y, ep);
     }
   } else {
     constexpr int kNone = 0x7fffffff;
-    for (int t = tid, q = 0; t < outs; t += kNct, ++q) {
+    for (int t = tid; t < outs; t += kNct) {
       const int64_t row = r0 + t;
-      const float sc = q < 2 ? (q == 0 ? pa[0] : pa[1]) : v.s[row];
+      const float sc = eo[t];
       const float val = rowval(sum(t), sc);
       g->y[row] = val;
       if (val == val && (best_i == kNone || val > best)) {  // ascending rows: ties keep the first
@@ -691,54 +702,6 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
 }
 
 // ---------------------------------------------------- attention phase --
-// Scores of one item for GT query heads per kv head (GT a power of two):
-// a warp takes PPI = 32 / GT positions at a time, each lane forms the 32
-// partial dot products (positions x heads) over its head_dim slice, and one
-// transpose reduction leaves lane l with (position l / GT, head l % GT).
-template <int GT>
-__device__ __forceinline__ void mk_scores(const float* q_s, const float* k_s, float* p_s, int nn, int hd, int cm,
-                                          float scale, int warp, int lane) {
-  constexpr int PPI = 32 / GT;
-  for (int jb = warp * PPI; jb < nn; jb += kMkConsumerWarps * PPI) {
-    float v[32];
-#pragma unroll
-    for (int pp = 0; pp < PPI; ++pp) {
-      const int j = jb + pp;
-      float kv[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) kv[i] = (j < nn && lane + 32 * i < hd) ? k_s[j * hd + lane + 32 * i] : 0.0f;
-#pragma unroll
-      for (int h = 0; h < GT; ++h) {
-        float d = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (lane + 32 * i < hd) d = fmaf(q_s[h * hd + lane + 32 * i], kv[i], d);
-        v[pp * GT + h] = d;
-      }
-    }
-    const float tot = warp_reduce_rows<32>(v, lane);
-    const int pp = lane / GT, h = lane % GT;
-    if (jb + pp < nn) p_s[h * cm + jb + pp] = tot * scale;
-  }
-}
-// Any head count: one warp reduction per (position, head).
-__device__ __forceinline__ void mk_scores_any(const float* q_s, const float* k_s, float* p_s, int Gq, int nn, int hd,
-                                              int cm, float scale, int warp, int lane) {
-  for (int j = warp; j < nn; j += kMkConsumerWarps) {
-    float kv[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) kv[i] = lane + 32 * i < hd ? k_s[j * hd + lane + 32 * i] : 0.0f;
-    for (int h = 0; h < Gq; ++h) {
-      float d = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (lane + 32 * i < hd) d = fmaf(q_s[h * hd + lane + 32 * i], kv[i], d);
-      d = warp_sum(d);
-      if (lane == 0) p_s[h * cm + j] = d * scale;
-    }
-  }
-}
-
 // ops/gqa/reference.ts:203-303 for one decode query (sEff = pos + 1): item
 // (kv head g, split sp) scans positions [j0, j1) for the Gq heads of g, with
 // K and V rows streamed into the ring by the producer.  The splits' softmax
@@ -750,7 +713,6 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, uint
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int G = gridDim.x, b = blockIdx.x;
   const int Gq = p.H / p.kvH, hd = p.head_dim, nsp = p.nsplit, cm = p.cmax;
-  float* red = reinterpret_cast<float*>(smem + p.off_red);
   float* q_s = reinterpret_cast<float*>(smem + p.off_xs);  // [Gq][hd]
   float* p_s = q_s + Gq * hd;                               // [Gq][cm]
   float* stat = p_s + Gq * cm;                              // [Gq][2]
@@ -812,15 +774,27 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, uint
     }
     named_bar_sync(1, kNct);
     mk_mark(p, phase, 1);
-    switch (Gq) {
-      case 1: mk_scores<1>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
-      case 2: mk_scores<2>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
-      case 4: mk_scores<4>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
-      case 8: mk_scores<8>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
-      case 16: mk_scores<16>(q_s, k_s, p_s, nn, hd, cm, p.attn_scale, warp, lane); break;
-      default: mk_scores_any(q_s, k_s, p_s, Gq, nn, hd, cm, p.attn_scale, warp, lane); break;
+    // Scores s[h][j] = (q[h] . k[j]) * scale, one (head, position) pair per
+    // thread.  Lane l walks the rows' 16-byte chunks from chunk l: the lanes
+    // of a quarter warp then read eight different bank groups of q and k.
+    const int nch = hd / 4;
+    for (int pr = tid; pr < Gq * nn; pr += kNct) {
+      const int h = pr % Gq, j = pr / Gq;
+      const float4* qr = reinterpret_cast<const float4*>(q_s + h * hd);
+      const float4* kr = reinterpret_cast<const float4*>(k_s + (size_t)j * hd);
+      float a0 = 0.0f, a1 = 0.0f;
+      int cc = lane % nch;
+      for (int c = 0; c < nch; ++c, cc = cc + 1 == nch ? 0 : cc + 1) {
+        const float4 qv = qr[cc], kv = kr[cc];
+        a0 = fmaf(qv.x, kv.x, a0);
+        a1 = fmaf(qv.y, kv.y, a1);
+        a0 = fmaf(qv.z, kv.z, a0);
+        a1 = fmaf(qv.w, kv.w, a1);
+      }
+      p_s[h * cm + j] = (a0 + a1) * p.attn_scale;
     }
     named_bar_sync(1, kNct);
+    mk_mark(p, phase, 4);
     // Max and sum of exp per head over this split.
     for (int h = warp; h < Gq; h += kMkConsumerWarps) {
       float mx = -INFINITY;
@@ -839,34 +813,24 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, uint
       }
     }
     named_bar_sync(1, kNct);
-    // P.V: thread (jg, c) reads V[j][c] for j = jg, jg + jgN, ... and
-    // accumulates up to 8 heads; the jgN partials are added in order.
-    const int jgN = kNct / hd, c = tid % hd, jg = tid / hd;
-    for (int hb = 0; hb < Gq; hb += 8) {
-      const int hn = min(8, Gq - hb);
-      if (jg < jgN) {
-        float acc[8];
-#pragma unroll
-        for (int h = 0; h < 8; ++h) acc[h] = 0.0f;
-        for (int j = jg; j < nn; j += jgN) {
-          const float vj = v_s[j * hd + c];
-#pragma unroll
-          for (int h = 0; h < 8; ++h)
-            if (h < hn) acc[h] = fmaf(p_s[(hb + h) * cm + j], vj, acc[h]);
-        }
-#pragma unroll
-        for (int h = 0; h < 8; ++h)
-          if (h < hn) red[(jg * 8 + h) * hd + c] = acc[h];
+    mk_mark(p, phase, 5);
+    // P.V, one (head, dim) output per thread over the split's positions
+    // (four partial sums), straight to the split's partial words.
+    for (int o = tid; o < Gq * hd; o += kNct) {
+      const int h = o / hd, d = o - h * hd;
+      const float* pr = p_s + h * cm;
+      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+      int j = 0;
+      for (; j + 3 < nn; j += 4) {
+        a0 = fmaf(pr[j], v_s[(size_t)j * hd + d], a0);
+        a1 = fmaf(pr[j + 1], v_s[(size_t)(j + 1) * hd + d], a1);
+        a2 = fmaf(pr[j + 2], v_s[(size_t)(j + 2) * hd + d], a2);
+        a3 = fmaf(pr[j + 3], v_s[(size_t)(j + 3) * hd + d], a3);
       }
-      named_bar_sync(1, kNct);
-      for (int o = tid; o < hn * hd; o += kNct) {
-        const int h = o / hd, cc = o - h * hd;
-        float sacc = 0.0f;
-        for (int jj = 0; jj < jgN; ++jj) sacc += red[(jj * 8 + h) * hd + cc];
-        st_tag1(p.part_acc + ((int64_t)(g * Gq + hb + h) * nsp + sp) * hd + cc, sacc, ep);
-      }
-      named_bar_sync(1, kNct);
+      for (; j < nn; ++j) a0 = fmaf(pr[j], v_s[(size_t)j * hd + d], a0);
+      st_tag1(p.part_acc + ((int64_t)(g * Gq + h) * nsp + sp) * hd + d, (a0 + a1) + (a2 + a3), ep);
     }
+    mk_mark(p, phase, 6);
     if (slot >= 0 && lane == 0) mbar_arrive(&empty[slot]);  // K and V rows consumed
     if (tid < Gq) {
       const int hh = g * Gq + tid;
@@ -914,6 +878,7 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, uint
         l = fmaf(lv[u], w, l);
         acc = fmaf(av[u], w, acc);
       }
+      if (o == o0) mk_mark(p, phase, 7);  // thread 0's merge inputs arrived
       l = warp_sum(l);
       acc = warp_sum(acc);
       if (lane < kMkReps) st_tag1(p.attn_out + lane * p.attn_rep + (int64_t)hh * hd + cc, acc / l, ep);
@@ -1058,7 +1023,7 @@ int mk_configure(MkParams& p, int kmax, size_t* smem_bytes, int* grid) {
   XPU_REQUIRE(coop, XPU_EINVAL, "persistent decode: the device has no cooperative launch");
   const int G = di.sm_count;
   XPU_REQUIRE(p.head_dim <= 128, XPU_EINVAL, "persistent decode: head_dim %d > 128", p.head_dim);
-  int64_t red_stride = 0, piece_max = 0;
+  int64_t red_stride = 0, piece_max = 0, ne_max = 0;
   int max_wpg = 1;
   int64_t max_u = 0;
   for (int i = 0; i < MK_KINDS; ++i) {
@@ -1085,23 +1050,26 @@ int mk_configure(MkParams& p, int kmax, size_t* smem_bytes, int* grid) {
     XPU_REQUIRE(g.piece_rows >= 1, XPU_EINVAL, "persistent decode: a row of K=%d does not fit a piece", g.K);
     piece_max = std::max<int64_t>(piece_max, (int64_t)g.ns * g.piece_rows * row_bytes);
     red_stride = std::max<int64_t>(red_stride, g.ns * share_max);
+    ne_max = std::max<int64_t>(ne_max, (g.epi == EPI_FFN || g.epi == EPI_RESID ? 2 : 1) * share_max);
     max_wpg = std::max(max_wpg, wpg);
-    max_u = std::max<int64_t>(max_u, g.U);
+    if (g.rg > 1) max_u = std::max<int64_t>(max_u, g.U);
     XPU_REQUIRE((int64_t)g.N % gr == 0, XPU_EINVAL, "persistent decode: QKV rows must pair");
   }
   // Attention: one item per CTA (kv head, split) where the heads allow.
   const int Gq = p.H / p.kvH;
   p.nsplit = std::max(1, G / p.kvH);
   p.cmax = (p.max_seq + p.nsplit - 1) / p.nsplit;
-  const int64_t red_floats = std::max<int64_t>({(int64_t)kMkRedMinFloats, red_stride * max_wpg,
-                                                (int64_t)Gq * p.nsplit});
-  const int64_t xs_floats = std::max<int64_t>({16 * (int64_t)mk_xs_pitch((int)max_u), (int64_t)kmax,
+  const int64_t red_floats = std::max<int64_t>({(int64_t)32, red_stride * max_wpg});
+  const int64_t xs_floats = std::max<int64_t>({16 * (int64_t)mk_xs_pitch((int)std::max<int64_t>(max_u, 1)),
                                                (int64_t)Gq * p.head_dim + (int64_t)Gq * p.cmax + 2 * Gq});
   auto up = [](size_t a) { return (a + 127) / 128 * 128; };
   p.red_stride = (int)red_stride;
   p.off_red = 0;
   p.off_xs = (uint32_t)up(p.off_red + 4 * (size_t)red_floats);
-  p.off_ring = (uint32_t)up(p.off_xs + 4 * (size_t)xs_floats);
+  p.off_xpow = (uint32_t)up(p.off_xs + 4 * (size_t)xs_floats);
+  p.epi_floats = (int)((ne_max + 31) / 32 * 32);
+  p.off_epi = (uint32_t)up(p.off_xpow + 4 * (size_t)max_u);
+  p.off_ring = (uint32_t)up(p.off_epi + 4 * (size_t)(2 * p.epi_floats));
   cudaFuncAttributes fa{};
   XPU_TRY_CUDA(cudaFuncGetAttributes(&fa, decode_mk_kernel));
   const size_t static_smem = fa.sharedSizeBytes;

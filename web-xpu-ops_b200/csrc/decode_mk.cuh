@@ -98,12 +98,14 @@ struct MkParams {
   // (all warps), 3 epilogue done, 4 its first weight stage ready, 5 the
   // total ns it waited for weight stages in the phase, 6 its own input words
   // arrived (GEMV phases); the producer at 7 when it issued the phase's last
-  // weight piece.  The buffer is zeroed
+  // weight piece.  Attention phases: 4 scores done, 5 softmax done, 6 thread
+  // 0's P.V outputs stored, 7 thread 0's first merge inputs arrived.  The buffer is zeroed
   // before a profiled step; events that did not happen stay 0.
   unsigned long long* trace;
   // shared-memory geometry
   uint32_t ring_bytes;
-  uint32_t off_red, off_xs, off_ring;
+  uint32_t off_red, off_xs, off_xpow, off_epi, off_ring;
+  int epi_floats;  // one of the two epilogue-operand buffers
   int red_stride;  // floats per warp slot of the partial-sum area
 };
 
