@@ -484,6 +484,18 @@ XPU_API int xpu_llama_poison_kv(xpu_llama* engine, float value);
 #define XPU_DECODE_PERSISTENT  1
 XPU_API int xpu_llama_set_decode_path(xpu_llama* engine, int32_t path);
 XPU_API int xpu_llama_decode_path(const xpu_llama* engine, int32_t* path);
+/* No counterpart in the reference (failure handling of the persistent decode
+ * step).  Every wait inside the step -- for a weight stage, for another
+ * CTA's output words -- gives up after this many seconds (default 2; range
+ * [0.001, 60]); the step then finishes without waiting and the call reports
+ * XPU_ETIMEOUT, after which the engine is usable again. */
+XPU_API int xpu_llama_set_wait_limit(xpu_llama* engine, double seconds);
+/* Test switch, no counterpart in the reference: from the next persistent
+ * step on, one CTA (the last one, which always has rows; in an attention
+ * phase the last item's) stores none of its output words in layer phase `phase`
+ * (5 l + {0 QKV, 1 attention, 2 O, 3 FFN, 4 down}), so the phase's
+ * consumers wait until the limit above runs out.  -1 turns it off. */
+XPU_API int xpu_llama_test_skip_phase_output(xpu_llama* engine, int32_t phase);
 XPU_API int xpu_llama_destroy(xpu_llama* engine);
 
 #ifdef __cplusplus

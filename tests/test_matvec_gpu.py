@@ -345,6 +345,27 @@ def test_quantize_reference_cases(N, D):
     np.testing.assert_array_equal(got["scales"], want_s)
 
 
+@pytest.mark.parametrize("N,K", [(3, 4), (5, 512), (9, 4096), (4, 4100), (3, 8192), (2, 16384), (2, 16388)])
+def test_quantize_single_pass_widths_bit_exact(N, K):
+    """Rows of whole float4s take the single-pass kernel (128-512 threads, 1-8
+    chunks per thread); 16388 is past its widest form and takes the general
+    kernel.  Exact ties (x * 127 / absmax = k + 0.5) are planted in every row:
+    codes, packed words and scales equal the oracle's bit for bit."""
+    x = fill_normal(N * K, 300 + K, 0.0, 0.02).reshape(N, K)
+    for r in range(N if K >= 10 else 0):
+        x[r, 0] = 127.0  # absmax 127: inverse 1, codes = Math.round(x)
+        x[r, 1:9] = np.arange(8) + 0.5  # ties round toward +inf
+        x[r, 9] = -62.5
+    x = x.astype(np.float32).ravel()
+    want_c, want_s = orc.quantize(x, N, K)
+    got = xpuops.quantize(x, N, K)
+    np.testing.assert_array_equal(got["output"], want_c)
+    np.testing.assert_array_equal(got["scales"], want_s)
+    packed = xpuops.quantizePackQ8(x, N, K)
+    np.testing.assert_array_equal(packed["weight"], orc.pack_q8(want_c, N, K))
+    np.testing.assert_array_equal(packed["scale"], want_s)
+
+
 def test_quantize_zero_nan_inf_rows():
     x = np.zeros((4, 16), np.float32)
     x[1, 3] = np.nan

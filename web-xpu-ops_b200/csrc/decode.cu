@@ -530,6 +530,8 @@ int setup_persistent(xpu_llama* e) {
   p.gen = e->d_gen;
   p.logits = e->logits;
   p.err = device_error_word();
+  p.wait_limit_ns = kWaitLimitNs;
+  p.skip_phase = -1;
   const int kmax = (int)std::max<int64_t>({h, qd, (int64_t)c.ffn_hidden});
   int rc = mk_configure(p, kmax, &e->mk_smem, &e->mk_grid);
   if (rc == XPU_EINVAL) {  // shapes outside the persistent step: keep the graph
@@ -1119,6 +1121,23 @@ int xpu_llama_set_decode_path(xpu_llama* e, int32_t path) {
   XPU_TRY_CUDA(cudaSetDevice(e->device));
   XPU_TRY_CUDA(cudaStreamSynchronize(e->stream));
   e->path = path;
+  return XPU_OK;
+}
+
+int xpu_llama_set_wait_limit(xpu_llama* e, double seconds) {
+  XPU_REQUIRE(e, XPU_EINVAL, "xpu_llama_set_wait_limit: null engine");
+  XPU_REQUIRE(seconds >= 1e-3 && seconds <= 60.0, XPU_EINVAL,
+              "xpu_llama_set_wait_limit: %g s is outside [0.001, 60]", seconds);
+  e->mk.wait_limit_ns = (uint64_t)(seconds * 1e9);
+  return XPU_OK;
+}
+
+int xpu_llama_test_skip_phase_output(xpu_llama* e, int32_t phase) {
+  XPU_REQUIRE(e, XPU_EINVAL, "xpu_llama_test_skip_phase_output: null engine");
+  XPU_REQUIRE(phase >= -1 && phase < 5 * e->c.num_layers, XPU_EINVAL,
+              "xpu_llama_test_skip_phase_output: phase %d is not -1 or a layer phase in [0, %d)", phase,
+              5 * e->c.num_layers);
+  e->mk.skip_phase = phase;
   return XPU_OK;
 }
 

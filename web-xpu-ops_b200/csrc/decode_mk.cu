@@ -101,9 +101,10 @@ __device__ __forceinline__ void mk_mark(const MkParams& p, int phase, int e) {
 }
 
 // Waits on an mbarrier unless the step was aborted; a timeout aborts it.
-__device__ __forceinline__ void mk_wait(uint64_t* bar, uint32_t parity, unsigned int* err, volatile int* abort_flag) {
+__device__ __forceinline__ void mk_wait(uint64_t* bar, uint32_t parity, unsigned int* err, volatile int* abort_flag,
+                                        uint64_t limit_ns) {
   if (*abort_flag) return;
-  if (!mbar_wait(bar, parity, err)) *abort_flag = 1;
+  if (!mbar_wait(bar, parity, err, limit_ns)) *abort_flag = 1;
 }
 
 // ------------------------------------------------------------- producer --
@@ -113,12 +114,12 @@ __device__ __forceinline__ void mk_wait(uint64_t* bar, uint32_t parity, unsigned
 // would pass the end starts again at offset 0) and released by consumers in
 // any order; the producer reclaims space oldest-first.
 __device__ __forceinline__ void mk_wait_sleepy(uint64_t* bar, uint32_t parity, unsigned int* err,
-                                               volatile int* abort_flag) {
+                                               volatile int* abort_flag, uint64_t limit_ns) {
   if (*abort_flag || mbar_try_wait(bar, parity)) return;
   const uint64_t t0 = global_timer_ns();
   while (!mbar_try_wait(bar, parity)) {
     __nanosleep(128);  // the producer waits off the consumers' issue slots
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       atomicOr(err, 1u);
       *abort_flag = 1;
       return;
@@ -231,7 +232,7 @@ __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, ui
         blocked = so < off + B && off < so + sl;
       }
       if (!blocked || *abort_flag) break;
-      mk_wait_sleepy(&empty[oldest % kMkSlots], (uint32_t)((oldest / kMkSlots) & 1), p.err, abort_flag);
+      mk_wait_sleepy(&empty[oldest % kMkSlots], (uint32_t)((oldest / kMkSlots) & 1), p.err, abort_flag, p.wait_limit_ns);
       ++oldest;
     }
     if (*abort_flag) return -1;
@@ -284,7 +285,7 @@ __device__ __forceinline__ void mk_producer(const MkParams& p, uint8_t* smem, ui
   }
   // Every issued copy lands before the CTA exits.
   for (int64_t k = (issued > kMkSlots ? issued - kMkSlots : 0); k < issued; ++k)
-    mbar_wait(&full[k % kMkSlots], (uint32_t)((k / kMkSlots) & 1), p.err);
+    mbar_wait(&full[k % kMkSlots], (uint32_t)((k / kMkSlots) & 1), p.err, p.wait_limit_ns);
 }
 
 // ------------------------------------------------------- tagged vectors --
@@ -320,14 +321,14 @@ __device__ __forceinline__ bool tag_is(unsigned long long w, uint32_t ep) { retu
 __device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
 
 // Bounded wait bookkeeping of a poll loop: false once the step was aborted
-// or the wait passed kWaitLimitNs (which aborts the step).
+// or the wait passed the step's limit (which aborts the step).
 struct MkPollClock {
   uint64_t t0 = 0;
   __device__ __forceinline__ bool keep_going(const MkParams& p, volatile int* abort_flag) {
     if (*abort_flag) return false;
     const uint64_t now = global_timer_ns();
     if (t0 == 0) t0 = now;
-    if (now - t0 > kWaitLimitNs) {
+    if (now - t0 > p.wait_limit_ns) {
       atomicOr(p.err, 1u);
       *abort_flag = 1;
       return false;
@@ -464,7 +465,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
     const int64_t gidx = pbase++;
     gslot = (int)(gidx % kMkSlots);
     if (warp < wpg) {
-      mk_wait(&full[gslot], (uint32_t)((gidx / kMkSlots) & 1), p.err, abort_flag);
+      mk_wait(&full[gslot], (uint32_t)((gidx / kMkSlots) & 1), p.err, abort_flag, p.wait_limit_ns);
       gs = reinterpret_cast<const float*>(smem + p.off_ring + slot_off[gslot]);
     }
   }
@@ -566,12 +567,12 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
       const uint32_t par = (uint32_t)((gidx / kMkSlots) & 1);
       if (p.trace && tid == 0) {
         const unsigned long long w0 = global_timer_ns();
-        mk_wait(&full[slot], par, p.err, abort_flag);
+        mk_wait(&full[slot], par, p.err, abort_flag, p.wait_limit_ns);
         const unsigned long long w1 = global_timer_ns();
         if (q == 0) first_ready = w1;
         waited += w1 - w0;
       } else {
-        mk_wait(&full[slot], par, p.err, abort_flag);
+        mk_wait(&full[slot], par, p.err, abort_flag, p.wait_limit_ns);
       }
       const int rows = n - q * P < P ? n - q * P : P;
       const int R = ns * rows;
@@ -638,6 +639,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   // Row value: sum * scale, rounded to f32 once (with the rmsnorm factor in
   // f64 where the phase normalises its input).
   auto rowval = [&](float s, float sc) { return norm ? (float)((double)s * rs * (double)sc) : __fmul_rn(s, sc); };
+  const int reps = phase == p.skip_phase && b == G - 1 ? 0 : kMkReps;  // the test switch: the last CTA stores nothing
   if (epi == EPI_QKV) {
     const int64_t qk_end = (int64_t)p.q_rows + p.kv_rows;
     for (int t = tid; t < outs; t += kNct) {
@@ -656,7 +658,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
         c = (float)(x0 * sn + x1 * cs);
       }
       if (row < p.q_rows) {
-        for (int r = 0; r < kMkReps; ++r) st_tag2(g->yt + r * g->yt_rep + row, a, c, ep);
+        for (int r = 0; r < reps; ++r) st_tag2(g->yt + r * g->yt_rep + row, a, c, ep);
       } else {
         // KV cache slot `pos` (llm/engine-q8-resident.ts:1848-1851), and the
         // same row as words for this step's attention.
@@ -666,7 +668,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
         float* dst = (is_k ? v.kcache : v.vcache) + ((h * p.max_seq + pos) * p.head_dim + d);
         dst[0] = a;
         dst[1] = c;
-        st_tag2((is_k ? p.knew : p.vnew) + local, a, c, ep);
+        if (reps) st_tag2((is_k ? p.knew : p.vnew) + local, a, c, ep);
       }
     }
   } else if (epi == EPI_FFN) {
@@ -676,14 +678,14 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
       const float gt_ = rowval(sum(t), sg);
       const float up = rowval(sum(n + t), su);
       const float y = __fmul_rn(silu_f32(gt_), up);
-      for (int r = 0; r < kMkReps; ++r) st_tag1(g->yt + r * g->yt_rep + row, y, ep);
+      for (int r = 0; r < reps; ++r) st_tag1(g->yt + r * g->yt_rep + row, y, ep);
     }
   } else if (epi == EPI_RESID) {
     for (int t = tid; t < outs; t += kNct) {
       const int64_t row = r0 + t;
       const float sc = eo[t], res = eo[n + t];
       const float y = __fadd_rn(res, rowval(sum(t), sc));
-      for (int r = 0; r < kMkReps; ++r) st_tag1(g->yt + r * g->yt_rep + row, y, ep);
+      for (int r = 0; r < reps; ++r) st_tag1(g->yt + r * g->yt_rep + row, y, ep);
     }
   } else {
     constexpr int kNone = 0x7fffffff;
@@ -746,7 +748,7 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, uint
     if (nn > 0) {
       const int64_t gidx = pbase++;
       slot = (int)(gidx % kMkSlots);
-      mk_wait(&full[slot], (uint32_t)((gidx / kMkSlots) & 1), p.err, abort_flag);
+      mk_wait(&full[slot], (uint32_t)((gidx / kMkSlots) & 1), p.err, abort_flag, p.wait_limit_ns);
       float* kv = reinterpret_cast<float*>(smem + p.off_ring + slot_off[slot]);
       k_s = kv;
       v_s = kv + nn * hd;
@@ -881,7 +883,7 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, uint
       if (o == o0) mk_mark(p, phase, 7);  // thread 0's merge inputs arrived
       l = warp_sum(l);
       acc = warp_sum(acc);
-      if (lane < kMkReps) st_tag1(p.attn_out + lane * p.attn_rep + (int64_t)hh * hd + cc, acc / l, ep);
+      if (lane < kMkReps && !(phase == p.skip_phase && it == items - 1)) st_tag1(p.attn_out + lane * p.attn_rep + (int64_t)hh * hd + cc, acc / l, ep);
     }
   }
   mk_mark(p, phase, 3);

@@ -92,6 +92,11 @@ struct MkParams {
   float* cand_v;  // [grid] per-CTA argmax candidates
   int* cand_i;
   unsigned int* err;
+  uint64_t wait_limit_ns;  // bound of every wait in the step (kWaitLimitNs by default)
+  // Test switch (xpu_llama_test_skip_phase_output): in this phase the last
+  // CTA (a GEMV phase) or the last attention item's CTA stores none of its
+  // output words, so its consumers' waits run out; -1 = off.
+  int skip_phase;
   // Optional profile: when non-null, CTA b writes %globaltimer at
   // trace[(phase * grid + b) * kMkTraceEvents + e]: thread 0 at e = 0 phase
   // start, 1 input staged (its producers' words arrived), 2 dot products done

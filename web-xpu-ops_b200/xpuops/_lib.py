@@ -167,6 +167,8 @@ SIGNATURES = {
     "xpu_llama_poison_kv": [P, C.c_float],
     "xpu_llama_set_decode_path": [P, I32],
     "xpu_llama_decode_path": [P, C.POINTER(I32)],
+    "xpu_llama_set_wait_limit": [P, C.c_double],
+    "xpu_llama_test_skip_phase_output": [P, I32],
     "xpu_llama_destroy": [P],
 }
 _RESTYPE = {"xpu_last_error": C.c_char_p}

@@ -310,6 +310,17 @@ class LlamaEngineQ8Resident:
         step does not apply to this engine's shapes."""
         check(lib().xpu_llama_set_decode_path(self._handle(), int(path)))
 
+    def setWaitLimit(self, seconds: float) -> None:
+        """Bound of every wait inside the persistent decode step (default 2 s);
+        a step whose wait runs out raises XpuError (XPU_ETIMEOUT) and leaves
+        the engine usable.  No reference counterpart."""
+        check(lib().xpu_llama_set_wait_limit(self._handle(), float(seconds)))
+
+    def _testSkipPhaseOutput(self, phase: int) -> None:
+        """Test switch: one CTA stores none of its output words in layer phase
+        `phase` of later persistent steps (-1 turns it off)."""
+        check(lib().xpu_llama_test_skip_phase_output(self._handle(), int(phase)))
+
     def stream(self) -> int:
         s = C.c_void_p()
         check(lib().xpu_llama_stream(self._handle(), C.byref(s)))
