@@ -200,13 +200,11 @@ def test_special_vectors_and_scales(tc):
 
 
 @pytest.mark.parametrize("N,K", [(16384, 6144), (20000, 8000)])
-def test_single_gemvs_with_dynamic_chunks(tc, N, K):
-    """Single GEMVs with at least 32 slices per CTA, 128 row tiles or more
-    and rows of at most 64 slices leave their last eighth of row tiles to
-    two-stage chunks that CTAs claim at run time and sum at the end: six
-    chunks per tile (K = 6144), and a partial last tile, a last chunk of
-    seven slices (two stages, the second of three) and a part slice
-    (N = 20000, K = 8000).  The oracle's results, bit-identical on repeats."""
+def test_single_large_gemvs(tc, N, K):
+    """Single GEMVs of 128+ row tiles split stream-K over every SM: 48 slices
+    per row (K = 6144), and a partial last tile with a last stage of three
+    slices and a part slice (N = 20000, K = 8000).  The oracle's results,
+    bit-identical on repeats."""
     w, s = _synth(N, K, 900 + K)
     x = fill_normal(K, 901 + K)
     dw, ds, dx = ops.DeviceBuffer.from_numpy(w), ops.DeviceBuffer.from_numpy(s), ops.DeviceBuffer.from_numpy(x)

@@ -33,15 +33,8 @@
 // [lo, hi) of one 128-row tile).  A tile split between CTAs combines the
 // exact int32 partial accumulators of its contributors: each writes its
 // partial to global memory and takes a ticket; the last arrival sums them
-// (in CTA order) and writes the outputs.  A single large GEMV with short
-// rows (at most 64 slices) keeps its last tiles out of the static split:
-// CTAs that finish their static range claim two-stage chunks of those tiles
-// (consecutive claims in different tiles) from an atomic counter, so SMs
-// that stream slower than others do less of the tail.  A chunk stores its int32 partial in its own slot; at its end a
-// CTA counts the slices of its chunks behind one fence, and the count that
-// completes a tile makes that CTA its finisher, summing the tile's slots
-// (integer sums: the result does not depend on the order).  Every wait is
-// bounded.
+// (in CTA order) and writes the outputs (integer sums: the result does not
+// depend on the order of arrival).  Every wait is bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <limits.h>
@@ -73,9 +66,6 @@ constexpr int kTcFlagNonFinite = 1;
 constexpr int kTcFlagInexact = 2;
 constexpr uint64_t kDigitBias = 0x8080808080808080ull;
 constexpr int64_t kTcMinUnits = 8;       // slices per CTA at least (small GEMVs)
-constexpr int kTcChunk = 2 * kTcG;         // slices per dynamic chunk (two stages)
-constexpr int kTcDynList = 64;             // chunk tiles a CTA remembers until its end
-constexpr int kDynFirst = 16, kDynLast = 32, kDynEnd = 64;  // DynDesc.info flags (bits 0-3: slices)
 
 struct TcArgs {
   const uint32_t* w;
@@ -86,14 +76,7 @@ struct TcArgs {
   unsigned int* ticket;  // [grid], zeroed by mv_xstat_kernel
   const float4* stats;   // [nstats] per-block (max |x|, min nonzero |x|, non-finite, -)
   int64_t ldw, mat_stride, s_stride, y_stride;
-  int64_t total;  // static units: t_dyn0 * S
-  int64_t t_dyn0;    // first tile of the dynamic chunks
-  int64_t n_dyn;     // dynamic tiles
-  int64_t n_chunks;  // dynamic chunks: n_dyn * cpt (0: none)
-  int cpt;           // chunks per tile; chunk c is part c / n_dyn of tile t_dyn0 + c % n_dyn
-  unsigned int* claim;   // next chunk to hand out
-  int4* cpart;           // [n_chunks][128 rows][4 x int4]: chunk partials
-  unsigned int* tcount;  // [n_dyn]: slices counted per dynamic tile
+  int64_t total;  // units: tiles * S
   int N, K, tiles_per_mat, S, nstats;
   uint32_t idesc;
   unsigned int* err;
@@ -239,13 +222,8 @@ __device__ __forceinline__ void write_limb_columns(uint8_t* tile, const float* _
 constexpr int kStatThreads = 256;
 __global__ void __launch_bounds__(kStatThreads) mv_xstat_kernel(const float* __restrict__ x, int K,
                                                                 float4* __restrict__ stats,
-                                                                unsigned int* __restrict__ ticket, int nticket,
-                                                                unsigned int* __restrict__ dyn, int64_t ndyn) {
+                                                                unsigned int* __restrict__ ticket, int nticket) {
   griddep_wait();
-  // The dynamic-chunk words (slice counts, the claim counter), zeroed by
-  // every block's share.
-  for (int64_t i = (int64_t)blockIdx.x * kStatThreads + threadIdx.x; i < ndyn; i += (int64_t)gridDim.x * kStatThreads)
-    dyn[i] = 0u;
   griddep_launch_dependents();
   __shared__ float smx[kStatThreads / 32], smn[kStatThreads / 32];
   __shared__ int sbad[kStatThreads / 32];
@@ -282,14 +260,6 @@ __global__ void __launch_bounds__(kStatThreads) mv_xstat_kernel(const float* __r
     for (int i = threadIdx.x; i < nticket; i += kStatThreads) ticket[i] = 0u;
 }
 
-// A dynamic stage as the producer publishes it to the MMA and limb warps.
-struct DynDesc {
-  long long tile;
-  int lo;     // first slice of the stage
-  int info;   // slices in the stage | kDynFirst | kDynLast | kDynEnd
-  int chunk;  // the chunk's index (its partial's slot)
-};
-
 // ---------------------------------------------------------------- kernel --
 __global__ void __launch_bounds__(kTcThreads, 1)
     mv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ TcArgs g) {
@@ -306,12 +276,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ float red_max[4], red_min[4];
   __shared__ int red_bad[4];
   __shared__ volatile int s_flag;  // warps 2-5: one thread's result for all
-  __shared__ __align__(8) uint64_t dready[kTcStages];  // dynamic stage published
-  __shared__ DynDesc ddesc[kTcStages];
-  __shared__ long long dyn_tiles[kTcDynList];            // chunk tiles this CTA stored partials of
-  __shared__ int dyn_units[kTcDynList];                  // ... and their slices
-  __shared__ unsigned int dyn_done[kTcDynList / 32];     // tiles this CTA's count completed
-  __shared__ int n_dyn_tiles;
   // The next launch of the stream may become resident now; every dependent
   // the library launches waits for this grid before reading its outputs.
   griddep_launch_dependents();
@@ -327,8 +291,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4);
     }
-    for (int s = 0; s < kTcStages; ++s) mbar_init(&dready[s], 1);
-    n_dyn_tiles = 0;
     mbar_init(&done, 1);
     abort_flag = 0;
     fence_mbar_init();
@@ -367,53 +329,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int q = 0; q < n; ++q) tma_load_3d(st + q * kTcSliceA, &tmA, (c + q) * kTcBK, rt * kTcBM, mi, &full[s]);
         }
         if (!ok) break;
-      }
-      // Dynamic chunks: claimed one at a time (the next claim is taken while
-      // a chunk's last stage streams), each stage published in ddesc before
-      // its copies are issued; an END stage closes the sequence.  The claim
-      // counter was zeroed by the stats kernel, visible after the wait.
-      if (g.n_chunks > 0 && !abort_flag) {
-        griddep_wait();
-        long long c = (long long)atomicAdd(g.claim, 1u);
-        long long tile = 0;
-        int cc = 0, hi = 0, lo = 0;
-        bool have = false;
-        for (;;) {
-          const int s = (int)(it % kTcStages);
-          if (it >= kTcStages && !mbar_wait(&empty[s], (uint32_t)(((it / kTcStages) + 1) & 1), g.err)) {
-            abort_flag = 1;
-            break;
-          }
-          if (!have) {
-            if (c >= g.n_chunks) {
-              ddesc[s].info = kDynEnd;
-              mbar_arrive(&dready[s]);
-              break;
-            }
-            tile = g.t_dyn0 + c % g.n_dyn;
-            lo = (int)(c / g.n_dyn) * kTcChunk;
-            hi = min(g.S, lo + kTcChunk);
-            cc = lo;
-            have = true;
-          }
-          const int n = min(kTcG, hi - cc);
-          const bool last = cc + kTcG >= hi;
-          ddesc[s].tile = tile;
-          ddesc[s].lo = cc;
-          ddesc[s].chunk = (int)c;
-          ddesc[s].info = n | (cc == lo ? kDynFirst : 0) | (last ? kDynLast : 0);
-          mbar_arrive(&dready[s]);
-          const int mi = (int)(tile / g.tiles_per_mat), rt = (int)(tile % g.tiles_per_mat);
-          uint8_t* st = smem + (size_t)s * kTcStageBytes;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)n * kTcSliceA);
-          for (int q = 0; q < n; ++q) tma_load_3d(st + q * kTcSliceA, &tmA, (cc + q) * kTcBK, rt * kTcBM, mi, &full[s]);
-          ++it;
-          cc += kTcG;
-          if (last) {
-            c = (long long)atomicAdd(g.claim, 1u);
-            have = false;
-          }
-        }
       }
       // Land every copy still in flight before the CTA may exit.
       for (int64_t i = (it > kTcStages ? it - kTcStages : 0); i < it; ++i)
@@ -456,50 +371,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         if (!ok) break;
         tc_commit(&tfull[b]);
-      }
-      // Dynamic chunks, stage by stage as published; segment j continues
-      // the accumulator alternation of the static segments.
-      if (g.n_chunks > 0 && !abort_flag) {
-        int64_t j = cur.nseg;
-        uint32_t dpar = 0;  // bit s: parity of the next wait on dready[s]
-        for (;;) {
-          const int s = (int)(it % kTcStages);
-          if (!mbar_wait(&dready[s], (dpar >> s) & 1u, g.err)) {
-            abort_flag = 1;
-            break;
-          }
-          dpar ^= 1u << s;
-          const int info = *(volatile int*)&ddesc[s].info;
-          if (info & kDynEnd) break;
-          const int n = info & 15, b = (int)(j & 1);
-          if (info & kDynFirst) {
-            if (j >= 2 && !mbar_wait(&tempty[b], (uint32_t)(((j / 2) + 1) & 1), g.err)) {
-              abort_flag = 1;
-              break;
-            }
-            tc_fence_after();
-          }
-          const uint32_t par = (uint32_t)((it / kTcStages) & 1);
-          if (!mbar_wait(&full[s], par, g.err) || !mbar_wait(&bready[s], par, g.err)) {
-            abort_flag = 1;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t acc = tmem + 16u * (uint32_t)b;
-          const uint32_t sa = smem_addr(smem + (size_t)s * kTcStageBytes), sb = sa + kTcStageA;
-          for (int q = 0; q < n; ++q) {
-#pragma unroll
-            for (int k4 = 0; k4 < kTcBK / 32; ++k4)
-              tc_mma_i8(acc, sw128_desc(sa + q * kTcSliceA + 32 * k4), sw128_desc(sb + q * kTcSliceB + 32 * k4),
-                        g.idesc, ((info & kDynFirst) && q == 0 && k4 == 0) ? 0u : 1u);
-          }
-          tc_commit(&empty[s]);
-          ++it;
-          if (info & kDynLast) {
-            tc_commit(&tfull[b]);
-            ++j;
-          }
-        }
       }
       tc_commit(&done);
     }
@@ -654,60 +525,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       return true;
     };
 
-    // Finishes dynamic tile `tile`, whose slices this CTA's count completed:
-    // the sum of its chunks' partials, four chunks per round of loads.
-    auto finish_dyn_tile = [&](long long tile) {
-      const int row = q * 32 + lane;
-      int sum[16] = {};
-      for (int p0 = 0; p0 < g.cpt; p0 += 4) {
-        int4 v[4][4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int64_t c = (int64_t)(p0 + u) * g.n_dyn + (tile - g.t_dyn0);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            v[u][i] = p0 + u < g.cpt ? __ldcg(g.cpart + (c * kTcBM + row) * 4 + i) : make_int4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            sum[4 * i] += v[u][i].x;
-            sum[4 * i + 1] += v[u][i].y;
-            sum[4 * i + 2] += v[u][i].z;
-            sum[4 * i + 3] += v[u][i].w;
-          }
-      }
-      finish_row(tile, row, sum, row_scale(tile, row));
-    };
-    // Counts the slices of every remembered dynamic tile behind one fence
-    // (the barrier orders all writers' partial stores before thread 0's
-    // fence); the count that completes a tile makes this CTA its one
-    // finisher (fenced again before its loads).  Then forgets them.
-    auto flush_dyn = [&]() {
-      named_bar_sync(kTcBarWriters, kTcWriters);
-      const int nt = n_dyn_tiles;
-      if (tid == 0) {
-        __threadfence();
-        unsigned int done = 0;
-        for (int i = 0; i < nt; ++i) {
-          const unsigned int u = (unsigned int)dyn_units[i];
-          if (atomicAdd(g.tcount + (dyn_tiles[i] - g.t_dyn0), u) + u == (unsigned int)g.S) done |= 1u << (i & 31);
-          if ((i & 31) == 31 || i == nt - 1) {
-            if (done) __threadfence();
-            dyn_done[i >> 5] = done;
-            done = 0;
-          }
-        }
-      }
-      named_bar_sync(kTcBarWriters, kTcWriters);
-      for (int i = 0; i < nt; ++i)
-        if ((dyn_done[i >> 5] >> (i & 31)) & 1u) finish_dyn_tile(dyn_tiles[i]);
-      named_bar_sync(kTcBarWriters, kTcWriters);
-      if (tid == 0) n_dyn_tiles = 0;
-      named_bar_sync(kTcBarWriters, kTcWriters);
-    };
-
     int64_t it = 0, ep = 0, ep_last = -1;  // next segment to finish, its last stage
     bool ok = true;
     if (cur.nseg > 0) ep_last = seg_stages(cur.get(0)) - 1;
@@ -740,125 +557,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!ok) break;
       }
     }
-    // A dynamic chunk's epilogue: its int32 partial into the chunk's slot;
-    // its tile and slices remembered for the count at the CTA's end.
-    auto finish_dyn = [&](long long tile, int64_t j, int units, int chunk) -> bool {
-      const int b = (int)(j & 1);
-      if (tid == 0) s_flag = !abort_flag && mbar_wait(&tfull[b], (uint32_t)((j / 2) & 1), g.err);
-      named_bar_sync(kTcBarWriters, kTcWriters);
-      const bool ready = s_flag;
-      named_bar_sync(kTcBarWriters, kTcWriters);
-      if (!ready) return false;
-      tc_fence_after();
-      int D[16];
-      tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + 16u * (uint32_t)b, D);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
-      int4* slot = g.cpart + ((int64_t)chunk * kTcBM + q * 32 + lane) * 4;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) __stcg(slot + i, make_int4(D[4 * i], D[4 * i + 1], D[4 * i + 2], D[4 * i + 3]));
-      if (tid == 0) {
-        int nt = n_dyn_tiles, k = 0;
-        while (k < nt && dyn_tiles[k] != tile) ++k;
-        if (k == nt && nt < kTcDynList) {
-          dyn_tiles[k] = tile;
-          dyn_units[k] = 0;
-          n_dyn_tiles = ++nt;
-        }
-        if (k < nt) dyn_units[k] += units;
-        s_flag = k == kTcDynList;  // list full: count what it holds now, then this chunk
-      }
-      named_bar_sync(kTcBarWriters, kTcWriters);
-      const bool full_list = s_flag;
-      named_bar_sync(kTcBarWriters, kTcWriters);
-      if (full_list) {
-        flush_dyn();
-        if (tid == 0) {
-          dyn_tiles[0] = tile;
-          dyn_units[0] = units;
-          n_dyn_tiles = 1;
-        }
-      }
-      return true;
-    };
-
-    if (ok && g.n_chunks > 0) {
-      // Dynamic stages as the producer publishes them, until END; static
-      // segments left to finish go first (they own the earlier accumulators).
-      uint32_t dpar = 0;
-      long long ptile[4];
-      int64_t pj[4], plast[4];
-      int punits[4], pchunk[4];
-      int np = 0, chunk_lo = 0;
-      int64_t jd = cur.nseg;
-      for (;;) {
-        const int s = (int)(it % kTcStages);
-        if (tid == 0) s_flag = !abort_flag && mbar_wait(&dready[s], (dpar >> s) & 1u, g.err);
-        named_bar_sync(kTcBarWriters, kTcWriters);
-        const bool got = s_flag;
-        named_bar_sync(kTcBarWriters, kTcWriters);
-        dpar ^= 1u << s;
-        if (!got) {
-          ok = false;
-          break;
-        }
-        const int info = *(volatile int*)&ddesc[s].info;
-        if (info & kDynEnd) break;
-        const long long tile = *(volatile long long*)&ddesc[s].tile;
-        const int lo = *(volatile int*)&ddesc[s].lo;
-        const int n = info & 15;
-        if (info & kDynFirst) chunk_lo = lo;
-        if (wl < n) {
-          uint8_t* tl = smem + (size_t)s * kTcStageBytes + kTcStageA + wl * kTcSliceB;
-          write_limb_columns(tl, g.x, (int64_t)(lo + wl) * kTcBK + 4 * lane, g.K, sc1, lane);
-          fence_proxy_async_smem();
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bready[s]);
-        if ((info & kDynLast) && np == 4) {  // cannot happen: at most 3 chunks are pending
-          ok = false;
-          break;
-        }
-        if (info & kDynLast) {
-          ptile[np] = tile;
-          pj[np] = jd;
-          plast[np] = it;
-          punits[np] = lo + n - chunk_lo;
-          pchunk[np] = *(volatile int*)&ddesc[s].chunk;
-          ++np;
-          ++jd;
-        }
-        while (ok && ep < cur.nseg && ep_last + (kTcStages - 1) <= it) {
-          ok = finish_segment(ep);
-          ++ep;
-          if (ep < cur.nseg) ep_last += seg_stages(cur.get(ep));
-        }
-        while (ok && ep >= cur.nseg && np > 0 && plast[0] + (kTcStages - 1) <= it) {
-          ok = finish_dyn(ptile[0], pj[0], punits[0], pchunk[0]);
-          for (int i = 1; i < np; ++i) {
-            ptile[i - 1] = ptile[i];
-            pj[i - 1] = pj[i];
-            plast[i - 1] = plast[i];
-            punits[i - 1] = punits[i];
-            pchunk[i - 1] = pchunk[i];
-          }
-          --np;
-        }
-        ++it;
-        if (!ok) break;
-      }
-      while (ok && ep < cur.nseg) {
-        ok = finish_segment(ep);
-        ++ep;
-      }
-      for (int i = 0; ok && i < np; ++i) ok = finish_dyn(ptile[i], pj[i], punits[i], pchunk[i]);
-      if (ok) flush_dyn();
-    } else {
-      while (ok && ep < cur.nseg) {
-        ok = finish_segment(ep);
-        ++ep;
-      }
+    while (ok && ep < cur.nseg) {
+      ok = finish_segment(ep);
+      ++ep;
     }
     if (!ok) abort_flag = 1;
   }
@@ -974,32 +675,17 @@ int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const f
   // partial per contributor, so small GEMVs run on fewer, fuller CTAs.
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(total / kTcMinUnits, di.sm_count));
   const int nstats = (int)std::max<int64_t>(1, std::min<int64_t>(di.sm_count, K / kStatThreads));
-  // A single GEMV of at least 32 slices per CTA, 128 row tiles or more and
-  // rows of at most 64 slices leaves its last eighth of tiles to dynamic
-  // chunks.  Measured: 28672 x 8192 goes from 47.3 to 45.1 us; with K =
-  // 28672 (64 tiles of 224 slices) the chunks made the GEMV slower (49 to
-  // 73 us), so long rows keep the static split, as does the stack, whose
-  // many matrices balance themselves.
-  const int64_t n_tiles = count * tiles_per_mat;
-  const bool dynamic = count == 1 && total >= 32 * (int64_t)grid && n_tiles >= 128 && S <= 64;
-  const int64_t dyn_tiles = dynamic ? n_tiles / 8 : 0;
-  const int cpt = (S + kTcChunk - 1) / kTcChunk;
-  const int64_t ndyn = dyn_tiles + 1;  // slice counts and the claim counter (words, zeroed)
   CUtensorMap ta;
   int rc = weight_map(TcMapKey{w, W, N, count, mat_stride}, &ta);
   if (rc) return rc;
 
-  // Scratch: the split-tile and chunk partials (written before they are
-  // read), the tickets and dynamic-chunk words (zeroed by the stats kernel)
-  // and the vector stats.
+  // Scratch: the split-tile partials (written before they are read), the
+  // tickets (zeroed by the stats kernel) and the vector stats.
   const size_t part_bytes = (size_t)grid * 2 * kTcBM * kTcLimbs * sizeof(int);
   const size_t ticket_bytes = ((size_t)grid * sizeof(unsigned int) + 15) / 16 * 16;
-  const size_t word_bytes = ((size_t)ndyn * sizeof(unsigned int) + 15) / 16 * 16;
-  const size_t cpart_bytes = (size_t)dyn_tiles * cpt * kTcBM * kTcLimbs * sizeof(int);
   const size_t stat_bytes = (size_t)nstats * sizeof(float4);
   uint8_t* scratch = nullptr;
-  XPU_TRY_CUDA(
-      scratch_alloc((void**)&scratch, part_bytes + ticket_bytes + word_bytes + cpart_bytes + stat_bytes, st));
+  XPU_TRY_CUDA(scratch_alloc((void**)&scratch, part_bytes + ticket_bytes + stat_bytes, st));
   TcArgs g{};
   g.w = w;
   g.x = x;
@@ -1007,20 +693,12 @@ int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const f
   g.y = y;
   g.part = reinterpret_cast<int4*>(scratch);
   g.ticket = reinterpret_cast<unsigned int*>(scratch + part_bytes);
-  unsigned int* dyn = reinterpret_cast<unsigned int*>(scratch + part_bytes + ticket_bytes);
-  g.tcount = dyn;
-  g.claim = dyn + dyn_tiles;
-  g.cpart = reinterpret_cast<int4*>(scratch + part_bytes + ticket_bytes + word_bytes);
-  g.t_dyn0 = n_tiles - dyn_tiles;
-  g.n_dyn = dyn_tiles;
-  g.n_chunks = dyn_tiles * cpt;
-  g.cpt = cpt;
-  g.stats = reinterpret_cast<const float4*>(scratch + part_bytes + ticket_bytes + word_bytes + cpart_bytes);
+  g.stats = reinterpret_cast<const float4*>(scratch + part_bytes + ticket_bytes);
   g.ldw = W;
   g.mat_stride = mat_stride;
   g.s_stride = N;
   g.y_stride = N;
-  g.total = g.t_dyn0 * S;
+  g.total = total;
   g.N = (int)N;
   g.K = (int)K;
   g.tiles_per_mat = tiles_per_mat;
@@ -1030,7 +708,7 @@ int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const f
   g.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcLimbs >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
   g.err = device_error_word();
   cudaError_t ce = launch_ex(mv_xstat_kernel, dim3(nstats), dim3(kStatThreads), 0, LaunchOpts{st, true}, x, (int)K,
-                             const_cast<float4*>(g.stats), g.ticket, (int)grid, dyn, (int64_t)ndyn);
+                             const_cast<float4*>(g.stats), g.ticket, (int)grid);
   if (ce == cudaSuccess) {
     const size_t smem = (size_t)kTcStages * kTcStageBytes + 1024;
     ce = ensure_smem_attr((const void*)mv_tc_kernel, smem);
