@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--oracle-tokens", type=int, default=4)
+
     ap.add_argument("--rows", type=int, default=ROWS, help=argparse.SUPPRESS)
     ap.add_argument("--cols", type=int, default=COLS, help=argparse.SUPPRESS)
     args = ap.parse_args()
@@ -213,10 +214,16 @@ def run_ours(args, rank, world, local):
     y_local = torch.empty(M * R, dtype=torch.float32, device="cuda")
     y_full = torch.empty(world * M * R, dtype=torch.float32, device="cuda")
 
-    def step():
+    def gemv():
         ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
+
+    def gather():
         if world > 1:
             dist.all_gather_into_tensor(y_full, y_local)
+
+    def step():
+        gemv()
+        gather()
 
     def barrier():
         torch.cuda.synchronize()
@@ -242,10 +249,9 @@ def run_ours(args, rank, world, local):
     t0.record(stream)
     for i in range(args.steps):
         g_events[i][0].record(stream)
-        ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
+        gemv()
         g_events[i][1].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(y_full, y_local)
+        gather()
     t1.record(stream)
     barrier()
     clocks = sampler.stop() if sampler else None
@@ -313,6 +319,7 @@ def run_ours(args, rank, world, local):
         target = run_target_gemv(torch, ops, weights, scales, x, R, K, sp, probe["bandwidth"] / 1e9)
 
     quant = run_quantize(torch, ops, sp) if world == 1 and rank == 0 else None
+    lm_head = run_lm_head(args, torch, ops, dist, rank, world, sp, barrier, max_over_ranks)
 
     decode = None
     if not args.no_decode:
@@ -342,6 +349,7 @@ def run_ours(args, rank, world, local):
                 "matrices": M, "N": ROWS, "K": COLS, "rows_per_gpu": R,
                 "bytes_per_step": bytes_job, "l2": "no flush: 18.8 GB / N of weights per step >> 126 MB L2",
                 "parallelism": f"row-shard x{world}",
+                "gather": "one NCCL all-gather of every matrix's slices per step" if world > 1 else None,
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -368,6 +376,7 @@ def run_ours(args, rank, world, local):
             "cpu_baseline": cpu,
             "decode": decode,
             "quantize": quant,
+            "lm_head": lm_head,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -439,6 +448,52 @@ def run_target_gemv(torch, ops, weights, scales, x, R, K, sp, stream_gbs):
     out["note"] = ("each GEMV its own launch (xpu_matvec_q8_dev), rotating over 8-16 matrices; auto = the "
                    "library's default path choice, whose kernel is named; frac of measured HBM peak")
     return out
+
+
+def run_lm_head(args, torch, ops, dist, rank, world, sp, barrier, max_over_ranks):
+    """Config 5(i): the LM-head shape, one Q8 GEMV of N = 128256 rows and
+    K = 8192 (1.05 GB of codes), rows sharded over the N GPUs and the output
+    slices all-gathered (NCCL) every step.  Weights are generated on the
+    device, each GPU its own rows of the same seeded matrix."""
+    from xpuops.synth import tensor_seed
+
+    N, K = 128256, 8192
+    if N % world:
+        return None
+    R, W = N // world, K // 4
+    w = torch.empty(R * W, dtype=torch.int32, device="cuda")
+    s = torch.empty(R, dtype=torch.float32, device="cuda")
+    tmp = torch.empty(R * K, dtype=torch.float32, device="cuda")
+    ops.fill_normal_dev(tmp, R * K, tensor_seed(5, 0), 0.0, 0.02, stream=sp, start=rank * R * K)
+    ops.quantizePackQ8_dev(tmp, R, K, w, s, stream=sp)
+    del tmp
+    x = torch.empty(K, dtype=torch.float32, device="cuda")
+    ops.fill_normal_dev(x, K, tensor_seed(5, 1), stream=sp)
+    y = torch.empty(R, dtype=torch.float32, device="cuda")
+    y_full = torch.empty(N, dtype=torch.float32, device="cuda")
+
+    def step():
+        ops.matvecQ8_dev(w, s, x, R, K, y, sp)
+        if world > 1:
+            dist.all_gather_into_tensor(y_full, y)
+
+    for _ in range(5):
+        step()
+    barrier()
+    steps = max(20, args.steps // 4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / steps
+    byts = algorithmic_bytes(R, K, 1) * world
+    del w, s
+    return {"workload": f"matvecQ8 LM head [{N} x {K}], rows sharded over {world} GPU(s)"
+                        + (", NCCL all-gather of y every step" if world > 1 else ""),
+            "steps": steps, "ms_per_step": round(ms, 4), "GBs": round(byts / (ms / 1e3) / 1e9, 1),
+            "rows_per_gpu": R, "kernel": "mv_tc_kernel" if tensor_cores_serve(1, R, K) else "mv_bulk_kernel"}
 
 
 def run_quantize(torch, ops, sp):
