@@ -213,17 +213,41 @@ def run_ours(args, rank, world, local):
     W = K // 4
     y_local = torch.empty(M * R, dtype=torch.float32, device="cuda")
     y_full = torch.empty(world * M * R, dtype=torch.float32, device="cuda")
+    # N > 1: the all-gather is fused into the GEMV (xpu_matvec_q8_stack_allgather_dev):
+    # its epilogue writes every row into every GPU's output over NVLink, the
+    # outputs mapped across the processes with CUDA IPC; two output buffers
+    # in turn, as a rank may run one call ahead.
+    fused = None
+    if world > 1:
+        outs = [ops.DeviceBuffer(4 * world * M * R) for _ in range(2)]
+        flags = ops.DeviceBuffer(4 * world)
+        flags.upload(np.zeros(world, np.uint32))
+        every = [None] * world
+        dist.all_gather_object(every, [ops.ipcHandle(o) for o in outs] + [ops.ipcHandle(flags)])
+        maps = [[ops.ipcOpen(h) for h in every[r]] if r != rank else [o.ptr for o in outs] + [flags.ptr]
+                for r in range(world)]
+        fused = {"outs": outs, "flags": flags, "maps": maps, "epoch": 0}
 
     def gemv():
-        ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
-
-    def gather():
-        if world > 1:
-            dist.all_gather_into_tensor(y_full, y_local)
+        if fused is None:
+            ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
+            return y_local
+        fused["epoch"] += 1
+        b = fused["epoch"] % 2
+        ops.matvecQ8StackAllGather_dev(weights, R * W, scales, x, M, R, K, rank, world,
+                                       [fused["maps"][r][b] for r in range(world)],
+                                       [fused["maps"][r][2] for r in range(world)], fused["epoch"], sp)
+        return fused["outs"][b]
 
     def step():
-        gemv()
-        gather()
+        return gemv()
+
+    def to_host(dst, src):
+        if isinstance(src, torch.Tensor):
+            dst.copy_(src, non_blocking=True)
+        else:  # a library buffer (the fused path's outputs)
+            from xpuops._lib import check, lib
+            check(lib().xpu_memcpy_d2h(dst.data_ptr(), src.ptr, dst.numel() * 4, sp))
 
     def barrier():
         torch.cuda.synchronize()
@@ -251,25 +275,45 @@ def run_ours(args, rank, world, local):
         g_events[i][0].record(stream)
         gemv()
         g_events[i][1].record(stream)
-        gather()
     t1.record(stream)
     barrier()
     clocks = sampler.stop() if sampler else None
     total_ms = max_over_ranks(t0.elapsed_time(t1))
     gemv_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in g_events))
 
+    # The same stack with an NCCL all-gather after each GEMV (the unfused
+    # form; comparison only).
+    nccl = None
+    if world > 1:
+        for _ in range(2):
+            ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
+            dist.all_gather_into_tensor(y_full, y_local)
+        barrier()
+        n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_steps = max(3, args.steps // 2)
+        n0.record(stream)
+        for _ in range(n_steps):
+            ops.matvecQ8Stack_dev(weights, R * W, scales, x, M, R, K, y_local, sp)
+            dist.all_gather_into_tensor(y_full, y_local)
+        n1.record(stream)
+        barrier()
+        nccl_ms = max_over_ranks(n0.elapsed_time(n1)) / n_steps
+        nccl = {"ms_per_step": round(nccl_ms, 4),
+                "value": round(algorithmic_bytes(R, K, M) * world / (nccl_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "what": "the same stack, then one NCCL all-gather per step (unfused)"}
+
     bytes_rank = algorithmic_bytes(R, K, M)
     bytes_job = bytes_rank * world
     value = bytes_job * args.steps / (total_ms / 1e3) / 1e9
-    # One persistent launch per step over the stack (on the tensor-core path
-    # preceded by a 600-byte memset of its tickets, inside the same events).
+    # One persistent GEMV launch per step over the stack, on the tensor-core
+    # path preceded by its vector-statistics kernel (inside the same events).
     avg_launch_s = gemv_ms / 1e3 / args.steps
     achieved = bytes_rank / avg_launch_s / 1e9
     peak, peak_src = measured_peaks()
     on_tc = tensor_cores_serve(M, R, K)
     kname = "mv_tc_kernel" if on_tc else "mv_bulk_kernel"
     traffic, traffic_cmd = ncu_traffic(kname, R, K)
-    launches_per_step = 1
+    launches_per_step = 2 if on_tc or world > 1 else 1  # mv_xstat_kernel + mv_tc_kernel
 
     # The other matvecQ8 path, pinned, on the same stack (comparison only).
     ops.setMatvecPath(ops.MATVEC_CUDA_CORES if on_tc else ops.MATVEC_TENSOR_CORES)
@@ -297,8 +341,7 @@ def run_ours(args, rank, world, local):
     y_host = torch.empty(world * M * R, dtype=torch.float32).pin_memory()
     for _ in range(3):
         x.copy_(x_host, non_blocking=True)
-        step()
-        y_host.copy_(y_full if world > 1 else y_local, non_blocking=True)
+        to_host(y_host, step())
         stream.synchronize()
     e2e_steps = max(10, args.steps // 4)
     barrier()
@@ -306,8 +349,7 @@ def run_ours(args, rank, world, local):
     e0.record(stream)
     for _ in range(e2e_steps):
         x.copy_(x_host, non_blocking=True)
-        step()
-        y_host.copy_(y_full if world > 1 else y_local, non_blocking=True)
+        to_host(y_host, step())
         stream.synchronize()  # the host reads y every step
     e1.record(stream)
     barrier()
@@ -349,7 +391,8 @@ def run_ours(args, rank, world, local):
                 "matrices": M, "N": ROWS, "K": COLS, "rows_per_gpu": R,
                 "bytes_per_step": bytes_job, "l2": "no flush: 18.8 GB / N of weights per step >> 126 MB L2",
                 "parallelism": f"row-shard x{world}",
-                "gather": "one NCCL all-gather of every matrix's slices per step" if world > 1 else None,
+                "gather": ("fused into the GEMV: its epilogue writes every row into every GPU's output over NVLink "
+                           "(CUDA IPC mappings), then a flag per GPU") if world > 1 else None,
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -367,6 +410,7 @@ def run_ours(args, rank, world, local):
                                     "mv_bulk_kernel (matvecQ8, bulk-copy path): one launch per step over the contiguous stack"),
                          "launch_ms": round(avg_launch_s * 1e3, 5)},
             "other_path": alt,
+            "nccl_gather": nccl,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": K * 4,
                     "d2h_bytes_per_step": world * M * R * 4, "ms_per_step": round(e2e_ms / e2e_steps, 4)},
             "gpu_launches": args.steps * world * launches_per_step,
@@ -380,6 +424,13 @@ def run_ours(args, rank, world, local):
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank still writes into a mapped output
+        if fused is not None:
+            for r in range(world):
+                if r != rank:
+                    for ptr in fused["maps"][r]:
+                        ops.ipcClose(ptr)
         dist.barrier()
         dist.destroy_process_group()
 

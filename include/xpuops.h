@@ -177,6 +177,33 @@ XPU_API int xpu_dist_matvec_q8_rowshard(xpu_dist* dist, const uint32_t* const* w
                                         const float* const* scales, const float* const* vectors, int64_t count,
                                         int64_t N, int64_t K, float* const* outputs);
 XPU_API int xpu_dist_destroy(xpu_dist* dist);
+/* For one process per GPU (torch.distributed, MPI): CUDA IPC.  The handle
+ * (64 bytes) of a buffer from xpu_malloc, and a mapping of another
+ * process's buffer into this one (close it with xpu_ipc_close_handle). */
+XPU_API int xpu_ipc_get_handle(const void* dev_ptr, void* handle);
+XPU_API int xpu_ipc_open_handle(const void* handle, void** dev_ptr);
+XPU_API int xpu_ipc_close_handle(void* dev_ptr);
+/* The row-sharded stack of xpu_dist_matvec_q8_rowshard for one process per
+ * GPU, with the all-gather done by the GEMV itself: rank `rank` of
+ * `nranks` (<= 8) holds `rows` rows of each of `count` matrices (its shard,
+ * laid out as for xpu_matvec_q8_stack_dev) and writes every finished row
+ * straight into every rank's output over NVLink: outputs[r] is rank r's
+ * [count][nranks * rows] buffer mapped in this process (xpu_ipc_open_handle;
+ * outputs[rank] this rank's own), row i of matrix m of this shard going to
+ * m * nranks * rows + rank * rows + i.  flags[r] is rank r's array of
+ * nranks words (zeroed once before the first call).  When the kernel
+ * completes on this GPU (stream order), every rank's rows have arrived in
+ * outputs[rank].  Every rank calls with the same sequence of epochs, each
+ * nonzero and larger than the last.  A rank may be one call ahead of
+ * another, so alternate two sets of outputs between calls whose results are
+ * read.  Needs the tensor-core path's shapes (weights on 16 bytes, rows and
+ * stride whole 16-byte slots, K <= 65536).  A rank that never arrives makes
+ * the others' wait give up after 2 s (XPU_ETIMEOUT at the next
+ * synchronising call). */
+XPU_API int xpu_matvec_q8_stack_allgather_dev(const uint32_t* weights, int64_t weight_stride, const float* scales,
+                                              const float* vector, int64_t count, int64_t rows, int64_t K,
+                                              int32_t rank, int32_t nranks, float* const* outputs,
+                                              uint32_t* const* flags, uint32_t epoch, void* stream);
 /* ops/gqa/reference.ts:203-303 `groupedAttention` for one decode query
  * (B = 1, L = 1, causal, queryOffset = s_eff - 1, no mask), as the resident
  * engine runs it each step (llm/engine-q8-resident.ts:1852-1853):

@@ -127,3 +127,86 @@ def test_single_process_group_equals_one_gpu(path):
         ops.setMatvecPath(ops.MATVEC_AUTO)
     for g in range(G):
         np.testing.assert_array_equal(outs[g].cpu().numpy(), single)
+
+
+def _fused_rank(rank, world, port, out):
+    """One process per GPU: this rank's shard through
+    xpu_matvec_q8_stack_allgather_dev, every rank's output mapped over CUDA
+    IPC; three calls (epochs 1-3, two output buffers in turn)."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from xpuops import ops
+    from xpuops.dist import shard_rows
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    first, rows, per = shard_rows(N, world, rank)
+    assert rows == per  # N divides
+    w, s, x = _shard(rows, first)
+    W = K // 4
+    outs = [ops.DeviceBuffer(4 * M * N) for _ in range(2)]
+    flags = ops.DeviceBuffer(4 * world)
+    flags.upload(np.zeros(world, np.uint32))
+    mine = [ops.ipcHandle(o) for o in outs] + [ops.ipcHandle(flags)]
+    every = [None] * world
+    dist.all_gather_object(every, mine)
+    peer = [[ops.ipcOpen(h) if r != rank else None for h in every[r]] for r in range(world)]
+    ptr = lambda r, i: (outs[i].ptr if i < 2 else flags.ptr) if r == rank else peer[r][i]
+    results = []
+    for epoch in (1, 2, 3):
+        b = epoch % 2
+        ops.matvecQ8StackAllGather_dev(w, rows * W, s, x, M, rows, K, rank, world, [ptr(r, b) for r in range(world)],
+                                       [ptr(r, 2) for r in range(world)], epoch)
+        ops.stream_sync()
+        results.append(outs[b].download(np.float32, M * N))
+    got_flags = flags.download(np.uint32, world)
+    dist.barrier()  # every rank's kernels are done before any mapping closes
+    for r in range(world):
+        for p_ in peer[r]:
+            if p_:
+                ops.ipcClose(p_)
+    dist.barrier()
+    if rank == 0:
+        np.save(out, np.stack(results))
+        np.save(str(out) + ".flags.npy", got_flags)
+    dist.destroy_process_group()
+
+
+def test_fused_allgather_two_processes_equals_one_gpu(tmp_path):
+    """xpu_matvec_q8_stack_allgather_dev on 2 GPUs, one process each: the
+    GEMV epilogue writes every row into both GPUs' outputs over NVLink, and
+    each call returns with the whole stack's output in place, bit-identical
+    to the unsharded tensor-core stack on one GPU, on three calls in a row."""
+    from xpuops import ops
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path / "fused.npy"
+    mp.start_processes(_fused_rank, args=(2, _port(), str(out)), nprocs=2, start_method="spawn", join=True)
+    torch.cuda.set_device(0)
+    ops.setMatvecPath(ops.MATVEC_TENSOR_CORES)
+    try:
+        single = _stack(N, 0).cpu().numpy()
+    finally:
+        ops.setMatvecPath(ops.MATVEC_AUTO)
+    got = np.load(out)
+    for i in range(3):
+        np.testing.assert_array_equal(got[i], single)
+    assert np.load(str(out) + ".flags.npy").tolist() == [3, 3]
+
+
+def test_fused_allgather_contract_errors():
+    """Argument checks happen before any device work."""
+    import xpuops
+    from xpuops import ops
+
+    z = ops.DeviceBuffer(4096)
+    with pytest.raises(xpuops.XpuInvalidArgument, match="rank 2 of 2"):
+        ops.matvecQ8StackAllGather_dev(z, 512, z, z, 1, 8, 2048, 2, 2, [z, z], [z, z], 1)
+    with pytest.raises(xpuops.XpuInvalidArgument, match="epoch 0"):
+        ops.matvecQ8StackAllGather_dev(z, 512, z, z, 1, 8, 2048, 0, 1, [z], [z], 0)
+    with pytest.raises(xpuops.XpuInvalidArgument, match="tensor-core path"):
+        ops.matvecQ8StackAllGather_dev(z, 513, z, z, 1, 8, 2050, 0, 1, [z], [z], 1)

@@ -11,6 +11,8 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <string.h>
+
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -228,6 +230,50 @@ int xpu_dist_matvec_q8_rowshard(xpu_dist* d, const uint32_t* const* weights, int
     if (!rc) rc = rc3;
   }
   return rc;
+}
+
+// CUDA IPC: one process per GPU maps the others' buffers.
+int xpu_ipc_get_handle(const void* dev_ptr, void* handle) {
+  XPU_REQUIRE(dev_ptr && handle, XPU_EINVAL, "xpu_ipc_get_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  XPU_TRY_CUDA(cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)));
+  memcpy(handle, &h, sizeof h);
+  return XPU_OK;
+}
+
+int xpu_ipc_open_handle(const void* handle, void** dev_ptr) {
+  XPU_REQUIRE(dev_ptr && handle, XPU_EINVAL, "xpu_ipc_open_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  *dev_ptr = nullptr;
+  XPU_TRY_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return XPU_OK;
+}
+
+int xpu_ipc_close_handle(void* dev_ptr) {
+  if (dev_ptr) XPU_TRY_CUDA(cudaIpcCloseMemHandle(dev_ptr));
+  return XPU_OK;
+}
+
+int xpu_matvec_q8_stack_allgather_dev(const uint32_t* weights, int64_t weight_stride, const float* scales,
+                                      const float* vector, int64_t count, int64_t rows, int64_t K, int32_t rank,
+                                      int32_t nranks, float* const* outputs, uint32_t* const* flags, uint32_t epoch,
+                                      void* stream) {
+  XPU_REQUIRE(weights && scales && vector && outputs && flags, XPU_EINVAL,
+              "xpu_matvec_q8_stack_allgather_dev: null pointer");
+  XPU_REQUIRE(nranks >= 1 && nranks <= 8 && rank >= 0 && rank < nranks, XPU_EINVAL,
+              "xpu_matvec_q8_stack_allgather_dev: rank %d of %d ranks (1 to 8)", rank, nranks);
+  XPU_REQUIRE(epoch != 0, XPU_EINVAL, "xpu_matvec_q8_stack_allgather_dev: epoch 0 is reserved");
+  for (int r = 0; r < nranks; ++r)
+    XPU_REQUIRE(outputs[r] && flags[r], XPU_EINVAL, "xpu_matvec_q8_stack_allgather_dev: null output or flags of rank %d",
+                r);
+  XPU_REQUIRE(count >= 1 && rows >= 1 && K >= 1, XPU_EINVAL,
+              "xpu_matvec_q8_stack_allgather_dev: need count, rows, K >= 1");
+  XPU_REQUIRE(matvec_tc_supports(weights, weight_stride, count, rows, K), XPU_EINVAL,
+              "xpu_matvec_q8_stack_allgather_dev: needs the tensor-core path (weights on 16 bytes, rows and the "
+              "stack stride whole 16-byte slots, K <= 65536)");
+  return matvec_tc_allgather_dev(weights, weight_stride, scales, vector, count, rows, K, rank, nranks, outputs,
+                                 reinterpret_cast<unsigned int* const*>(flags), epoch, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -39,6 +39,13 @@ int run_matvec(MvParams p, int epi, int pro, const LaunchOpts& o);
 int set_matvec_path(int path);
 int matvec_path();
 bool matvec_tc_applies(const uint32_t* w, int64_t mat_stride, int64_t count, int64_t N, int64_t K);
+// The shape and alignment conditions of the tensor-core path alone.
+bool matvec_tc_supports(const uint32_t* w, int64_t mat_stride, int64_t count, int64_t N, int64_t K);
+// The tensor-core stack of one rank's row shard with the all-gather fused
+// into the epilogue (include/xpuops.h xpu_matvec_q8_stack_allgather_dev).
+int matvec_tc_allgather_dev(const uint32_t* w, int64_t mat_stride, const float* s, const float* x, int64_t count,
+                            int64_t R, int64_t K, int rank, int nranks, float* const* outs, unsigned int* const* flags,
+                            unsigned int epoch, cudaStream_t st);
 int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const float* x, int64_t count, int64_t N,
                   int64_t K, float* y, cudaStream_t st);
 

@@ -55,6 +55,7 @@ constexpr int kTcLimbs = 16;               // two levels of eight limbs (MMA N)
 constexpr int kTcG = 4;                    // slices per stage
 constexpr int kTcStages = 3;
 constexpr int kTcThreads = 192;
+constexpr int kTcMaxRanks = 8;             // GPUs of a fused all-gather
 constexpr int kTcWriters = 128;            // warps 2-5
 constexpr uint32_t kTcSliceA = kTcBM * kTcBK;      // 16 KB
 constexpr uint32_t kTcSliceB = kTcLimbs * kTcBK;   // 2 KB
@@ -71,9 +72,20 @@ struct TcArgs {
   const uint32_t* w;
   const float* x;
   const float* s;
-  float* y;
+  // Outputs: row `grow` of matrix m goes to out[r][m * y_stride + y_off +
+  // grow] for every r < nranks (one rank: out[0] = y, y_off = 0).  With
+  // epoch != 0 the rows are rank `rank`'s shard of a row-sharded stack and
+  // out[r] is rank r's [count][nranks R] output in its own GPU's memory:
+  // the all-gather is these stores.  The last CTA then writes `epoch` to
+  // word `rank` of every rank's flags and waits until its own flags all
+  // carry `epoch` or a later one.
+  float* out[kTcMaxRanks];
+  unsigned int* flags[kTcMaxRanks];
+  int64_t y_off;
+  int nranks, rank;
+  unsigned int epoch;
   int4* part;            // [grid][2][128 rows][4 x int4]: split-tile partials
-  unsigned int* ticket;  // [grid], zeroed by mv_xstat_kernel
+  unsigned int* ticket;  // [grid + 1], zeroed by mv_xstat_kernel (the last word counts finished CTAs)
   const float4* stats;   // [nstats] per-block (max |x|, min nonzero |x|, non-finite, -)
   int64_t ldw, mat_stride, s_stride, y_stride;
   int64_t total;  // units: tiles * S
@@ -445,7 +457,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           v += (double)code * (double)g.x[k];
         }
       }
-      g.y[mi * g.y_stride + grow] = (float)(v * sc);
+      const float val = (float)(v * sc);
+      const int64_t at = mi * g.y_stride + g.y_off + grow;
+      for (int r = 0; r < g.nranks; ++r) g.out[r][at] = val;
     };
 
     // Epilogue of segment j (its accumulator is in buffer j & 1).  Returns
@@ -565,6 +579,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (g.epoch != 0 && threadIdx.x == 0) {
+    // Fused all-gather: the barrier ordered every writer's stores (to every
+    // rank's output) before this fence; the CTA that finishes last publishes
+    // this rank's epoch to all ranks, then waits for theirs.
+    __threadfence_system();
+    const unsigned int n = atomicAdd(&g.ticket[gridDim.x], 1u);
+    if (n == gridDim.x - 1) {
+      __threadfence_system();
+      for (int r = 0; r < g.nranks; ++r)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(g.flags[r] + g.rank), "r"(g.epoch) : "memory");
+      const uint64_t t0 = global_timer_ns();
+      for (int r = 0; r < g.nranks; ++r) {
+        unsigned int v = 0;
+        for (;;) {
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(g.flags[g.rank] + r) : "memory");
+          if ((int)(v - g.epoch) >= 0) break;
+          if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(g.err, 1u);
+            r = g.nranks;
+            break;
+          }
+        }
+      }
+    }
+  }
   if (warp == 1) {
     if (lane == 0) mbar_wait(&done, 0, g.err);
     __syncwarp();
@@ -608,12 +647,17 @@ constexpr int64_t kTcMinBytes = 512ll << 20;
 constexpr int64_t kTcMinBytesLongRows = 64ll << 20;
 constexpr int64_t kTcLongRows = 16384;
 
-bool matvec_tc_applies(const uint32_t* w, int64_t mat_stride, int64_t count, int64_t N, int64_t K) {
+bool matvec_tc_supports(const uint32_t* w, int64_t mat_stride, int64_t count, int64_t N, int64_t K) {
   const int64_t W = (K + 3) / 4;
   // K <= 65536 keeps |D| <= 128 * 128 * K within int32.
   if (N <= 0 || K <= 0 || count <= 0 || K > 65536 || W % 4 || mat_stride % 4) return false;
   if (reinterpret_cast<uintptr_t>(w) % 16) return false;
-  if (count > 65535 || N > (int64_t)INT_MAX - kTcBM) return false;
+  return count <= 65535 && N <= (int64_t)INT_MAX - kTcBM;
+}
+
+bool matvec_tc_applies(const uint32_t* w, int64_t mat_stride, int64_t count, int64_t N, int64_t K) {
+  if (!matvec_tc_supports(w, mat_stride, count, N, K)) return false;
+  const int64_t W = (K + 3) / 4;
   const int path = g_matvec_path.load(std::memory_order_relaxed);
   if (path == XPU_MATVEC_CUDA_CORES) return false;
   if (path == XPU_MATVEC_TENSOR_CORES) return true;
@@ -664,8 +708,9 @@ static int weight_map(const TcMapKey& key, CUtensorMap* out) {
 // y[m][n] = matvecQ8 of matrix m (words at w + m * mat_stride, scales at
 // s + m * N, outputs at y + m * N) on one x, m < count.  The caller checked
 // matvec_tc_applies().
-int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const float* x, int64_t count, int64_t N,
-                  int64_t K, float* y, cudaStream_t st) {
+static int matvec_tc_launch(const uint32_t* w, int64_t mat_stride, const float* s, const float* x, int64_t count,
+                            int64_t N, int64_t K, float* const* outs, unsigned int* const* flags, int rank, int nranks,
+                            unsigned int epoch, cudaStream_t st) {
   const int64_t W = (K + 3) / 4;
   const DeviceInfo& di = device_info();
   const int tiles_per_mat = (int)((N + kTcBM - 1) / kTcBM);
@@ -682,7 +727,7 @@ int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const f
   // Scratch: the split-tile partials (written before they are read), the
   // tickets (zeroed by the stats kernel) and the vector stats.
   const size_t part_bytes = (size_t)grid * 2 * kTcBM * kTcLimbs * sizeof(int);
-  const size_t ticket_bytes = ((size_t)grid * sizeof(unsigned int) + 15) / 16 * 16;
+  const size_t ticket_bytes = ((size_t)(grid + 1) * sizeof(unsigned int) + 15) / 16 * 16;
   const size_t stat_bytes = (size_t)nstats * sizeof(float4);
   uint8_t* scratch = nullptr;
   XPU_TRY_CUDA(scratch_alloc((void**)&scratch, part_bytes + ticket_bytes + stat_bytes, st));
@@ -690,14 +735,21 @@ int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const f
   g.w = w;
   g.x = x;
   g.s = s;
-  g.y = y;
+  for (int r = 0; r < nranks; ++r) {
+    g.out[r] = outs[r];
+    g.flags[r] = flags ? flags[r] : nullptr;
+  }
+  g.nranks = nranks;
+  g.rank = rank;
+  g.epoch = epoch;
+  g.y_off = (int64_t)rank * N;
   g.part = reinterpret_cast<int4*>(scratch);
   g.ticket = reinterpret_cast<unsigned int*>(scratch + part_bytes);
   g.stats = reinterpret_cast<const float4*>(scratch + part_bytes + ticket_bytes);
   g.ldw = W;
   g.mat_stride = mat_stride;
   g.s_stride = N;
-  g.y_stride = N;
+  g.y_stride = N * nranks;
   g.total = total;
   g.N = (int)N;
   g.K = (int)K;
@@ -708,7 +760,7 @@ int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const f
   g.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcLimbs >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
   g.err = device_error_word();
   cudaError_t ce = launch_ex(mv_xstat_kernel, dim3(nstats), dim3(kStatThreads), 0, LaunchOpts{st, true}, x, (int)K,
-                             const_cast<float4*>(g.stats), g.ticket, (int)grid);
+                             const_cast<float4*>(g.stats), g.ticket, (int)grid + 1);
   if (ce == cudaSuccess) {
     const size_t smem = (size_t)kTcStages * kTcStageBytes + 1024;
     ce = ensure_smem_attr((const void*)mv_tc_kernel, smem);
@@ -718,6 +770,19 @@ int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const f
   if (ce != cudaSuccess) rc = cuda_status(ce, "mv_tc_kernel");
   scratch_free(scratch, st);
   return rc;
+}
+
+int matvec_tc_dev(const uint32_t* w, int64_t mat_stride, const float* s, const float* x, int64_t count, int64_t N,
+                  int64_t K, float* y, cudaStream_t st) {
+  float* outs[1] = {y};
+  return matvec_tc_launch(w, mat_stride, s, x, count, N, K, outs, nullptr, 0, 1, 0u, st);
+}
+
+// The row-sharded stack with the all-gather fused into the epilogue (TcArgs).
+int matvec_tc_allgather_dev(const uint32_t* w, int64_t mat_stride, const float* s, const float* x, int64_t count,
+                            int64_t R, int64_t K, int rank, int nranks, float* const* outs, unsigned int* const* flags,
+                            unsigned int epoch, cudaStream_t st) {
+  return matvec_tc_launch(w, mat_stride, s, x, count, R, K, outs, flags, rank, nranks, epoch, st);
 }
 
 }  // namespace xpu

@@ -146,6 +146,10 @@ SIGNATURES = {
     "xpu_dist_create": [I32, C.POINTER(I32), C.POINTER(P)],
     "xpu_dist_matvec_q8_rowshard": [P, C.POINTER(P), I64, C.POINTER(P), C.POINTER(P), I64, I64, I64, C.POINTER(P)],
     "xpu_dist_destroy": [P],
+    "xpu_ipc_get_handle": [P, P],
+    "xpu_ipc_open_handle": [P, C.POINTER(P)],
+    "xpu_ipc_close_handle": [P],
+    "xpu_matvec_q8_stack_allgather_dev": [P, I64, P, P, I64, I64, I64, I32, I32, C.POINTER(P), C.POINTER(P), C.c_uint32, P],
     "xpu_matvec_path": [C.POINTER(I32)],
     "xpu_gqa_decode_dev": [P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P],
     "xpu_gqa_decode_noalloc": [P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P],

@@ -295,3 +295,36 @@ def measureRoofline(stream_bytes: int = 0, runs: int = 0) -> dict:
     check(lib().xpu_measure_roofline(stream_bytes, runs, C.byref(r)))
     return {"bandwidth": r.bandwidth, "compute": r.compute, "loadBandwidth": r.load_bandwidth,
             "bulkBandwidth": r.bulk_bandwidth, "streamBytes": r.stream_bytes}
+
+
+# ---- one process per GPU: CUDA IPC and the fused all-gather ----------------
+
+def ipcHandle(buf) -> bytes:
+    """The 64-byte CUDA IPC handle of a device buffer (xpu_malloc'ed base)."""
+    h = C.create_string_buffer(64)
+    check(lib().xpu_ipc_get_handle(_ptr(buf), h))
+    return h.raw
+
+
+def ipcOpen(handle: bytes) -> int:
+    """Maps another process's buffer into this one; returns the pointer."""
+    p = C.c_void_p()
+    hb = C.create_string_buffer(bytes(handle), 64)
+    check(lib().xpu_ipc_open_handle(hb, C.byref(p)))
+    return p.value or 0
+
+
+def ipcClose(ptr: int) -> None:
+    check(lib().xpu_ipc_close_handle(ptr))
+
+
+def matvecQ8StackAllGather_dev(weights, weight_stride: int, scales, vector, count: int, rows: int, K: int,
+                               rank: int, nranks: int, outputs, flags, epoch: int, stream=None) -> None:
+    """xpu_matvec_q8_stack_allgather_dev: this rank's row shard of a stack,
+    every finished row written into every rank's output (pointers in this
+    process: `outputs[r]`, `flags[r]`)."""
+    outs = (C.c_void_p * nranks)(*[_ptr(o) for o in outputs])
+    fls = (C.c_void_p * nranks)(*[_ptr(f) for f in flags])
+    check(lib().xpu_matvec_q8_stack_allgather_dev(_ptr(weights), int(weight_stride), _ptr(scales), _ptr(vector),
+                                                  int(count), int(rows), int(K), int(rank), int(nranks), outs, fls,
+                                                  int(epoch), _ptr(stream) or None))
