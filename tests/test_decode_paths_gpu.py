@@ -165,11 +165,13 @@ def test_shapes_outside_the_persistent_step_keep_the_graph():
 
 
 def test_ragged_rows_with_several_staging_passes():
-    """Hidden 1030 and FFN 2050 (rows of 258 and 513 words): every decode GEMV
-    takes the general kernel with its rmsnorm prologue, QKV/RoPE, FFN and
-    residual epilogues, and x spans more than one staging pass of the CTA."""
+    """Hidden 1030 and FFN 2050 (rows of 258 and 513 words): the layer GEMVs
+    take the general kernel with its rmsnorm prologue, QKV/RoPE, FFN and
+    residual epilogues, x spanning more than one staging pass of the CTA; the
+    16400-row LM head (16.9 MB) takes the class-map kernel with the rmsnorm
+    prologue, over two phase classes of rows."""
     cfg = xpuops.LlamaConfig(numLayers=2, hiddenSize=1030, numHeads=2, numKvHeads=1, headDim=64, ffnHidden=2050,
-                             vocabSize=300, ropeTheta=10000.0, rmsNormEps=1e-5, maxSeqLen=16)
+                             vocabSize=16400, ropeTheta=10000.0, rmsNormEps=1e-5, maxSeqLen=16)
     weights = random_llama(cfg, seed=4)
     oracle = orc.LlamaOracle(cfg, weights)
     with LlamaEngineQ8Resident.create(cfg, weights) as eng:

@@ -220,6 +220,48 @@ def test_misaligned_device_pointers(offset, N, K):
     check_matvec(dy.download(np.float32, N), packed, scales, x, N, K)
 
 
+def _slack_buffer(packed, o):
+    """packed at word o of a buffer with 0x7F7F7F7F (code 127) in the slack on
+    both sides: a kernel that counted a neighbour's word would be visibly off."""
+    buf = np.full(packed.size + 8, 0x7F7F7F7F, np.uint32)
+    buf[o:o + packed.size] = packed
+    return ops.DeviceBuffer.from_numpy(buf)
+
+
+@pytest.mark.parametrize("offset", [0, 4, 12])
+@pytest.mark.parametrize("N,K", [(4099, 4097), (4099, 4102), (4099, 4096), (32001, 2050), (77, 2600), (41, 22),
+                                 (130, 8190), (3, 1)])
+def test_ragged_kernel_phase_classes(offset, N, K):
+    """Rows off the 16-byte grid: odd W (four phase classes of rows), W = 2
+    mod 4 (two), and whole slots behind a pointer off the grid (one), each in
+    the plain, FFN and residual forms, with the weights at three offsets
+    within 16 bytes.  Matrices from 16 MB take the class-map kernel (32001 x
+    2050 with two row groups), the FFN form and the smaller ones the general
+    kernel.  N is not a multiple of the class count or of a unit."""
+    W = (K + 3) // 4
+    if W % 4 == 0 and offset == 0:
+        pytest.skip("16-byte rows: the bulk kernel")
+    o = offset // 4
+    _, wg, sg = _synth_q8(N, K, 1300 + K)
+    _, wu, su = _synth_q8(N, K, 1301 + K)
+    x = fill_normal(K, 1302)
+    r = fill_normal(N, 1303)
+    dg, du = _slack_buffer(wg, o), _slack_buffer(wu, o)
+    dsg, dsu, dx, dr = (ops.DeviceBuffer.from_numpy(a) for a in (sg, su, x, r))
+    dy = ops.DeviceBuffer(4 * N)
+    ops.matvecQ8_dev(du.ptr + offset, dsu, dx, N, K, dy)
+    ops.stream_sync()
+    check_matvec(dy.download(np.float32, N), wu, su, x, N, K)
+    ops.matvecQ8Ffn_dev(dg.ptr + offset, dsg, du.ptr + offset, dsu, dx, N, K, dy)
+    ops.stream_sync()
+    assert agree(dy.download(np.float32, N), orc.matvec_q8_ffn(wg, sg, wu, su, x, N, K), rel=1e-4,
+                 abs_=1e-5) is None
+    ops.matvecQ8Residual_dev(dg.ptr + offset, dsg, dx, dr, N, K, dy)
+    ops.stream_sync()
+    assert agree(dy.download(np.float32, N), orc.matvec_q8_residual(wg, sg, x, r, N, K), rel=1e-4,
+                 abs_=1e-5) is None
+
+
 @pytest.mark.parametrize("N,K", [(64, 16), (64, 2048), (256, 32768), (3, 40000)])
 def test_bulk_and_general_kernel_shapes(N, K):
     """16-byte-aligned rows (bulk-copy kernel, incl. the largest K it takes)

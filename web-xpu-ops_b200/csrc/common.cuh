@@ -3,6 +3,8 @@
 // programmatic dependent launch) and the int8 unpack used by every GEMV.
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -44,6 +46,10 @@ struct DeviceInfo {
   int max_smem_optin = 0;
 };
 const DeviceInfo& device_info();  // of the current device (cached per device)
+
+// The driver's cuTensorMapEncodeTiled (null if the driver lacks it), looked
+// up once.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // Stream-ordered scratch for per-call workspaces (limb splits, attention
 // partials): a memory pool of the library's own per device whose freed

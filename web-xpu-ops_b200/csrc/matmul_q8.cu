@@ -301,20 +301,6 @@ __global__ void __launch_bounds__(kMmThreads, 1)
 }
 
 // ------------------------------------------------------------------- host --
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static std::once_flag once;
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    cudaGetLastError();
-  });
-  return fn;
-}
-
 // 2-D int8 tensor map over rows x cols bytes (row pitch `pitch`), boxes of
 // box_rows x 128 bytes with 128-byte swizzle; reads past the edges give 0.
 int encode_i8_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t pitch, int box_rows) {

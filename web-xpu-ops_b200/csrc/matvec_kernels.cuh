@@ -67,17 +67,19 @@ __device__ __forceinline__ float silu_f32(float g) {
 
 // Writes output row(s) of a unit given `sum(r)`, the finished dot product of
 // unit row r (gate rows [0, RB) and up rows [RB, 2RB) for FFN): one call per
-// output row, per row pair for QKV (call t handles unit rows 2t, 2t+1).
+// output row, per row pair for QKV (call t handles unit rows 2t, 2t+1).  Unit
+// row t is output row row0 + rstride * t (rstride 1 for QKV).
 template <int EPI, typename SumFn>
-__device__ __forceinline__ void mv_epilogue(const MvParams& p, int64_t row0, int t, int RB, SumFn sum) {
+__device__ __forceinline__ void mv_epilogue(const MvParams& p, int64_t row0, int t, int RB, SumFn sum,
+                                            int64_t rstride = 1) {
   if constexpr (EPI == EPI_PLAIN) {
-    int64_t row = row0 + t;
+    int64_t row = row0 + rstride * t;
     if (row < p.N) p.y[row] = __fmul_rn(sum(t), p.s[row]);
   } else if constexpr (EPI == EPI_RESID) {
-    int64_t row = row0 + t;
+    int64_t row = row0 + rstride * t;
     if (row < p.N) p.y[row] = __fadd_rn(p.residual[row], __fmul_rn(sum(t), p.s[row]));
   } else if constexpr (EPI == EPI_FFN) {
-    int64_t row = row0 + t;
+    int64_t row = row0 + rstride * t;
     if (row < p.N) {
       float g = __fmul_rn(sum(t), p.s[row]);
       float u = __fmul_rn(sum(RB + t), p.s2[row]);
@@ -332,6 +334,259 @@ __global__ void __launch_bounds__(CPT >= 4 ? 512 : 576, 1) mv_bulk_kernel(MvPara
             if ((r % RB) < rows)
               dot16(*reinterpret_cast<const uint4*>(smem + col + (uint32_t)r * row_bytes), xr[j], acc[i]);
           }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // the stage may be refilled
+
+    float v[RPT];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) v[i] = hsum2(acc[i]);
+    const float tot = warp_reduce_rows<RPT>(v, lane);
+    if (!first_round && !mbar_wait(&rempty[slot], rph ^ 1u, p.err)) {
+      abort_flag = 1;
+      break;
+    }
+    if (lane % (32 / RPT) == 0) red[(slot * 16 + warp) * 8 + lane / (32 / RPT)] = tot;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&rfull[slot]);
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
+    if (++slot == RS) {
+      slot = 0;
+      rph ^= 1u;
+      first_round = false;
+    }
+  }
+}
+
+// ---------------------------------------------------------- ragged kernel --
+// The bulk kernel's pipeline for rows that are not whole 16-byte slots
+// (W % 4 != 0) or a weight pointer off the 16-byte grid.  Row r starts at
+// word off + r W of the 16-byte grid, at phase (off + r W) & 3, so its
+// 16-byte chunk c holds the codes of x[16c - 4o .. 16c - 4o + 15] for that
+// phase o.  Rows r = phi (mod C) all have the same phase (C = 4 for odd W,
+// 2 for W = 2 mod 4, 1 when only the pointer is off the grid), and C W is a
+// multiple of 4 words, so the rows of class phi form a 2-D tensor of 16-byte
+// chunks with a row stride of 16 C W / 4 bytes: the TMA copies a block of
+// them in one box, landing every row on the 16-byte grid of shared memory.
+// CTA b takes only class phi = b % C; each consumer thread holds its x slices
+// at its class's phase, zero outside [0, K), so the chunk bytes outside the
+// row (up to three words of the neighbouring rows at either end, read from
+// the same 16-byte chunk of memory) and the zeros the TMA writes past the
+// tensor's edges count nothing, as in the reference, which never reads them.
+//
+// A row's chunks may be wider than one box (256 8-byte elements), so a unit
+// is nbox boxes per weight stream, box j holding chunks [j cpb, (j+1) cpb) of
+// RB rows, box_bytes = 16 cpb bytes per row, at j * region in the stream's
+// half of the stage.
+struct alignas(64) MvClassMaps {
+  CUtensorMap w[4];   // class phi of the weight (gate for FFN)
+  CUtensorMap w2[4];  // class phi of the up weight (FFN)
+  int classes;        // C
+  int off_words;      // words from the 16-byte grid to the weight
+  int uc;             // chunks a row touches at the worst phase
+  int cpb;            // chunks per box row
+  int nbox;           // boxes per row block
+  uint32_t box_bytes; // 16 cpb
+  uint32_t region;    // bytes between the boxes of a stream in a stage
+  uint32_t half;      // bytes of one stream's boxes in a stage
+};
+
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+// load_x_cols at phase o: xr[j][i] = (x[16c - 4o + 2i], x[16c - 4o + 2i + 1])
+// for column c = ti + j nt, zero outside [0, K).  Row group 0's columns cover
+// [0, K) exactly once, so its threads count sum(x^2) for PRO_RMSNORM.
+template <int CPT, int PRO>
+__device__ __forceinline__ void load_x_phase(const MvParams& p, int tid, int nthreads, int ti, int nt, int o,
+                                             bool counts, double* red_d, int bar, f2 (&xr)[CPT][8]) {
+  float xv[CPT][16];
+  double ss = 0.0;
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int64_t k = 16 * (ti + (int64_t)j * nt) - 4 * o + i;
+      xv[j][i] = (k >= 0 && k < p.K) ? p.x[k] : 0.0f;
+      if constexpr (PRO == PRO_RMSNORM) ss += (double)xv[j][i] * (double)xv[j][i];
+    }
+  }
+  if constexpr (PRO == PRO_RMSNORM) {
+    const double sw = warp_sum_d(counts ? ss : 0.0);
+    const int warp = tid / 32, lane = tid % 32, nw = nthreads / 32;
+    if (lane == 0) red_d[warp] = sw;
+    named_bar_sync(bar, nthreads);
+    double tot = 0.0;
+    for (int w = 0; w < nw; ++w) tot += red_d[w];
+    const double scale = 1.0 / sqrt(tot / (double)p.K + p.eps);
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int64_t k = 16 * (ti + (int64_t)j * nt) - 4 * o + i;
+        if (k >= 0 && k < p.K) xv[j][i] = (float)((double)xv[j][i] * scale * (double)p.gamma[k]);
+      }
+    }
+    named_bar_sync(bar, nthreads);  // red_d is reused by the caller
+  }
+#pragma unroll
+  for (int j = 0; j < CPT; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xr[j][i] = make_f2(xv[j][2 * i], xv[j][2 * i + 1]);
+}
+
+// Warp roles, reduction ring and epilogue as in mv_bulk_kernel; the grid is
+// a multiple of C, CTA b taking class b % C, and a unit is RB consecutive
+// rows of the class (matrix rows phi + C j), read by nbox TMA boxes per
+// stream.  Rows of a class past its end come in as zeros (the TMA's fill)
+// and their outputs are not written, so every unit runs whole.
+template <int RPT, int CPT, int EPI, int PRO, bool GROUPED>
+__global__ void __launch_bounds__(CPT >= 4 ? 512 : 576, 1)
+    mv_ragged_kernel(MvParams p, const __grid_constant__ MvClassMaps cm) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int NSTREAM = EPI == EPI_FFN ? 2 : 1;
+  constexpr int RS = kRedSlots;
+  const int ncw = p.ncw, nct = ncw * 32, S = p.stages;
+  const int rg = GROUPED ? p.rg : 1, wpg = GROUPED ? p.wpg : ncw;
+  const int RT = RPT * rg, RB = RT / NSTREAM;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  uint64_t* rfull = empty + S;
+  uint64_t* rempty = rfull + RS;
+  float* red = reinterpret_cast<float*>(rempty + RS);            // [RS][16][8]
+  double* red_d = reinterpret_cast<double*>(red + RS * 16 * 8);  // [16]
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
+  const int C = cm.classes, phi = (int)(blockIdx.x % C), cb = (int)(blockIdx.x / C), nb = (int)(gridDim.x / C);
+  const int o = (int)((cm.off_words + (int64_t)phi * p.W) & 3);  // the class's phase
+  const int64_t n_cls = p.N > phi ? (p.N - phi + C - 1) / C : 0;  // rows of the class
+  const int64_t units = (n_cls + RB - 1) / RB;
+
+  griddep_launch_dependents();
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ncw);
+    }
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&rfull[s], ncw);
+      mbar_init(&rempty[s], 1);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == ncw) {
+    // ---------------- producer: nbox boxes per stream and unit ----------------
+    if (lane != 0) return;
+    const uint64_t policy = evict_first_policy();
+    const CUtensorMap* m1 = &cm.w[phi];
+    const CUtensorMap* m2 = &cm.w2[phi];
+    const uint32_t bytes = (uint32_t)cm.nbox * cm.box_bytes * (uint32_t)RB * NSTREAM;  // fills included
+    int64_t issued = 0;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int64_t u = cb; u < units && !abort_flag; u += nb, ++issued) {
+      if (issued >= S && !mbar_wait(&empty[s], ph ^ 1u, p.err)) {
+        abort_flag = 1;
+        break;
+      }
+      uint8_t* dst = smem + p.stage_off + (size_t)s * p.stage_stride;
+      const int y = (int)(u * RB);
+      mbar_arrive_expect_tx(&full[s], bytes);
+      for (int j = 0; j < cm.nbox; ++j) {
+        tma_load_2d_hint(dst + (size_t)j * cm.region, m1, 2 * cm.cpb * j, y, &full[s], policy);
+        if constexpr (NSTREAM == 2)
+          tma_load_2d_hint(dst + cm.half + (size_t)j * cm.region, m2, 2 * cm.cpb * j, y, &full[s], policy);
+      }
+      if (++s == S) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+    for (int64_t i = (issued > S ? issued - S : 0); i < issued; ++i)
+      mbar_wait(&full[(int)(i % S)], (uint32_t)((i / S) & 1), p.err);
+    return;
+  }
+
+  if (warp == ncw + 1) {
+    // ---------------- epilogue: finish the rows of every unit ----------------
+    griddep_wait();
+    const int outs = mv_outputs_per_unit<EPI>(RB);
+    int slot = 0;
+    uint32_t rph = 0;
+    for (int64_t u = cb; u < units; u += nb) {
+      if (!mbar_wait(&rfull[slot], rph, p.err)) {
+        abort_flag = 1;
+        break;
+      }
+      if (abort_flag) break;
+      const float* rb = red + slot * 16 * 8;
+      auto sum = [&](int r) {
+        const int g = r % rg, i = r / rg;
+        float v = 0.0f;
+        for (int w = g * wpg; w < (g + 1) * wpg; ++w) v += rb[w * 8 + i];
+        return v;
+      };
+      // Unit row t is matrix row phi + C (u RB + t).
+      for (int t = lane; t < outs; t += 32) mv_epilogue<EPI>(p, phi + (int64_t)C * u * RB, t, RB, sum, C);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[slot]);
+      if (++slot == RS) {
+        slot = 0;
+        rph ^= 1u;
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  griddep_wait();
+  const int group = warp / wpg, gt = wpg * 32, ti = (warp - group * wpg) * 32 + lane;
+  f2 xr[CPT][8];
+  load_x_phase<CPT, PRO>(p, tid, nct, ti, gt, o, group == 0, red_d, 1, xr);
+  // Byte offset of each of the thread's chunks within a row block (-1: none).
+  int32_t coff[CPT];
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = ti + j * gt;
+    coff[j] = c < cm.uc ? (int32_t)((c / cm.cpb) * cm.region + (c % cm.cpb) * 16) : -1;
+  }
+  const f2 zero2 = make_f2(0.0f, 0.0f);
+  int s = 0, slot = 0;
+  uint32_t ph = 0, rph = 0;
+  bool first_round = true;
+  for (int64_t u = cb; u < units; u += nb) {
+    if (abort_flag || !mbar_wait(&full[s], ph, p.err)) {
+      abort_flag = 1;
+      break;
+    }
+    const uint32_t st = p.stage_off + (uint32_t)s * p.stage_stride;
+    f2 acc[RPT][2];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) acc[i][0] = acc[i][1] = zero2;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      if (coff[j] >= 0) {
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+          const int r = group + rg * i;  // unit row over the streams
+          const uint32_t row = NSTREAM == 2 && r >= RB ? cm.half + (uint32_t)(r - RB) * cm.box_bytes
+                                                       : (uint32_t)r * cm.box_bytes;
+          dot16(*reinterpret_cast<const uint4*>(smem + st + row + (uint32_t)coff[j]), xr[j], acc[i]);
         }
       }
     }

@@ -11,12 +11,14 @@ namespace xpu {
 // Geometry chosen by plan_matvec().
 struct MvPlan {
   bool bulk = false;  // bulk-copy (TMA) kernel, else the general kernel
+  bool ragged = false;  // the bulk pipeline for rows off the 16-byte grid (mv_ragged_kernel)
   int rt = 0;         // bulk: rows per thread per unit; general: rows per unit
   bool grouped = false;  // bulk: row groups in use
   int cpt = 0, ncw = 0, stages = 0;
   dim3 grid, block;
   size_t smem = 0;
-  int64_t off_words = 0;  // general kernel: words from the 16-byte grid to w
+  int64_t off_words = 0;  // general and ragged kernels: words from the 16-byte grid to w
+  MvClassMaps maps{};     // ragged: the phase classes' tensor maps and box geometry
 };
 
 // Chooses the kernel and its geometry; XPU_OK or XPU_EINVAL (with message).
@@ -81,7 +83,10 @@ int launch_mv_impl(const MvParams& p, const MvPlan& plan, const LaunchOpts& o) {
   if (!plan.grouped && plan.rt == RT_ && plan.cpt == CPT_) k = mv_bulk_kernel<RT_, CPT_, EPI, PRO, false>;
 #define XPU_MV_CASE_G(RT_)                                                      \
   if (plan.grouped && plan.rt == RT_ && plan.cpt == 1) k = mv_bulk_kernel<RT_, 1, EPI, PRO, true>;
-    XPU_MV_CASE(1, 1) XPU_MV_CASE(1, 2) XPU_MV_CASE(1, 3) XPU_MV_CASE(1, 4)
+    // One row per unit cannot split into two streams or a row pair.
+    if constexpr (EPI != EPI_QKV && EPI != EPI_FFN) {
+      XPU_MV_CASE(1, 1) XPU_MV_CASE(1, 2) XPU_MV_CASE(1, 3) XPU_MV_CASE(1, 4)
+    }
     XPU_MV_CASE(2, 1) XPU_MV_CASE(2, 2) XPU_MV_CASE(2, 3) XPU_MV_CASE(2, 4)
     XPU_MV_CASE(4, 1) XPU_MV_CASE(4, 2)
     XPU_MV_CASE(8, 1)
@@ -94,6 +99,27 @@ int launch_mv_impl(const MvParams& p, const MvPlan& plan, const LaunchOpts& o) {
     }
     XPU_TRY_CUDA(ensure_smem_attr((const void*)k, plan.smem));
     XPU_TRY_CUDA(launch_ex(k, plan.grid, plan.block, plan.smem, o, p));
+  } else if (plan.ragged) {
+    void (*r)(MvParams, MvClassMaps) = nullptr;
+#define XPU_MVR_CASE(RT_, CPT_)                                                 \
+  if (!plan.grouped && plan.rt == RT_ && plan.cpt == CPT_) r = mv_ragged_kernel<RT_, CPT_, EPI, PRO, false>;
+#define XPU_MVR_CASE_G(RT_)                                                     \
+  if (plan.grouped && plan.rt == RT_ && plan.cpt == 1) r = mv_ragged_kernel<RT_, 1, EPI, PRO, true>;
+    if constexpr (EPI != EPI_QKV && EPI != EPI_FFN) {
+      XPU_MVR_CASE(1, 1) XPU_MVR_CASE(1, 2) XPU_MVR_CASE(1, 3) XPU_MVR_CASE(1, 4)
+    }
+    XPU_MVR_CASE(2, 1) XPU_MVR_CASE(2, 2) XPU_MVR_CASE(2, 3) XPU_MVR_CASE(2, 4)
+    XPU_MVR_CASE(4, 1) XPU_MVR_CASE(4, 2)
+    XPU_MVR_CASE(8, 1)
+    XPU_MVR_CASE_G(1) XPU_MVR_CASE_G(2) XPU_MVR_CASE_G(4) XPU_MVR_CASE_G(8)
+#undef XPU_MVR_CASE
+#undef XPU_MVR_CASE_G
+    if (!r) {
+      set_error("matvecQ8: no ragged kernel for rpt=%d cpt=%d", plan.rt, plan.cpt);
+      return XPU_EINVAL;
+    }
+    XPU_TRY_CUDA(ensure_smem_attr((const void*)r, plan.smem));
+    XPU_TRY_CUDA(launch_ex(r, plan.grid, plan.block, plan.smem, o, p, plan.maps));
   } else {
     void (*g)(MvParams, int64_t) = mv_gen_kernel<2, EPI, PRO>;
     XPU_TRY_CUDA(ensure_smem_attr((const void*)g, plan.smem));

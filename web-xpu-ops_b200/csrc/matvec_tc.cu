@@ -613,20 +613,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ------------------------------------------------------------------- host --
-PFN_cuTensorMapEncodeTiled_v12000 encoder() {
-  static std::once_flag once;
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    cudaGetLastError();
-  });
-  return fn;
-}
-
 std::atomic<int> g_matvec_path{XPU_MATVEC_AUTO};
 
 }  // namespace
@@ -687,7 +673,7 @@ static int weight_map(const TcMapKey& key, CUtensorMap* out) {
         return XPU_OK;
       }
   }
-  auto enc = encoder();
+  auto enc = tensor_map_encoder();
   XPU_REQUIRE(enc, XPU_ECUDA, "matvecQ8: cuTensorMapEncodeTiled is not available");
   const cuuint64_t dims[3] = {(cuuint64_t)(4 * key.W), (cuuint64_t)key.N, (cuuint64_t)key.count};
   const cuuint64_t strides[2] = {(cuuint64_t)(4 * key.W), (cuuint64_t)(4 * key.mat_stride)};
