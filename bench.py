@@ -438,66 +438,116 @@ def run_ours(args, rank, world, local):
 def run_target_gemv(torch, ops, weights, scales, x, R, K, sp, stream_gbs):
     """The BASELINE target: single matvecQ8 GEMVs, each its own launch (no
     fusion), 28672 x 8192 (matrices of the stack) and 8192 x 28672 (eight
-    fresh matrices), rotating over the matrices so that L2 never holds the
-    weights being read.  CUDA events on the launching stream.  Each shape is
-    timed under the library's default choice (XPU_MATVEC_AUTO) and on each
-    path pinned, and the entry names the kernel AUTO ran."""
+    fresh matrices), plus config 2's rows that are not whole 16-byte slots,
+    11008 x 4097 and 8192 x 28676, rotating over the matrices so that L2 never
+    holds the weights being read.  CUDA events on the launching stream.  The
+    aligned shapes are timed under the library's default choice
+    (XPU_MATVEC_AUTO) and on each path pinned; every entry names the kernel
+    AUTO ran and adds `graph_us`, the same launches replayed from a CUDA graph
+    (no host submission between them), which separates the fixed cost of a
+    launch from the kernel's streaming rate."""
     from xpuops.synth import tensor_seed
 
     peak, _ = measured_peaks()
     out = {}
-    W = K // 4
-    y = torch.empty(R, dtype=torch.float32, device="cuda")
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
 
     def time_launches(launch, n, reps=5):
         for i in range(n):
-            launch(i)
+            launch(i, sp)
         torch.cuda.synchronize()
         ev[0].record()
         for _ in range(reps):
             for i in range(n):
-                launch(i)
+                launch(i, sp)
         ev[1].record()
         torch.cuda.synchronize()
         return ev[0].elapsed_time(ev[1]) / 1e3 / (reps * n)
 
-    def entry(N, Kx, launch, n):
+    def time_graph(launch, n, reps=5):
+        g = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream()
+        with torch.cuda.stream(cs):
+            with torch.cuda.graph(g, stream=cs):
+                for _ in range(reps):
+                    for i in range(n):
+                        launch(i, cs.cuda_stream)
+        g.replay()
+        torch.cuda.synchronize()
+        ev[0].record()
+        g.replay()
+        ev[1].record()
+        torch.cuda.synchronize()
+        t = ev[0].elapsed_time(ev[1]) / 1e3 / (reps * n)
+        del g
+        return t
+
+    def fig(b, t):
+        return {"us": round(t * 1e6, 2), "GBs": round(b / t / 1e9, 1), "frac": round(b / t / 1e9 / peak, 4),
+                "frac_stream_probe": round(b / t / 1e9 / stream_gbs, 4),
+                "frac_spec": round(b / t / 1e9 / SPEC_GBS, 4)}
+
+    def kernel_name(N, Kx):
+        Wx = (Kx + 3) // 4
+        if Wx % 4 == 0:
+            return "mv_tc_kernel" if tensor_cores_serve(1, N, Kx) else "mv_bulk_kernel"
+        # the planner's rule for rows off the 16-byte grid (csrc/matvec.cu)
+        uc = (Wx + 6) // 4
+        ncw = min(max(-(-uc // 32), 1), 16)
+        cpt = -(-uc // (32 * ncw))
+        if cpt >= 4:
+            cpt = -(-uc // (32 * 14))
+        return "mv_ragged_kernel" if N * Wx * 4 >= (16 << 20) and cpt <= 4 else "mv_gen_kernel"
+
+    def entry(N, Kx, launch, n, paths=True):
         b = algorithmic_bytes(N, Kx, 1)
         res = {}
         for name, path in (("auto", ops.MATVEC_AUTO), ("cuda_cores", ops.MATVEC_CUDA_CORES),
                            ("tensor_cores", ops.MATVEC_TENSOR_CORES)):
+            if name != "auto" and not paths:
+                continue
             ops.setMatvecPath(path)
             try:
-                t = time_launches(launch, n)
+                res[name] = fig(b, time_launches(launch, n))
             finally:
                 ops.setMatvecPath(ops.MATVEC_AUTO)
-            res[name] = {"us": round(t * 1e6, 2), "GBs": round(b / t / 1e9, 1), "frac": round(b / t / 1e9 / peak, 4),
-                         "frac_stream_probe": round(b / t / 1e9 / stream_gbs, 4),
-                         "frac_spec": round(b / t / 1e9 / SPEC_GBS, 4)}
-        on_tc = tensor_cores_serve(1, N, Kx)
-        res["auto"]["kernel"] = "mv_tc_kernel" if on_tc else "mv_bulk_kernel"
+        res["auto"]["kernel"] = kernel_name(N, Kx)
+        res["auto"]["graph_us"] = round(time_graph(launch, n) * 1e6, 2)
+        res["auto"]["graph_frac"] = round(b / (res["auto"]["graph_us"] * 1e-6) / 1e9 / peak, 4)
         return res
 
+    def fresh(N2, K2, count, seed):
+        W2 = (K2 + 3) // 4
+        w2 = torch.empty(count * N2 * W2, dtype=torch.int32, device="cuda")
+        s2 = torch.empty(count * N2, dtype=torch.float32, device="cuda")
+        tmp = torch.empty(N2 * K2, dtype=torch.float32, device="cuda")
+        for i in range(count):
+            ops.fill_normal_dev(tmp, N2 * K2, tensor_seed(seed, i), 0.0, 0.02, stream=sp)
+            ops.quantizePackQ8_dev(tmp, N2, K2, w2.data_ptr() + 4 * i * N2 * W2, s2.data_ptr() + 4 * i * N2,
+                                   stream=sp)
+        del tmp
+        x2 = torch.empty(K2, dtype=torch.float32, device="cuda")
+        ops.fill_normal_dev(x2, K2, tensor_seed(seed + 1, 0), stream=sp)
+        y2 = torch.empty(N2, dtype=torch.float32, device="cuda")
+
+        def launch(i, st):
+            ops.matvecQ8_dev(w2.data_ptr() + 4 * i * N2 * W2, s2.data_ptr() + 4 * i * N2, x2, N2, K2, y2, st)
+        return launch, (w2, s2, x2, y2)
+
+    W = K // 4
+    y = torch.empty(R, dtype=torch.float32, device="cuda")
     n = min(16, weights.numel() // (R * W))
-    out[f"{R}x{K}"] = entry(R, K, lambda i: ops.matvecQ8_dev(weights.data_ptr() + 4 * i * R * W,
-                                                             scales.data_ptr() + 4 * i * R, x, R, K, y, sp), n)
-    N2, K2 = K, R  # the other orientation
-    W2 = K2 // 4
-    w2 = torch.empty(8 * N2 * W2, dtype=torch.int32, device="cuda")
-    s2 = torch.empty(8 * N2, dtype=torch.float32, device="cuda")
-    tmp = torch.empty(N2 * K2, dtype=torch.float32, device="cuda")
-    for i in range(8):
-        ops.fill_normal_dev(tmp, N2 * K2, tensor_seed(2, i), 0.0, 0.02, stream=sp)
-        ops.quantizePackQ8_dev(tmp, N2, K2, w2.data_ptr() + 4 * i * N2 * W2, s2.data_ptr() + 4 * i * N2, stream=sp)
-    del tmp
-    x2 = torch.empty(K2, dtype=torch.float32, device="cuda")
-    ops.fill_normal_dev(x2, K2, tensor_seed(3, 0), stream=sp)
-    y2 = torch.empty(N2, dtype=torch.float32, device="cuda")
-    out[f"{N2}x{K2}"] = entry(N2, K2, lambda i: ops.matvecQ8_dev(w2.data_ptr() + 4 * i * N2 * W2,
-                                                                s2.data_ptr() + 4 * i * N2, x2, N2, K2, y2, sp), 8)
+    out[f"{R}x{K}"] = entry(R, K, lambda i, st: ops.matvecQ8_dev(weights.data_ptr() + 4 * i * R * W,
+                                                                 scales.data_ptr() + 4 * i * R, x, R, K, y, st), n)
+    for (N2, K2, count, seed, paths) in ((K, R, 8, 2, True), (11008, 4097, 16, 20, False),
+                                         (8192, 28676, 8, 22, False)):
+        launch, keep = fresh(N2, K2, count, seed)
+        out[f"{N2}x{K2}"] = entry(N2, K2, launch, count, paths)
+        del keep
     out["note"] = ("each GEMV its own launch (xpu_matvec_q8_dev), rotating over 8-16 matrices; auto = the "
-                   "library's default path choice, whose kernel is named; frac of measured HBM peak")
+                   "library's default path choice, whose kernel is named; frac of measured HBM peak; graph_us = "
+                   "the same launches replayed from one CUDA graph; 11008x4097 and 8192x28676 (config 2, rows off "
+                   "the 16-byte grid) have no tensor-core path")
     return out
 
 
