@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--oracle-tokens", type=int, default=4)
+    ap.add_argument("--gemv", metavar="NxK", default=None,
+                    help="time single matvecQ8 launches of one N x K shape instead (a profiling case)")
 
     ap.add_argument("--rows", type=int, default=ROWS, help=argparse.SUPPRESS)
     ap.add_argument("--cols", type=int, default=COLS, help=argparse.SUPPRESS)
@@ -968,9 +970,60 @@ def reference_sample(R, K, threads):
     return packed, sc, orc.fill_normal(K, tensor_seed(1, 0))
 
 
+def run_gemv(args):
+    """`--gemv NxK`: single matvecQ8 launches (xpu_matvec_q8_dev, library
+    default path) of one shape, rotating over enough matrices (up to 16, at
+    least 1 GB) that L2 never holds the weights read; --warmup rounds over the
+    matrices untimed, then --steps timed rounds.  Prints one JSON line.  This
+    is the small, self-contained case the kernel profiles are captured on."""
+    import torch
+
+    from xpuops import ops
+    from xpuops.synth import tensor_seed
+
+    N, K = (int(v) for v in args.gemv.lower().split("x"))
+    W = (K + 3) // 4
+    torch.cuda.set_device(0)
+    sp = torch.cuda.current_stream().cuda_stream
+    count = max(2, min(16, -(-(1 << 30) // (4 * N * W))))
+    w = torch.empty(count * N * W, dtype=torch.int32, device="cuda")
+    sc = torch.empty(count * N, dtype=torch.float32, device="cuda")
+    tmp = torch.empty(N * K, dtype=torch.float32, device="cuda")
+    for i in range(count):
+        ops.fill_normal_dev(tmp, N * K, tensor_seed(30, i), 0.0, 0.02, stream=sp)
+        ops.quantizePackQ8_dev(tmp, N, K, w.data_ptr() + 4 * i * N * W, sc.data_ptr() + 4 * i * N, stream=sp)
+    del tmp
+    x = torch.empty(K, dtype=torch.float32, device="cuda")
+    ops.fill_normal_dev(x, K, tensor_seed(31, 0), stream=sp)
+    y = torch.empty(N, dtype=torch.float32, device="cuda")
+
+    def rounds(n):
+        for _ in range(n):
+            for i in range(count):
+                ops.matvecQ8_dev(w.data_ptr() + 4 * i * N * W, sc.data_ptr() + 4 * i * N, x, N, K, y, sp)
+
+    rounds(max(1, args.warmup))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    rounds(args.steps)
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / (args.steps * count)
+    b = algorithmic_bytes(N, K, 1)
+    peak, _ = measured_peaks()
+    print(json.dumps({"metric": "matvecQ8 single GEMV, each its own launch", "workload": f"{N}x{K}",
+                      "matrices": count, "launches": args.steps * count, "us": round(t * 1e6, 2),
+                      "GBs": round(b / t / 1e9, 1), "frac": round(b / t / 1e9 / peak, 4),
+                      "bytes_per_launch": b}), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.gemv:
+        run_gemv(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
