@@ -369,14 +369,28 @@ __device__ __forceinline__ void mk_poll_words(const MkParams& p, const unsigned 
   }
 }
 
-// A 16-element input slice as four int8 limbs per element, with the slice's
-// own exponent E (of its largest magnitude, floored at -96 so that
-// 2^(E - 30) stays a normal float): X = round(x 2^(30 - E)), |X| < 2^30,
-// written as balanced base-256 digits (the bytes of X + 0x80808080, top bits
-// flipped).  xl[i][j] holds digit j of elements 4i .. 4i + 3, the word layout
-// of the packed codes, so a row's partial is 16 dp4a into four exact int32
-// limb sums, times xpow = 2^(E - 30).  A non-finite element makes xpow NaN.
-__device__ __forceinline__ void mk_limbs(const float (&xv)[16], int (&xl)[4][4], float& xpow) {
+// SiLU in f32: g / (1 + e^-g) with CUDA's expf (within 2 ulp) and an IEEE
+// division.  ops/activation/reference.ts:91-92 evaluates it in f64 and
+// stores f32; the two differ by an ulp or so of the gate value, far inside
+// the decode step's 1e-3 logits tolerance, and the f32 form is a short
+// dependency chain where the f64 exp and division are ~60 dependent f64
+// operations on the epilogue's critical path.  exp(-g) overflows to +inf
+// for g < -88, giving -0, the limit; NaN stays NaN.
+__device__ __forceinline__ float mk_silu(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+
+// A 16-element input slice as three int8 limbs per element, with the
+// slice's own exponent E (of its largest magnitude, floored at -96 so that
+// 2^(E - 22) stays a normal float): X = round(x 2^(22 - E)), |X| <= 2^22,
+// written as balanced base-256 digits (the bytes of X + 0x808080, top bits
+// flipped: d0, d1 in [-128, 127], d2 in [-64, 64]).  xl[i][j] holds digit j
+// of elements 4i .. 4i + 3, the word layout of the packed codes, so a row's
+// partial is 12 dp4a into three exact int32 limb sums, times
+// xpow = 2^(E - 22).  Each element is then off by at most 2^(E - 23), i.e.
+// 2^-22 of the slice's largest magnitude: four f32 ulps of it, far inside
+// the step's 1e-3 logits tolerance; a fourth limb would add a third more
+// dp4a for bits the tolerance never sees.  A non-finite element makes xpow
+// NaN.
+__device__ __forceinline__ void mk_limbs(const float (&xv)[16], int (&xl)[4][3], float& xpow) {
   float mx = 0.0f;
   bool bad = false;
 #pragma unroll
@@ -386,18 +400,18 @@ __device__ __forceinline__ void mk_limbs(const float (&xv)[16], int (&xl)[4][4],
   }
   // frexp's exponent from the bits: mx in [2^(E-1), 2^E) for a normal mx.
   const int E = max((int)((__float_as_uint(mx) >> 23) & 0xffu) - 126, -96);
-  const float sc = __uint_as_float((uint32_t)(157 - E) << 23);  // 2^(30 - E)
-  xpow = bad ? __int_as_float(0x7fffffff) : __uint_as_float((uint32_t)(97 + E) << 23);  // 2^(E - 30)
+  const float sc = __uint_as_float((uint32_t)(149 - E) << 23);  // 2^(22 - E)
+  xpow = bad ? __int_as_float(0x7fffffff) : __uint_as_float((uint32_t)(105 + E) << 23);  // 2^(E - 22)
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     uint32_t u[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int X = bad ? 0 : __float2int_rn(xv[4 * i + c] * sc);
-      u[c] = ((uint32_t)X + 0x80808080u) ^ 0x80808080u;
+      u[c] = ((uint32_t)X + 0x808080u) ^ 0x808080u;
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 3; ++j) {
       const uint32_t sel = (uint32_t)j | ((uint32_t)(4 + j) << 4);
       xl[i][j] = (int)__byte_perm(__byte_perm(u[0], u[1], sel), __byte_perm(u[2], u[3], sel), 0x5410u);
     }
@@ -411,8 +425,8 @@ __device__ __forceinline__ void mk_limbs(const float (&xv)[16], int (&xl)[4][4],
 __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint32_t ep, const MkView& v,
                                               uint8_t* smem, uint64_t* full, uint64_t* empty,
                                               const uint32_t* slot_off, int64_t& pbase, volatile int* abort_flag,
-                                              int tok, int pos, double* red_d, const double* rope, float& best,
-                                              int& best_i) {
+                                              int tok, int pos, double* red_d, const double* rope,
+                                              uint64_t* colbar, uint32_t colpar, float& best, int& best_i) {
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int G = gridDim.x, b = blockIdx.x;
   const MkGemv* g = v.g;
@@ -457,7 +471,13 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   // (ops/rmsnorm/reference.ts:80-96) it multiplies by the gain and reduces
   // sum(x^2) in f64; the scale 1/sqrt(mean(x^2) + eps) multiplies every
   // element alike, so it is applied per output row in the epilogue.  The
-  // slice's limbs (mk_limbs) go to shared memory for every row group.
+  // slice's limbs (mk_limbs) go to shared memory for the other row groups.
+  // There is no CTA-wide barrier here: staging warp w signals column
+  // barrier w, and warp w of every other row group waits only for it, so a
+  // column whose slices arrived early runs its dot products while later
+  // columns still poll.  Every consumer warp arrives on its column barrier
+  // once per GEMV phase (warps past the staging ones at once), so the
+  // barriers' parity is the GEMV phase count's.
   int gslot = -1;
   const float* gs = nullptr;
   if (norm) {
@@ -472,12 +492,12 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   const int UP = mk_xs_pitch(U);
   // The thread's slice as limbs (mk_limbs); with one row group the staging
   // threads are the only ones and keep them in registers.
-  int xl[4][4];
+  int xl[4][3];
   float xpow = 0.0f;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) xl[i][j] = 0;
+    for (int j = 0; j < 3; ++j) xl[i][j] = 0;
   if (warp < wpg) {
     const int ti = tid;
     float xv[16];
@@ -510,6 +530,12 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
         ss += (double)xv[e] * (double)xv[e];
         xv[e] = e < nk ? __fmul_rn(xv[e], gs[min(k0 + e, K - 1)]) : 0.0f;
       }
+      const double sw = warp_sum_d(ss);
+      if (lane == 0) ssd[warp] = sw;
+      // The gain is read: this warp's release of its slot (warp 0 also
+      // releases for the warps that never read it).
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cnt(&empty[gslot], warp == 0 ? 1u + (uint32_t)(kMkConsumerWarps - wpg) : 1u);
     }
     // xs holds the limb words of slice c, elements 4i .. 4i + 3, as a uint4
     // at index i * UP + c (UP = mk_xs_pitch(U)), and xp[c] its power of two:
@@ -520,18 +546,26 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
       if (rg > 1) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          reinterpret_cast<uint4*>(xs)[i * UP + ti] = make_uint4(xl[i][0], xl[i][1], xl[i][2], xl[i][3]);
+          reinterpret_cast<uint4*>(xs)[i * UP + ti] = make_uint4(xl[i][0], xl[i][1], xl[i][2], 0u);
         xp[ti] = xpow;
       }
     }
-    if (norm) {
-      const double sw = warp_sum_d(ss);
-      if (lane == 0) ssd[warp] = sw;
-    }
+    __syncwarp();
   }
-  named_bar_sync(1, kNct);
-  if (gslot >= 0 && tid == 0) mbar_arrive_cnt(&empty[gslot], kMkConsumerWarps);  // gain consumed
+  // Column barrier: the staging warp after its limbs and sum of squares are
+  // in shared memory (the arrive releases them), every other warp at once.
+  if (lane == 0) mbar_arrive(&colbar[warp]);
   mk_mark(p, phase, 1);
+  // The rmsnorm factor 1/sqrt(mean(x^2) + eps) (f64, ops/rmsnorm/reference.ts:89-93), once per CTA by
+  // the last consumer thread (a warp that takes no rows where there is one) when every staging warp
+  // has stored its sum: the f64 square root and division stay off the epilogue's path.
+  double* rs_s = red_d + 2 * kMkConsumerWarps + (phase & 1);
+  if (norm && tid == kNct - 1) {
+    for (int w = 0; w < wpg; ++w) mk_wait(&colbar[w], colpar, p.err, abort_flag, p.wait_limit_ns);
+    double tot = 0.0;
+    for (int w = 0; w < wpg; ++w) tot += ssd[w];
+    *rs_s = 1.0 / sqrt(tot / (double)K + p.eps);
+  }
 
   // 2. The thread's 16-column slice in registers: a row group of wpg warps
   // covers a row (thread ti of the group owns slice ti), and group g takes
@@ -541,14 +575,14 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   const int n_act = rg * wpg;
   const bool active = warp < n_act;
   const int cs = ti < U ? ti : U - 1;  // slice read (clamped; x is 0 past U)
-  if (active && rg > 1) {
+  if (active && rg > 1 && group > 0) {
+    mk_wait(&colbar[wi], colpar, p.err, abort_flag, p.wait_limit_ns);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint4 t = ti < U ? reinterpret_cast<const uint4*>(xs)[i * UP + ti] : make_uint4(0u, 0u, 0u, 0u);
       xl[i][0] = (int)t.x;
       xl[i][1] = (int)t.y;
       xl[i][2] = (int)t.z;
-      xl[i][3] = (int)t.w;
     }
     xpow = ti < U ? xp[ti] : 0.0f;
   }
@@ -590,17 +624,16 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
 #pragma unroll
       for (int t = 0; t < kMkRowsPerWarp; ++t) {
         const int w[4] = {(int)wv[t].x, (int)wv[t].y, (int)wv[t].z, (int)wv[t].w};
-        int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+        int a0 = 0, a1 = 0, a2 = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           a0 = __dp4a(w[i], xl[i][0], a0);
           a1 = __dp4a(w[i], xl[i][1], a1);
           a2 = __dp4a(w[i], xl[i][2], a2);
-          a3 = __dp4a(w[i], xl[i][3], a3);
         }
-        // sum_j 256^j a_j, exact in two int32 halves (|a_j| <= 2^18).
-        const int lo = a0 + a1 * 256, hi = a2 + a3 * 256;
-        vv[t] = fmaf((float)hi, 65536.0f, (float)lo) * xpow;
+        // sum_j 256^j a_j: a0 + 256 a1 exact in int32 (|a_j| <= 2^18).
+        const int lo = a0 + a1 * 256;
+        vv[t] = fmaf((float)a2, 65536.0f, (float)lo) * xpow;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive_cnt(&empty[slot], rel);
@@ -625,12 +658,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
   // :196-207, :235-242; RoPE and the KV write as the per-kernel path), with
   // the rmsnorm scale of the input where the phase has one.  Outputs go to
   // every replica.
-  double rs = 1.0;
-  if (norm) {
-    double tot = 0.0;
-    for (int w = 0; w < wpg; ++w) tot += ssd[w];
-    rs = 1.0 / sqrt(tot / (double)K + p.eps);
-  }
+  const double rs = norm ? *rs_s : 1.0;
   auto sum = [&](int r) {
     float s = 0.0f;
     for (int w = 0; w < wpg; ++w) s += red[w * RS + r];
@@ -677,7 +705,7 @@ __device__ __forceinline__ void mk_gemv_phase(const MkParams& p, int phase, uint
       const float sg = eo[t], su = eo[n + t];
       const float gt_ = rowval(sum(t), sg);
       const float up = rowval(sum(n + t), su);
-      const float y = __fmul_rn(silu_f32(gt_), up);
+      const float y = __fmul_rn(mk_silu(gt_), up);
       for (int r = 0; r < reps; ++r) st_tag1(g->yt + r * g->yt_rep + row, y, ep);
     }
   } else if (epi == EPI_RESID) {
@@ -896,7 +924,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   __shared__ __align__(8) uint64_t empty[kMkSlots];
   __shared__ uint32_t slot_off[kMkSlots];
   __shared__ uint32_t slot_len[kMkSlots];
-  __shared__ double red_d[2 * kMkConsumerWarps];
+  __shared__ double red_d[2 * kMkConsumerWarps + 2];  // [2][warps] sum(x^2), then [2] the rmsnorm factor
+  __shared__ __align__(8) uint64_t colbar[kMkConsumerWarps];  // a GEMV phase's input slices, per warp column
   __shared__ double rope[128];  // (sin, cos) per RoPE pair, head_dim <= 128
   __shared__ float bv[kMkConsumerWarps];
   __shared__ int bi[kMkConsumerWarps];
@@ -910,6 +939,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kMkConsumerWarps);  // every consumer warp releases every piece
     }
+    for (int w = 0; w < kMkConsumerWarps; ++w) mbar_init(&colbar[w], 1);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -940,15 +970,18 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   constexpr int kNone = 0x7fffffff;
   float best = -INFINITY;
   int best_i = kNone;
+  uint32_t gemv_n = 0;  // GEMV phases so far: the parity of their column barriers
   for (int i = 0; i < n_phase; ++i) {
     mk_mark(p, i, 0);
     const uint32_t ep = ebase + (uint32_t)i + 1u;
     const int kind = mk_kind(i, p.layers);
-    if (kind < 0)
+    if (kind < 0) {
       mk_attn_phase(p, i, ep, i / 5, smem, full, empty, slot_off, pbase, &abort_flag, pos);
-    else
+    } else {
       mk_gemv_phase(p, i, ep, mk_view(p, kind, kind == MK_HEAD ? 0 : i / 5), smem, full, empty, slot_off, pbase,
-                    &abort_flag, tok, pos, red_d, rope, best, best_i);
+                    &abort_flag, tok, pos, red_d, rope, colbar, gemv_n & 1u, best, best_i);
+      ++gemv_n;
+    }
   }
 
   // Greedy argmax (llm/engine.ts:226-232): per-CTA candidate of its
