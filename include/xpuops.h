@@ -228,9 +228,11 @@ XPU_API int xpu_gqa_decode_dev(const float* q, const float* k_cache, const float
  * floats, or contexts needing more position splits than that array holds
  * (about 33,000 positions at H = 32, D = 64), are rejected (XPU_EINVAL);
  * shapes that fit fewer position splits than xpu_gqa_decode_dev uses run
- * with fewer splits (equal up to f32 summation order).  The first call on a device looks up the array's device
- * address; make it before any stream capture.  All calls share the array, so
- * calls whose kernels overlap on the GPU race. */
+ * with fewer splits (equal up to f32 summation order).  The first call on
+ * a device looks up the array's device address and keeps it for the life
+ * of the process: make it before any stream capture, and do not reset the
+ * device (cudaDeviceReset) after it.  All calls share the array, so calls
+ * whose kernels overlap on the GPU race. */
 XPU_API int xpu_gqa_decode_noalloc(const float* q, const float* k_cache, const float* v_cache,
                                    int32_t H, int32_t kv_heads, int32_t D, int32_t S,
                                    int32_t s_eff, float scale, float* out, void* stream);

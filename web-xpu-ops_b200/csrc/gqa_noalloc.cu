@@ -32,7 +32,10 @@ static __device__ __align__(256) float g_gqa_noalloc_scratch[kScratchFloats];
 
 // In host code `g_gqa_noalloc_scratch` only stands for the symbol; its
 // device address comes from cudaGetSymbolAddress, queried once per device
-// with that device current and cached.
+// with that device current and cached for the life of the process.  A
+// cudaDeviceReset after the first call is not supported: it unloads the
+// module, and the cached address would then name freed memory of the old
+// context (the library itself never resets a device).
 int scratch_address(float** out) {
   static std::mutex mu;
   static std::unordered_map<int, float*> cache;
