@@ -116,8 +116,10 @@ struct MkParams {
 
 // Replicas of every vector that all CTAs read: CTA b polls replica
 // b % kMkReps, so a line of a vector is polled by ~G / kMkReps CTAs instead
-// of all of them (the polls of one line queue at one L2 slice).
-constexpr int kMkReps = 16;
+// of all of them (the polls of one line queue at one L2 slice), at the cost
+// of kMkReps stores per output.  Measured on config 4 (ms per token): 1
+// replica 0.803, 2 0.771, 4 0.744, 8 0.755, 16 0.762.
+constexpr int kMkReps = 4;
 constexpr int kMkConsumerWarps = 15;  // + 1 producer warp = 512 threads: 128 registers each
 constexpr int kMkThreads = 32 * (kMkConsumerWarps + 1);
 constexpr int kMkRowsPerWarp = 8;  // rows a row group takes from one piece
