@@ -363,6 +363,7 @@ def run_ours(args, rank, world, local):
         target = run_target_gemv(torch, ops, weights, scales, x, R, K, sp, probe["bandwidth"] / 1e9)
 
     quant = run_quantize(torch, ops, sp) if world == 1 and rank == 0 else None
+    small = run_small_configs(torch, ops, sp) if world == 1 and rank == 0 else None
     lm_head = run_lm_head(args, torch, ops, dist, rank, world, sp, barrier, max_over_ranks)
 
     decode = None
@@ -422,6 +423,7 @@ def run_ours(args, rank, world, local):
             "cpu_baseline": cpu,
             "decode": decode,
             "quantize": quant,
+            "configs_1_3": small,
             "lm_head": lm_head,
         }
         print(json.dumps(line), flush=True)
@@ -640,6 +642,124 @@ def run_quantize(torch, ops, sp):
             "bit_exact_vs_oracle": exact,
             "cpu_baseline": {"us": round(ct * 1e6, 1), "GBs": round(b / ct / 1e9, 4), "cores": 1, "kind": "port",
                              "sample": "the oracle's quantize + pack of the same matrix, one pass, one thread"}}
+
+
+def run_small_configs(torch, ops, sp):
+    """BASELINE configs 1 and 3 as GPU launches with the oracle beside them
+    (one thread, as JavaScript runs reference.ts): config 1's single
+    4096 x 4096 matvecQ8, and config 3's decoder-layer GEMVs (hidden 2048,
+    16 query / 4 KV heads of 128: q 2048 x 2048, k and v 512 x 2048, o
+    2048 x 2048, gate/up 5632 x 2048 as one matvecQ8Ffn, down 2048 x 5632).
+    Each GPU figure rotates over 8 copies of its matrices (past L2) with
+    CUDA events around 5 rounds; each result is checked against the oracle
+    within the matvecQ8 bound."""
+    import oracle.oracle as orc
+    from xpuops.synth import tensor_seed
+
+    peak, _ = measured_peaks()
+
+    def weights(N, K, seed, copies=8):
+        W = (K + 3) // 4
+        w = torch.empty(copies, N * W, dtype=torch.int32, device="cuda")
+        sc = torch.empty(copies, N, dtype=torch.float32, device="cuda")
+        tmp = torch.empty(N * K, dtype=torch.float32, device="cuda")
+        for i in range(copies):
+            ops.fill_normal_dev(tmp, N * K, tensor_seed(seed, i), 0.0, 0.02, stream=sp)
+            ops.quantizePackQ8_dev(tmp, N, K, w[i], sc[i], stream=sp)
+        return w, sc
+
+    def timed(launch, reps=5, copies=8):
+        for i in range(copies):
+            launch(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for i in range(copies):
+                launch(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / (reps * copies)
+
+    out = {}
+    # Config 1.
+    N = K = 4096
+    w, sc = weights(N, K, 50)
+    x = torch.empty(K, dtype=torch.float32, device="cuda")
+    ops.fill_normal_dev(x, K, tensor_seed(51, 0), stream=sp)
+    y = torch.empty(N, dtype=torch.float32, device="cuda")
+    t = timed(lambda i: ops.matvecQ8_dev(w[i], sc[i], x, N, K, y, sp))
+    wh, sh, xh = w[7].cpu().numpy().view(np.uint32), sc[7].cpu().numpy(), x.cpu().numpy()
+    c0 = time.perf_counter()
+    want = orc.matvec_q8(wh, sh, xh, N, K)
+    ct = time.perf_counter() - c0
+    ops.matvecQ8_dev(w[7], sc[7], x, N, K, y, sp)
+    got = y.cpu().numpy()
+    lim = 1e-5 * orc.matvec_q8_bound(wh, sh, xh, N, K) + np.spacing(np.abs(want).astype(np.float32))
+    ok = bool(np.all(np.abs(got.astype(np.float64) - want) <= lim))
+    b = algorithmic_bytes(N, K, 1)
+    out["config1"] = {"workload": "matvecQ8 4096 x 4096 (seeded N(0, 0.02^2) weights, x ~ N(0, 1))",
+                      "us": round(t * 1e6, 2), "GBs": round(b / t / 1e9, 1), "frac": round(b / t / 1e9 / peak, 4),
+                      "within_bound_of_oracle": ok,
+                      "cpu_baseline": {"us": round(ct * 1e6, 1), "GBs": round(b / ct / 1e9, 4), "cores": 1,
+                                       "kind": "port", "sample": "the oracle's matvecQ8 of the same matrix, once"}}
+    del w, sc
+    # Config 3.
+    h, kv, ffn = 2048, 512, 5632
+    layer = [("q", h, h), ("k", kv, h), ("v", kv, h), ("o", h, h), ("gate", ffn, h), ("up", ffn, h),
+             ("down", h, ffn)]
+    mats = {name: weights(n, k, 60 + j) for j, (name, n, k) in enumerate(layer)}
+    xs = {k: torch.empty(k, dtype=torch.float32, device="cuda") for k in (h, ffn)}
+    for k, v in xs.items():
+        ops.fill_normal_dev(v, k, tensor_seed(70, k), stream=sp)
+    ys = {n: torch.empty(n, dtype=torch.float32, device="cuda") for n in (h, kv, ffn)}
+
+    rows = {name: n for name, n, _ in layer}
+
+    def layer_launch(i, st=None):
+        st = st or sp
+        for name in ("q", "k", "v", "o"):
+            ops.matvecQ8_dev(mats[name][0][i], mats[name][1][i], xs[h], rows[name], h, ys[rows[name]], st)
+        ops.matvecQ8Ffn_dev(mats["gate"][0][i], mats["gate"][1][i], mats["up"][0][i], mats["up"][1][i], xs[h], ffn,
+                            h, ys[ffn], st)
+        ops.matvecQ8_dev(mats["down"][0][i], mats["down"][1][i], xs[ffn], h, ffn, ys[h], st)
+
+    t = timed(layer_launch)
+    # The same launches replayed from one CUDA graph (no host submission
+    # between them).
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(g, stream=cs):
+            for _ in range(5):
+                for i in range(8):
+                    layer_launch(i, cs.cuda_stream)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    tg = e0.elapsed_time(e1) / 1e3 / 40
+    del g
+    b = sum(algorithmic_bytes(n, k, 1) for _, n, k in layer)
+    host = {name: (m[0][7].cpu().numpy().view(np.uint32), m[1][7].cpu().numpy()) for name, m in mats.items()}
+    xh = {k: v.cpu().numpy() for k, v in xs.items()}
+    c0 = time.perf_counter()
+    for name, n, k in layer:
+        if name == "gate":
+            orc.matvec_q8_ffn(host["gate"][0], host["gate"][1], host["up"][0], host["up"][1], xh[h], n, k)
+        elif name != "up":
+            orc.matvec_q8(host[name][0], host[name][1], xh[k], n, k)
+    ct = time.perf_counter() - c0
+    out["config3"] = {"workload": "one decoder layer's decode GEMVs: q 2048x2048, k/v 512x2048, o 2048x2048, "
+                                  "gate/up 5632x2048 (one matvecQ8Ffn), down 2048x5632; 6 launches",
+                      "us": round(t * 1e6, 2), "GBs": round(b / t / 1e9, 1), "frac": round(b / t / 1e9 / peak, 4),
+                      "graph_us": round(tg * 1e6, 2), "graph_frac": round(b / tg / 1e9 / peak, 4),
+                      "cpu_baseline": {"us": round(ct * 1e6, 1), "GBs": round(b / ct / 1e9, 4), "cores": 1,
+                                       "kind": "port", "sample": "the oracle's GEMVs of the same layer, once"}}
+    return out
 
 
 def cpu_baseline(weights, scales, x, R, K, seconds):
