@@ -196,6 +196,51 @@ def build_stack(torch, ops, rank, world, matrices, stream):
     return weights, scales, x, R
 
 
+def check_stack_output(torch, dist, ops, rank, world, weights, scales, x, M, R, K, y_dev, to_host):
+    """The last timed step's output against the oracle
+    (ops/matvec/reference.ts:117-131): 8 rows of this rank's shard in the
+    first and the last matrix, from the weights this GPU streamed, checked
+    in every rank's copy of the output (at N > 1 the rows other GPUs'
+    epilogues wrote into it) within 1e-5 * |scale| * sum|code * x| plus one
+    f32 ulp."""
+    import oracle.oracle as orc
+
+    W = K // 4
+    xh = x.cpu().numpy()
+    mine = []
+    for m in sorted({0, M - 1}):
+        for i in np.linspace(0, R - 1, 8).astype(np.int64):
+            r = m * R + int(i)
+            wrow = weights[r * W:(r + 1) * W].cpu().numpy().view(np.uint32)
+            srow = scales[r:r + 1].cpu().numpy()
+            want = float(orc.matvec_q8(wrow, srow, xh, 1, K)[0])
+            bound = float(orc.matvec_q8_bound(wrow, srow, xh, 1, K)[0])
+            mine.append((m * world * R + rank * R + int(i), want, bound))
+    rows = [mine]
+    if world > 1:
+        rows = [None] * world
+        dist.all_gather_object(rows, mine)
+    yh = torch.empty(world * M * R, dtype=torch.float32).pin_memory()
+    to_host(yh, y_dev)
+    torch.cuda.synchronize()
+    yh = yh.numpy()
+    worst, n = 0.0, 0
+    for part in rows:
+        for idx, want, bound in part:
+            lim = 1e-5 * bound + float(np.spacing(np.float32(abs(want))))
+            worst = max(worst, abs(float(yh[idx]) - want) / lim)
+            n += 1
+    verdicts = [(worst, n)]
+    if world > 1:
+        verdicts = [None] * world
+        dist.all_gather_object(verdicts, (worst, n))
+    w = max(v[0] for v in verdicts)
+    return {"rows_checked": int(sum(v[1] for v in verdicts)), "within_bound": bool(w <= 1.0),
+            "worst_error_over_bound": round(w, 6),
+            "what": "sampled rows of the first and last matrix of every shard, against the oracle, read from "
+                    "every GPU's copy of the output"}
+
+
 def run_ours(args, rank, world, local):
     import torch
     import torch.distributed as dist
@@ -273,15 +318,17 @@ def run_ours(args, rank, world, local):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     g_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t0.record(stream)
+    last = None
     for i in range(args.steps):
         g_events[i][0].record(stream)
-        gemv()
+        last = gemv()
         g_events[i][1].record(stream)
     t1.record(stream)
     barrier()
     clocks = sampler.stop() if sampler else None
     total_ms = max_over_ranks(t0.elapsed_time(t1))
     gemv_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in g_events))
+    output_check = check_stack_output(torch, dist, ops, rank, world, weights, scales, x, M, R, K, last, to_host)
 
     # The same stack with an NCCL all-gather after each GEMV (the unfused
     # form; comparison only).
@@ -423,6 +470,7 @@ def run_ours(args, rank, world, local):
             "cpu_baseline": cpu,
             "decode": decode,
             "quantize": quant,
+            "output_check": output_check,
             "configs_1_3": small,
             "lm_head": lm_head,
         }
