@@ -844,21 +844,32 @@ __device__ __forceinline__ void mk_attn_phase(const MkParams& p, int phase, uint
     }
     named_bar_sync(1, kNct);
     mk_mark(p, phase, 5);
-    // P.V, one (head, dim) output per thread over the split's positions
-    // (four partial sums), straight to the split's partial words.
-    for (int o = tid; o < Gq * hd; o += kNct) {
-      const int h = o / hd, d = o - h * hd;
+    // P.V, two adjacent (head, dim) outputs per thread over the split's
+    // positions (two partial sums each), straight to the split's partial
+    // words: Gq * hd / 2 pairs fit the consumer threads in one round where
+    // Gq * hd outputs would take two (8 heads of 64: 256 pairs against 512
+    // outputs for 480 threads).  head_dim is even, so a pair is one 8-byte
+    // load of V and one 16-byte store of words.
+    const int hd2 = hd / 2;
+    for (int o2 = tid; o2 < Gq * hd2; o2 += kNct) {
+      const int h = o2 / hd2, d = 2 * (o2 - h * hd2);
       const float* pr = p_s + h * cm;
-      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+      float2 a = make_float2(0.0f, 0.0f), c = make_float2(0.0f, 0.0f);
       int j = 0;
-      for (; j + 3 < nn; j += 4) {
-        a0 = fmaf(pr[j], v_s[(size_t)j * hd + d], a0);
-        a1 = fmaf(pr[j + 1], v_s[(size_t)(j + 1) * hd + d], a1);
-        a2 = fmaf(pr[j + 2], v_s[(size_t)(j + 2) * hd + d], a2);
-        a3 = fmaf(pr[j + 3], v_s[(size_t)(j + 3) * hd + d], a3);
+      for (; j + 1 < nn; j += 2) {
+        const float2 v0 = *reinterpret_cast<const float2*>(v_s + (size_t)j * hd + d);
+        const float2 v1 = *reinterpret_cast<const float2*>(v_s + (size_t)(j + 1) * hd + d);
+        a.x = fmaf(pr[j], v0.x, a.x);
+        a.y = fmaf(pr[j], v0.y, a.y);
+        c.x = fmaf(pr[j + 1], v1.x, c.x);
+        c.y = fmaf(pr[j + 1], v1.y, c.y);
       }
-      for (; j < nn; ++j) a0 = fmaf(pr[j], v_s[(size_t)j * hd + d], a0);
-      st_tag1(p.part_acc + ((int64_t)(g * Gq + h) * nsp + sp) * hd + d, (a0 + a1) + (a2 + a3), ep);
+      if (j < nn) {
+        const float2 v0 = *reinterpret_cast<const float2*>(v_s + (size_t)j * hd + d);
+        a.x = fmaf(pr[j], v0.x, a.x);
+        a.y = fmaf(pr[j], v0.y, a.y);
+      }
+      st_tag2(p.part_acc + ((int64_t)(g * Gq + h) * nsp + sp) * hd + d, a.x + c.x, a.y + c.y, ep);
     }
     mk_mark(p, phase, 6);
     if (slot >= 0 && lane == 0) mbar_arrive(&empty[slot]);  // K and V rows consumed
