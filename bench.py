@@ -606,8 +606,11 @@ def run_target_gemv(torch, ops, weights, scales, x, R, K, sp, stream_gbs):
 def run_lm_head(args, torch, ops, dist, rank, world, sp, barrier, max_over_ranks):
     """Config 5(i): the LM-head shape, one Q8 GEMV of N = 128256 rows and
     K = 8192 (1.05 GB of codes), rows sharded over the N GPUs and the output
-    slices all-gathered (NCCL) every step.  Weights are generated on the
-    device, each GPU its own rows of the same seeded matrix."""
+    slices all-gathered every step: at N > 1 both by the tensor-core GEMV
+    itself (xpu_matvec_q8_stack_allgather_dev, outputs mapped over CUDA IPC;
+    the line's figure) and, for comparison, by the library default GEMV then
+    one NCCL all-gather.  Weights are generated on the device, each GPU its
+    own rows of the same seeded matrix."""
     from xpuops.synth import tensor_seed
 
     N, K = 128256, 8192
@@ -630,23 +633,58 @@ def run_lm_head(args, torch, ops, dist, rank, world, sp, barrier, max_over_ranks
         if world > 1:
             dist.all_gather_into_tensor(y_full, y)
 
-    for _ in range(5):
-        step()
-    barrier()
-    steps = max(20, args.steps // 4)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
-    barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1)) / steps
+    def timed(fn):
+        for _ in range(5):
+            fn()
+        barrier()
+        steps = max(20, args.steps // 4)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        barrier()
+        return steps, max_over_ranks(e0.elapsed_time(e1)) / steps
+
     byts = algorithmic_bytes(R, K, 1) * world
-    del w, s
-    return {"workload": f"matvecQ8 LM head [{N} x {K}], rows sharded over {world} GPU(s)"
+    steps, ms = timed(step)
+    nccl = {"workload": f"matvecQ8 LM head [{N} x {K}], rows sharded over {world} GPU(s)"
                         + (", NCCL all-gather of y every step" if world > 1 else ""),
             "steps": steps, "ms_per_step": round(ms, 4), "GBs": round(byts / (ms / 1e3) / 1e9, 1),
             "rows_per_gpu": R, "kernel": "mv_tc_kernel" if tensor_cores_serve(1, R, K) else "mv_bulk_kernel"}
+    if world == 1:
+        del w, s
+        return nccl
+    # The all-gather fused into the tensor-core GEMV: two output buffers in
+    # turn and a flag array of its own, mapped into every rank.
+    outs = [ops.DeviceBuffer(4 * N) for _ in range(2)]
+    flags = ops.DeviceBuffer(4 * world)
+    flags.upload(np.zeros(world, np.uint32))
+    every = [None] * world
+    dist.all_gather_object(every, [ops.ipcHandle(o) for o in outs] + [ops.ipcHandle(flags)])
+    maps = [[ops.ipcOpen(h) for h in every[r]] if r != rank else [o.ptr for o in outs] + [flags.ptr]
+            for r in range(world)]
+    state = {"epoch": 0}
+
+    def fused_step():
+        state["epoch"] += 1
+        b = state["epoch"] % 2
+        ops.matvecQ8StackAllGather_dev(w, R * W, s, x, 1, R, K, rank, world, [maps[r][b] for r in range(world)],
+                                       [maps[r][2] for r in range(world)], state["epoch"], sp)
+
+    fsteps, fms = timed(fused_step)
+    torch.cuda.synchronize()
+    dist.barrier()  # no rank still writes into a mapped output
+    for r in range(world):
+        if r != rank:
+            for ptr in maps[r]:
+                ops.ipcClose(ptr)
+    dist.barrier()
+    del w, s
+    return {"workload": f"matvecQ8 LM head [{N} x {K}], rows sharded over {world} GPU(s), the all-gather fused into "
+                        "the tensor-core GEMV (every row stored into every GPU's output over NVLink)",
+            "steps": fsteps, "ms_per_step": round(fms, 4), "GBs": round(byts / (fms / 1e3) / 1e9, 1),
+            "rows_per_gpu": R, "kernel": "mv_tc_kernel", "nccl_gather": nccl}
 
 
 def run_quantize(torch, ops, sp):
